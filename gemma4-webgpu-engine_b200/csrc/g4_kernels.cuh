@@ -1,0 +1,135 @@
+// g4_kernels.cuh -- launch interface of the sm_100a kernels (internal to libgemma4_cuda.so).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace g4 {
+
+// Activation prologue a quantized linear applies before snapping its input to int8 codes.
+enum Prologue : int {
+  PRO_X = 0,        // x = src
+  PRO_NORM = 1,     // x = norm(src) * g1
+  PRO_JOIN = 2,     // h = (res + norm(src) * g1) * alpha -> hidden_out; x = norm(h) * g2
+  PRO_NORMRES = 3,  // h = res + norm(src) * g1 -> hidden_out; x = h
+  PRO_GELU = 4,     // x = gelu(src) * up[up_off + k]
+};
+
+struct GemvSeg {
+  const uint8_t *w;    // packed codes, row-major [N, K * bits / 8]
+  const uint16_t *s;   // f16 row scales [N]
+  float *y;            // [cols, N]
+  int32_t *acc_out;    // optional exact accumulators [cols, N]
+  int N;
+  int block_begin;     // first block index of this segment in the launch
+  float in_scale, out_scale;
+};
+
+struct GemvArgs {
+  GemvSeg seg[3];
+  int nseg;
+  int K;
+  int cols;
+  int rpw;             // rows per warp (block = 8 warps)
+  int ppr;             // 512-byte pieces per row
+  int pro;
+  const float *src; int ld_src;
+  const float *res; int ld_res;
+  const float *g1; const float *g2; float alpha; float eps;
+  float *hidden_out;   // PRO_JOIN / PRO_NORMRES: written by block 0, ld = ld_res
+  const float *up; int ld_up; int up_off;
+  // lm_head epilogue: softcap, optional logits store, per-block argmax partials
+  int head;
+  float softcap;
+  float *logits; int ld_logits;
+  float *part_val; int32_t *part_idx; int n_blocks_total;
+};
+
+// Choose rows per warp / pieces per row for a shape; returns 0 if unsupported.
+bool gemv_geometry(int bits, int K, int N_total, int *rpw, int *ppr);
+cudaError_t launch_gemv(const GemvArgs &a, int bits, int n_blocks, cudaStream_t st, bool pdl);
+
+// Per-column step addressing shared by the embed, attention and head kernels.
+struct ColRefs {
+  const int32_t *seq;   // sequence slot per column (nullable: 0)
+  const int32_t *pos;   // absolute position per column (nullable: pos_base + c)
+  int pos_base;
+};
+
+cudaError_t launch_embed(const int32_t *tokens, int cols, const uint8_t *embed_w,
+                         const uint16_t *embed_s, float embed_scale, const uint8_t *const *ple_slices,
+                         int ple_rows_per_slice, const uint16_t *ple_s, int H, int ple_cols,
+                         int ple_group, float *residual, float *ple_id, cudaStream_t st, bool pdl);
+
+cudaError_t launch_embed_op(const uint8_t *codes, const uint16_t *scales, const int32_t *ids,
+                            float *dst, int slots, int cols, int group, float out_scale,
+                            int slice_start, int slice_rows, cudaStream_t st, bool pdl);
+
+cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K,
+                              int cols, float alpha, cudaStream_t st, bool pdl);
+
+cudaError_t launch_ple_combine(const float *proj, const float *identity, const float *gain,
+                               float *out, int cols, int groups, int group_dim, float eps,
+                               float scale, cudaStream_t st, bool pdl);
+
+struct AttnPro {
+  int cols, heads, hd;
+  const float *q; int q_ld;          // [cols, q_ld], head h at h * hd
+  const float *k; const float *v; int kv_ld;  // nullable: no KV store
+  const float *qgain; const float *kgain;
+  const float *cos_tab; const float *sin_tab;  // [rows, hd / 2]
+  const int32_t *tab_row;            // nullable: row = c
+  float *qr;                         // [cols, heads * hd]
+  int rows_per_col_tab;              // op use: q rows per table row (engine: 1 column = 1 row)
+  float *cache; size_t seq_stride;   // packed [2, max_ctx, hd] per sequence
+  int max_ctx;
+  ColRefs refs;
+  float eps;
+};
+cudaError_t launch_attn_prologue(const AttnPro &a, cudaStream_t st, bool pdl);
+
+struct AttnArgs {
+  int cols, heads, hd, window, max_ctx;
+  int kv_cap;                        // > 0: attend j < kv_cap as well as j <= p
+  const float *qr;                   // [cols, heads * hd]
+  const float *cache; size_t seq_stride;
+  ColRefs refs;
+  int max_blocks;                    // partial slots per column
+  float *part_o; float *part_m; float *part_l;
+  float *out;                        // [cols, heads * hd]
+};
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
+
+// Decode chain: position[c] += 1 after a step (its argmax already sits in the token slot).
+cudaError_t launch_advance(int32_t *pos, int cols, cudaStream_t st, bool pdl);
+
+cudaError_t launch_argmax_final(const float *part_val, const int32_t *part_idx, int n_parts,
+                                int cols, int32_t *token_dev, int32_t *token_out,
+                                float *value_out, cudaStream_t st, bool pdl);
+
+// Standalone norm / elementwise kernels (operator API).
+cudaError_t launch_rms_norm(const float *src, const float *gain, float *dst, int rows, int width,
+                            float eps, cudaStream_t st);
+cudaError_t launch_norm_residual(const float *src, const float *gain, const float *res,
+                                 float *dst, int rows, int width, float eps, cudaStream_t st);
+cudaError_t launch_norm_residual_norm(const float *src, const float *gain, const float *res,
+                                      const float *gain2, float alpha, float *hidden, float *dst,
+                                      int rows, int width, float eps, cudaStream_t st);
+cudaError_t launch_gelu_mul(const float *gate, const float *up, float *dst, int n, float srq,
+                            cudaStream_t st);
+cudaError_t launch_softcap_partials(const float *logits, float *capped, int n, float cap,
+                                    float *part_val, int32_t *part_idx, int n_parts,
+                                    cudaStream_t st);
+cudaError_t launch_math_probe(const float *x, float *e, float *t, float *ce, float *ct, int n,
+                              cudaStream_t st);
+
+// Synthetic weight generators (counter hash of seed, tensor stream and element index).
+cudaError_t launch_gen_words(uint32_t *dst, size_t n_words, uint64_t key, size_t index0,
+                             cudaStream_t st);
+cudaError_t launch_gen_f16(uint16_t *dst, size_t n, uint64_t key, double lo, double hi,
+                           cudaStream_t st);
+cudaError_t launch_gen_bf16_f32(float *dst, size_t n, uint64_t key, double lo, double hi,
+                                cudaStream_t st);
+cudaError_t launch_gen_plmp(uint16_t *dst, size_t n, uint64_t key, double amp, cudaStream_t st);
+
+}  // namespace g4

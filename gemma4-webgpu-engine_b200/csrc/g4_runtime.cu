@@ -1,0 +1,1439 @@
+// g4_runtime.cu -- context, weights, executor and C ABI of libgemma4_cuda.so.
+//
+// The executor replaces src/execute.ts (resolveStep), src/runtime.ts (GpuExecutor encode and
+// submit), src/buffers.ts (slot and weight buffers), src/kv.ts (cache layout) and
+// src/tableSplit.ts (PLE vocab-row slices). Steps are recorded once per (columns, layer range,
+// head) into CUDA graphs instead of being re-encoded per token (src/runtime.ts:702-770).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/g4.h"
+#include "g4_device.cuh"
+#include "g4_kernels.cuh"
+
+using namespace g4;
+
+// ================================================================================ errors
+
+static thread_local std::string tl_error;
+
+struct Linear {
+  uint8_t *w = nullptr;
+  uint16_t *s = nullptr;
+  int N = 0, K = 0, bits = 4;
+  float in_scale = 0, out_scale = 0;
+  std::string module;
+};
+
+struct Layer {
+  int hd = 256;
+  bool global = false, producer = false;
+  int cache_layer = 0;
+  Linear q, k, v, o, gate, up, down, pleg, plep;
+  float *ln_in, *ln_post_attn, *ln_pre_ffn, *ln_post_ffn, *ln_post_ple, *q_norm, *k_norm;
+  float layer_scalar = 1.0f;
+};
+
+struct TensorRef {
+  void *ptr;
+  uint64_t bytes;
+  bool sliced;  // the PLE code table split into vocab-row slices
+};
+
+struct GraphKey {
+  int cols, layers, head, advance;
+  bool operator<(const GraphKey &o) const {
+    return std::tie(cols, layers, head, advance) < std::tie(o.cols, o.layers, o.head, o.advance);
+  }
+};
+
+struct g4_ctx {
+  int dev = 0;
+  cudaStream_t st = nullptr;
+  g4_config cfg;
+  std::string err;
+  int H = 0, V = 0, PD = 0, NL = 0, ple_cols = 0, ffn = 0, maxc = 0, head_cols = 0;
+  // weights
+  void *arena = nullptr;
+  size_t arena_bytes = 0, arena_used = 0;
+  std::vector<void *> ple_slices;
+  uint8_t **d_ple_slices = nullptr;
+  int ple_rps = 0;
+  uint64_t ple_slice_bytes = 0;
+  std::vector<Layer> layers;
+  uint8_t *embed_w = nullptr;
+  uint16_t *embed_s = nullptr, *ple_s = nullptr, *plmp_w = nullptr;
+  float *plmp_norm = nullptr, *final_norm = nullptr;
+  Linear lm;
+  std::map<std::string, TensorRef> tensors;
+  bool weights_ready = false;
+  // KV caches, per producer layer [max_seqs][2][max_ctx][hd]
+  std::vector<float *> kv;
+  std::vector<size_t> kv_stride;
+  std::vector<int32_t> kv_len;
+  uint64_t kv_bytes = 0;
+  // rope tables [max_ctx][pairs]
+  float *cos_s = nullptr, *sin_s = nullptr, *cos_g = nullptr, *sin_g = nullptr;
+  // activations
+  float *res[2] = {nullptr, nullptr};
+  float *ple_id, *ple_proj, *ple_in, *q, *k, *v, *qr, *attn, *proj, *gate, *up, *pleg_out;
+  float *part_o, *part_m, *part_l;
+  int att_blocks_sliding = 0, att_blocks_global = 0;
+  float *logits = nullptr;
+  float *head_pv = nullptr;
+  int32_t *head_pi = nullptr;
+  int head_blocks = 0;
+  int32_t *d_step = nullptr;   // [3][maxc]: seq, pos, token
+  int32_t *d_tok_out = nullptr;
+  float *d_val_out = nullptr;
+  int32_t *h_step = nullptr;   // pinned mirror of d_step
+  int32_t *h_tok = nullptr;    // pinned token outputs
+  uint64_t other_bytes = 0;
+  std::map<GraphKey, cudaGraphExec_t> graphs;
+  int launches = 0;
+  int last_cols = 0;
+  int staged_cols = 0;
+  std::vector<int32_t> staged_seq, staged_pos;
+  int prologue_graphs = 0;
+};
+
+static int fail(g4_ctx *c, int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  tl_error = buf;
+  return code;
+}
+
+#define CK(call)                                                                          \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess)                                                                \
+      return fail(ctx, e_ == cudaErrorMemoryAllocation ? G4_ERR_OOM : G4_ERR_CUDA,        \
+                  "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+  } while (0)
+
+extern "C" const char *g4_last_error(const g4_ctx *ctx) {
+  return ctx ? ctx->err.c_str() : tl_error.c_str();
+}
+
+extern "C" const char *g4_version(void) { return "gemma4_cuda 0.1 sm_100a"; }
+
+// ========================================================================== configuration
+
+extern "C" int g4_arch_default(g4_arch *a) {
+  if (!a) return fail(nullptr, G4_ERR_INVALID, "g4_arch_default: null arch");
+  memset(a, 0, sizeof(*a));
+  a->layer_count = 35;
+  a->hidden_size = 1536;
+  a->query_heads = 8;
+  a->kv_heads = 1;
+  a->sliding_head_dim = 256;
+  a->global_head_dim = 512;
+  a->global_layer_mask = (1ull << 4) | (1ull << 9) | (1ull << 14) | (1ull << 19) | (1ull << 24) |
+                         (1ull << 29) | (1ull << 34);
+  a->sliding_window = 512;
+  a->kv_producer_layers = 15;
+  a->producer_intermediate = 6144;
+  a->consumer_intermediate = 6144;
+  a->vocab_size = 262144;
+  a->ple_dim = 256;
+  a->attn_bits = 4;
+  a->mlp_bits = 4;
+  a->ple_bits = 8;
+  a->rms_eps = 1e-6f;
+  a->final_softcap = 30.0f;
+  a->rope_theta_sliding = 1e4f;
+  a->rope_theta_global = 1e6f;
+  a->partial_rotary_factor = 0.25f;
+  return G4_OK;
+}
+
+extern "C" int g4_config_default(g4_config *cfg) {
+  if (!cfg) return fail(nullptr, G4_ERR_INVALID, "g4_config_default: null config");
+  memset(cfg, 0, sizeof(*cfg));
+  g4_arch_default(&cfg->arch);
+  cfg->max_seqs = 1;
+  cfg->max_context = 2048;
+  cfg->max_step_columns = 64;
+  cfg->use_graphs = 1;
+  cfg->ple_slice_bytes = 0;
+  return G4_OK;
+}
+
+// planTableSplit (src/tableSplit.ts:125-215).
+extern "C" int g4_plan_table_split(uint64_t rows, uint64_t row_bytes, uint64_t limit_bytes,
+                                   uint64_t slice_bytes, int32_t *n_slices,
+                                   int32_t *rows_per_slice, int32_t *last_rows) {
+  if (row_bytes == 0) return fail(nullptr, G4_ERR_INVALID, "plan_table_split: row_bytes 0");
+  uint64_t total = rows * row_bytes;
+  bool fits = total > 0 && total <= limit_bytes;
+  uint64_t cap = slice_bytes < limit_bytes ? slice_bytes : limit_bytes;
+  if (cap < 1) cap = 1;
+  uint64_t per = (fits ? limit_bytes : cap) / row_bytes;
+  if (per < 1)
+    return fail(nullptr, G4_ERR_INVALID, "plan_table_split: one row of %llu bytes exceeds the cap",
+                (unsigned long long)row_bytes);
+  uint64_t aligned = per >= 16 ? per - (per % 16) : per;
+  uint64_t ps = rows < aligned ? rows : aligned;
+  uint64_t n = ps ? (rows + ps - 1) / ps : 1;
+  if (n == 0) n = 1;
+  if (n_slices) *n_slices = (int32_t)n;
+  if (rows_per_slice) *rows_per_slice = (int32_t)ps;
+  if (last_rows) *last_rows = (int32_t)(rows - (n - 1) * ps);
+  return G4_OK;
+}
+
+static bool is_global(const g4_arch &a, int L) { return (a.global_layer_mask >> L) & 1ull; }
+
+// =============================================================================== context
+
+static void *arena_take(g4_ctx *c, size_t bytes) {
+  size_t off = (c->arena_used + 255) & ~(size_t)255;
+  if (off + bytes > c->arena_bytes) return nullptr;
+  c->arena_used = off + bytes;
+  return (uint8_t *)c->arena + off;
+}
+
+static const char *LMP = "model.language_model.";
+
+static std::string layer_name(int L, const char *suffix) {
+  return std::string(LMP) + "layers." + std::to_string(L) + "." + suffix;
+}
+
+static int make_linear(g4_ctx *ctx, Linear &lin, const std::string &module, int N, int K, int bits) {
+  lin.N = N;
+  lin.K = K;
+  lin.bits = bits;
+  lin.module = module;
+  size_t wb = (size_t)N * K * bits / 8;
+  lin.w = (uint8_t *)arena_take(ctx, wb);
+  lin.s = (uint16_t *)arena_take(ctx, (size_t)N * 2);
+  if (!lin.w || !lin.s) return fail(ctx, G4_ERR_OOM, "weight arena exhausted at %s", module.c_str());
+  ctx->tensors[module + ".weight"] = {lin.w, wb, false};
+  ctx->tensors[module + ".weight_scale"] = {lin.s, (uint64_t)N * 2, false};
+  return G4_OK;
+}
+
+static float *make_f32(g4_ctx *ctx, const std::string &name, size_t n) {
+  float *p = (float *)arena_take(ctx, n * 4);
+  if (p) ctx->tensors[name] = {p, n * 4, false};
+  return p;
+}
+
+static size_t weight_arena_bytes(const g4_arch &a) {
+  size_t H = a.hidden_size, total = 0;
+  auto lin = [&](size_t N, size_t K, int bits) { total += ((N * K * bits / 8 + 255) & ~255ull) + ((N * 2 + 255) & ~255ull); };
+  for (int L = 0; L < a.layer_count; L++) {
+    size_t hd = is_global(a, L) ? a.global_head_dim : a.sliding_head_dim;
+    bool prod = L < a.kv_producer_layers;
+    size_t ffn = prod ? a.producer_intermediate : a.consumer_intermediate;
+    lin(a.query_heads * hd, H, 4);
+    if (prod) {
+      lin(hd, H, 4);
+      lin(hd, H, 4);
+    }
+    lin(H, a.query_heads * hd, 4);
+    lin(ffn, H, 4);
+    lin(ffn, H, 4);
+    lin(H, ffn, 4);
+    lin(a.ple_dim, H, 8);
+    lin(H, a.ple_dim, 8);
+    total += 5 * ((H * 4 + 255) & ~255ull) + 2 * ((hd * 4 + 255) & ~255ull);
+  }
+  size_t V = a.vocab_size, ple_cols = (size_t)a.layer_count * a.ple_dim;
+  total += V * H / 2 + 256 + V * 2 + 256;                 // embed (tied lm_head)
+  total += V * a.layer_count * 2 + 256;                    // PLE scales
+  total += ple_cols * H * 2 + 256;                         // PLMP bf16
+  total += a.ple_dim * 4 + 256 + H * 4 + 256;              // norms
+  return total + (1 << 20);
+}
+
+static int alloc_weights(g4_ctx *ctx) {
+  const g4_arch &a = ctx->cfg.arch;
+  ctx->arena_bytes = weight_arena_bytes(a);
+  CK(cudaMalloc(&ctx->arena, ctx->arena_bytes));
+  ctx->arena_used = 0;
+  const int H = ctx->H;
+  ctx->layers.assign(a.layer_count, Layer());
+  for (int L = 0; L < a.layer_count; L++) {
+    Layer &ly = ctx->layers[L];
+    ly.global = is_global(a, L);
+    ly.producer = L < a.kv_producer_layers;
+    ly.hd = ly.global ? a.global_head_dim : a.sliding_head_dim;
+    int ffn = ly.producer ? a.producer_intermediate : a.consumer_intermediate;
+    int qrows = a.query_heads * ly.hd;
+    int rc;
+    if ((rc = make_linear(ctx, ly.q, layer_name(L, "self_attn.q_proj"), qrows, H, 4))) return rc;
+    if (ly.producer) {
+      if ((rc = make_linear(ctx, ly.k, layer_name(L, "self_attn.k_proj"), ly.hd, H, 4))) return rc;
+      if ((rc = make_linear(ctx, ly.v, layer_name(L, "self_attn.v_proj"), ly.hd, H, 4))) return rc;
+    }
+    if ((rc = make_linear(ctx, ly.o, layer_name(L, "self_attn.o_proj"), H, qrows, 4))) return rc;
+    if ((rc = make_linear(ctx, ly.gate, layer_name(L, "mlp.gate_proj"), ffn, H, 4))) return rc;
+    if ((rc = make_linear(ctx, ly.up, layer_name(L, "mlp.up_proj"), ffn, H, 4))) return rc;
+    if ((rc = make_linear(ctx, ly.down, layer_name(L, "mlp.down_proj"), H, ffn, 4))) return rc;
+    if ((rc = make_linear(ctx, ly.pleg, layer_name(L, "per_layer_input_gate"), a.ple_dim, H, 8))) return rc;
+    if ((rc = make_linear(ctx, ly.plep, layer_name(L, "per_layer_projection"), H, a.ple_dim, 8))) return rc;
+    ly.ln_in = make_f32(ctx, layer_name(L, "input_layernorm.weight"), H);
+    ly.ln_post_attn = make_f32(ctx, layer_name(L, "post_attention_layernorm.weight"), H);
+    ly.ln_pre_ffn = make_f32(ctx, layer_name(L, "pre_feedforward_layernorm.weight"), H);
+    ly.ln_post_ffn = make_f32(ctx, layer_name(L, "post_feedforward_layernorm.weight"), H);
+    ly.ln_post_ple = make_f32(ctx, layer_name(L, "post_per_layer_input_norm.weight"), H);
+    ly.q_norm = make_f32(ctx, layer_name(L, "self_attn.q_norm.weight"), ly.hd);
+    ly.k_norm = make_f32(ctx, layer_name(L, "self_attn.k_norm.weight"), ly.hd);
+    if (!ly.ln_in || !ly.ln_post_attn || !ly.ln_pre_ffn || !ly.ln_post_ffn || !ly.ln_post_ple ||
+        !ly.q_norm || !ly.k_norm)
+      return fail(ctx, G4_ERR_OOM, "weight arena exhausted at layer %d norms", L);
+    // kvRoleForLayer (src/kv.ts:76-88): consumers read the last producer of their type.
+    if (ly.producer) {
+      ly.cache_layer = L;
+    } else {
+      int last = -1;
+      for (int p = 0; p < a.kv_producer_layers; p++)
+        if (is_global(a, p) == ly.global) last = p;
+      ly.cache_layer = last;
+    }
+  }
+  size_t V = ctx->V;
+  ctx->embed_w = (uint8_t *)arena_take(ctx, V * H / 2);
+  ctx->embed_s = (uint16_t *)arena_take(ctx, V * 2);
+  ctx->ple_s = (uint16_t *)arena_take(ctx, V * ctx->NL * 2);
+  ctx->plmp_w = (uint16_t *)arena_take(ctx, (size_t)ctx->ple_cols * H * 2);
+  ctx->plmp_norm = make_f32(ctx, std::string(LMP) + "per_layer_projection_norm.weight", ctx->PD);
+  ctx->final_norm = make_f32(ctx, std::string(LMP) + "norm.weight", H);
+  if (!ctx->embed_w || !ctx->embed_s || !ctx->ple_s || !ctx->plmp_w || !ctx->plmp_norm || !ctx->final_norm)
+    return fail(ctx, G4_ERR_OOM, "weight arena exhausted at the embedding tables");
+  ctx->tensors[std::string(LMP) + "embed_tokens.embedding_quantized"] = {ctx->embed_w, V * H / 2, false};
+  ctx->tensors[std::string(LMP) + "embed_tokens.embedding_scale"] = {ctx->embed_s, V * 2, false};
+  ctx->tensors[std::string(LMP) + "embed_tokens_per_layer.embedding_scale"] = {ctx->ple_s, V * ctx->NL * 2, false};
+  ctx->tensors[std::string(LMP) + "per_layer_model_projection.weight"] = {ctx->plmp_w, (uint64_t)ctx->ple_cols * H * 2, false};
+  // lm_head is tied to embed_tokens (src/execute.ts:207-214).
+  ctx->lm.w = ctx->embed_w;
+  ctx->lm.s = ctx->embed_s;
+  ctx->lm.N = ctx->V;
+  ctx->lm.K = H;
+  ctx->lm.bits = 4;
+  ctx->lm.module = "lm_head";
+  // The PLE code table: one buffer or vocab-row slices (src/tableSplit.ts:125-215).
+  const uint64_t row_bytes = (uint64_t)ctx->ple_cols / 2;
+  const uint64_t total = row_bytes * V;
+  int32_t n = 1, rps = ctx->V, last = ctx->V;
+  if (ctx->cfg.ple_slice_bytes > 0) {
+    int rc = g4_plan_table_split(V, row_bytes, ctx->cfg.ple_slice_bytes, ctx->cfg.ple_slice_bytes, &n, &rps, &last);
+    if (rc) return fail(ctx, rc, "%s", tl_error.c_str());
+  }
+  ctx->ple_rps = rps;
+  ctx->ple_slices.assign(n, nullptr);
+  for (int i = 0; i < n; i++) {
+    size_t rows = i + 1 < n ? (size_t)rps : (size_t)last;
+    CK(cudaMalloc(&ctx->ple_slices[i], rows * row_bytes));
+  }
+  CK(cudaMalloc(&ctx->d_ple_slices, sizeof(uint8_t *) * n));
+  CK(cudaMemcpy(ctx->d_ple_slices, ctx->ple_slices.data(), sizeof(uint8_t *) * n, cudaMemcpyHostToDevice));
+  ctx->ple_slice_bytes = total;
+  ctx->tensors[std::string(LMP) + "embed_tokens_per_layer.embedding_quantized"] = {nullptr, total, true};
+  return G4_OK;
+}
+
+static int alloc_runtime(g4_ctx *ctx) {
+  const g4_arch &a = ctx->cfg.arch;
+  const int maxc = ctx->maxc, H = ctx->H, mctx = ctx->cfg.max_context;
+  // KV caches.
+  ctx->kv.assign(a.kv_producer_layers, nullptr);
+  ctx->kv_stride.assign(a.kv_producer_layers, 0);
+  for (int L = 0; L < a.kv_producer_layers; L++) {
+    size_t hd = ctx->layers[L].hd;
+    ctx->kv_stride[L] = 2 * (size_t)mctx * hd;
+    size_t bytes = ctx->kv_stride[L] * ctx->cfg.max_seqs * 4;
+    CK(cudaMalloc(&ctx->kv[L], bytes));
+    CK(cudaMemset(ctx->kv[L], 0, bytes));
+    ctx->kv_bytes += bytes;
+  }
+  ctx->kv_len.assign(ctx->cfg.max_seqs, 0);
+  // Rope tables (ropeTables, src/kernels/rope.ts:149-191), f64 on the host, f32 on the device.
+  auto tables = [&](int hd, int rot_pairs, double theta, float **cd, float **sd) -> int {
+    int pairs = hd / 2;
+    std::vector<float> cs((size_t)mctx * pairs), sn((size_t)mctx * pairs);
+    for (int p = 0; p < mctx; p++)
+      for (int i = 0; i < pairs; i++) {
+        double inv = i < rot_pairs ? std::pow(theta, (-2.0 * i) / (double)hd) : 0.0;
+        double ang = (double)p * inv;
+        cs[(size_t)p * pairs + i] = (float)std::cos(ang);
+        sn[(size_t)p * pairs + i] = (float)std::sin(ang);
+      }
+    CK(cudaMalloc(cd, cs.size() * 4));
+    CK(cudaMalloc(sd, sn.size() * 4));
+    CK(cudaMemcpy(*cd, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(*sd, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    ctx->other_bytes += cs.size() * 8;
+    return G4_OK;
+  };
+  int rc;
+  if ((rc = tables(a.sliding_head_dim, a.sliding_head_dim / 2, (double)a.rope_theta_sliding, &ctx->cos_s, &ctx->sin_s))) return rc;
+  int grot = (int)(a.partial_rotary_factor * a.global_head_dim / 2);
+  if ((rc = tables(a.global_head_dim, grot, (double)a.rope_theta_global, &ctx->cos_g, &ctx->sin_g))) return rc;
+  // Activation slots, sized once for the widest step (src/execute.ts:248-317).
+  const size_t ghd = a.global_head_dim, nh = a.query_heads, ffn = std::max(a.producer_intermediate, a.consumer_intermediate);
+  auto take = [&](float **p, size_t n) -> int {
+    CK(cudaMalloc(p, n * 4));
+    CK(cudaMemset(*p, 0, n * 4));
+    ctx->other_bytes += n * 4;
+    return G4_OK;
+  };
+  if ((rc = take(&ctx->res[0], (size_t)maxc * H))) return rc;
+  if ((rc = take(&ctx->res[1], (size_t)maxc * H))) return rc;
+  if ((rc = take(&ctx->ple_id, (size_t)maxc * ctx->ple_cols))) return rc;
+  if ((rc = take(&ctx->ple_proj, (size_t)maxc * ctx->ple_cols))) return rc;
+  if ((rc = take(&ctx->ple_in, (size_t)maxc * ctx->ple_cols))) return rc;
+  if ((rc = take(&ctx->q, (size_t)maxc * nh * ghd))) return rc;
+  if ((rc = take(&ctx->k, (size_t)maxc * ghd))) return rc;
+  if ((rc = take(&ctx->v, (size_t)maxc * ghd))) return rc;
+  if ((rc = take(&ctx->qr, (size_t)maxc * nh * ghd))) return rc;
+  if ((rc = take(&ctx->attn, (size_t)maxc * nh * ghd))) return rc;
+  if ((rc = take(&ctx->proj, (size_t)maxc * H))) return rc;
+  if ((rc = take(&ctx->gate, (size_t)maxc * ffn))) return rc;
+  if ((rc = take(&ctx->up, (size_t)maxc * ffn))) return rc;
+  if ((rc = take(&ctx->pleg_out, (size_t)maxc * a.ple_dim))) return rc;
+  ctx->att_blocks_sliding = (a.sliding_window + 63) / 64 + 1;
+  ctx->att_blocks_global = (mctx + 63) / 64;
+  int mb = std::max(ctx->att_blocks_sliding, ctx->att_blocks_global);
+  if ((rc = take(&ctx->part_o, (size_t)maxc * mb * nh * ghd))) return rc;
+  if ((rc = take(&ctx->part_m, (size_t)maxc * mb * nh))) return rc;
+  if ((rc = take(&ctx->part_l, (size_t)maxc * mb * nh))) return rc;
+  ctx->head_cols = std::min(maxc, std::max(ctx->cfg.max_seqs, 1));
+  if ((rc = take(&ctx->logits, (size_t)ctx->head_cols * ctx->V))) return rc;
+  int rpw, ppr;
+  gemv_geometry(4, H, ctx->V, &rpw, &ppr);
+  ctx->head_blocks = (ctx->V + 8 * rpw - 1) / (8 * rpw);
+  if ((rc = take(&ctx->head_pv, (size_t)ctx->head_cols * ctx->head_blocks))) return rc;
+  CK(cudaMalloc(&ctx->head_pi, (size_t)ctx->head_cols * ctx->head_blocks * 4));
+  CK(cudaMalloc(&ctx->d_step, (size_t)3 * maxc * 4));
+  CK(cudaMemset(ctx->d_step, 0, (size_t)3 * maxc * 4));
+  CK(cudaMalloc(&ctx->d_tok_out, (size_t)maxc * 4));
+  CK(cudaMalloc(&ctx->d_val_out, (size_t)maxc * 4));
+  CK(cudaMallocHost(&ctx->h_step, (size_t)3 * maxc * 4));
+  CK(cudaMallocHost(&ctx->h_tok, (size_t)maxc * 4));
+  return G4_OK;
+}
+
+extern "C" int g4_ctx_create(int cuda_device, const g4_config *cfg_in, g4_ctx **out) {
+  if (!out) return fail(nullptr, G4_ERR_INVALID, "g4_ctx_create: null out");
+  *out = nullptr;
+  g4_config cfg;
+  if (cfg_in) cfg = *cfg_in; else g4_config_default(&cfg);
+  const g4_arch &a = cfg.arch;
+  if (a.kv_heads != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "only one KV head is supported");
+  if (a.query_heads != 8) return fail(nullptr, G4_ERR_UNSUPPORTED, "the attention kernels are built for 8 query heads");
+  if (a.attn_bits != 4 || a.mlp_bits != 4 || a.ple_bits != 8)
+    return fail(nullptr, G4_ERR_UNSUPPORTED, "weight widths attn 4 / mlp 4 / ple 8 only (2-bit families are not built)");
+  if (a.hidden_size % 256 != 0 || a.hidden_size > 2048)
+    return fail(nullptr, G4_ERR_UNSUPPORTED, "hidden size must be a multiple of 256 up to 2048");
+  if ((a.sliding_head_dim != 256 && a.sliding_head_dim != 512) || (a.global_head_dim != 256 && a.global_head_dim != 512))
+    return fail(nullptr, G4_ERR_UNSUPPORTED, "head dims 256 or 512 only");
+  if (a.ple_dim % 256 != 0 || a.layer_count > 64 || a.kv_producer_layers < 1 || a.kv_producer_layers > a.layer_count)
+    return fail(nullptr, G4_ERR_INVALID, "bad PLE or layer geometry");
+  if (cfg.max_seqs < 1 || cfg.max_context < 1 || cfg.max_step_columns < 1)
+    return fail(nullptr, G4_ERR_INVALID, "max_seqs, max_context and max_step_columns must be positive");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || cuda_device < 0 || cuda_device >= ndev)
+    return fail(nullptr, G4_ERR_CUDA, "CUDA device %d is not available", cuda_device);
+  g4_ctx *ctx = new g4_ctx();
+  ctx->dev = cuda_device;
+  ctx->cfg = cfg;
+  ctx->H = a.hidden_size;
+  ctx->V = a.vocab_size;
+  ctx->PD = a.ple_dim;
+  ctx->NL = a.layer_count;
+  ctx->ple_cols = a.layer_count * a.ple_dim;
+  ctx->ffn = std::max(a.producer_intermediate, a.consumer_intermediate);
+  ctx->maxc = cfg.max_step_columns;
+  int rc = G4_OK;
+  if (cudaSetDevice(cuda_device) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking) != cudaSuccess) {
+    rc = fail(ctx, G4_ERR_CUDA, "cannot initialise device %d", cuda_device);
+  }
+  if (!rc) rc = alloc_weights(ctx);
+  if (!rc) rc = alloc_runtime(ctx);
+  if (rc) {
+    std::string msg = ctx->err;
+    g4_ctx_destroy(ctx);
+    return fail(nullptr, rc, "%s", msg.c_str());
+  }
+  *out = ctx;
+  return G4_OK;
+}
+
+extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->dev);
+  if (ctx->st) cudaStreamSynchronize(ctx->st);
+  for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
+  cudaFree(ctx->arena);
+  for (void *p : ctx->ple_slices) cudaFree(p);
+  cudaFree(ctx->d_ple_slices);
+  for (float *p : ctx->kv) cudaFree(p);
+  float *fs[] = {ctx->cos_s, ctx->sin_s, ctx->cos_g, ctx->sin_g, ctx->res[0], ctx->res[1],
+                 ctx->ple_id, ctx->ple_proj, ctx->ple_in, ctx->q, ctx->k, ctx->v, ctx->qr,
+                 ctx->attn, ctx->proj, ctx->gate, ctx->up, ctx->pleg_out, ctx->part_o,
+                 ctx->part_m, ctx->part_l, ctx->logits, ctx->head_pv, ctx->d_val_out};
+  for (float *p : fs) cudaFree(p);
+  cudaFree(ctx->head_pi);
+  cudaFree(ctx->d_step);
+  cudaFree(ctx->d_tok_out);
+  cudaFreeHost(ctx->h_step);
+  cudaFreeHost(ctx->h_tok);
+  if (ctx->st) cudaStreamDestroy(ctx->st);
+  delete ctx;
+}
+
+extern "C" int g4_ctx_memory(const g4_ctx *ctx, uint64_t *w, uint64_t *kvb, uint64_t *o) {
+  if (!ctx) return fail(nullptr, G4_ERR_INVALID, "null context");
+  if (w) *w = ctx->arena_bytes + ctx->ple_slice_bytes;
+  if (kvb) *kvb = ctx->kv_bytes;
+  if (o) *o = ctx->other_bytes;
+  return G4_OK;
+}
+
+extern "C" void *g4_ctx_stream(g4_ctx *ctx) { return ctx ? (void *)ctx->st : nullptr; }
+
+extern "C" int g4_last_launches(const g4_ctx *ctx, int32_t *n) {
+  if (!ctx || !n) return fail(nullptr, G4_ERR_INVALID, "null argument");
+  *n = ctx->launches;
+  return G4_OK;
+}
+
+// ================================================================================ weights
+
+// Synthetic tensor kinds; a layer tensor's hash stream is ((layer + 1) << 8) | kind.
+enum {
+  TK_Q_W = 0, TK_Q_S, TK_K_W, TK_K_S, TK_V_W, TK_V_S, TK_O_W, TK_O_S,
+  TK_GATE_W, TK_GATE_S, TK_UP_W, TK_UP_S, TK_DOWN_W, TK_DOWN_S,
+  TK_PLEG_W, TK_PLEG_S, TK_PLEP_W, TK_PLEP_S,
+  TK_LN_IN, TK_LN_POST_ATTN, TK_LN_PRE_FFN, TK_LN_POST_FFN, TK_LN_POST_PLE,
+  TK_QNORM, TK_KNORM, TK_LAYER_SCALAR, TK_SRQ,
+  TK_EMBED_W = 40, TK_EMBED_S, TK_PLE_W, TK_PLE_S, TK_PLMP_W, TK_PLMP_NORM, TK_FINAL_NORM
+};
+enum { S_Q = 0, S_K, S_V, S_O, S_GATE, S_UP, S_DOWN, S_PLEG, S_PLEP, S_LM, N_SITES };
+// Static activation scales: max |x| / 127 of a seeded 16-token warm-up forward per site, each
+// layer's value jittered by (0.9 + 0.2 u). lm_head's output is not snapped.
+static const double SRQ_BASE_IN[N_SITES] = {0.04, 0.04, 0.04, 0.04, 0.033, 0.033, 1.0, 0.085, 0.34, 0.024};
+static const double SRQ_BASE_OUT[N_SITES] = {0.11, 0.097, 0.092, 0.2, 0.108, 0.11, 3.9, 0.225, 0.085, 0.0};
+
+static uint64_t layer_stream(int L, int kind) { return ((uint64_t)(L + 1) << 8) | (uint64_t)kind; }
+
+static float synth_srq(uint64_t seed, int L, int site, int out) {
+  double base = out ? SRQ_BASE_OUT[site] : SRQ_BASE_IN[site];
+  if (base == 0.0) return 0.0f;
+  uint64_t h = keyed(stream_key(seed, layer_stream(L, TK_SRQ)), (uint64_t)(site * 2 + out));
+  return (float)(base * (0.9 + 0.2 * unit24(h)));
+}
+
+static float bf16_round(float f) {
+  uint32_t b = (uint32_t)f32_to_bf16_bits(f) << 16;
+  float r;
+  memcpy(&r, &b, 4);
+  return r;
+}
+
+static int gen_linear(g4_ctx *ctx, Linear &lin, uint64_t seed, int L, int kw, int ks, int site) {
+  size_t wb = (size_t)lin.N * lin.K * lin.bits / 8;
+  CK(launch_gen_words((uint32_t *)lin.w, wb / 4, stream_key(seed, layer_stream(L, kw)), 0, ctx->st));
+  double div = lin.bits == 8 ? 16.0 : 1.0;
+  CK(launch_gen_f16(lin.s, (size_t)lin.N, stream_key(seed, layer_stream(L, ks)), 1e-3 / div, 1e-2 / div, ctx->st));
+  lin.in_scale = synth_srq(seed, L, site, 0);
+  lin.out_scale = synth_srq(seed, L, site, 1);
+  return G4_OK;
+}
+
+static int gen_gain(g4_ctx *ctx, float *p, size_t n, uint64_t seed, int L, int kind) {
+  CK(launch_gen_bf16_f32(p, n, stream_key(seed, layer_stream(L, kind)), 0.5, 1.5, ctx->st));
+  return G4_OK;
+}
+
+extern "C" int g4_init_random(g4_ctx *ctx, uint64_t seed) {
+  if (!ctx) return fail(nullptr, G4_ERR_INVALID, "null context");
+  CK(cudaSetDevice(ctx->dev));
+  const int H = ctx->H;
+  int rc;
+  for (int L = 0; L < ctx->NL; L++) {
+    Layer &ly = ctx->layers[L];
+    if ((rc = gen_linear(ctx, ly.q, seed, L, TK_Q_W, TK_Q_S, S_Q))) return rc;
+    if (ly.producer) {
+      if ((rc = gen_linear(ctx, ly.k, seed, L, TK_K_W, TK_K_S, S_K))) return rc;
+      if ((rc = gen_linear(ctx, ly.v, seed, L, TK_V_W, TK_V_S, S_V))) return rc;
+    }
+    if ((rc = gen_linear(ctx, ly.o, seed, L, TK_O_W, TK_O_S, S_O))) return rc;
+    if ((rc = gen_linear(ctx, ly.gate, seed, L, TK_GATE_W, TK_GATE_S, S_GATE))) return rc;
+    if ((rc = gen_linear(ctx, ly.up, seed, L, TK_UP_W, TK_UP_S, S_UP))) return rc;
+    if ((rc = gen_linear(ctx, ly.down, seed, L, TK_DOWN_W, TK_DOWN_S, S_DOWN))) return rc;
+    if ((rc = gen_linear(ctx, ly.pleg, seed, L, TK_PLEG_W, TK_PLEG_S, S_PLEG))) return rc;
+    if ((rc = gen_linear(ctx, ly.plep, seed, L, TK_PLEP_W, TK_PLEP_S, S_PLEP))) return rc;
+    if ((rc = gen_gain(ctx, ly.ln_in, H, seed, L, TK_LN_IN))) return rc;
+    if ((rc = gen_gain(ctx, ly.ln_post_attn, H, seed, L, TK_LN_POST_ATTN))) return rc;
+    if ((rc = gen_gain(ctx, ly.ln_pre_ffn, H, seed, L, TK_LN_PRE_FFN))) return rc;
+    if ((rc = gen_gain(ctx, ly.ln_post_ffn, H, seed, L, TK_LN_POST_FFN))) return rc;
+    if ((rc = gen_gain(ctx, ly.ln_post_ple, H, seed, L, TK_LN_POST_PLE))) return rc;
+    if ((rc = gen_gain(ctx, ly.q_norm, ly.hd, seed, L, TK_QNORM))) return rc;
+    if ((rc = gen_gain(ctx, ly.k_norm, ly.hd, seed, L, TK_KNORM))) return rc;
+    double u = unit24(keyed(stream_key(seed, layer_stream(L, TK_LAYER_SCALAR)), 0));
+    ly.layer_scalar = bf16_round((float)(0.03 + (0.9 - 0.03) * u));
+  }
+  const size_t V = ctx->V;
+  CK(launch_gen_words((uint32_t *)ctx->embed_w, V * H / 8, stream_key(seed, layer_stream(-1, TK_EMBED_W)), 0, ctx->st));
+  CK(launch_gen_f16(ctx->embed_s, V, stream_key(seed, layer_stream(-1, TK_EMBED_S)), 1e-3, 1e-2, ctx->st));
+  CK(launch_gen_f16(ctx->ple_s, V * ctx->NL, stream_key(seed, layer_stream(-1, TK_PLE_S)), 1e-3, 1e-2, ctx->st));
+  CK(launch_gen_plmp(ctx->plmp_w, (size_t)ctx->ple_cols * H, stream_key(seed, layer_stream(-1, TK_PLMP_W)), 0.04419417382415922, ctx->st));
+  if ((rc = gen_gain(ctx, ctx->plmp_norm, ctx->PD, seed, -1, TK_PLMP_NORM))) return rc;
+  if ((rc = gen_gain(ctx, ctx->final_norm, H, seed, -1, TK_FINAL_NORM))) return rc;
+  // The PLE table by absolute word index, into whichever slice holds the row.
+  {
+    const size_t words_per_row = (size_t)ctx->ple_cols / 8;
+    const uint64_t key = stream_key(seed, layer_stream(-1, TK_PLE_W));
+    size_t n = ctx->ple_slices.size();
+    for (size_t i = 0; i < n; i++) {
+      size_t row0 = i * (size_t)ctx->ple_rps;
+      size_t rows = std::min((size_t)ctx->ple_rps, V - row0);
+      // Each slice starts at word row0 * words_per_row of the table's counter stream.
+      uint32_t *dst = (uint32_t *)ctx->ple_slices[i];
+      size_t nw = rows * words_per_row;
+      CK(launch_gen_words(dst, nw, key, row0 * words_per_row, ctx->st));
+    }
+  }
+  ctx->lm.in_scale = synth_srq(seed, -1, S_LM, 0);
+  ctx->lm.out_scale = synth_srq(seed, -1, S_LM, 1);
+  CK(cudaStreamSynchronize(ctx->st));
+  ctx->weights_ready = true;
+  for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
+  ctx->graphs.clear();
+  return G4_OK;
+}
+
+static int find_tensor(g4_ctx *ctx, const char *name, TensorRef *ref) {
+  auto it = ctx->tensors.find(name);
+  if (it == ctx->tensors.end()) return fail(ctx, G4_ERR_NOT_FOUND, "unknown tensor %s", name);
+  *ref = it->second;
+  return G4_OK;
+}
+
+extern "C" int g4_upload_weight(g4_ctx *ctx, const char *name, const void *bytes, uint64_t offset,
+                                uint64_t n, uint64_t total) {
+  if (!ctx || !name || (!bytes && n)) return fail(ctx, G4_ERR_INVALID, "g4_upload_weight: null argument");
+  TensorRef r;
+  int rc = find_tensor(ctx, name, &r);
+  if (rc) return rc;
+  if (total != r.bytes) return fail(ctx, G4_ERR_INVALID, "%s holds %llu bytes, upload says %llu", name, (unsigned long long)r.bytes, (unsigned long long)total);
+  if (offset + n > total) return fail(ctx, G4_ERR_INVALID, "%s: bytes [%llu, %llu) past the end", name, (unsigned long long)offset, (unsigned long long)(offset + n));
+  CK(cudaSetDevice(ctx->dev));
+  if (!r.sliced) {
+    CK(cudaMemcpy((uint8_t *)r.ptr + offset, bytes, n, cudaMemcpyHostToDevice));
+  } else {
+    const uint64_t slice_bytes = (uint64_t)ctx->ple_rps * (ctx->ple_cols / 2);
+    uint64_t done = 0;
+    while (done < n) {
+      uint64_t pos = offset + done;
+      uint64_t si = pos / slice_bytes, so = pos % slice_bytes;
+      uint64_t take = std::min(n - done, slice_bytes - so);
+      CK(cudaMemcpy((uint8_t *)ctx->ple_slices[si] + so, (const uint8_t *)bytes + done, take, cudaMemcpyHostToDevice));
+      done += take;
+    }
+  }
+  ctx->weights_ready = true;
+  return G4_OK;
+}
+
+extern "C" int g4_download_weight(g4_ctx *ctx, const char *name, void *bytes, uint64_t *n) {
+  if (!ctx || !name || !n) return fail(ctx, G4_ERR_INVALID, "g4_download_weight: null argument");
+  TensorRef r;
+  int rc = find_tensor(ctx, name, &r);
+  if (rc) return rc;
+  if (!bytes || *n < r.bytes) {
+    *n = r.bytes;
+    return bytes ? fail(ctx, G4_ERR_INVALID, "%s needs %llu bytes", name, (unsigned long long)r.bytes) : G4_OK;
+  }
+  CK(cudaSetDevice(ctx->dev));
+  CK(cudaStreamSynchronize(ctx->st));
+  if (!r.sliced) {
+    CK(cudaMemcpy(bytes, r.ptr, r.bytes, cudaMemcpyDeviceToHost));
+  } else {
+    const uint64_t row_bytes = ctx->ple_cols / 2;
+    uint64_t off = 0;
+    for (size_t i = 0; i < ctx->ple_slices.size(); i++) {
+      uint64_t rows = std::min((uint64_t)ctx->ple_rps, (uint64_t)ctx->V - i * ctx->ple_rps);
+      CK(cudaMemcpy((uint8_t *)bytes + off, ctx->ple_slices[i], rows * row_bytes, cudaMemcpyDeviceToHost));
+      off += rows * row_bytes;
+    }
+  }
+  *n = r.bytes;
+  return G4_OK;
+}
+
+static Linear *linear_by_module(g4_ctx *ctx, const std::string &mod) {
+  if (mod == "lm_head") return &ctx->lm;
+  for (int L = 0; L < ctx->NL; L++) {
+    Layer &ly = ctx->layers[L];
+    Linear *all[] = {&ly.q, &ly.k, &ly.v, &ly.o, &ly.gate, &ly.up, &ly.down, &ly.pleg, &ly.plep};
+    for (Linear *l : all)
+      if (l->w && l->module == mod) return l;
+  }
+  return nullptr;
+}
+
+static bool parse_scalar(g4_ctx *ctx, const std::string &name, float **slot) {
+  static const char *sfx[] = {".input_activation_scale", ".output_activation_scale"};
+  for (int i = 0; i < 2; i++) {
+    size_t ls = strlen(sfx[i]);
+    if (name.size() > ls && name.compare(name.size() - ls, ls, sfx[i]) == 0) {
+      Linear *l = linear_by_module(ctx, name.substr(0, name.size() - ls));
+      if (!l) return false;
+      *slot = i == 0 ? &l->in_scale : &l->out_scale;
+      return true;
+    }
+  }
+  int L;
+  char tail[64];
+  if (sscanf(name.c_str(), "model.language_model.layers.%d.%63s", &L, tail) == 2 &&
+      strcmp(tail, "layer_scalar") == 0 && L >= 0 && L < ctx->NL) {
+    *slot = &ctx->layers[L].layer_scalar;
+    return true;
+  }
+  return false;
+}
+
+extern "C" int g4_set_scalar(g4_ctx *ctx, const char *name, float value) {
+  if (!ctx || !name) return fail(ctx, G4_ERR_INVALID, "g4_set_scalar: null argument");
+  float *slot;
+  if (!parse_scalar(ctx, name, &slot)) return fail(ctx, G4_ERR_NOT_FOUND, "unknown scalar %s", name);
+  *slot = value;
+  for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
+  ctx->graphs.clear();
+  return G4_OK;
+}
+
+extern "C" int g4_get_scalar(const g4_ctx *cctx, const char *name, float *value) {
+  g4_ctx *ctx = const_cast<g4_ctx *>(cctx);
+  if (!ctx || !name || !value) return fail(ctx, G4_ERR_INVALID, "g4_get_scalar: null argument");
+  float *slot;
+  if (!parse_scalar(ctx, name, &slot)) return fail(ctx, G4_ERR_NOT_FOUND, "unknown scalar %s", name);
+  *value = *slot;
+  return G4_OK;
+}
+
+// =============================================================================== executor
+
+struct Seg {
+  const Linear *lin;
+  float *y;
+};
+
+// One quantized linear launch (or several, 8 columns each) with a fused prologue.
+static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs proto,
+                      bool head = false) {
+  const Linear *l0 = segs.begin()->lin;
+  int N_total = 0;
+  for (auto &s : segs) N_total += s.lin->N;
+  int rpw, ppr;
+  if (!gemv_geometry(l0->bits, l0->K, N_total, &rpw, &ppr))
+    return fail(ctx, G4_ERR_UNSUPPORTED, "no GEMV geometry for %d-bit K %d", l0->bits, l0->K);
+  for (int c0 = 0; c0 < cols; c0 += 8) {
+    GemvArgs a = proto;
+    a.K = l0->K;
+    a.cols = std::min(8, cols - c0);
+    a.rpw = rpw;
+    a.ppr = ppr;
+    a.nseg = 0;
+    int blocks = 0;
+    for (auto &s : segs) {
+      GemvSeg &g = a.seg[a.nseg++];
+      g.w = s.lin->w;
+      g.s = s.lin->s;
+      g.y = s.y ? s.y + (size_t)c0 * s.lin->N : nullptr;
+      g.acc_out = nullptr;
+      g.N = s.lin->N;
+      g.block_begin = blocks;
+      g.in_scale = s.lin->in_scale;
+      g.out_scale = s.lin->out_scale;
+      blocks += (s.lin->N + 8 * rpw - 1) / (8 * rpw);
+    }
+    if (a.src) a.src += (size_t)c0 * a.ld_src;
+    if (a.res) a.res += (size_t)c0 * a.ld_res;
+    if (a.hidden_out) a.hidden_out += (size_t)c0 * a.ld_res;
+    if (a.up) a.up += (size_t)c0 * a.ld_up;
+    if (head) {
+      a.head = 1;
+      a.logits = ctx->logits + (size_t)c0 * ctx->V;
+      a.ld_logits = ctx->V;
+      a.part_val = ctx->head_pv + (size_t)c0 * blocks;
+      a.part_idx = ctx->head_pi + (size_t)c0 * blocks;
+      a.n_blocks_total = blocks;
+      ctx->head_blocks = blocks;
+    }
+    CK(launch_gemv(a, l0->bits, blocks, ctx->st, true));
+    ctx->launches++;
+  }
+  return G4_OK;
+}
+
+static GemvArgs pro_args(int pro) {
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.pro = pro;
+  a.alpha = 1.0f;
+  return a;
+}
+
+// Record the launches of one step: `cols` columns (already staged in d_step), layers
+// [0, n_layers), then the head when asked. Step order is planDecodeStep / planPrefillChunk
+// (src/plan.ts:487-824) with the fusions of the decode plan.
+static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false) {
+  const g4_arch &a = ctx->cfg.arch;
+  const int H = ctx->H, PD = ctx->PD;
+  const float eps = a.rms_eps;
+  int32_t *d_seq = ctx->d_step, *d_pos = ctx->d_step + ctx->maxc, *d_tok = ctx->d_step + 2 * ctx->maxc;
+  ctx->launches = 0;
+  // ---- embed phase (planEmbed, src/plan.ts:727-736)
+  CK(launch_embed(d_tok, cols, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
+                  (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H,
+                  ctx->ple_cols, PD, ctx->res[0], ctx->ple_id, ctx->st, true));
+  ctx->launches++;
+  CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, H, cols,
+                       (float)std::pow((double)H, -0.5), ctx->st, true));
+  ctx->launches += (cols + 7) / 8;
+  CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, ctx->NL, PD,
+                        eps, (float)0.7071067811865476, ctx->st, true));
+  ctx->launches++;
+  int cur = 0;
+  int rc;
+  for (int L = 0; L < n_layers; L++) {
+    Layer &ly = ctx->layers[L];
+    const int hd = ly.hd, nh = a.query_heads, qrows = nh * hd;
+    // ---- q, k, v with the input norm (layer 0) or the previous layer's tail join fused in
+    {
+      GemvArgs p;
+      if (L == 0) {
+        p = pro_args(PRO_NORM);
+        p.src = ctx->res[cur];
+        p.ld_src = H;
+        p.g1 = ly.ln_in;
+      } else {
+        Layer &pv = ctx->layers[L - 1];
+        p = pro_args(PRO_JOIN);
+        p.src = ctx->proj;
+        p.ld_src = H;
+        p.res = ctx->res[cur];
+        p.ld_res = H;
+        p.g1 = pv.ln_post_ple;
+        p.g2 = ly.ln_in;
+        p.alpha = pv.layer_scalar;
+        p.hidden_out = ctx->res[cur ^ 1];
+      }
+      p.eps = eps;
+      if (ly.producer)
+        rc = run_linear(ctx, {{&ly.q, ctx->q}, {&ly.k, ctx->k}, {&ly.v, ctx->v}}, cols, p);
+      else
+        rc = run_linear(ctx, {{&ly.q, ctx->q}}, cols, p);
+      if (rc) return rc;
+      if (L > 0) cur ^= 1;
+    }
+    // ---- attention prologue: q-norm-rope, kv-norm-rope-store (src/kernels/attnPrologue.ts)
+    {
+      AttnPro ap;
+      memset(&ap, 0, sizeof(ap));
+      ap.cols = cols;
+      ap.heads = nh;
+      ap.hd = hd;
+      ap.q = ctx->q;
+      ap.q_ld = qrows;
+      ap.k = ly.producer ? ctx->k : nullptr;
+      ap.v = ly.producer ? ctx->v : nullptr;
+      ap.kv_ld = hd;
+      ap.qgain = ly.q_norm;
+      ap.kgain = ly.k_norm;
+      ap.cos_tab = ly.global ? ctx->cos_g : ctx->cos_s;
+      ap.sin_tab = ly.global ? ctx->sin_g : ctx->sin_s;
+      ap.tab_row = d_pos;
+      ap.rows_per_col_tab = 1;
+      ap.qr = ctx->qr;
+      ap.cache = ly.producer ? ctx->kv[L] : nullptr;
+      ap.seq_stride = ly.producer ? ctx->kv_stride[L] : 0;
+      ap.max_ctx = ctx->cfg.max_context;
+      ap.refs.seq = d_seq;
+      ap.refs.pos = d_pos;
+      ap.eps = eps;
+      CK(launch_attn_prologue(ap, ctx->st, true));
+      ctx->launches++;
+    }
+    // ---- attention over the producer cache (kvRoleForLayer)
+    {
+      AttnArgs at;
+      memset(&at, 0, sizeof(at));
+      at.cols = cols;
+      at.heads = nh;
+      at.hd = hd;
+      at.window = ly.global ? 0 : a.sliding_window;
+      at.max_ctx = ctx->cfg.max_context;
+      at.kv_cap = 0;
+      at.qr = ctx->qr;
+      at.cache = ctx->kv[ly.cache_layer];
+      at.seq_stride = ctx->kv_stride[ly.cache_layer];
+      at.refs.seq = d_seq;
+      at.refs.pos = d_pos;
+      at.max_blocks = ly.global ? ctx->att_blocks_global : ctx->att_blocks_sliding;
+      at.part_o = ctx->part_o;
+      at.part_m = ctx->part_m;
+      at.part_l = ctx->part_l;
+      at.out = ctx->attn;
+      CK(launch_attention(at, ctx->st, true));
+      ctx->launches += 2;
+    }
+    // ---- o_proj
+    {
+      GemvArgs p = pro_args(PRO_X);
+      p.src = ctx->attn;
+      p.ld_src = qrows;
+      if ((rc = run_linear(ctx, {{&ly.o, ctx->proj}}, cols, p))) return rc;
+    }
+    // ---- gate, up with the post-attention join fused in (alpha 1)
+    {
+      GemvArgs p = pro_args(PRO_JOIN);
+      p.src = ctx->proj;
+      p.ld_src = H;
+      p.res = ctx->res[cur];
+      p.ld_res = H;
+      p.g1 = ly.ln_post_attn;
+      p.g2 = ly.ln_pre_ffn;
+      p.alpha = 1.0f;
+      p.hidden_out = ctx->res[cur ^ 1];
+      p.eps = eps;
+      if ((rc = run_linear(ctx, {{&ly.gate, ctx->gate}, {&ly.up, ctx->up}}, cols, p))) return rc;
+      cur ^= 1;
+    }
+    // ---- down_proj over gelu(gate) * up (the fused gelu prologue)
+    {
+      GemvArgs p = pro_args(PRO_GELU);
+      p.src = ctx->gate;
+      p.ld_src = ly.gate.N;
+      p.up = ctx->up;
+      p.ld_up = ly.up.N;
+      p.up_off = 0;
+      if ((rc = run_linear(ctx, {{&ly.down, ctx->proj}}, cols, p))) return rc;
+    }
+    // ---- per_layer_input_gate over the post-FFN norm-residual (the residual itself)
+    {
+      GemvArgs p = pro_args(PRO_NORMRES);
+      p.src = ctx->proj;
+      p.ld_src = H;
+      p.res = ctx->res[cur];
+      p.ld_res = H;
+      p.g1 = ly.ln_post_ffn;
+      p.hidden_out = ctx->res[cur ^ 1];
+      p.eps = eps;
+      if ((rc = run_linear(ctx, {{&ly.pleg, ctx->pleg_out}}, cols, p))) return rc;
+      cur ^= 1;
+    }
+    // ---- per_layer_projection over gelu(gate) * the layer's per-layer input row
+    {
+      GemvArgs p = pro_args(PRO_GELU);
+      p.src = ctx->pleg_out;
+      p.ld_src = PD;
+      p.up = ctx->ple_in;
+      p.ld_up = ctx->ple_cols;
+      p.up_off = L * PD;
+      if ((rc = run_linear(ctx, {{&ly.plep, ctx->proj}}, cols, p))) return rc;
+    }
+  }
+  if (head) {
+    Layer &last = ctx->layers[n_layers - 1];
+    GemvArgs p = pro_args(PRO_JOIN);
+    p.src = ctx->proj;
+    p.ld_src = H;
+    p.res = ctx->res[cur];
+    p.ld_res = H;
+    p.g1 = last.ln_post_ple;
+    p.g2 = ctx->final_norm;
+    p.alpha = last.layer_scalar;
+    p.hidden_out = ctx->res[cur ^ 1];
+    p.eps = eps;
+    p.softcap = a.final_softcap;
+    if ((rc = run_linear(ctx, {{&ctx->lm, nullptr}}, cols, p, true))) return rc;
+    CK(launch_argmax_final(ctx->head_pv, ctx->head_pi, ctx->head_blocks, cols, d_tok,
+                           ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
+    ctx->launches++;
+    if (advance) {
+      CK(launch_advance(d_pos, cols, ctx->st, true));
+      ctx->launches++;
+    }
+  }
+  return G4_OK;
+}
+
+static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false) {
+  if (!ctx->cfg.use_graphs) return record_step(ctx, cols, n_layers, head, advance);
+  GraphKey key{cols, n_layers, head ? 1 : 0, advance ? 1 : 0};
+  auto it = ctx->graphs.find(key);
+  if (it == ctx->graphs.end()) {
+    // First use: run eagerly (sets kernel attributes, validates), then capture.
+    int rc = record_step(ctx, cols, n_layers, head, advance);
+    if (rc) return rc;
+    int launches = ctx->launches;
+    CK(cudaStreamSynchronize(ctx->st));
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(ctx->st, cudaStreamCaptureModeThreadLocal));
+    rc = record_step(ctx, cols, n_layers, head, advance);
+    cudaError_t e = cudaStreamEndCapture(ctx->st, &g);
+    if (rc) return rc;
+    CK(e);
+    cudaGraphExec_t ex;
+    CK(cudaGraphInstantiate(&ex, g, 0));
+    cudaGraphDestroy(g);
+    ctx->graphs[key] = ex;
+    ctx->launches = launches;
+    // The eager run already advanced the step; the graph serves the next calls.
+    return G4_OK;
+  }
+  CK(cudaGraphLaunch(it->second, ctx->st));
+  return G4_OK;
+}
+
+static int check_seq_pos(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t n) {
+  if (!ctx->weights_ready) return fail(ctx, G4_ERR_STATE, "no weights: call g4_init_random or g4_upload_weight first");
+  if (seq < 0 || seq >= ctx->cfg.max_seqs) return fail(ctx, G4_ERR_INVALID, "sequence %d outside 0..%d", seq, ctx->cfg.max_seqs - 1);
+  if (pos < 0 || n < 1 || pos + n > ctx->cfg.max_context)
+    return fail(ctx, G4_ERR_INVALID, "positions %d..%d outside the context of %d", pos, pos + n - 1, ctx->cfg.max_context);
+  if (pos > ctx->kv_len[seq])
+    return fail(ctx, G4_ERR_INVALID, "position %d leaves a gap after the %d cached positions of sequence %d", pos, ctx->kv_len[seq], seq);
+  return G4_OK;
+}
+
+static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos, const int32_t *toks,
+                 bool tokens_too) {
+  for (int i = 0; i < cols; i++) {
+    ctx->h_step[i] = seqs[i];
+    ctx->h_step[ctx->maxc + i] = pos[i];
+    if (tokens_too) ctx->h_step[2 * ctx->maxc + i] = toks[i];
+  }
+  CK(cudaMemcpyAsync(ctx->d_step, ctx->h_step, (size_t)ctx->maxc * 4 * (tokens_too ? 3 : 2), cudaMemcpyHostToDevice, ctx->st));
+  return G4_OK;
+}
+
+static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
+  CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)cols * 4, cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaStreamSynchronize(ctx->st));
+  for (int i = 0; i < cols; i++) out[i] = ctx->h_tok[i];
+  return G4_OK;
+}
+
+extern "C" int g4_prefill(g4_ctx *ctx, int32_t seq, const int32_t *ids, int32_t n, int32_t start_pos,
+                          int32_t is_last, int32_t *out_token) {
+  if (!ctx || !ids) return fail(ctx, G4_ERR_INVALID, "g4_prefill: null argument");
+  int rc = check_seq_pos(ctx, seq, start_pos, n);
+  if (rc) return rc;
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= ctx->V) return fail(ctx, G4_ERR_INVALID, "token id %d outside the vocabulary", ids[i]);
+  CK(cudaSetDevice(ctx->dev));
+  const int nl_all = ctx->NL, nl_prod = ctx->cfg.arch.kv_producer_layers;
+  std::vector<int32_t> sq(ctx->maxc, seq), ps(ctx->maxc);
+  // A last chunk runs every layer and the head on its final position; the positions before it
+  // need all layers only for their KV (which only producers write), so they run as the
+  // producer-only chunk (src/plan.ts:160-192, 812-824).
+  int body = is_last ? n - 1 : n;
+  for (int c0 = 0; c0 < body; c0 += ctx->maxc) {
+    int cols = std::min(ctx->maxc, body - c0);
+    for (int i = 0; i < cols; i++) ps[i] = start_pos + c0 + i;
+    if ((rc = stage(ctx, cols, sq.data(), ps.data(), ids + c0, true))) return rc;
+    if ((rc = record_step(ctx, cols, nl_prod, false))) return rc;
+  }
+  if (is_last) {
+    ps[0] = start_pos + n - 1;
+    if ((rc = stage(ctx, 1, sq.data(), ps.data(), ids + n - 1, true))) return rc;
+    if ((rc = run_step(ctx, 1, nl_all, true))) return rc;
+    int32_t tok;
+    if ((rc = fetch_tokens(ctx, 1, &tok))) return rc;
+    if (out_token) *out_token = tok;
+  } else {
+    CK(cudaStreamSynchronize(ctx->st));
+    if (out_token) *out_token = -1;
+  }
+  ctx->kv_len[seq] = start_pos + n;
+  ctx->last_cols = 1;
+  return G4_OK;
+}
+
+extern "C" int g4_decode(g4_ctx *ctx, int32_t seq, int32_t prev_token, int32_t pos, int32_t *out_token) {
+  if (!ctx || !out_token) return fail(ctx, G4_ERR_INVALID, "g4_decode: null argument");
+  int rc = check_seq_pos(ctx, seq, pos, 1);
+  if (rc) return rc;
+  if (prev_token < 0 || prev_token >= ctx->V) return fail(ctx, G4_ERR_INVALID, "token id %d outside the vocabulary", prev_token);
+  CK(cudaSetDevice(ctx->dev));
+  if ((rc = stage(ctx, 1, &seq, &pos, &prev_token, true))) return rc;
+  if ((rc = run_step(ctx, 1, ctx->NL, true))) return rc;
+  if ((rc = fetch_tokens(ctx, 1, out_token))) return rc;
+  ctx->kv_len[seq] = pos + 1;
+  ctx->last_cols = 1;
+  return G4_OK;
+}
+
+extern "C" int g4_decode_ahead(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t *out_token) {
+  if (!ctx || !out_token) return fail(ctx, G4_ERR_INVALID, "g4_decode_ahead: null argument");
+  int rc = check_seq_pos(ctx, seq, pos, 1);
+  if (rc) return rc;
+  CK(cudaSetDevice(ctx->dev));
+  if ((rc = stage(ctx, 1, &seq, &pos, nullptr, false))) return rc;
+  if ((rc = run_step(ctx, 1, ctx->NL, true))) return rc;
+  if ((rc = fetch_tokens(ctx, 1, out_token))) return rc;
+  ctx->kv_len[seq] = pos + 1;
+  ctx->last_cols = 1;
+  return G4_OK;
+}
+
+extern "C" int g4_decode_batch(g4_ctx *ctx, int32_t B, const int32_t *seqs, const int32_t *tokens,
+                               const int32_t *positions, int32_t *out_tokens) {
+  if (!ctx || !seqs || !tokens || !positions || !out_tokens) return fail(ctx, G4_ERR_INVALID, "g4_decode_batch: null argument");
+  if (B < 1 || B > ctx->maxc || B > ctx->head_cols)
+    return fail(ctx, G4_ERR_INVALID, "batch %d outside 1..%d", B, std::min(ctx->maxc, ctx->head_cols));
+  int rc;
+  for (int i = 0; i < B; i++) {
+    if ((rc = check_seq_pos(ctx, seqs[i], positions[i], 1))) return rc;
+    if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, G4_ERR_INVALID, "token id %d outside the vocabulary", tokens[i]);
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == seqs[i]) return fail(ctx, G4_ERR_INVALID, "sequence %d appears twice in one batch", seqs[i]);
+  }
+  CK(cudaSetDevice(ctx->dev));
+  if ((rc = stage(ctx, B, seqs, positions, tokens, true))) return rc;
+  if ((rc = run_step(ctx, B, ctx->NL, true))) return rc;
+  if ((rc = fetch_tokens(ctx, B, out_tokens))) return rc;
+  for (int i = 0; i < B; i++) ctx->kv_len[seqs[i]] = positions[i] + 1;
+  ctx->last_cols = B;
+  return G4_OK;
+}
+
+extern "C" int g4_step_stage(g4_ctx *ctx, int32_t B, const int32_t *seqs, const int32_t *tokens,
+                             const int32_t *positions) {
+  if (!ctx || !seqs || !tokens || !positions) return fail(ctx, G4_ERR_INVALID, "g4_step_stage: null argument");
+  if (B < 1 || B > ctx->maxc || B > ctx->head_cols) return fail(ctx, G4_ERR_INVALID, "batch %d too wide", B);
+  int rc;
+  for (int i = 0; i < B; i++)
+    if ((rc = check_seq_pos(ctx, seqs[i], positions[i], 1))) return rc;
+  CK(cudaSetDevice(ctx->dev));
+  if ((rc = stage(ctx, B, seqs, positions, tokens, true))) return rc;
+  CK(cudaStreamSynchronize(ctx->st));
+  ctx->staged_cols = B;
+  ctx->staged_seq.assign(seqs, seqs + B);
+  ctx->staged_pos.assign(positions, positions + B);
+  return G4_OK;
+}
+
+extern "C" int g4_step_run_device(g4_ctx *ctx, int32_t B, int32_t advance) {
+  if (!ctx) return fail(nullptr, G4_ERR_INVALID, "null context");
+  if (B < 1 || B > ctx->maxc || B > ctx->head_cols) return fail(ctx, G4_ERR_INVALID, "batch %d too wide", B);
+  if (B != ctx->staged_cols) return fail(ctx, G4_ERR_STATE, "g4_step_stage staged %d columns, not %d", ctx->staged_cols, B);
+  for (int i = 0; i < B; i++) {
+    int32_t s = ctx->staged_seq[i], p = ctx->staged_pos[i];
+    if (p >= ctx->cfg.max_context)
+      return fail(ctx, G4_ERR_INVALID, "sequence %d would step past the context of %d", s, ctx->cfg.max_context);
+  }
+  int rc = run_step(ctx, B, ctx->NL, true, advance != 0);
+  if (rc) return rc;
+  for (int i = 0; i < B; i++) {
+    ctx->kv_len[ctx->staged_seq[i]] = std::max(ctx->kv_len[ctx->staged_seq[i]], ctx->staged_pos[i] + 1);
+    if (advance) ctx->staged_pos[i]++;
+  }
+  ctx->last_cols = B;
+  return G4_OK;
+}
+
+extern "C" int g4_step_read_tokens(g4_ctx *ctx, int32_t B, int32_t *out_tokens) {
+  if (!ctx || !out_tokens) return fail(ctx, G4_ERR_INVALID, "null argument");
+  return fetch_tokens(ctx, B, out_tokens);
+}
+
+extern "C" int g4_kv_truncate(g4_ctx *ctx, int32_t seq, int32_t n) {
+  if (!ctx) return fail(nullptr, G4_ERR_INVALID, "null context");
+  if (seq < 0 || seq >= ctx->cfg.max_seqs) return fail(ctx, G4_ERR_INVALID, "sequence %d out of range", seq);
+  if (n < 0 || n > ctx->kv_len[seq]) return fail(ctx, G4_ERR_INVALID, "truncate %d outside 0..%d", n, ctx->kv_len[seq]);
+  ctx->kv_len[seq] = n;
+  return G4_OK;
+}
+
+extern "C" int g4_kv_length(const g4_ctx *ctx, int32_t seq, int32_t *n) {
+  if (!ctx || !n) return fail(nullptr, G4_ERR_INVALID, "null argument");
+  if (seq < 0 || seq >= ctx->cfg.max_seqs) return fail(const_cast<g4_ctx *>(ctx), G4_ERR_INVALID, "sequence %d out of range", seq);
+  *n = ctx->kv_len[seq];
+  return G4_OK;
+}
+
+extern "C" int g4_read_logits(g4_ctx *ctx, int32_t col, float *out, int32_t n) {
+  if (!ctx || !out) return fail(ctx, G4_ERR_INVALID, "g4_read_logits: null argument");
+  if (col < 0 || col >= ctx->head_cols || n < 0 || n > ctx->V) return fail(ctx, G4_ERR_INVALID, "bad column or count");
+  CK(cudaStreamSynchronize(ctx->st));
+  CK(cudaMemcpy(out, ctx->logits + (size_t)col * ctx->V, (size_t)n * 4, cudaMemcpyDeviceToHost));
+  return G4_OK;
+}
+
+// ============================================================================ operator API
+
+#define OPCK(call)                                                                           \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess) return fail(nullptr, G4_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, float in_scale,
+                           float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
+                           int32_t *acc_out, void *stream) {
+  if (!wq || !scales || !x || !y) return fail(nullptr, G4_ERR_INVALID, "g4_op_qgemv: null pointer");
+  if (bits != 4 && bits != 8) return fail(nullptr, G4_ERR_INVALID, "bits must be 4 or 8");
+  const int span = bits == 4 ? 256 : 128;
+  if (N < 1 || K < span || K % span != 0 || cols < 1)
+    return fail(nullptr, G4_ERR_INVALID, "qgemv-%dbit needs K a multiple of %d, got %d (N %d, cols %d)", bits, span, K, N, cols);
+  if (in_scale == 0.0f && cols != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "the f32 path takes one column");
+  int rpw, ppr;
+  if (!gemv_geometry(bits, K, N, &rpw, &ppr)) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  if (in_scale != 0.0f && (size_t)8 * K > 56 * 1024) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  cudaStream_t st = (cudaStream_t)stream;
+  for (int c0 = 0; c0 < cols; c0 += 8) {
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.pro = PRO_X;
+    a.alpha = 1.0f;
+    a.K = K;
+    a.cols = std::min(8, cols - c0);
+    a.rpw = rpw;
+    a.ppr = ppr;
+    a.nseg = 1;
+    a.seg[0].w = (const uint8_t *)wq;
+    a.seg[0].s = (const uint16_t *)scales;
+    a.seg[0].y = y + (size_t)c0 * N;
+    a.seg[0].acc_out = acc_out ? acc_out + (size_t)c0 * N : nullptr;
+    a.seg[0].N = N;
+    a.seg[0].in_scale = in_scale;
+    a.seg[0].out_scale = out_scale;
+    a.src = x + (size_t)c0 * K;
+    a.ld_src = K;
+    int blocks = (N + 8 * rpw - 1) / (8 * rpw);
+    OPCK(launch_gemv(a, bits, blocks, st, false));
+  }
+  OPCK(cudaGetLastError());
+  return G4_OK;
+}
+
+extern "C" int g4_op_qgemv_gelu(const void *wq, const void *scales, const float *gate, const float *up,
+                                int32_t up_offset, int32_t up_stride, float in_scale, float out_scale,
+                                int32_t bits, int32_t N, int32_t K, int32_t cols, float *y, void *stream) {
+  if (!wq || !scales || !gate || !up || !y) return fail(nullptr, G4_ERR_INVALID, "g4_op_qgemv_gelu: null pointer");
+  const int span = bits == 4 ? 256 : 128;
+  if ((bits != 4 && bits != 8) || N < 1 || K < span || K % span || cols < 1)
+    return fail(nullptr, G4_ERR_INVALID, "bad qgemv-gelu shape");
+  if (in_scale == 0.0f && cols != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "the f32 path takes one column");
+  int rpw, ppr;
+  if (!gemv_geometry(bits, K, N, &rpw, &ppr)) return fail(nullptr, G4_ERR_UNSUPPORTED, "K too wide");
+  cudaStream_t st = (cudaStream_t)stream;
+  for (int c0 = 0; c0 < cols; c0 += 8) {
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.pro = PRO_GELU;
+    a.alpha = 1.0f;
+    a.K = K;
+    a.cols = std::min(8, cols - c0);
+    a.rpw = rpw;
+    a.ppr = ppr;
+    a.nseg = 1;
+    a.seg[0].w = (const uint8_t *)wq;
+    a.seg[0].s = (const uint16_t *)scales;
+    a.seg[0].y = y + (size_t)c0 * N;
+    a.seg[0].N = N;
+    a.seg[0].in_scale = in_scale;
+    a.seg[0].out_scale = out_scale;
+    a.src = gate + (size_t)c0 * K;
+    a.ld_src = K;
+    a.up = up + (size_t)c0 * up_stride;
+    a.ld_up = up_stride;
+    a.up_off = up_offset;
+    int blocks = (N + 8 * rpw - 1) / (8 * rpw);
+    OPCK(launch_gemv(a, bits, blocks, st, false));
+  }
+  return G4_OK;
+}
+
+static int check_width(int width) {
+  if (width < 4 || width % 4 != 0) return fail(nullptr, G4_ERR_INVALID, "width %d must be a positive multiple of 4", width);
+  return G4_OK;
+}
+
+extern "C" int g4_op_rms_norm(const float *src, const float *gain, float *dst, int32_t rows,
+                              int32_t width, float eps, void *stream) {
+  if (!src || !dst || rows < 1) return fail(nullptr, G4_ERR_INVALID, "g4_op_rms_norm: bad argument");
+  if (int rc = check_width(width)) return rc;
+  OPCK(launch_rms_norm(src, gain, dst, rows, width, eps, (cudaStream_t)stream));
+  return G4_OK;
+}
+
+extern "C" int g4_op_norm_residual(const float *src, const float *gain, const float *residual,
+                                   float *dst, int32_t rows, int32_t width, float eps, void *stream) {
+  if (!src || !gain || !residual || !dst || rows < 1) return fail(nullptr, G4_ERR_INVALID, "g4_op_norm_residual: bad argument");
+  if (int rc = check_width(width)) return rc;
+  OPCK(launch_norm_residual(src, gain, residual, dst, rows, width, eps, (cudaStream_t)stream));
+  return G4_OK;
+}
+
+extern "C" int g4_op_norm_residual_norm(const float *src, const float *gain, const float *residual,
+                                        const float *gain2, float alpha, float *hidden, float *dst,
+                                        int32_t rows, int32_t width, float eps, void *stream) {
+  if (!src || !gain || !residual || !gain2 || !hidden || !dst || rows < 1)
+    return fail(nullptr, G4_ERR_INVALID, "g4_op_norm_residual_norm: bad argument");
+  if (int rc = check_width(width)) return rc;
+  OPCK(launch_norm_residual_norm(src, gain, residual, gain2, alpha, hidden, dst, rows, width, eps, (cudaStream_t)stream));
+  return G4_OK;
+}
+
+extern "C" int g4_op_gelu_mul(const float *gate, const float *up, float *dst, int32_t n, float srq_scale,
+                              void *stream) {
+  if (!gate || !up || !dst || n < 1) return fail(nullptr, G4_ERR_INVALID, "g4_op_gelu_mul: bad argument");
+  OPCK(launch_gelu_mul(gate, up, dst, n, srq_scale, (cudaStream_t)stream));
+  return G4_OK;
+}
+
+extern "C" int g4_op_q_norm_rope(const float *src, const float *gain, const float *cos_tab,
+                                 const float *sin_tab, float *dst, int32_t rows, int32_t width,
+                                 int32_t rows_per_position, float eps, void *stream) {
+  if (!src || !gain || !cos_tab || !sin_tab || !dst || rows < 1 || rows_per_position < 1)
+    return fail(nullptr, G4_ERR_INVALID, "g4_op_q_norm_rope: bad argument");
+  if (width % 8 != 0 || width > 4096) return fail(nullptr, G4_ERR_INVALID, "width %d unsupported", width);
+  AttnPro a;
+  memset(&a, 0, sizeof(a));
+  a.cols = rows;
+  a.heads = 1;
+  a.hd = width;
+  a.q = src;
+  a.q_ld = width;
+  a.qgain = gain;
+  a.cos_tab = cos_tab;
+  a.sin_tab = sin_tab;
+  a.rows_per_col_tab = rows_per_position;
+  a.qr = dst;
+  a.eps = eps;
+  OPCK(launch_attn_prologue(a, (cudaStream_t)stream, false));
+  return G4_OK;
+}
+
+extern "C" int g4_op_kv_norm_rope_store(const float *k, const float *v, const float *gain,
+                                        const float *cos_tab, const float *sin_tab, float *cache,
+                                        int32_t tokens, int32_t head_dim, int32_t start_pos,
+                                        int32_t max_context, float eps, void *stream) {
+  if (!k || !v || !gain || !cos_tab || !sin_tab || !cache || tokens < 1)
+    return fail(nullptr, G4_ERR_INVALID, "g4_op_kv_norm_rope_store: bad argument");
+  if (start_pos < 0 || start_pos + tokens > max_context)
+    return fail(nullptr, G4_ERR_INVALID, "rows %d..%d outside 0..%d", start_pos, start_pos + tokens - 1, max_context - 1);
+  if (head_dim % 8 != 0 || head_dim > 4096) return fail(nullptr, G4_ERR_INVALID, "head_dim %d unsupported", head_dim);
+  AttnPro a;
+  memset(&a, 0, sizeof(a));
+  a.cols = tokens;
+  a.heads = 0;
+  a.hd = head_dim;
+  a.k = k;
+  a.v = v;
+  a.kv_ld = head_dim;
+  a.kgain = gain;
+  a.cos_tab = cos_tab;
+  a.sin_tab = sin_tab;
+  a.rows_per_col_tab = 1;
+  a.cache = cache;
+  a.seq_stride = 0;
+  a.max_ctx = max_context;
+  a.refs.pos_base = start_pos;
+  a.eps = eps;
+  OPCK(launch_attn_prologue(a, (cudaStream_t)stream, false));
+  return G4_OK;
+}
+
+extern "C" int g4_op_attention(const float *q, const float *cache, float *out, int32_t heads,
+                               int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,
+                               int32_t window, int32_t max_context, void *stream) {
+  if (!q || !cache || !out) return fail(nullptr, G4_ERR_INVALID, "g4_op_attention: null pointer");
+  if (heads != 8) return fail(nullptr, G4_ERR_UNSUPPORTED, "the attention kernel is built for 8 query heads");
+  if (head_dim != 256 && head_dim != 512) return fail(nullptr, G4_ERR_UNSUPPORTED, "head_dim 256 or 512");
+  if (q_count < 1 || q_start < 0 || kv_len < 1 || q_start + q_count > kv_len || kv_len > max_context)
+    return fail(nullptr, G4_ERR_INVALID, "attention: query positions extend past kv_len; store KV before attending");
+  int max_blocks = window > 0 ? (window + 63) / 64 + 1 : (kv_len + 63) / 64;
+  cudaStream_t st = (cudaStream_t)stream;
+  float *scratch = nullptr;
+  size_t n_o = (size_t)q_count * max_blocks * heads * head_dim, n_ml = (size_t)q_count * max_blocks * heads;
+  OPCK(cudaMallocAsync((void **)&scratch, (n_o + 2 * n_ml) * 4, st));
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.cols = q_count;
+  a.heads = heads;
+  a.hd = head_dim;
+  a.window = window;
+  a.max_ctx = max_context;
+  a.kv_cap = kv_len;
+  a.qr = q;
+  a.cache = cache;
+  a.seq_stride = 0;
+  a.refs.pos_base = q_start;
+  a.max_blocks = max_blocks;
+  a.part_o = scratch;
+  a.part_m = scratch + n_o;
+  a.part_l = scratch + n_o + n_ml;
+  a.out = out;
+  cudaError_t e = launch_attention(a, st, false);
+  cudaFreeAsync(scratch, st);
+  OPCK(e);
+  return G4_OK;
+}
+
+extern "C" int g4_op_embed_gather(const void *codes, const void *scales, const int32_t *ids, float *dst,
+                                  int32_t slots, int32_t cols, int32_t group_size, float out_scale,
+                                  int32_t slice_start, int32_t slice_rows, void *stream) {
+  if (!codes || !scales || !ids || !dst || slots < 1) return fail(nullptr, G4_ERR_INVALID, "g4_op_embed_gather: bad argument");
+  if (cols % 8 != 0 || group_size < 8 || group_size % 8 != 0 || cols % group_size != 0)
+    return fail(nullptr, G4_ERR_INVALID, "embed gather: cols %d / group %d", cols, group_size);
+  OPCK(launch_embed_op((const uint8_t *)codes, (const uint16_t *)scales, ids, dst, slots, cols,
+                       group_size, out_scale, slice_start, slice_rows, (cudaStream_t)stream, false));
+  return G4_OK;
+}
+
+extern "C" int g4_op_dense_bf16(const void *w, const float *x, float *y, int32_t N, int32_t K,
+                                int32_t cols, float alpha, void *stream) {
+  if (!w || !x || !y || N < 1 || cols < 1) return fail(nullptr, G4_ERR_INVALID, "g4_op_dense_bf16: bad argument");
+  if (K % 8 != 0 || K > 2048) return fail(nullptr, G4_ERR_UNSUPPORTED, "dense K %d (multiple of 8 up to 2048)", K);
+  OPCK(launch_dense_bf16((const uint16_t *)w, x, K, y, N, K, cols, alpha, (cudaStream_t)stream, false));
+  return G4_OK;
+}
+
+extern "C" int g4_op_softcap_argmax(const float *logits, float *capped, int32_t *token, int32_t n,
+                                    float cap, void *stream) {
+  if (!logits || !token || n < 1) return fail(nullptr, G4_ERR_INVALID, "g4_op_softcap_argmax: bad argument");
+  cudaStream_t st = (cudaStream_t)stream;
+  int parts = (n + 4095) / 4096;
+  float *pv = nullptr;
+  OPCK(cudaMallocAsync((void **)&pv, (size_t)parts * 8, st));
+  int32_t *pi = (int32_t *)(pv + parts);
+  cudaError_t e = launch_softcap_partials(logits, capped, n, cap, pv, pi, parts, st);
+  float *val = nullptr;
+  if (e == cudaSuccess) e = launch_argmax_final(pv, pi, parts, 1, nullptr, token, (float *)(token + 1), st, false);
+  (void)val;
+  cudaFreeAsync(pv, st);
+  OPCK(e);
+  return G4_OK;
+}
+
+extern "C" int g4_op_math_probe(const float *x, float *exp_out, float *tanh_out, float *cuda_exp,
+                                float *cuda_tanh, int32_t n, void *stream) {
+  if (!x || !exp_out || !tanh_out || !cuda_exp || !cuda_tanh || n < 1)
+    return fail(nullptr, G4_ERR_INVALID, "g4_op_math_probe: bad argument");
+  OPCK(launch_math_probe(x, exp_out, tanh_out, cuda_exp, cuda_tanh, n, (cudaStream_t)stream));
+  return G4_OK;
+}

@@ -1,0 +1,314 @@
+"""Pure host-side planning, mirroring the reference's src/plan.ts, src/kv.ts and src/tableSplit.ts.
+
+Nothing here touches a GPU. The C++ executor in libgemma4_cuda.so runs the same step order that
+`plan_decode_step` lists; `census` lets a caller check a recorded step count against it.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+# ---------------------------------------------------------------- architecture (plan.ts:29-82)
+
+
+@dataclass(frozen=True)
+class Gemma4Arch:
+    layer_count: int = 35
+    hidden_size: int = 1536
+    query_heads: int = 8
+    kv_heads: int = 1
+    sliding_head_dim: int = 256
+    global_head_dim: int = 512
+    global_layers: tuple = (4, 9, 14, 19, 24, 29, 34)
+    sliding_window: int = 512
+    kv_producer_layers: int = 15
+    producer_intermediate: int = 6144
+    consumer_intermediate: int = 6144  # the checkpoint's 12288 belongs to the 2-bit family
+    vocab_size: int = 262144
+    ple_dim: int = 256
+    rms_eps: float = 1e-6
+    final_softcap: float = 30.0
+    rope_theta_sliding: float = 1e4
+    rope_theta_global: float = 1e6
+    partial_rotary_factor: float = 0.25
+
+
+GEMMA4_E2B = Gemma4Arch()
+
+
+def is_global_layer(arch: Gemma4Arch, layer: int) -> bool:
+    return layer in arch.global_layers
+
+
+def is_kv_producer(arch: Gemma4Arch, layer: int) -> bool:
+    return 0 <= layer < arch.kv_producer_layers
+
+
+def head_dim_for_layer(arch: Gemma4Arch, layer: int) -> int:
+    return arch.global_head_dim if is_global_layer(arch, layer) else arch.sliding_head_dim
+
+
+def kv_role_for_layer(arch: Gemma4Arch, layer: int) -> dict:
+    """kvRoleForLayer (src/kv.ts:76-88): producers read their own cache, consumers the last
+    producer of the same attention type."""
+    if not (0 <= layer < arch.layer_count):
+        raise ValueError(f"kvRoleForLayer: layer {layer} outside 0..{arch.layer_count - 1}")
+    if is_kv_producer(arch, layer):
+        return {"kind": "producer", "layer": layer}
+    want = is_global_layer(arch, layer)
+    last = -1
+    for p in range(arch.kv_producer_layers):
+        if is_global_layer(arch, p) == want:
+            last = p
+    if last < 0:
+        raise ValueError(f"kvRoleForLayer: no producer of the same type as layer {layer}")
+    return {"kind": "consumer", "layer": layer, "readsFrom": last}
+
+
+# ---------------------------------------------------------------- prefill chunks (plan.ts:160-192)
+
+DEFAULT_PREFILL_CHUNK = 64
+
+
+@dataclass(frozen=True)
+class PrefillChunk:
+    start: int
+    end: int
+    length: int
+
+
+def prefill_chunks(start: int, prompt_length: int, chunk_size: int = DEFAULT_PREFILL_CHUNK):
+    """Positions [start, prompt_length) in chunks of at most chunk_size; the last chunk is exactly
+    the final position, so every earlier chunk stops at the KV producers."""
+    if not isinstance(start, int) or start < 0:
+        raise ValueError(f"prefillChunks: bad from {start}")
+    if not isinstance(prompt_length, int) or prompt_length < start:
+        raise ValueError(f"prefillChunks: promptLength {prompt_length} below from {start}")
+    if not isinstance(chunk_size, int) or chunk_size <= 0:
+        raise ValueError(f"prefillChunks: chunkSize must be a positive integer, got {chunk_size}")
+    chunks = []
+    last = prompt_length - 1
+    s = start
+    while s < last:
+        e = min(s + chunk_size, last)
+        chunks.append(PrefillChunk(s, e, e - s))
+        s += chunk_size
+    if prompt_length > start:
+        chunks.append(PrefillChunk(last, prompt_length, 1))
+    return chunks
+
+
+# ---------------------------------------------------------------- dispatch lists (plan.ts:487-784)
+
+
+@dataclass(frozen=True)
+class DispatchStep:
+    kernel: str
+    phase: str
+    layer: int
+    role: str
+
+
+def plan_layer(arch: Gemma4Arch, layer: int) -> list:
+    """One decode layer as the fused steps this build launches, each named by the reference
+    roles it covers."""
+    producer = is_kv_producer(arch, layer)
+    s = []
+    add = lambda k, ph, r: s.append(DispatchStep(k, ph, layer, r))
+    pre = "input_layernorm" if layer == 0 else "previous tail join"
+    add("qgemv-4bit", "attn", f"{pre}; q_proj" + (", k_proj, v_proj" if producer else ""))
+    add("attn-prologue", "attn", "q_norm per head, rope q" +
+        ("; k_norm, v_norm weightless, rope k, kv store" if producer else ""))
+    add("attention-blocks", "attn", "attention")
+    add("attention-merge", "attn", "attention split fold")
+    add("qgemv-4bit", "attn", "o_proj")
+    add("qgemv-4bit", "mlp", "post_attention_layernorm plus residual, pre_feedforward_layernorm; "
+        "gate_proj, up_proj")
+    add("qgemv-4bit", "mlp", "gelu times up, down_proj")
+    add("qgemv-8bit", "ple", "post_feedforward_layernorm plus residual; per_layer_input_gate")
+    add("qgemv-8bit", "ple", "gate times per layer row, per_layer_projection")
+    return s
+
+
+def plan_embed(arch: Gemma4Arch) -> list:
+    return [
+        DispatchStep("embed-gather", "embed", -1, "embed_tokens gather, per layer embedding gather"),
+        DispatchStep("dense-bf16", "embed", -1, "per_layer_model_projection"),
+        DispatchStep("ple-combine", "embed", -1,
+                     "per_layer_projection_norm, per layer inputs add, per layer inputs scale"),
+    ]
+
+
+def plan_head(arch: Gemma4Arch) -> list:
+    return [
+        DispatchStep("qgemv-4bit-head", "head", -1,
+                     "post_per_layer_input_norm plus residual, layer_scalar, final norm; lm_head; "
+                     "tanh(logits / 30) * 30; argmax partials"),
+        DispatchStep("argmax-final", "head", -1, "argmax final"),
+    ]
+
+
+def plan_decode_step(arch: Gemma4Arch = GEMMA4_E2B) -> list:
+    steps = list(plan_embed(arch))
+    for layer in range(arch.layer_count):
+        steps += plan_layer(arch, layer)
+    steps += plan_head(arch)
+    return steps
+
+
+def plan_prefill_chunk(arch: Gemma4Arch, is_last: bool) -> list:
+    steps = list(plan_embed(arch))
+    n = arch.layer_count if is_last else arch.kv_producer_layers
+    for layer in range(n):
+        steps += plan_layer(arch, layer)
+    if is_last:
+        steps += plan_head(arch)
+    return steps
+
+
+def census(steps) -> dict:
+    out: dict = {}
+    for s in steps:
+        out[s.kernel] = out.get(s.kernel, 0) + 1
+    return out
+
+
+# ---------------------------------------------------------------- KV reuse (kv.ts:150-286)
+
+
+@dataclass
+class KvReusePlan:
+    action: str
+    reuse: int
+    prefill_from: int
+    prefill_count: int
+
+
+def plan_kv_reuse(cached, nxt) -> KvReusePlan:
+    """planKvReuse (src/kv.ts:194-218): extend, rewind, or reset."""
+    if len(nxt) == 0:
+        raise ValueError("planKvReuse: next must hold at least one token")
+    o = 0
+    while o < len(cached) and o < len(nxt) and cached[o] == nxt[o]:
+        o += 1
+    if o == len(nxt) or o == 0:
+        return KvReusePlan("reset", 0, 0, len(nxt))
+    if o == len(cached):
+        return KvReusePlan("extend", o, o, len(nxt) - o)
+    return KvReusePlan("rewind", o, o, len(nxt) - o)
+
+
+@dataclass
+class KvCacheState:
+    """KvCacheState (src/kv.ts:230-286): which token ids the caches hold, host bookkeeping."""
+    tokens: list = field(default_factory=list)
+
+    @property
+    def length(self) -> int:
+        return len(self.tokens)
+
+    def truncate(self, n: int) -> None:
+        if not isinstance(n, int) or n < 0 or n > len(self.tokens):
+            raise ValueError(f"KvCacheState.truncate: {n} outside 0..{len(self.tokens)}")
+        del self.tokens[n:]
+
+    def reset(self) -> None:
+        self.tokens.clear()
+
+    def append(self, ids) -> None:
+        for i in ids:
+            if not isinstance(i, int) or i < 0:
+                raise ValueError(f"KvCacheState.append: bad token id {i}")
+        self.tokens.extend(ids)
+
+    def accept_prompt(self, nxt) -> KvReusePlan:
+        plan = plan_kv_reuse(self.tokens, nxt)
+        if plan.action == "reset":
+            self.reset()
+        elif plan.action == "rewind":
+            self.truncate(plan.reuse)
+        return plan
+
+
+# ---------------------------------------------------------------- table split (tableSplit.ts)
+
+DEFAULT_MAX_SLICE_BYTES = 256 * 1024 * 1024
+
+
+@dataclass(frozen=True)
+class TableSplitPlan:
+    rows: int
+    row_bytes: int
+    rows_per_slice: int
+    slices: tuple  # (index, start_row, row_count)
+    single: bool
+
+
+def plan_table_split(rows: int, row_bytes: int, max_binding: int, max_buffer: int,
+                     max_slice_bytes: int = DEFAULT_MAX_SLICE_BYTES):
+    """planTableSplit (src/tableSplit.ts:125-215): one buffer when the table fits the limit,
+    otherwise vocab-row slices of at most the cap, 16-row aligned. None when a row cannot fit."""
+    rows = max(0, int(rows))
+    row_bytes = max(1, int(row_bytes))
+    total = rows * row_bytes
+    limit = max(0, min(int(max_binding), int(max_buffer)))
+    fits = 0 < total <= limit
+    cap = max(1, min(limit, int(max_slice_bytes)))
+    per = (limit if fits else cap) // row_bytes
+    if per < 1:
+        return None
+    aligned = per - per % 16 if per >= 16 else per
+    per_slice = min(rows, aligned)
+    slices = []
+    s = 0
+    while s < rows:
+        slices.append((len(slices), s, min(per_slice, rows - s)))
+        s += per_slice
+    if not slices:
+        slices.append((0, 0, 0))
+    return TableSplitPlan(rows, row_bytes, per_slice, tuple(slices), len(slices) == 1)
+
+
+# ---------------------------------------------------------------- synthetic prompts
+
+_M64 = (1 << 64) - 1
+
+
+def _mix64(z: int) -> int:
+    z ^= z >> 30
+    z = (z * 0xBF58476D1CE4E5B9) & _M64
+    z ^= z >> 27
+    z = (z * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+def synth_prompt(seed: int, n: int, vocab: int = 262144) -> list:
+    """Seeded prompt ids uniform over the vocabulary: the counter hash of (seed, stream 50, i),
+    the same generator the library uses for the synthetic weights."""
+    key = _mix64((seed ^ (50 * 0x9E3779B97F4A7C15)) & _M64)
+    return [_mix64((key + i * 0xD1B54A32D192ED03) & _M64) % vocab for i in range(n)]
+
+
+# ---------------------------------------------------------------- greedy loop (plan.ts:905-999)
+
+
+def run_greedy_loop(first_token: int, max_new_tokens: int, eos_ids, start_position: int,
+                    decode, is_aborted=lambda: False, decode_ahead=None):
+    """The greedy schedule: yields (token, index). The first token comes from the prefill; a stop
+    token ends the loop and is not yielded. With `decode_ahead`, the next step reads its input
+    token from the device (the tokens are the same)."""
+    budget = max(0, int(max_new_tokens))
+    if budget == 0 or is_aborted():
+        return
+    if first_token in eos_ids:
+        return
+    yield first_token, 0
+    prev = first_token
+    for index in range(1, budget):
+        if is_aborted():
+            return
+        pos = start_position + index - 1
+        token = decode_ahead(pos) if decode_ahead else decode(prev, pos)
+        if token in eos_ids:
+            return
+        yield token, index
+        prev = token

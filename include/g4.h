@@ -1,0 +1,311 @@
+/*
+ * g4.h -- C ABI of libgemma4_cuda.so, the sm_100a (B200) implementation of the quantized
+ * decode/prefill hot path of the gemma4-webgpu-engine (Gemma-4-E2B).
+ *
+ * Every entry point is plain C: integers, floats, host pointers, device pointers and sizes. No
+ * C++ or torch type crosses this line. Each declaration names the reference interface it
+ * replaces as `path:line` inside the reference project (TypeScript + WGSL).
+ *
+ * Conventions (mirroring the reference, src/kernels/registry.ts:23-70 and src/runtime.ts:73-88):
+ *   - Every call returns an int status: G4_OK (0) or a negative G4_ERR_* class. The message of
+ *     the last failure on a context is g4_last_error(ctx); context-free calls (g4_op_*) report
+ *     through g4_last_error(NULL), which is thread-local.
+ *   - The context owns all device memory it allocates. Host pointers are borrowed for the call.
+ *     Device pointers passed to g4_op_* stay owned by the caller.
+ *   - One context per GPU; calls on one context are not re-entrant (the reference serialises its
+ *     host side on one encode chain, src/runtime.ts:530-537). Different contexts may run on
+ *     different threads or processes.
+ *   - Arithmetic contract: calibrated linears accumulate int4/int8 weight codes times int8
+ *     activation codes in exact int32 (src/kernels/qgemv.ts:1131-1176); every f32 operation is a
+ *     single correctly rounded IEEE operation in a fixed order, so results do not depend on the
+ *     batch width, the grid or the stream.
+ */
+#ifndef G4_H
+#define G4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------------ status */
+
+#define G4_OK 0
+#define G4_ERR_INVALID (-1)     /* bad argument: shape, id, position, null pointer */
+#define G4_ERR_CUDA (-2)        /* a CUDA runtime call failed; the message names it */
+#define G4_ERR_OOM (-3)         /* device allocation failed */
+#define G4_ERR_STATE (-4)       /* call not valid in the current state (no weights, ...) */
+#define G4_ERR_UNSUPPORTED (-5) /* a configuration this build does not implement */
+#define G4_ERR_NOT_FOUND (-6)   /* unknown tensor or scalar name */
+#define G4_ERR_TIMEOUT (-7)     /* a bounded device wait gave up and set the error flag */
+
+typedef struct g4_ctx g4_ctx;
+
+/*
+ * Message of the last failure on `ctx`, or of the last context-free call on this thread when
+ * `ctx` is NULL. Never NULL; "" when nothing failed. Replaces the thrown Error prose of the
+ * reference (src/execute.ts:321-347, src/runtime.ts:415-445).
+ */
+const char *g4_last_error(const g4_ctx *ctx);
+
+/* Library version string, e.g. "gemma4_cuda 0.1 sm_100a". */
+const char *g4_version(void);
+
+/* ------------------------------------------------------------------------ architecture */
+
+/*
+ * The architecture contract, GEMMA4_E2B in src/plan.ts:29-82 plus the per-site weight widths of
+ * gemvBitsForSite (src/plan.ts:116-120). Global layers are a bit mask over layer indices.
+ */
+typedef struct g4_arch {
+  int32_t layer_count;           /* 35 */
+  int32_t hidden_size;           /* 1536 */
+  int32_t query_heads;           /* 8 */
+  int32_t kv_heads;              /* 1 (multi-query); the only supported value */
+  int32_t sliding_head_dim;      /* 256 */
+  int32_t global_head_dim;       /* 512 */
+  uint64_t global_layer_mask;    /* bits 4, 9, 14, 19, 24, 29, 34 */
+  int32_t sliding_window;        /* 512, inclusive of the query position */
+  int32_t kv_producer_layers;    /* 15 */
+  int32_t producer_intermediate; /* 6144 */
+  int32_t consumer_intermediate; /* 6144 in the synthetic model (12288 in the checkpoint) */
+  int32_t vocab_size;            /* 262144 */
+  int32_t ple_dim;               /* 256 */
+  int32_t attn_bits;             /* 4 */
+  int32_t mlp_bits;              /* 4 (the checkpoint's 2-bit consumer MLP is not built) */
+  int32_t ple_bits;              /* 8, the I8 PLE linears (src/quant.ts:610-620) */
+  float rms_eps;                 /* 1e-6 */
+  float final_softcap;           /* 30 */
+  float rope_theta_sliding;      /* 1e4 */
+  float rope_theta_global;       /* 1e6 */
+  float partial_rotary_factor;   /* 0.25 */
+} g4_arch;
+
+/* Fill `arch` with the Gemma-4-E2B-shaped synthetic architecture of the benchmark configs. */
+int g4_arch_default(g4_arch *arch);
+
+/* --------------------------------------------------------------------------- context */
+
+typedef struct g4_config {
+  g4_arch arch;
+  int32_t max_seqs;          /* sequence slots, each with its own KV region */
+  int32_t max_context;       /* positions per sequence (kv.ts DEFAULT_MAX_CONTEXT is 2048) */
+  int32_t max_step_columns;  /* widest step: a prefill chunk or a decode batch */
+  int32_t use_graphs;        /* 1: record decode steps into CUDA graphs (default) */
+  uint64_t ple_slice_bytes;  /* 0: PLE table is one buffer; else the vocab-row slice cap */
+} g4_config;
+
+/* Defaults: g4_arch_default, max_seqs 1, max_context 2048, max_step_columns 64, graphs on. */
+int g4_config_default(g4_config *cfg);
+
+/*
+ * Create a context on CUDA device `cuda_device`. Allocates activations, KV caches (f32, K then V
+ * per producer layer, src/kv.ts:116-148) and rope tables; weights are added afterwards by
+ * g4_init_random or g4_upload_weight. Replaces GpuExecutor construction and
+ * BufferManager/createKvLayout (src/runtime.ts:193-358, src/buffers.ts:203, src/kv.ts:116).
+ */
+int g4_ctx_create(int cuda_device, const g4_config *cfg, g4_ctx **out);
+void g4_ctx_destroy(g4_ctx *ctx);
+
+/* Bytes of device memory the context holds (weights + KV + activations). */
+int g4_ctx_memory(const g4_ctx *ctx, uint64_t *weight_bytes, uint64_t *kv_bytes, uint64_t *other_bytes);
+
+/* ---------------------------------------------------------------------------- weights */
+
+/*
+ * Build the seeded synthetic model on the device: int4 linears with f16 row scales, I8 PLE
+ * linears, int4 embedding (tied lm_head) and PLE tables, bf16 per_layer_model_projection, f32
+ * norm gains, layer scalars and static activation scales. The generator is a counter hash of
+ * (seed, tensor, element), so any tensor can be regenerated on the host for checking.
+ * Replaces Gemma4Mobile.load's weight stream (src/engine.ts:369-603, src/cache.ts:1057).
+ */
+int g4_init_random(g4_ctx *ctx, uint64_t seed);
+
+/*
+ * Upload bytes [offset, offset + n) of the tensor `name` (checkpoint naming, e.g.
+ * "model.language_model.layers.0.self_attn.q_proj.weight"), whose full size is `total` bytes.
+ * Mirrors BufferManager.uploadWeight (src/buffers.ts:369-486). Storage per family:
+ *   *.weight (linear)           packed codes, row major, packed axis last (src/quant.ts:11-15)
+ *   *.weight_scale              f16, one per output row
+ *   *.embedding_quantized       int4 rows; *.embedding_scale f16 (embed) or f16 [rows, 35] (PLE)
+ *   *norm*.weight               f32 (the reference widens bf16 at load, src/engine.ts:550-556)
+ *   per_layer_model_projection  bf16, [8960, 1536] (src/quant.ts:396-398)
+ */
+int g4_upload_weight(g4_ctx *ctx, const char *name, const void *bytes, uint64_t offset,
+                     uint64_t n, uint64_t total);
+
+/* Copy a resident tensor back to the host (for checks). `*n` in: capacity, out: bytes. */
+int g4_download_weight(g4_ctx *ctx, const char *name, void *bytes, uint64_t *n);
+
+/*
+ * Four-byte checkpoint scalars: `<module>.input_activation_scale`,
+ * `<module>.output_activation_scale` and `layers.N.layer_scalar`. 0.0 means uncalibrated.
+ * Mirrors the host scalars map (src/engine.ts:547-549, src/runtime.ts:63-70).
+ */
+int g4_set_scalar(g4_ctx *ctx, const char *name, float value);
+int g4_get_scalar(const g4_ctx *ctx, const char *name, float *value);
+
+/*
+ * Split the PLE table into vocab-row slices of at most `slice_bytes`, one device buffer per
+ * slice, rows aligned to 16 (planTableSplit, src/tableSplit.ts:125-215; declareSplit,
+ * src/buffers.ts:291-326). Must precede weight creation. Reports the plan through the out
+ * arguments (nullable).
+ */
+int g4_plan_table_split(uint64_t rows, uint64_t row_bytes, uint64_t limit_bytes,
+                        uint64_t slice_bytes, int32_t *n_slices, int32_t *rows_per_slice,
+                        int32_t *last_rows);
+
+/* ---------------------------------------------------------------------------- forward */
+
+/*
+ * ForwardExecutor.prefill (src/runtime.ts:960-973): run `n` prompt tokens of sequence `seq` at
+ * positions start_pos.., storing their KV. A chunk that is not the last runs the 15 KV producer
+ * layers only (src/plan.ts:812-824); the last chunk runs all layers and the head and writes the
+ * argmax of its final position to *out_token (-1 otherwise).
+ */
+int g4_prefill(g4_ctx *ctx, int32_t seq, const int32_t *ids, int32_t n, int32_t start_pos,
+               int32_t is_last, int32_t *out_token);
+
+/*
+ * ForwardExecutor.decode (src/runtime.ts:975-983): one decode step of `seq` with prev_token at
+ * `pos`; returns the greedy argmax in *out_token.
+ */
+int g4_decode(g4_ctx *ctx, int32_t seq, int32_t prev_token, int32_t pos, int32_t *out_token);
+
+/*
+ * ForwardExecutor.decodeAhead (src/runtime.ts:1016-1023): as g4_decode, but the input token is
+ * the one the previous step of this context left on the device, so the host need not have read
+ * it. `*out_token` receives this step's argmax.
+ */
+int g4_decode_ahead(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t *out_token);
+
+/*
+ * Batched decode (new; the reference has no batch dimension): B independent sequences, one
+ * column each, every column computed with exactly the arithmetic of a one-sequence step (the
+ * column-for-column contract of src/kernels/qgemvWide.ts:8-71).
+ */
+int g4_decode_batch(g4_ctx *ctx, int32_t B, const int32_t *seqs, const int32_t *tokens,
+                    const int32_t *positions, int32_t *out_tokens);
+
+/*
+ * Device-resident decode loop (no host copies per step). g4_step_stage copies B columns
+ * (sequence, token, position) into the context's device step buffer once; each
+ * g4_step_run_device then runs one decode step of those columns without waiting for the host.
+ * With `advance` nonzero the step leaves its argmax token and position + 1 in the buffer, so
+ * consecutive calls continue every sequence greedily (the decodeAhead chain of
+ * src/runtime.ts:518-536, entirely on the device). g4_step_read_tokens waits and returns the
+ * last step's tokens.
+ */
+int g4_step_stage(g4_ctx *ctx, int32_t B, const int32_t *seqs, const int32_t *tokens,
+                  const int32_t *positions);
+int g4_step_run_device(g4_ctx *ctx, int32_t B, int32_t advance);
+int g4_step_read_tokens(g4_ctx *ctx, int32_t B, int32_t *out_tokens);
+
+/* KvCacheState.truncate (src/kv.ts:247-254): host bookkeeping of the valid length of `seq`. */
+int g4_kv_truncate(g4_ctx *ctx, int32_t seq, int32_t n);
+int g4_kv_length(const g4_ctx *ctx, int32_t seq, int32_t *n);
+
+/*
+ * Diagnostics of the last step: the softcapped logits of column `col` (`n` floats, n <= vocab)
+ * and its top-2 (value, index) pairs. Mirrors lastLogits (src/engine.ts:820-878).
+ */
+int g4_read_logits(g4_ctx *ctx, int32_t col, float *out, int32_t n);
+
+/* Device stream the context launches on (a cudaStream_t), for callers that time on it. */
+void *g4_ctx_stream(g4_ctx *ctx);
+
+/* Launch count of the last forward call, as recorded by the executor. */
+int g4_last_launches(const g4_ctx *ctx, int32_t *launches);
+
+/* ------------------------------------------------------------------ per-operator calls */
+/*
+ * The operator API (the registry's Kernel.bind, src/kernels/registry.ts:108-119), one entry per
+ * kernel family, on caller-owned device pointers and a caller stream (NULL = default stream).
+ * They launch the same kernels the executor records into its graphs.
+ */
+
+/*
+ * Quantized linear, `cols` activation columns (qgemv-4bit / qgemv-8bit / qgemm-4bit, and the
+ * M-wide family: src/kernels/qgemv.ts:413-690, 1131-1176; src/kernels/qgemm.ts:532-552;
+ * src/kernels/qgemvWide.ts:452). wq: packed weights [N, K*bits/8] bytes; scales: f16 [N];
+ * x: f32 [cols, K]; y: f32 [cols, N]; acc_out: int32 [cols, N] or NULL (the exact integer
+ * accumulators on a calibrated site). bits is 4 or 8; K a multiple of 256 (4-bit) or 128
+ * (8-bit) (src/kernels/qgemv.ts:1258, 1305-1310). in_scale 0 selects the f32 path.
+ */
+int g4_op_qgemv(const void *wq, const void *scales, const float *x, float in_scale,
+                float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
+                int32_t *acc_out, void *stream);
+
+/* The fused gelu prologue build (qgemv-Nbit-gelu, src/kernels/qgemv.ts:371-400): the GEMV over
+ * gelu_tanh(gate) * up[up_offset..], snapped by in_scale. gate/up: f32 [cols, K]. */
+int g4_op_qgemv_gelu(const void *wq, const void *scales, const float *gate, const float *up,
+                     int32_t up_offset, int32_t up_stride, float in_scale, float out_scale,
+                     int32_t bits, int32_t N, int32_t K, int32_t cols, float *y, void *stream);
+
+/* rms-norm / rms-norm-weightless (src/kernels/rmsNorm.ts:131-208): gain NULL = weightless. */
+int g4_op_rms_norm(const float *src, const float *gain, float *dst, int32_t rows,
+                   int32_t width, float eps, void *stream);
+
+/* norm-residual (src/kernels/mlpEpilogue.ts:109-220): dst = residual + norm(src) * gain. */
+int g4_op_norm_residual(const float *src, const float *gain, const float *residual,
+                        float *dst, int32_t rows, int32_t width, float eps, void *stream);
+
+/* norm-residual-norm (src/kernels/blockJoin.ts:73-160): hidden = alpha * (residual +
+ * norm(src) * gain); dst = norm(hidden) * gain2. */
+int g4_op_norm_residual_norm(const float *src, const float *gain, const float *residual,
+                             const float *gain2, float alpha, float *hidden, float *dst,
+                             int32_t rows, int32_t width, float eps, void *stream);
+
+/* gelu-mul with the SRQ snap (src/kernels/geluMul.ts:101-240). */
+int g4_op_gelu_mul(const float *gate, const float *up, float *dst, int32_t n, float srq_scale,
+                   void *stream);
+
+/* q-norm-rope (src/kernels/attnPrologue.ts:83-170): rows (position, head) of `width`;
+ * cos/sin tables [positions, width/2]; rows_per_position rows share one table row. */
+int g4_op_q_norm_rope(const float *src, const float *gain, const float *cos_tab,
+                      const float *sin_tab, float *dst, int32_t rows, int32_t width,
+                      int32_t rows_per_position, float eps, void *stream);
+
+/* kv-norm-rope-store (src/kernels/attnPrologue.ts:172-260): k, v [tokens, head_dim] into the
+ * packed cache [2, max_context, head_dim] at start_pos. */
+int g4_op_kv_norm_rope_store(const float *k, const float *v, const float *gain,
+                             const float *cos_tab, const float *sin_tab, float *cache,
+                             int32_t tokens, int32_t head_dim, int32_t start_pos,
+                             int32_t max_context, float eps, void *stream);
+
+/* attention-decode / attention-prefill (src/kernels/attention.ts:339-752, oracle 858-903):
+ * q [q_count, heads, head_dim]; cache packed K then V [2, max_context, head_dim]; window 0 =
+ * global. Scale 1.0 (src/kernels/attention.ts:81). */
+int g4_op_attention(const float *q, const float *cache, float *out, int32_t heads,
+                    int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,
+                    int32_t window, int32_t max_context, void *stream);
+
+/* embed-gather (int4 rows here) and ple-gather-4bit(-sliced) (src/kernels/embedGather.ts:
+ * 176-261, 319-344, 547-577). codes: row-major int4; scales f16 [rows, groups]; ids int32
+ * [slots]; dst f32 [slots, cols]. A sliced call writes only the slots whose id lies in
+ * [slice_start, slice_start + slice_rows) and reads codes relative to slice_start. */
+int g4_op_embed_gather(const void *codes, const void *scales, const int32_t *ids, float *dst,
+                       int32_t slots, int32_t cols, int32_t group_size, float out_scale,
+                       int32_t slice_start, int32_t slice_rows, void *stream);
+
+/* dense-bf16-matmul (src/kernels/denseMatmul.ts:93-222): y[c, r] = alpha * dot(w[r], x[c]). */
+int g4_op_dense_bf16(const void *w, const float *x, float *y, int32_t N, int32_t K,
+                     int32_t cols, float alpha, void *stream);
+
+/* logit-softcap then the two-stage argmax (src/kernels/logitSoftcap.ts:54-120,
+ * src/kernels/argmax.ts:43-310): capped may be NULL; token receives (index, value bits). */
+int g4_op_softcap_argmax(const float *logits, float *capped, int32_t *token, int32_t n,
+                         float cap, void *stream);
+
+/* Elementwise probes of the library's f32 exp and tanh (used by the attention softmax, GELU
+ * and the softcap), for checking them against CUDA's expf/tanhf within error bounds. */
+int g4_op_math_probe(const float *x, float *exp_out, float *tanh_out, float *cuda_exp,
+                     float *cuda_tanh, int32_t n, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* G4_H */

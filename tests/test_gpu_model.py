@@ -1,0 +1,175 @@
+"""End-to-end parity of the CUDA executor (through the C ABI) against the CPU oracle's forward.
+
+Greedy tokens must be identical and the logits bit-identical: every integer accumulation is
+exact and every f32 operation is the same single rounding in the same order on both sides.
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import __graft_entry__ as entry
+
+pytestmark = pytest.mark.gpu
+SEED = 0x6E6D6134
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def tiny(pkg, O, cuda):
+    a = entry.tiny_arch(pkg)
+    om = O.Model(SEED, entry.oracle_arch(O, a))
+    return a, om
+
+
+def make_ctx(pkg, a, **kw):
+    kw.setdefault("max_seqs", 4)
+    kw.setdefault("max_context", 128)
+    kw.setdefault("max_step_columns", 16)
+    ctx = pkg.engine.Context(device=0, arch=a, **kw)
+    ctx.init_random(SEED)
+    return ctx
+
+
+def oracle_run(O, om, prompt, new, max_ctx=128):
+    s = O.Sequence(om, max_ctx)
+    tok, logits, _ = s.forward(prompt[:-1], 0, False, False) if len(prompt) > 1 else (None, None, None)
+    tok, logits, _ = s.forward(prompt[-1:], len(prompt) - 1, True, True, want_logits=True)
+    toks, all_logits = [tok], [logits]
+    for i in range(1, new):
+        tok, logits, _ = s.forward(np.array([toks[-1]], np.int32), len(prompt) + i - 1, True, True,
+                                   want_logits=True)
+        toks.append(tok)
+        all_logits.append(logits)
+    return toks, all_logits
+
+
+def test_weights_match_generator(pkg, O, tiny):
+    a, om = tiny
+    ctx = make_ctx(pkg, a)
+    names = ["model.language_model.layers.0.self_attn.q_proj.weight",
+             "model.language_model.layers.1.self_attn.k_proj.weight_scale",
+             "model.language_model.layers.3.mlp.down_proj.weight",
+             "model.language_model.layers.2.per_layer_input_gate.weight",
+             "model.language_model.layers.2.per_layer_projection.weight_scale",
+             "model.language_model.layers.1.self_attn.q_norm.weight",
+             "model.language_model.embed_tokens.embedding_quantized",
+             "model.language_model.embed_tokens_per_layer.embedding_quantized",
+             "model.language_model.embed_tokens_per_layer.embedding_scale",
+             "model.language_model.per_layer_model_projection.weight",
+             "model.language_model.norm.weight"]
+    for n in names:
+        np.testing.assert_array_equal(ctx.download(n), om.tensor(n), err_msg=n)
+    for n in ["model.language_model.layers.0.self_attn.q_proj.input_activation_scale",
+              "model.language_model.layers.3.mlp.down_proj.output_activation_scale",
+              "model.language_model.layers.2.layer_scalar", "lm_head.input_activation_scale"]:
+        assert np.float32(ctx.scalar(n)) == np.float32(om.scalar(n)), n
+    ctx.close()
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_generation_bit_exact(pkg, O, tiny, graphs):
+    a, om = tiny
+    ctx = make_ctx(pkg, a, use_graphs=graphs)
+    prompt = O.synth_prompt(SEED, 20, a.vocab_size)
+    want, want_logits = oracle_run(O, om, prompt, 8)
+    first = ctx.prefill(0, prompt, 0, True)
+    got = [first]
+    np.testing.assert_array_equal(ctx.logits(0).view(np.uint32), want_logits[0].view(np.uint32))
+    for i in range(1, 8):
+        got.append(ctx.decode(0, got[-1], len(prompt) + i - 1))
+        np.testing.assert_array_equal(ctx.logits(0).view(np.uint32), want_logits[i].view(np.uint32))
+    assert got == want
+    ctx.close()
+
+
+def test_engine_generate_lookahead(pkg, O, tiny):
+    a, om = tiny
+    ctx = make_ctx(pkg, a)
+    model = pkg.engine.Gemma4Mobile(ctx)
+    prompt = O.synth_prompt(SEED + 1, 33, a.vocab_size)
+    want, _ = om.generate(prompt, 10, 128)
+    assert list(model.generate(prompt, 10)) == list(want)
+    # A second turn that extends the transcript reuses the KV prefix (kv.ts planKvReuse) and
+    # matches a cold run of the longer prompt.
+    longer = np.concatenate([prompt, np.array(want[:5], np.int32), [7, 8]]).astype(np.int32)
+    want2, _ = om.generate(longer, 6, 128)
+    assert list(model.generate(longer, 6, lookahead=False)) == list(want2)
+    ctx.close()
+
+
+def test_batch_matches_single(pkg, O, tiny):
+    """Column-for-column contract: a batched step computes each sequence exactly as alone."""
+    a, om = tiny
+    ctx = make_ctx(pkg, a, max_seqs=12, max_step_columns=16)
+    B = 11  # more than one 8-column launch group
+    prompts = [O.synth_prompt(SEED + 10 + b, 5 + b, a.vocab_size) for b in range(B)]
+    toks = [ctx.prefill(b, prompts[b], 0, True) for b in range(B)]
+    pos = [len(p) for p in prompts]
+    for step in range(3):
+        out = ctx.decode_batch(np.arange(B), toks, pos)
+        for b in range(B):
+            ref, _ = om.generate(prompts[b], step + 2, 128)
+            assert out[b] == ref[step + 1], (step, b)
+        toks = list(out)
+        pos = [p + 1 for p in pos]
+    ctx.close()
+
+
+def test_prefill_chunking_and_sliced_table(pkg, O, tiny):
+    a, om = tiny
+    prompt = O.synth_prompt(SEED + 3, 40, a.vocab_size)
+    want, _ = om.generate(prompt, 4, 128)
+    # max_step_columns 8 forces five producer chunks; a 256 KiB PLE slice cap splits the
+    # 4096-row table (512 B rows) into 8 slices of 512 rows.
+    ctx = make_ctx(pkg, a, max_step_columns=8, ple_slice_bytes=256 * 1024)
+    t = ctx.prefill(0, prompt, 0, True)
+    got = [t]
+    for i in range(1, 4):
+        got.append(ctx.decode_ahead(0, len(prompt) + i - 1))
+    assert got == list(want)
+    ctx.close()
+
+
+def test_invalid_calls(pkg, tiny):
+    a, _ = tiny
+    ctx = make_ctx(pkg, a)
+    with pytest.raises(pkg.G4Error, match="outside the vocabulary"):
+        ctx.decode(0, a.vocab_size, 0)
+    with pytest.raises(pkg.G4Error, match="gap"):
+        ctx.decode(0, 1, 5)
+    with pytest.raises(pkg.G4Error, match="sequence"):
+        ctx.decode(9, 1, 0)
+    with pytest.raises(pkg.G4Error, match="outside the context"):
+        ctx.prefill(0, np.ones(200, np.int32), 0, True)
+    with pytest.raises(pkg.G4Error, match="unknown tensor"):
+        ctx.download("model.language_model.layers.99.mlp.up_proj.weight")
+    ctx.close()
+
+
+def test_config2_full_model_greedy_128(pkg, O, cuda):
+    """BASELINE config 2 on the full Gemma-4-E2B shape: 128-token prompt, 128 greedy tokens,
+    identical to the oracle's tokens (tests/golden/config2_tokens.json, regenerated by
+    tests/golden/make_golden.py), with the first steps' logits checked bit for bit live."""
+    g = json.loads((GOLDEN / "config2_tokens.json").read_text())
+    prompt = np.array(g["prompt"], np.int32)
+    ctx = pkg.engine.Context(device=0, max_seqs=1, max_context=256, max_step_columns=64)
+    ctx.init_random(SEED)
+    om = O.Model(SEED)
+    s = O.Sequence(om, 256)
+    s.forward(prompt[:-1], 0, False, False)
+    t0, l0, _ = s.forward(prompt[-1:], 127, True, True, want_logits=True)
+    first = ctx.prefill(0, prompt, 0, True)
+    np.testing.assert_array_equal(ctx.logits(0).view(np.uint32), l0.view(np.uint32))
+    toks = [first]
+    for i in range(1, 128):
+        toks.append(ctx.decode_ahead(0, 128 + i - 1))
+        if i < 3:
+            t, li, _ = s.forward(np.array([toks[-2]], np.int32), 128 + i - 1, True, True, want_logits=True)
+            np.testing.assert_array_equal(ctx.logits(0).view(np.uint32), li.view(np.uint32))
+    assert toks == g["tokens"]
+    ctx.close()
+    om.close()
