@@ -4,14 +4,7 @@ The product is libgemma4_cuda.so (csrc/, C ABI in include/g4.h). This package is
 the ctypes binding (`_abi`), the reference's host interfaces (`engine`: Gemma4Mobile and the
 ForwardExecutor seam; `plan`: prefill chunks, dispatch lists, KV reuse, table split).
 """
-from . import _abi, plan  # noqa: F401
+from . import _abi, engine, plan  # noqa: F401
 from ._abi import G4Error, load  # noqa: F401
 
 __all__ = ["G4Error", "load", "plan", "engine"]
-
-
-def __getattr__(name):
-    if name == "engine":
-        from . import engine as _engine
-        return _engine
-    raise AttributeError(name)

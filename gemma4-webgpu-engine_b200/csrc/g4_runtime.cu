@@ -95,7 +95,11 @@ struct g4_ctx {
   int32_t *d_step = nullptr;   // [3][maxc]: seq, pos, token
   int32_t *d_tok_out = nullptr;
   float *d_val_out = nullptr;
-  int32_t *h_step = nullptr;   // pinned mirror of d_step
+  // Pinned staging ring: slot i is reused only after the copy that read it has executed.
+  static constexpr int kStageSlots = 4;
+  int32_t *h_step[kStageSlots] = {nullptr, nullptr, nullptr, nullptr};
+  cudaEvent_t stage_ev[kStageSlots] = {nullptr, nullptr, nullptr, nullptr};
+  int stage_next = 0;
   int32_t *h_tok = nullptr;    // pinned token outputs
   uint64_t other_bytes = 0;
   std::map<GraphKey, cudaGraphExec_t> graphs;
@@ -424,7 +428,10 @@ static int alloc_runtime(g4_ctx *ctx) {
   CK(cudaMemset(ctx->d_step, 0, (size_t)3 * maxc * 4));
   CK(cudaMalloc(&ctx->d_tok_out, (size_t)maxc * 4));
   CK(cudaMalloc(&ctx->d_val_out, (size_t)maxc * 4));
-  CK(cudaMallocHost(&ctx->h_step, (size_t)3 * maxc * 4));
+  for (int i = 0; i < g4_ctx::kStageSlots; i++) {
+    CK(cudaMallocHost(&ctx->h_step[i], (size_t)3 * maxc * 4));
+    CK(cudaEventCreateWithFlags(&ctx->stage_ev[i], cudaEventDisableTiming));
+  }
   CK(cudaMallocHost(&ctx->h_tok, (size_t)maxc * 4));
   return G4_OK;
 }
@@ -493,7 +500,10 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   cudaFree(ctx->head_pi);
   cudaFree(ctx->d_step);
   cudaFree(ctx->d_tok_out);
-  cudaFreeHost(ctx->h_step);
+  for (int i = 0; i < g4_ctx::kStageSlots; i++) {
+    cudaFreeHost(ctx->h_step[i]);
+    if (ctx->stage_ev[i]) cudaEventDestroy(ctx->stage_ev[i]);
+  }
   cudaFreeHost(ctx->h_tok);
   if (ctx->st) cudaStreamDestroy(ctx->st);
   delete ctx;
@@ -1017,14 +1027,22 @@ static int check_seq_pos(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t n) {
   return G4_OK;
 }
 
+// Copy one step's columns into the device step buffer. The pinned source slot is rewritten only
+// once the copy that last read it has executed on the stream (consecutive prefill chunks are
+// enqueued without a host wait).
 static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos, const int32_t *toks,
                  bool tokens_too) {
+  const int slot = ctx->stage_next;
+  ctx->stage_next = (slot + 1) % g4_ctx::kStageSlots;
+  CK(cudaEventSynchronize(ctx->stage_ev[slot]));
+  int32_t *h = ctx->h_step[slot];
   for (int i = 0; i < cols; i++) {
-    ctx->h_step[i] = seqs[i];
-    ctx->h_step[ctx->maxc + i] = pos[i];
-    if (tokens_too) ctx->h_step[2 * ctx->maxc + i] = toks[i];
+    h[i] = seqs[i];
+    h[ctx->maxc + i] = pos[i];
+    if (tokens_too) h[2 * ctx->maxc + i] = toks[i];
   }
-  CK(cudaMemcpyAsync(ctx->d_step, ctx->h_step, (size_t)ctx->maxc * 4 * (tokens_too ? 3 : 2), cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaMemcpyAsync(ctx->d_step, h, (size_t)ctx->maxc * 4 * (tokens_too ? 3 : 2), cudaMemcpyHostToDevice, ctx->st));
+  CK(cudaEventRecord(ctx->stage_ev[slot], ctx->st));
   return G4_OK;
 }
 
@@ -1223,7 +1241,7 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
     a.src = x + (size_t)c0 * K;
     a.ld_src = K;
     int blocks = (N + 8 * rpw - 1) / (8 * rpw);
-    OPCK(launch_gemv(a, bits, blocks, st, false));
+    OPCK(launch_gemv(a, bits, blocks, st, true));
   }
   OPCK(cudaGetLastError());
   return G4_OK;

@@ -14,8 +14,21 @@ pytestmark = pytest.mark.gpu
 RNG = np.random.default_rng(0x6E6D6134)
 
 
+_KEEP = []
+
+
+@pytest.fixture(autouse=True)
+def _keep_alive():
+    """Device tensors passed to the C ABI as raw pointers stay referenced for the whole test,
+    so the caching allocator cannot hand their memory to the next argument."""
+    yield
+    _KEEP.clear()
+
+
 def dev(cuda, a):
-    return cuda.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = cuda.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
 
 
 def host(t):
