@@ -129,6 +129,9 @@ static int fail(g4_ctx *c, int code, const char *fmt, ...) {
                   "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
   } while (0)
 
+// For the other translation units of the library: record a context-free error message.
+void g4_internal_set_error(const char *msg) { tl_error = msg; }
+
 extern "C" const char *g4_last_error(const g4_ctx *ctx) {
   return ctx ? ctx->err.c_str() : tl_error.c_str();
 }

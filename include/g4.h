@@ -299,6 +299,23 @@ int g4_op_dense_bf16(const void *w, const float *x, float *y, int32_t N, int32_t
 int g4_op_softcap_argmax(const float *logits, float *capped, int32_t *token, int32_t n,
                          float cap, void *stream);
 
+/*
+ * g4_op_attention without any device allocation. No counterpart in the reference: the WebGPU
+ * engine has no allocator-free path. It exists for callers that cannot allocate device memory
+ * (a host that has handed all memory to its own pools, a server that must not block on or fail
+ * in the allocator once running, an embedding whose allocator belongs to someone else). Same
+ * arguments and results as g4_op_attention; the per-block scratch is a fixed 4 MiB file-scope
+ * device array (1,048,576 floats; needed: q_count * blocks * heads * (head_dim + 2), blocks =
+ * window ? ceil(window / 64) + 1 : ceil(kv_len / 64)) that each device loading the library keeps until
+ * the process exits. Larger requests return G4_ERR_INVALID. The first call on a device looks up
+ * the array's device address with that device current; make that first call before any stream
+ * capture. Calls share the array: two calls that overlap on the GPU (different streams, or
+ * different host threads) race on it and must be serialised by the caller.
+ */
+int g4_op_attention_noalloc(const float *q, const float *cache, float *out, int32_t heads,
+                            int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,
+                            int32_t window, int32_t max_context, void *stream);
+
 /* Elementwise probes of the library's f32 exp and tanh (used by the attention softmax, GELU
  * and the softcap), for checking them against CUDA's expf/tanhf within error bounds. */
 int g4_op_math_probe(const float *x, float *exp_out, float *tanh_out, float *cuda_exp,
