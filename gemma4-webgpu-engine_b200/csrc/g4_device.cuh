@@ -145,6 +145,27 @@ __device__ __forceinline__ float srq_out(float v, float s) {
   return __fmul_rn(q, s);
 }
 
+// The same snaps through a precomputed reciprocal r = RN(1 / s). t = RN(x * r) lies within
+// |x / s| * 2^-23 of x / s, and so does RN(x / s); for |x / s| < 130 both are within 1.6e-5 of
+// x / s, so whenever t is more than 1e-4 away from a half-integer, rint(t) equals
+// rint(RN(x / s)) exactly. Closer to a tie the exact division decides. |t| >= 130 clamps either
+// way. Bit-identical to srq_code / srq_out, without a division per element.
+__device__ __forceinline__ float srq_q_r(float x, float s, float r) {
+  const float t = __fmul_rn(x, r);
+  if (fabsf(t) < 130.0f) {
+    const float f = __fsub_rn(t, floorf(t));
+    if (fabsf(__fsub_rn(f, 0.5f)) > 1e-4f) return fminf(fmaxf(rintf(t), -128.0f), 127.0f);
+    return fminf(fmaxf(rintf(__fdiv_rn(x, s)), -128.0f), 127.0f);
+  }
+  return t > 0.0f ? 127.0f : -128.0f;
+}
+__device__ __forceinline__ int srq_code_r(float x, float s, float r) { return (int)srq_q_r(x, s, r); }
+// The quotient stays a float so a negative value that rounds to zero keeps its sign (-0.0).
+__device__ __forceinline__ float srq_out_r(float v, float s, float r) {
+  if (s == 0.0f) return v;
+  return __fmul_rn(srq_q_r(v, s, r), s);
+}
+
 // ---------------------------------------------------------------------- reductions
 // The 32-lane XOR butterfly, masks 1, 2, 4, 8, 16: every lane ends with the same balanced
 // pairwise tree.

@@ -41,8 +41,9 @@ static cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t s
 struct ChunkPro {
   // Snap four activations of column c at chunk ch to codes and store them in the dp4a layout.
   template <int BITS>
-  static __device__ __forceinline__ int store(uint8_t *codes, int ch, float4 x, float s) {
-    int q0 = srq_code(x.x, s), q1 = srq_code(x.y, s), q2 = srq_code(x.z, s), q3 = srq_code(x.w, s);
+  static __device__ __forceinline__ int store(uint8_t *codes, int ch, float4 x, float s, float r) {
+    int q0 = srq_code_r(x.x, s, r), q1 = srq_code_r(x.y, s, r), q2 = srq_code_r(x.z, s, r),
+        q3 = srq_code_r(x.w, s, r);
     if (BITS == 4) {
       uint16_t *cw = reinterpret_cast<uint16_t *>(codes);
       int g = ch >> 1, half = ch & 1;
@@ -79,6 +80,7 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, int c, float
   const int t = threadIdx.x;
   const int K = a.K;
   const int nc = K >> 2;
+  const float in_r = __fdiv_rn(1.0f, in_scale);
   int xs = 0;
   if (a.pro == PRO_X || a.pro == PRO_GELU) {
     const float4 *src = reinterpret_cast<const float4 *>(a.src + (size_t)c * a.ld_src);
@@ -88,7 +90,7 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, int c, float
     for (int ch = t; ch < nc; ch += 256) {
       float4 x = src[ch];
       if (a.pro == PRO_GELU) x = f4_gelu_mul(x, up[ch]);
-      xs += ChunkPro::store<BITS>(codes, ch, x, in_scale);
+      xs += ChunkPro::store<BITS>(codes, ch, x, in_scale, in_r);
     }
     return xs;
   }
@@ -131,168 +133,8 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, int c, float
   }
 #pragma unroll
   for (int i = 0; i < 2; i++)
-    if (i < cnt) xs += ChunkPro::store<BITS>(codes, t + 256 * i, xv[i], in_scale);
+    if (i < cnt) xs += ChunkPro::store<BITS>(codes, t + 256 * i, xv[i], in_scale, in_r);
   return xs;
-}
-
-template <int BITS, int COLS, int RPW, int PPR>
-__global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int bid = blockIdx.x;
-  int s = 0;
-  if (a.nseg > 1 && bid >= a.seg[1].block_begin) s = 1;
-  if (a.nseg > 2 && bid >= a.seg[2].block_begin) s = 2;
-  const GemvSeg sg = a.seg[s];
-  const int K = a.K;
-  const int row_bytes = K * BITS / 8;
-  const int row0 = (bid - sg.block_begin) * (8 * RPW) + warp * RPW;
-
-  uint8_t *codes = smem;                                       // [COLS][K]
-  int *xsum = reinterpret_cast<int *>(smem + COLS * K);        // [8]
-  float *red = reinterpret_cast<float *>(xsum + 8);            // [8]
-  float *cand_v = red + 8;                                     // [8][COLS]
-  int *cand_i = reinterpret_cast<int *>(cand_v + 8 * COLS);    // [8][COLS]
-
-  // Weight stream first: it does not depend on the previous kernel.
-  uint4 wv[RPW][PPR];
-#pragma unroll
-  for (int rr = 0; rr < RPW; rr++) {
-    const int row = row0 + rr;
-#pragma unroll
-    for (int i = 0; i < PPR; i++) {
-      const int off = lane * 16 + 512 * i;
-      if (row < sg.N && off < row_bytes)
-        wv[rr][i] = ldg_stream(sg.w + (size_t)row * row_bytes + off);
-      else
-        wv[rr][i] = make_uint4(0, 0, 0, 0);
-    }
-  }
-  float wscale[RPW];
-#pragma unroll
-  for (int rr = 0; rr < RPW; rr++)
-    wscale[rr] = (row0 + rr < sg.N) ? f16_bits_to_f32(__ldg(sg.s + row0 + rr)) : 0.0f;
-  if (t < 8) xsum[t] = 0;
-  grid_launch_dependents();
-  grid_wait();
-
-  // Prologue: activation codes for every column into shared memory.
-  int xs_local[COLS];
-#pragma unroll
-  for (int c = 0; c < COLS; c++) {
-    xs_local[c] = 0;
-    if (c < a.cols)
-      xs_local[c] = gemv_prologue_col<BITS>(a, c, sg.in_scale, codes + c * K, red,
-                                            bid == 0 && a.hidden_out != nullptr);
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < COLS; c++) {
-    int v = warp_sum_int(xs_local[c]);
-    if (lane == 0 && c < a.cols) atomicAdd(&xsum[c], v);
-  }
-  __syncthreads();
-
-  // Exact integer code dot.
-  int acc[RPW][COLS];
-#pragma unroll
-  for (int rr = 0; rr < RPW; rr++)
-#pragma unroll
-    for (int c = 0; c < COLS; c++) acc[rr][c] = 0;
-#pragma unroll
-  for (int rr = 0; rr < RPW; rr++) {
-#pragma unroll
-    for (int i = 0; i < PPR; i++) {
-      const int off = lane * 16 + 512 * i;
-      if (off < row_bytes) {
-        const uint4 w = wv[rr][i];
-#pragma unroll
-        for (int c = 0; c < COLS; c++) {
-          if (BITS == 4) {
-            const uint4 *xp = reinterpret_cast<const uint4 *>(codes + c * K + 2 * off);
-            const uint4 x01 = xp[0], x23 = xp[1];
-            const uint32_t M = 0x0F0F0F0Fu;
-            int v = acc[rr][c];
-            v = dp4a_us(w.x & M, x01.x, v);
-            v = dp4a_us((w.x >> 4) & M, x01.y, v);
-            v = dp4a_us(w.y & M, x01.z, v);
-            v = dp4a_us((w.y >> 4) & M, x01.w, v);
-            v = dp4a_us(w.z & M, x23.x, v);
-            v = dp4a_us((w.z >> 4) & M, x23.y, v);
-            v = dp4a_us(w.w & M, x23.z, v);
-            v = dp4a_us((w.w >> 4) & M, x23.w, v);
-            acc[rr][c] = v;
-          } else {
-            const uint4 xv = *reinterpret_cast<const uint4 *>(codes + c * K + off);
-            int v = acc[rr][c];
-            v = dp4a_ss(w.x, xv.x, v);
-            v = dp4a_ss(w.y, xv.y, v);
-            v = dp4a_ss(w.z, xv.z, v);
-            v = dp4a_ss(w.w, xv.w, v);
-            acc[rr][c] = v;
-          }
-        }
-      }
-    }
-  }
-
-  // Epilogue: one f32 multiply to fold the input scale into the row scale, one against the
-  // exact sum, then the output snap (src/kernels/qgemv.ts:681-686, 1168-1172).
-  float best_v[COLS];
-  int best_i[COLS];
-#pragma unroll
-  for (int c = 0; c < COLS; c++) {
-    best_v[c] = -FLT_MAX;
-    best_i[c] = 0x7fffffff;
-  }
-#pragma unroll
-  for (int rr = 0; rr < RPW; rr++) {
-    const int row = row0 + rr;
-#pragma unroll
-    for (int c = 0; c < COLS; c++) {
-      int v = warp_sum_int(acc[rr][c]);
-      if (lane == 0 && row < sg.N && c < a.cols) {
-        int exact = BITS == 4 ? v - 8 * xsum[c] : v;
-        float y = __fmul_rn(__fmul_rn(sg.in_scale, wscale[rr]), (float)exact);
-        y = srq_out(y, sg.out_scale);
-        if (sg.acc_out) sg.acc_out[(size_t)c * sg.N + row] = exact;
-        if (a.head) {
-          if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
-          if (a.logits) a.logits[(size_t)c * a.ld_logits + row] = y;
-          if (y > best_v[c]) {
-            best_v[c] = y;
-            best_i[c] = row;
-          }
-        } else {
-          sg.y[(size_t)c * sg.N + row] = y;
-        }
-      }
-    }
-  }
-  if (a.head) {
-    if (lane == 0) {
-#pragma unroll
-      for (int c = 0; c < COLS; c++) {
-        cand_v[warp * COLS + c] = best_v[c];
-        cand_i[warp * COLS + c] = best_i[c];
-      }
-    }
-    __syncthreads();
-    if (t < COLS && t < a.cols) {
-      float bv = -FLT_MAX;
-      int bi = 0x7fffffff;
-      for (int w = 0; w < 8; w++) {
-        float v = cand_v[w * COLS + t];
-        int i = cand_i[w * COLS + t];
-        if (v > bv || (v == bv && i < bi)) {
-          bv = v;
-          bi = i;
-        }
-      }
-      a.part_val[(size_t)t * a.n_blocks_total + bid] = bv;
-      a.part_idx[(size_t)t * a.n_blocks_total + bid] = bi;
-    }
-  }
 }
 
 // The f32 path of an uncalibrated site (in_scale == 0, src/kernels/qgemv.ts:666-675), one column:
@@ -342,57 +184,380 @@ __global__ void __launch_bounds__(256) k_gemv_f32(const GemvArgs a) {
   }
 }
 
-bool gemv_geometry(int bits, int K, int N_total, int *rpw, int *ppr) {
-  const int row_bytes = K * bits / 8;
-  if (row_bytes % 16 != 0) return false;
-  int p = (row_bytes + 511) / 512;
-  static const int caps[] = {1, 2, 3, 4, 6, 8};
-  int cap = 0;
-  for (int c : caps)
-    if (c >= p) {
-      cap = c;
-      break;
-    }
-  if (!cap) return false;
-  int r = 1;
-  // Wider rows per warp only where the geometry is instantiated and the launch stays >= 2 waves.
-  if (bits == 4 && cap == 2 && N_total / 32 >= 296) r = 4;
-  else if (bits == 4 && (cap == 2 || cap == 4) && N_total / 16 >= 296) r = 2;
-  else if (bits == 8 && cap == 1 && N_total / 32 >= 296) r = 4;
-  else if (bits == 8 && (cap == 1 || cap == 3) && N_total / 16 >= 296) r = 2;
-  *rpw = r;
-  *ppr = cap;
-  return true;
+// =====================================================================================
+// Streaming quantized linear. One CTA per SM (or fewer): CTA i of a segment owns the contiguous
+// rows [N i / nb, N (i + 1) / nb), a contiguous byte range of the packed weights, and streams it
+// through a shared-memory ring with TMA bulk copies (cp.async.bulk, completion on an mbarrier).
+// The first stages are requested before the programmatic-dependency wait, so a launch's weight
+// stream starts while the previous kernel is still finishing; the CTA may also pull the weights
+// of later launches into L2 (cp.async.bulk.prefetch.L2). Arithmetic is k_gemv's: exact int32
+// dp4a code dots and the same epilogue.
+// =====================================================================================
+
+__device__ int g4_dev_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.b32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase: false once the iteration limit is reached.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 22); i++)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void l2_prefetch(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-template <int BITS, int COLS, int RPW, int PPR>
-static cudaError_t launch_gemv_t(const GemvArgs &a, int n_blocks, cudaStream_t st, bool pdl) {
-  size_t smem = (size_t)COLS * a.K + 16 * 4 + 8 * COLS * 8;
-  auto k = k_gemv<BITS, COLS, RPW, PPR>;
+constexpr int GS_RING = 96 * 1024;   // shared-memory ring per CTA
+constexpr int GS_MAX_STAGES = 8;
+
+// A long row is processed as RS "virtual rows" of at most 1 KB (the integer code dot of a row is
+// the exact sum of its parts, so the split changes no value).
+__host__ __device__ __forceinline__ int gs_row_split(int row_bytes) {
+  if (row_bytes <= 1024) return 1;
+  if (row_bytes % 2 == 0 && row_bytes / 2 <= 1024 && (row_bytes / 2) % 16 == 0) return 2;
+  return 4;
+}
+// Virtual rows per stage: whole 32-row groups (eight warps x four rows), at most 32 KB.
+__host__ __device__ __forceinline__ int gs_stage_vrows(int vrow_bytes) {
+  int k = (32 * 1024) / (32 * vrow_bytes);
+  return 32 * (k < 1 ? 1 : k);
+}
+
+// Split `bytes` at `p` into this CTA's 16-byte-aligned share and prefetch it into L2.
+__device__ __forceinline__ void l2_prefetch_share(const void *p, uint64_t bytes, int i, int n) {
+  if (!p || bytes == 0) return;
+  uint64_t lo = (bytes * (uint64_t)i / n) & ~(uint64_t)15, hi = (bytes * (uint64_t)(i + 1) / n) & ~(uint64_t)15;
+  if (i + 1 == n) hi = bytes & ~(uint64_t)15;
+  for (uint64_t o = lo; o < hi; o += 65536) {
+    uint64_t len = hi - o < 65536 ? hi - o : 65536;
+    l2_prefetch((const uint8_t *)p + o, (uint32_t)len);
+  }
+}
+
+template <int BITS, int COLS, int RS>
+__global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *ring = smem;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + GS_RING);
+  int *xsum = reinterpret_cast<int *>(bars + GS_MAX_STAGES);
+  float *red = reinterpret_cast<float *>(xsum + 8);
+  float *cand_v = red + 8;
+  int *cand_i = reinterpret_cast<int *>(cand_v + 8 * COLS);
+  uint8_t *codes = reinterpret_cast<uint8_t *>(cand_i + 8 * COLS);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int bid = blockIdx.x;
+  int s = 0;
+  if (a.nseg > 1 && bid >= a.seg[1].block_begin) s = 1;
+  if (a.nseg > 2 && bid >= a.seg[2].block_begin) s = 2;
+  const GemvSeg sg = a.seg[s];
+  const int nb = (s + 1 < a.nseg ? a.seg[s + 1].block_begin : a.n_blocks_total) - sg.block_begin;
+  const int ib = bid - sg.block_begin;
+  const int r0 = (int)(((long long)sg.N * ib) / nb);
+  const int r1 = (int)(((long long)sg.N * (ib + 1)) / nb);
+  const int K = a.K;
+  const int row_bytes = K * BITS / 8;
+  const int vb = row_bytes / RS;                 // bytes per virtual row
+  const int svrows = gs_stage_vrows(vb);         // virtual rows per stage
+  const int srows = svrows / RS;                 // real rows per stage
+  const int stage_bytes = srows * row_bytes;
+  int nstages = GS_RING / stage_bytes;
+  if (nstages > GS_MAX_STAGES) nstages = GS_MAX_STAGES;
+  const int nchunks = (r1 - r0 + srows - 1) / srows;
+
+  if (t == 0) {
+    for (int i = 0; i < nstages; i++) mbar_init(&bars[i], 1);
+    mbar_fence_init();
+  }
+  if (t < 8) xsum[t] = 0;
+  __syncthreads();
+  auto issue = [&](int c) {
+    const int st = c % nstages;
+    const int cr0 = r0 + c * srows;
+    const int rows = min(srows, r1 - cr0);
+    const uint32_t bytes = (uint32_t)(rows * row_bytes);
+    mbar_expect_tx(&bars[st], bytes);
+    bulk_g2s(ring + st * stage_bytes, sg.w + (size_t)cr0 * row_bytes, bytes, &bars[st]);
+  };
+  if (t == 0)
+    for (int c = 0; c < nchunks && c < nstages; c++) issue(c);
+  if (t == 32)
+    for (int i = 0; i < 4; i++) l2_prefetch_share(a.prefetch[i], a.prefetch_bytes[i], bid, gridDim.x);
+  grid_launch_dependents();
+  grid_wait();
+
+  int xs_local[COLS];
+#pragma unroll
+  for (int c = 0; c < COLS; c++) {
+    xs_local[c] = 0;
+    if (c < a.cols)
+      xs_local[c] = gemv_prologue_col<BITS>(a, c, sg.in_scale, codes + c * K, red,
+                                            bid == 0 && a.hidden_out != nullptr);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < COLS; c++) {
+    int v = warp_sum_int(xs_local[c]);
+    if (lane == 0 && c < a.cols) atomicAdd(&xsum[c], v);
+  }
+  __syncthreads();
+
+  float best_v[COLS];
+  int best_i[COLS];
+#pragma unroll
+  for (int c = 0; c < COLS; c++) {
+    best_v[c] = -FLT_MAX;
+    best_i[c] = 0x7fffffff;
+  }
+  const float out_r = sg.out_scale != 0.0f ? __fdiv_rn(1.0f, sg.out_scale) : 0.0f;
+  for (int ch = 0; ch < nchunks; ch++) {
+    const int st = ch % nstages;
+    const bool ok = mbar_wait(&bars[st], (uint32_t)((ch / nstages) & 1));
+    if (!__syncthreads_and(ok)) {
+      // A copy never completed: record it, give the copies still in flight a bounded wait so
+      // none lands in released shared memory, and leave.
+      if (t == 0) {
+        atomicExch(&g4_dev_error, 1);
+        for (int c2 = ch; c2 < nchunks && c2 < ch + nstages; c2++)
+          mbar_wait(&bars[c2 % nstages], (uint32_t)((c2 / nstages) & 1));
+      }
+      __syncthreads();
+      return;
+    }
+    const int cr0 = r0 + ch * srows;
+    const int vrows = min(srows, r1 - cr0) * RS;
+    const uint8_t *sw = ring + st * stage_bytes;
+    // Each warp takes groups of four virtual rows; the four dot products run as independent
+    // chains and close with one transposed reduction, after which lanes 0, 8, 16 and 24 hold
+    // the four totals; the parts of a split row are then added and its lanes finish the rows
+    // in parallel.
+    for (int g0 = warp * 4; g0 < vrows; g0 += 32) {
+      int acc[4][COLS];
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+#pragma unroll
+        for (int c = 0; c < COLS; c++) acc[q][c] = 0;
+      for (int off = lane * 16; off < vb; off += 512) {
+        uint4 w[4];
+        int koff[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const int vr = g0 + q;
+          koff[q] = (vr % RS) * vb + off;  // byte offset of this piece inside its real row
+          w[q] = vr < vrows ? *reinterpret_cast<const uint4 *>(sw + (size_t)vr * vb + off)
+                            : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int c = 0; c < COLS; c++) {
+          // RS == 1: all four rows read the same activation codes; RS == 2: rows 0/2 and 1/3.
+          constexpr int NX = RS == 1 ? 1 : (RS == 2 ? 2 : 4);
+          uint4 xa[NX], xb[NX];
+#pragma unroll
+          for (int j = 0; j < NX; j++) {
+            if (BITS == 4) {
+              const uint4 *xp = reinterpret_cast<const uint4 *>(codes + c * K + 2 * koff[j]);
+              xa[j] = xp[0];
+              xb[j] = xp[1];
+            } else {
+              xa[j] = *reinterpret_cast<const uint4 *>(codes + c * K + koff[j]);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const uint4 x01 = xa[q % NX];
+            int v = acc[q][c];
+            if (BITS == 4) {
+              const uint4 x23 = xb[q % NX];
+              const uint32_t M = 0x0F0F0F0Fu;
+              v = dp4a_us(w[q].x & M, x01.x, v);
+              v = dp4a_us((w[q].x >> 4) & M, x01.y, v);
+              v = dp4a_us(w[q].y & M, x01.z, v);
+              v = dp4a_us((w[q].y >> 4) & M, x01.w, v);
+              v = dp4a_us(w[q].z & M, x23.x, v);
+              v = dp4a_us((w[q].z >> 4) & M, x23.y, v);
+              v = dp4a_us(w[q].w & M, x23.z, v);
+              v = dp4a_us((w[q].w >> 4) & M, x23.w, v);
+            } else {
+              v = dp4a_ss(w[q].x, x01.x, v);
+              v = dp4a_ss(w[q].y, x01.y, v);
+              v = dp4a_ss(w[q].z, x01.z, v);
+              v = dp4a_ss(w[q].w, x01.w, v);
+            }
+            acc[q][c] = v;
+          }
+        }
+      }
+      // Transposed reduction of four rows: lanes < 16 keep rows 0-1, lanes >= 16 rows 2-3;
+      // bit 3 of the lane then picks one row; three more butterflies close it. Integer adds,
+      // so the grouping cannot change the sum.
+      const bool hi16 = lane >= 16, hi8 = (lane & 8) != 0;
+      const int my_vrow = (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
+#pragma unroll
+      for (int c = 0; c < COLS; c++) {
+        int b0 = (hi16 ? acc[2][c] : acc[0][c]) + __shfl_xor_sync(0xffffffffu, hi16 ? acc[0][c] : acc[2][c], 16);
+        int b1 = (hi16 ? acc[3][c] : acc[1][c]) + __shfl_xor_sync(0xffffffffu, hi16 ? acc[1][c] : acc[3][c], 16);
+        int v = (hi8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, hi8 ? b0 : b1, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        if (RS >= 2) v += __shfl_xor_sync(0xffffffffu, v, 8);   // parts 0+1 (and 2+3)
+        if (RS >= 4) v += __shfl_xor_sync(0xffffffffu, v, 16);  // parts (0+1)+(2+3)
+        acc[0][c] = v;
+      }
+      const int vr = g0 + my_vrow;
+      if ((lane & (8 * RS - 1)) == 0 && vr < vrows) {
+        const int row = cr0 + vr / RS;
+        const float wscale = f16_bits_to_f32(__ldg(sg.s + row));
+#pragma unroll
+        for (int c = 0; c < COLS; c++) {
+          if (c < a.cols) {
+            const int exact = BITS == 4 ? acc[0][c] - 8 * xsum[c] : acc[0][c];
+            float y = __fmul_rn(__fmul_rn(sg.in_scale, wscale), (float)exact);
+            y = srq_out_r(y, sg.out_scale, out_r);
+            if (sg.acc_out) sg.acc_out[(size_t)c * sg.N + row] = exact;
+            if (a.head) {
+              if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
+              if (a.logits) a.logits[(size_t)c * a.ld_logits + row] = y;
+              if (y > best_v[c] || (y == best_v[c] && row < best_i[c])) {
+                best_v[c] = y;
+                best_i[c] = row;
+              }
+            } else {
+              sg.y[(size_t)c * sg.N + row] = y;
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (t == 0 && ch + nstages < nchunks) issue(ch + nstages);
+  }
+  if (a.head) {
+#pragma unroll
+    for (int c = 0; c < COLS; c++) {
+      // The candidates sit in lanes 0, 8, 16, 24 of each warp; every other lane carries -FLT_MAX.
+#pragma unroll
+      for (int o = 8; o < 32; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best_v[c], o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i[c], o);
+        if (ov > best_v[c] || (ov == best_v[c] && oi < best_i[c])) {
+          best_v[c] = ov;
+          best_i[c] = oi;
+        }
+      }
+      if (lane == 0) {
+        cand_v[warp * COLS + c] = best_v[c];
+        cand_i[warp * COLS + c] = best_i[c];
+      }
+    }
+    __syncthreads();
+    if (t < COLS && t < a.cols) {
+      float bv = -FLT_MAX;
+      int bi = 0x7fffffff;
+      for (int w = 0; w < 8; w++) {
+        const float v = cand_v[w * COLS + t];
+        const int i = cand_i[w * COLS + t];
+        if (v > bv || (v == bv && i < bi)) {
+          bv = v;
+          bi = i;
+        }
+      }
+      a.part_val[(size_t)t * a.n_blocks_total + bid] = bv;
+      a.part_idx[(size_t)t * a.n_blocks_total + bid] = bi;
+    }
+  }
+}
+
+int gemv_stream_partition(GemvArgs &a, int sms) {
+  long long total = 0;
+  for (int i = 0; i < a.nseg; i++) total += a.seg[i].N;
+  int target = (int)(total < sms ? total : sms);
+  int begin = 0;
+  for (int i = 0; i < a.nseg; i++) {
+    long long nb = (a.seg[i].N * (long long)target + total - 1) / total;
+    if (nb < 1) nb = 1;
+    if (nb > a.seg[i].N) nb = a.seg[i].N;
+    a.seg[i].block_begin = begin;
+    begin += (int)nb;
+  }
+  a.n_blocks_total = begin;
+  return begin;
+}
+
+template <int BITS, int COLS, int RS>
+static cudaError_t launch_stream_t(const GemvArgs &a, cudaStream_t st, bool pdl) {
+  const size_t smem = GS_RING + GS_MAX_STAGES * 8 + 16 * 4 + 8 * COLS * 8 + (size_t)COLS * a.K;
+  auto k = k_qgemv_stream<BITS, COLS, RS>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr_set = true;
   }
-  return launch_k(k, dim3(n_blocks), dim3(256), smem, st, pdl, a);
+  return launch_k(k, dim3(a.n_blocks_total), dim3(256), smem, st, pdl, a);
 }
 
 template <int BITS, int COLS>
-static cudaError_t launch_gemv_c(const GemvArgs &a, int n_blocks, cudaStream_t st, bool pdl) {
-  const int r = a.rpw, p = a.ppr;
-#define G4_CASE(R, P) \
-  if (r == R && p == P) return launch_gemv_t<BITS, COLS, R, P>(a, n_blocks, st, pdl);
-  G4_CASE(1, 1) G4_CASE(1, 2) G4_CASE(1, 3) G4_CASE(1, 4) G4_CASE(1, 6) G4_CASE(1, 8)
-  if (BITS == 4) {
-    G4_CASE(2, 2) G4_CASE(2, 4) G4_CASE(4, 2)
-  } else {
-    G4_CASE(2, 1) G4_CASE(2, 3) G4_CASE(4, 1)
+static cudaError_t launch_stream_c(const GemvArgs &a, int rs, cudaStream_t st, bool pdl) {
+  if (rs == 1) return launch_stream_t<BITS, COLS, 1>(a, st, pdl);
+  if (rs == 2) return launch_stream_t<BITS, COLS, 2>(a, st, pdl);
+  return launch_stream_t<BITS, COLS, 4>(a, st, pdl);
+}
+
+cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, bool pdl) {
+  const int row_bytes = a.K * bits / 8;
+  const int rs = gs_row_split(row_bytes);
+  if (row_bytes % 16 != 0 || row_bytes % rs != 0 || row_bytes / rs > 1024 || (row_bytes / rs) % 16 != 0)
+    return cudaErrorInvalidConfiguration;
+  const int c = a.cols;
+  if (bits == 4) {
+    if (c <= 1) return launch_stream_c<4, 1>(a, rs, st, pdl);
+    if (c <= 2) return launch_stream_c<4, 2>(a, rs, st, pdl);
+    if (c <= 4) return launch_stream_c<4, 4>(a, rs, st, pdl);
+    if (c <= 8) return launch_stream_c<4, 8>(a, rs, st, pdl);
+  } else if (bits == 8) {
+    if (c <= 1) return launch_stream_c<8, 1>(a, rs, st, pdl);
+    if (c <= 2) return launch_stream_c<8, 2>(a, rs, st, pdl);
+    if (c <= 4) return launch_stream_c<8, 4>(a, rs, st, pdl);
+    if (c <= 8) return launch_stream_c<8, 8>(a, rs, st, pdl);
   }
-#undef G4_CASE
   return cudaErrorInvalidConfiguration;
 }
 
-cudaError_t launch_gemv(const GemvArgs &a, int bits, int n_blocks, cudaStream_t st, bool pdl) {
+int device_error_take() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g4_dev_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g4_dev_error, &zero, sizeof(int));
+  return v;
+}
+
+cudaError_t launch_gemv(const GemvArgs &a, int bits, cudaStream_t st, bool pdl) {
   if (a.seg[0].in_scale == 0.0f) {
     // Uncalibrated f32 path: one column, one segment, x or gelu prologue only.
     if (a.cols != 1 || a.nseg != 1 || !(a.pro == PRO_X || a.pro == PRO_GELU) || a.head)
@@ -406,19 +571,7 @@ cudaError_t launch_gemv(const GemvArgs &a, int bits, int n_blocks, cudaStream_t 
     cudaFuncSetAttribute(k_gemv_f32<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
     return launch_k(k_gemv_f32<8>, dim3(blocks), dim3(256), smem, st, pdl, a);
   }
-  const int c = a.cols;
-  if (bits == 4) {
-    if (c <= 1) return launch_gemv_c<4, 1>(a, n_blocks, st, pdl);
-    if (c <= 2) return launch_gemv_c<4, 2>(a, n_blocks, st, pdl);
-    if (c <= 4) return launch_gemv_c<4, 4>(a, n_blocks, st, pdl);
-    if (c <= 8) return launch_gemv_c<4, 8>(a, n_blocks, st, pdl);
-  } else if (bits == 8) {
-    if (c <= 1) return launch_gemv_c<8, 1>(a, n_blocks, st, pdl);
-    if (c <= 2) return launch_gemv_c<8, 2>(a, n_blocks, st, pdl);
-    if (c <= 4) return launch_gemv_c<8, 4>(a, n_blocks, st, pdl);
-    if (c <= 8) return launch_gemv_c<8, 8>(a, n_blocks, st, pdl);
-  }
-  return cudaErrorInvalidConfiguration;
+  return launch_gemv_stream(a, bits, st, pdl);
 }
 
 // =====================================================================================
@@ -839,6 +992,404 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl) {
     e = cudaErrorInvalidValue;
   }
   return e;
+}
+
+// =====================================================================================
+// Decode attention, fused (src/kernels/attnPrologue.ts:83-260 then src/kernels/attention.ts:
+// 339-752 for a step whose columns are distinct sequences at one new position each). Block
+// (c, bi) of a column:
+//   * before the dependency wait, pulls its K and V rows into L2 (a prefetch only: the
+//     position read there may be stale, which costs nothing but a wasted prefetch);
+//   * requests its V rows (all but the new position) as one bulk copy into shared memory;
+//   * normalises and rotates the 8 query heads itself (warp h: head h; the sum of squares
+//     follows block_sumsq256's chunk order exactly), and, in the block holding the new position
+//     of a producer layer, the K row (gain, rotation) and V row (weightless norm), which it
+//     stores to the cache and keeps in shared memory;
+//   * scores, block max, exp, and the weighted V sum exactly as k_attn_blocks;
+//   * writes its partial; the last block of the column to finish folds the partials in
+//     ascending block order exactly as k_attn_merge (a single block divides directly).
+// =====================================================================================
+
+// Normalise (gain optional) and rotate (cos/sin optional) one head row with one warp. Lane l
+// holds vec4 chunks l + 32 g (g < HD / 128), so its loads go out together and it owns whole
+// rotation pairs (chunk l + 32 g pairs with chunk l + 32 (g + HD / 256)). The sum of squares
+// follows block_sumsq256's order: thread i < HD / 4 squares chunk i, warp g's butterfly sums
+// chunks 32 g .. 32 g + 31, and the warp sums are added in ascending order.
+template <int HD>
+__device__ __forceinline__ void head_norm_rope_warp(const float *src, const float *gain,
+                                                    const float *ct, const float *stb, float eps,
+                                                    float *dst_s, float *dst_g, int lane) {
+  constexpr int NW = HD / 128, NP = NW / 2;
+  float4 x[NW], g[NW], cs[NP], sn[NP];
+#pragma unroll
+  for (int i = 0; i < NW; i++) {
+    x[i] = reinterpret_cast<const float4 *>(src)[32 * i + lane];
+    if (gain) g[i] = reinterpret_cast<const float4 *>(gain)[32 * i + lane];
+  }
+  if (ct) {
+#pragma unroll
+    for (int i = 0; i < NP; i++) {
+      cs[i] = reinterpret_cast<const float4 *>(ct)[32 * i + lane];
+      sn[i] = reinterpret_cast<const float4 *>(stb)[32 * i + lane];
+    }
+  }
+  float total = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NW; i++) {
+    float acc = 0.0f;
+    acc = fmaf(x[i].x, x[i].x, acc);
+    acc = fmaf(x[i].y, x[i].y, acc);
+    acc = fmaf(x[i].z, x[i].z, acc);
+    acc = fmaf(x[i].w, x[i].w, acc);
+    acc = warp_sum_bfly(acc);
+    total = i == 0 ? acc : __fadd_rn(total, acc);
+  }
+  const float inv = rms_inv(total, HD, eps);
+#pragma unroll
+  for (int i = 0; i < NW; i++) {
+    x[i].x = __fmul_rn(x[i].x, inv);
+    x[i].y = __fmul_rn(x[i].y, inv);
+    x[i].z = __fmul_rn(x[i].z, inv);
+    x[i].w = __fmul_rn(x[i].w, inv);
+    if (gain) {
+      x[i].x = __fmul_rn(x[i].x, g[i].x);
+      x[i].y = __fmul_rn(x[i].y, g[i].y);
+      x[i].z = __fmul_rn(x[i].z, g[i].z);
+      x[i].w = __fmul_rn(x[i].w, g[i].w);
+    }
+  }
+  if (ct) {
+#pragma unroll
+    for (int i = 0; i < NP; i++) {
+      const float4 lo = x[i], hi = x[i + NP], cc = cs[i], ss = sn[i];
+      float4 r0, r1;
+      r0.x = __fsub_rn(__fmul_rn(lo.x, cc.x), __fmul_rn(hi.x, ss.x));
+      r0.y = __fsub_rn(__fmul_rn(lo.y, cc.y), __fmul_rn(hi.y, ss.y));
+      r0.z = __fsub_rn(__fmul_rn(lo.z, cc.z), __fmul_rn(hi.z, ss.z));
+      r0.w = __fsub_rn(__fmul_rn(lo.w, cc.w), __fmul_rn(hi.w, ss.w));
+      r1.x = __fadd_rn(__fmul_rn(hi.x, cc.x), __fmul_rn(lo.x, ss.x));
+      r1.y = __fadd_rn(__fmul_rn(hi.y, cc.y), __fmul_rn(lo.y, ss.y));
+      r1.z = __fadd_rn(__fmul_rn(hi.z, cc.z), __fmul_rn(lo.z, ss.z));
+      r1.w = __fadd_rn(__fmul_rn(hi.w, cc.w), __fmul_rn(lo.w, ss.w));
+      x[i] = r0;
+      x[i + NP] = r1;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NW; i++) {
+    reinterpret_cast<float4 *>(dst_s)[32 * i + lane] = x[i];
+    if (dst_g) reinterpret_cast<float4 *>(dst_g)[32 * i + lane] = x[i];
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
+  constexpr int NH = 8;
+  constexpr int NC = HD / 4;
+  constexpr int HPG = HD / 128;
+  extern __shared__ __align__(16) float sm[];
+  float *vs = sm;                     // [64][HD]   (bulk copy destination)
+  float *qs = vs + ATT_BLK * HD;      // [NH][HD]
+  float *kc = qs + NH * HD;           // [HD]       K row of the new position
+  float *ss = kc + HD;                // [NH][64]
+  float *ps = ss + NH * ATT_BLK;      // [NH][64]
+  float *ms = ps + NH * ATT_BLK;      // [NH]
+  uint64_t *bar = reinterpret_cast<uint64_t *>(ms + NH);   // 8-byte aligned: offsets above are
+  int *flag = reinterpret_cast<int *>(bar + 1);            // multiples of 8 floats
+  const int c = blockIdx.x, bi = blockIdx.y, t = threadIdx.x, lane = t & 31, w = t >> 5;
+
+  grid_launch_dependents();
+  if (t == 0) {
+    mbar_init(bar, 1);
+    mbar_fence_init();
+    // L2 prefetch of this block's rows from a possibly stale position (clamped in bounds).
+    int p = a.refs.pos ? a.refs.pos[c] : a.refs.pos_base + c;
+    int sq = a.refs.seq ? a.refs.seq[c] : 0;
+    if (p >= 0 && p < a.max_ctx && sq >= 0 && sq < a.max_seqs) {
+      const int lo = a.window > 0 ? max(0, p - a.window + 1) : 0;
+      const int b = lo / ATT_BLK + bi;
+      if (b * ATT_BLK <= p) {
+        const int j0 = max(b * ATT_BLK, lo), j1 = min(b * ATT_BLK + ATT_BLK - 1, p);
+        const float *K = a.cache + (size_t)sq * a.seq_stride;
+        const uint32_t bytes = (uint32_t)(j1 - j0 + 1) * HD * 4;
+        l2_prefetch(K + (size_t)j0 * HD, bytes);
+        l2_prefetch(K + (size_t)a.max_ctx * HD + (size_t)j0 * HD, bytes);
+      }
+    }
+  }
+  grid_wait();
+  int p, lo, hi;
+  {
+    AttnArgs r;
+    r.refs = a.refs;
+    r.window = a.window;
+    r.kv_cap = 0;
+    attn_range(r, c, &p, &lo, &hi);
+  }
+  const int b = lo / ATT_BLK + bi;
+  if (b * ATT_BLK > hi) return;
+  const int nb = hi / ATT_BLK - lo / ATT_BLK + 1;
+  const int j0 = max(b * ATT_BLK, lo), j1 = min(b * ATT_BLK + ATT_BLK - 1, hi);
+  const int seq = a.refs.seq ? a.refs.seq[c] : 0;
+  float *K = a.cache + (size_t)seq * a.seq_stride;
+  float *V = K + (size_t)a.max_ctx * HD;
+  const bool cur = a.k != nullptr && j1 == p;     // this block writes and uses row p itself
+  const int jv1 = cur ? p - 1 : j1;
+  const uint32_t vbytes = jv1 >= j0 ? (uint32_t)(jv1 - j0 + 1) * HD * 4 : 0u;
+  __syncthreads();   // barrier initialised
+  if (t == 0 && vbytes) {
+    mbar_expect_tx(bar, vbytes);
+    bulk_g2s(vs + (size_t)(j0 - b * ATT_BLK) * HD, V + (size_t)j0 * HD, vbytes, bar);
+  }
+
+  // Query heads (warp h), then the new position's K (warp 0) and V (warp 1) rows.
+  {
+    const float *ct = a.cos_tab + (size_t)p * (HD / 2);
+    const float *stb = a.sin_tab + (size_t)p * (HD / 2);
+    head_norm_rope_warp<HD>(a.q + (size_t)c * a.q_ld + (size_t)w * HD, a.qgain, ct, stb, a.eps,
+                            qs + w * HD, nullptr, lane);
+    if (cur && w == 0)
+      head_norm_rope_warp<HD>(a.k + (size_t)c * HD, a.kgain, ct, stb, a.eps, kc,
+                              K + (size_t)p * HD, lane);
+    if (cur && w == 1)
+      head_norm_rope_warp<HD>(a.v + (size_t)c * HD, nullptr, nullptr, nullptr, a.eps,
+                              vs + (size_t)(p - b * ATT_BLK) * HD, V + (size_t)p * HD, lane);
+  }
+  __syncthreads();
+
+  // Scores (as k_attn_blocks).
+  {
+    const int jl = t >> 2, m = t & 3;
+    const int j = b * ATT_BLK + jl;
+    const bool valid = j >= j0 && j <= j1;
+    float acc[NH];
+#pragma unroll
+    for (int h = 0; h < NH; h++) acc[h] = 0.0f;
+    if (valid) {
+      const float4 *kr = reinterpret_cast<const float4 *>(cur && j == p ? kc : K + (size_t)j * HD);
+      constexpr int PER = NC / 4, BATCH = PER < 16 ? PER : 16;
+#pragma unroll
+      for (int i0 = 0; i0 < PER; i0 += BATCH) {
+        float4 k4[BATCH];
+#pragma unroll
+        for (int i = 0; i < BATCH; i++) k4[i] = kr[m + 4 * (i0 + i)];
+#pragma unroll
+        for (int i = 0; i < BATCH; i++) {
+          const int cc = m + 4 * (i0 + i);
+#pragma unroll
+          for (int h = 0; h < NH; h++) {
+            const float4 q4 = reinterpret_cast<const float4 *>(qs + h * HD)[cc];
+            float v = acc[h];
+            v = fmaf(q4.x, k4[i].x, v);
+            v = fmaf(q4.y, k4[i].y, v);
+            v = fmaf(q4.z, k4[i].z, v);
+            v = fmaf(q4.w, k4[i].w, v);
+            acc[h] = v;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < NH; h++) {
+      float v1 = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 1));
+      float v2 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, 2));
+      if (m == 0) ss[h * ATT_BLK + jl] = valid ? v2 : -FLT_MAX;
+    }
+  }
+  __syncthreads();
+  {
+    const int h = w;
+    float s0 = ss[h * ATT_BLK + lane], s1 = ss[h * ATT_BLK + lane + 32];
+    float mx = fmaxf(s0, s1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int ja = b * ATT_BLK + lane, jb = ja + 32;
+    ps[h * ATT_BLK + lane] = (ja >= j0 && ja <= j1) ? g4_exp(__fsub_rn(s0, mx)) : 0.0f;
+    ps[h * ATT_BLK + lane + 32] = (jb >= j0 && jb <= j1) ? g4_exp(__fsub_rn(s1, mx)) : 0.0f;
+    if (lane == 0) ms[h] = mx;
+  }
+  // V rows: bounded wait on the bulk copy; on a timeout the error flag is raised, the copy is
+  // waited for once more (bounded), and the block finishes with whatever arrived.
+  if (vbytes) {
+    if (!mbar_wait(bar, 0)) {
+      if (t == 0) atomicExch(&g4_dev_error, 2);
+      mbar_wait(bar, 0);
+    }
+  }
+  __syncthreads();
+  const int dc = t % NC, hg = t / NC;
+  float4 o[HPG];
+  float l[HPG];
+#pragma unroll
+  for (int hh = 0; hh < HPG; hh++) {
+    o[hh] = make_float4(0.f, 0.f, 0.f, 0.f);
+    l[hh] = 0.0f;
+  }
+#pragma unroll 4
+  for (int j = j0; j <= j1; j++) {
+    const int jl = j - b * ATT_BLK;
+    const float4 v4 = reinterpret_cast<const float4 *>(vs + (size_t)jl * HD)[dc];
+#pragma unroll
+    for (int hh = 0; hh < HPG; hh++) {
+      const float pj = ps[(hg * HPG + hh) * ATT_BLK + jl];
+      o[hh].x = fmaf(pj, v4.x, o[hh].x);
+      o[hh].y = fmaf(pj, v4.y, o[hh].y);
+      o[hh].z = fmaf(pj, v4.z, o[hh].z);
+      o[hh].w = fmaf(pj, v4.w, o[hh].w);
+      l[hh] = __fadd_rn(l[hh], pj);
+    }
+  }
+  if (nb == 1) {
+#pragma unroll
+    for (int hh = 0; hh < HPG; hh++) {
+      const int h = hg * HPG + hh;
+      float4 r;
+      r.x = __fdiv_rn(o[hh].x, l[hh]);
+      r.y = __fdiv_rn(o[hh].y, l[hh]);
+      r.z = __fdiv_rn(o[hh].z, l[hh]);
+      r.w = __fdiv_rn(o[hh].w, l[hh]);
+      reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD + (size_t)h * HD)[dc] = r;
+    }
+    return;
+  }
+#pragma unroll
+  for (int hh = 0; hh < HPG; hh++) {
+    const int h = hg * HPG + hh;
+    const size_t slot = ((size_t)c * a.max_blocks + bi) * NH + h;
+    reinterpret_cast<float4 *>(a.part_o + slot * HD)[dc] = o[hh];
+    if (dc == 0) {
+      a.part_m[slot] = ms[h];
+      a.part_l[slot] = l[hh];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (t == 0) *flag = atomicAdd(a.counter + c, 1) == nb - 1;
+  __syncthreads();
+  if (!*flag) return;
+  __threadfence();
+  // The merge, in k_attn_merge's order. Per head, M_k = max(m_0..m_k) is an exact prefix max,
+  // so lane k of warp h computes ea_k = exp(M_{k-1} - M_k), ec_k = exp(m_k - M_k) and
+  // l_k * ec_k in parallel; lane 0 then runs L_k = L_{k-1} * ea_k + l_k * ec_k. Each thread
+  // folds its vec4s of the partial outputs block after block with the same factors.
+  const size_t base = (size_t)c * a.max_blocks * NH;
+  float *fa = vs;                          // [nb][NH] ea_k  (vs is free after the PV loop)
+  float *fc = vs + (size_t)a.max_blocks * NH;      // [nb][NH] ec_k
+  float *fl = fc + (size_t)a.max_blocks * NH;      // [nb][NH] l_k * ec_k
+  float *Lh = fl + (size_t)a.max_blocks * NH;      // [NH] final L
+  constexpr int F = HD / 128;              // vec4s per thread per block: 8 * HD / 4 / 256
+  constexpr int KB = 16 / F;               // blocks loaded per round
+  float4 O[F];
+  float4 nx[KB][F];
+  const float4 *po = reinterpret_cast<const float4 *>(a.part_o + base * HD);
+#pragma unroll
+  for (int i = 0; i < F; i++) O[i] = __ldcg(po + t + 256 * i);
+#pragma unroll
+  for (int kk = 0; kk < KB; kk++)
+    if (1 + kk < nb) {
+#pragma unroll
+      for (int i = 0; i < F; i++) nx[kk][i] = __ldcg(po + (size_t)(1 + kk) * NH * HD / 4 + t + 256 * i);
+    }
+  {
+    const int h = w;
+    float carry = -FLT_MAX, Lrun = 0.0f;
+    for (int k0 = 0; k0 < nb; k0 += 32) {
+      const int k = k0 + lane;
+      const float mk = k < nb ? __ldcg(a.part_m + base + (size_t)k * NH + h) : -FLT_MAX;
+      const float lk = k < nb ? __ldcg(a.part_l + base + (size_t)k * NH + h) : 0.0f;
+      float Mk = mk;   // inclusive prefix max within the chunk, then with the carry
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, Mk, o);
+        if (lane >= o) Mk = fmaxf(Mk, u);
+      }
+      Mk = fmaxf(Mk, carry);
+      float Mp = __shfl_up_sync(0xffffffffu, Mk, 1);
+      if (lane == 0) Mp = carry;
+      if (k < nb) {
+        if (k == 0) {
+          fl[h] = lk;
+        } else {
+          const float ea = g4_exp(__fsub_rn(Mp, Mk)), ec = g4_exp(__fsub_rn(mk, Mk));
+          fa[k * NH + h] = ea;
+          fc[k * NH + h] = ec;
+          fl[k * NH + h] = __fmul_rn(lk, ec);
+        }
+      }
+      carry = __shfl_sync(0xffffffffu, Mk, 31);
+      __syncwarp();
+      if (lane == 0) {
+        const int kend = min(nb, k0 + 32);
+        for (int kk = k0; kk < kend; kk++)
+          Lrun = kk == 0 ? fl[h] : __fadd_rn(__fmul_rn(Lrun, fa[kk * NH + h]), fl[kk * NH + h]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) Lh[h] = Lrun;
+  }
+  __syncthreads();
+  for (int k0 = 1; k0 < nb; k0 += KB) {
+#pragma unroll
+    for (int kk = 0; kk < KB; kk++) {
+      const int k = k0 + kk;
+      if (k < nb) {
+#pragma unroll
+        for (int i = 0; i < F; i++) {
+          const int h = (4 * (t + 256 * i)) / HD;
+          const float ea = fa[k * NH + h], ec = fc[k * NH + h];
+          O[i].x = __fadd_rn(__fmul_rn(O[i].x, ea), __fmul_rn(nx[kk][i].x, ec));
+          O[i].y = __fadd_rn(__fmul_rn(O[i].y, ea), __fmul_rn(nx[kk][i].y, ec));
+          O[i].z = __fadd_rn(__fmul_rn(O[i].z, ea), __fmul_rn(nx[kk][i].z, ec));
+          O[i].w = __fadd_rn(__fmul_rn(O[i].w, ea), __fmul_rn(nx[kk][i].w, ec));
+        }
+      }
+    }
+    // next round's partials
+#pragma unroll
+    for (int kk = 0; kk < KB; kk++)
+      if (k0 + KB + kk < nb) {
+#pragma unroll
+        for (int i = 0; i < F; i++)
+          nx[kk][i] = __ldcg(po + (size_t)(k0 + KB + kk) * NH * HD / 4 + t + 256 * i);
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < F; i++) {
+    const int h = (4 * (t + 256 * i)) / HD;
+    const float L = Lh[h];
+    float4 r;
+    r.x = __fdiv_rn(O[i].x, L);
+    r.y = __fdiv_rn(O[i].y, L);
+    r.z = __fdiv_rn(O[i].z, L);
+    r.w = __fdiv_rn(O[i].w, L);
+    reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD)[t + 256 * i] = r;
+  }
+  if (t == 0) a.counter[c] = 0;
+}
+
+template <int HD>
+static size_t attn_decode_smem() {
+  return ((size_t)ATT_BLK * HD + 8 * HD + HD + 2 * 8 * ATT_BLK + 8) * 4 + 16;
+}
+
+template <int HD>
+static cudaError_t launch_attn_decode_t(const AttnDec &a, cudaStream_t st, bool pdl) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)attn_decode_smem<HD>());
+    attr_set = true;
+  }
+  return launch_k(k_attn_decode<HD>, dim3(a.cols, a.max_blocks), dim3(256), attn_decode_smem<HD>(),
+                  st, pdl, a);
+}
+
+cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl) {
+  // The merge keeps three factors per (block, head) in the 64-row V buffer.
+  if ((size_t)3 * a.max_blocks * 8 + 8 > (size_t)ATT_BLK * a.hd) return cudaErrorInvalidValue;
+  if (a.hd == 256) return launch_attn_decode_t<256>(a, st, pdl);
+  if (a.hd == 512) return launch_attn_decode_t<512>(a, st, pdl);
+  return cudaErrorInvalidValue;
 }
 
 // =====================================================================================

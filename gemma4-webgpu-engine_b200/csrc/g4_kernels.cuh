@@ -30,8 +30,6 @@ struct GemvArgs {
   int nseg;
   int K;
   int cols;
-  int rpw;             // rows per warp (block = 8 warps)
-  int ppr;             // 512-byte pieces per row
   int pro;
   const float *src; int ld_src;
   const float *res; int ld_res;
@@ -43,11 +41,21 @@ struct GemvArgs {
   float softcap;
   float *logits; int ld_logits;
   float *part_val; int32_t *part_idx; int n_blocks_total;
+  // Weights of later steps to pull into L2 while this launch runs (split across its CTAs).
+  const void *prefetch[4]; uint64_t prefetch_bytes[4];
 };
 
-// Choose rows per warp / pieces per row for a shape; returns 0 if unsupported.
-bool gemv_geometry(int bits, int K, int N_total, int *rpw, int *ppr);
-cudaError_t launch_gemv(const GemvArgs &a, int bits, int n_blocks, cudaStream_t st, bool pdl);
+// The streaming GEMV: one CTA per SM (or fewer), each streaming a contiguous row slice of one
+// segment through a shared-memory ring filled by TMA bulk copies. Fills seg[i].block_begin and
+// n_blocks_total for `sms` CTAs and returns the CTA count.
+int gemv_stream_partition(GemvArgs &a, int sms);
+cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, bool pdl);
+// Nonzero when a bounded device wait gave up since the last call (then cleared).
+int device_error_take();
+
+// A quantized linear launch (the streaming kernel, or the f32 path when in_scale is 0).
+// Calibrated launches need gemv_stream_partition first.
+cudaError_t launch_gemv(const GemvArgs &a, int bits, cudaStream_t st, bool pdl);
 
 // Per-column step addressing shared by the embed, attention and head kernels.
 struct ColRefs {
@@ -99,6 +107,25 @@ struct AttnArgs {
   float *out;                        // [cols, heads * hd]
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
+
+// Decode attention in one launch (every column a distinct sequence at one new position): the
+// q-norm-rope of all heads, the K/V row of the new position (producer layers: k != nullptr),
+// the 64-position blocks, and the merge, done by the last block of a column to finish
+// (counter[c] counts finished blocks and is left at 0).
+struct AttnDec {
+  int cols, hd, window, max_ctx, max_seqs, max_blocks;
+  const float *q; int q_ld;          // raw q rows [cols, q_ld]
+  const float *k; const float *v;    // raw k / v rows [cols, hd]; nullable: cache already holds p
+  const float *qgain; const float *kgain;
+  const float *cos_tab; const float *sin_tab;  // row = position
+  float *cache; size_t seq_stride;   // this layer's (or its producer's) cache
+  ColRefs refs;
+  float *part_o; float *part_m; float *part_l;
+  int32_t *counter;                  // [cols]
+  float *out;                        // [cols, 8 * hd]
+  float eps;
+};
+cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl);
 
 // Decode chain: position[c] += 1 after a step (its argmax already sits in the token slot).
 cudaError_t launch_advance(int32_t *pos, int cols, cudaStream_t st, bool pdl);

@@ -88,6 +88,7 @@ struct g4_ctx {
   float *ple_id, *ple_proj, *ple_in, *q, *k, *v, *qr, *attn, *proj, *gate, *up, *pleg_out;
   float *part_o, *part_m, *part_l;
   int att_blocks_sliding = 0, att_blocks_global = 0;
+  int32_t *att_count = nullptr;     // finished attention blocks per column (decode steps)
   float *logits = nullptr;
   float *head_pv = nullptr;
   int32_t *head_pi = nullptr;
@@ -103,6 +104,7 @@ struct g4_ctx {
   int32_t *h_tok = nullptr;    // pinned token outputs
   uint64_t other_bytes = 0;
   std::map<GraphKey, cudaGraphExec_t> graphs;
+  int sms = 148;
   int launches = 0;
   int last_cols = 0;
   int staged_cols = 0;
@@ -420,11 +422,12 @@ static int alloc_runtime(g4_ctx *ctx) {
   if ((rc = take(&ctx->part_o, (size_t)maxc * mb * nh * ghd))) return rc;
   if ((rc = take(&ctx->part_m, (size_t)maxc * mb * nh))) return rc;
   if ((rc = take(&ctx->part_l, (size_t)maxc * mb * nh))) return rc;
+  CK(cudaMalloc(&ctx->att_count, (size_t)maxc * 4));
+  CK(cudaMemset(ctx->att_count, 0, (size_t)maxc * 4));
   ctx->head_cols = std::min(maxc, std::max(ctx->cfg.max_seqs, 1));
   if ((rc = take(&ctx->logits, (size_t)ctx->head_cols * ctx->V))) return rc;
-  int rpw, ppr;
-  gemv_geometry(4, H, ctx->V, &rpw, &ppr);
-  ctx->head_blocks = (ctx->V + 8 * rpw - 1) / (8 * rpw);
+  CK(cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, ctx->dev));
+  ctx->head_blocks = std::min(2 * ctx->sms, ctx->V);
   if ((rc = take(&ctx->head_pv, (size_t)ctx->head_cols * ctx->head_blocks))) return rc;
   CK(cudaMalloc(&ctx->head_pi, (size_t)ctx->head_cols * ctx->head_blocks * 4));
   CK(cudaMalloc(&ctx->d_step, (size_t)3 * maxc * 4));
@@ -501,6 +504,7 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
                  ctx->part_m, ctx->part_l, ctx->logits, ctx->head_pv, ctx->d_val_out};
   for (float *p : fs) cudaFree(p);
   cudaFree(ctx->head_pi);
+  cudaFree(ctx->att_count);
   cudaFree(ctx->d_step);
   cudaFree(ctx->d_tok_out);
   for (int i = 0; i < g4_ctx::kStageSlots; i++) {
@@ -751,23 +755,25 @@ struct Seg {
   float *y;
 };
 
-// One quantized linear launch (or several, 8 columns each) with a fused prologue.
+struct WRef {
+  const void *p;
+  uint64_t bytes;
+};
+
+static WRef wref(const Linear &l) {
+  return {l.w, l.w ? (uint64_t)l.N * l.K * l.bits / 8 : 0};
+}
+
+// One quantized linear launch (or several, 8 columns each) with a fused prologue, streaming its
+// weights; `prefetch` names weights of later launches to pull into L2 meanwhile.
 static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs proto,
-                      bool head = false) {
+                      bool head = false, std::initializer_list<WRef> prefetch = {}) {
   const Linear *l0 = segs.begin()->lin;
-  int N_total = 0;
-  for (auto &s : segs) N_total += s.lin->N;
-  int rpw, ppr;
-  if (!gemv_geometry(l0->bits, l0->K, N_total, &rpw, &ppr))
-    return fail(ctx, G4_ERR_UNSUPPORTED, "no GEMV geometry for %d-bit K %d", l0->bits, l0->K);
   for (int c0 = 0; c0 < cols; c0 += 8) {
     GemvArgs a = proto;
     a.K = l0->K;
     a.cols = std::min(8, cols - c0);
-    a.rpw = rpw;
-    a.ppr = ppr;
     a.nseg = 0;
-    int blocks = 0;
     for (auto &s : segs) {
       GemvSeg &g = a.seg[a.nseg++];
       g.w = s.lin->w;
@@ -775,11 +781,17 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
       g.y = s.y ? s.y + (size_t)c0 * s.lin->N : nullptr;
       g.acc_out = nullptr;
       g.N = s.lin->N;
-      g.block_begin = blocks;
       g.in_scale = s.lin->in_scale;
       g.out_scale = s.lin->out_scale;
-      blocks += (s.lin->N + 8 * rpw - 1) / (8 * rpw);
     }
+    const int blocks = gemv_stream_partition(a, 2 * ctx->sms);
+    int np = 0;
+    if (c0 == 0)
+      for (auto &w : prefetch)
+        if (np < 4 && w.p) {
+          a.prefetch[np] = w.p;
+          a.prefetch_bytes[np++] = w.bytes;
+        }
     if (a.src) a.src += (size_t)c0 * a.ld_src;
     if (a.res) a.res += (size_t)c0 * a.ld_res;
     if (a.hidden_out) a.hidden_out += (size_t)c0 * a.ld_res;
@@ -790,10 +802,9 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
       a.ld_logits = ctx->V;
       a.part_val = ctx->head_pv + (size_t)c0 * blocks;
       a.part_idx = ctx->head_pi + (size_t)c0 * blocks;
-      a.n_blocks_total = blocks;
       ctx->head_blocks = blocks;
     }
-    CK(launch_gemv(a, l0->bits, blocks, ctx->st, true));
+    CK(launch_gemv(a, l0->bits, ctx->st, true));
     ctx->launches++;
   }
   return G4_OK;
@@ -854,14 +865,46 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       }
       p.eps = eps;
       if (ly.producer)
-        rc = run_linear(ctx, {{&ly.q, ctx->q}, {&ly.k, ctx->k}, {&ly.v, ctx->v}}, cols, p);
+        rc = run_linear(ctx, {{&ly.q, ctx->q}, {&ly.k, ctx->k}, {&ly.v, ctx->v}}, cols, p, false,
+                        {wref(ly.gate), wref(ly.up)});
       else
-        rc = run_linear(ctx, {{&ly.q, ctx->q}}, cols, p);
+        rc = run_linear(ctx, {{&ly.q, ctx->q}}, cols, p, false, {wref(ly.gate), wref(ly.up)});
       if (rc) return rc;
       if (L > 0) cur ^= 1;
     }
+    // ---- decode steps: prologue, attention and merge in one launch per layer
+    if (head) {
+      AttnDec ad;
+      memset(&ad, 0, sizeof(ad));
+      ad.cols = cols;
+      ad.hd = hd;
+      ad.window = ly.global ? 0 : a.sliding_window;
+      ad.max_ctx = ctx->cfg.max_context;
+      ad.max_seqs = ctx->cfg.max_seqs;
+      ad.max_blocks = ly.global ? ctx->att_blocks_global : ctx->att_blocks_sliding;
+      ad.q = ctx->q;
+      ad.q_ld = qrows;
+      ad.k = ly.producer ? ctx->k : nullptr;
+      ad.v = ly.producer ? ctx->v : nullptr;
+      ad.qgain = ly.q_norm;
+      ad.kgain = ly.k_norm;
+      ad.cos_tab = ly.global ? ctx->cos_g : ctx->cos_s;
+      ad.sin_tab = ly.global ? ctx->sin_g : ctx->sin_s;
+      ad.cache = ctx->kv[ly.cache_layer];
+      ad.seq_stride = ctx->kv_stride[ly.cache_layer];
+      ad.refs.seq = d_seq;
+      ad.refs.pos = d_pos;
+      ad.part_o = ctx->part_o;
+      ad.part_m = ctx->part_m;
+      ad.part_l = ctx->part_l;
+      ad.counter = ctx->att_count;
+      ad.out = ctx->attn;
+      ad.eps = eps;
+      CK(launch_attn_decode(ad, ctx->st, true));
+      ctx->launches++;
+    }
     // ---- attention prologue: q-norm-rope, kv-norm-rope-store (src/kernels/attnPrologue.ts)
-    {
+    if (!head) {
       AttnPro ap;
       memset(&ap, 0, sizeof(ap));
       ap.cols = cols;
@@ -889,7 +932,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       ctx->launches++;
     }
     // ---- attention over the producer cache (kvRoleForLayer)
-    {
+    if (!head) {
       AttnArgs at;
       memset(&at, 0, sizeof(at));
       at.cols = cols;
@@ -916,7 +959,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       GemvArgs p = pro_args(PRO_X);
       p.src = ctx->attn;
       p.ld_src = qrows;
-      if ((rc = run_linear(ctx, {{&ly.o, ctx->proj}}, cols, p))) return rc;
+      if ((rc = run_linear(ctx, {{&ly.o, ctx->proj}}, cols, p, false, {wref(ly.down)}))) return rc;
     }
     // ---- gate, up with the post-attention join fused in (alpha 1)
     {
@@ -930,7 +973,9 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       p.alpha = 1.0f;
       p.hidden_out = ctx->res[cur ^ 1];
       p.eps = eps;
-      if ((rc = run_linear(ctx, {{&ly.gate, ctx->gate}, {&ly.up, ctx->up}}, cols, p))) return rc;
+      if ((rc = run_linear(ctx, {{&ly.gate, ctx->gate}, {&ly.up, ctx->up}}, cols, p, false,
+                           {wref(ly.pleg), wref(ly.plep)})))
+        return rc;
       cur ^= 1;
     }
     // ---- down_proj over gelu(gate) * up (the fused gelu prologue)
@@ -941,7 +986,11 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       p.up = ctx->up;
       p.ld_up = ly.up.N;
       p.up_off = 0;
-      if ((rc = run_linear(ctx, {{&ly.down, ctx->proj}}, cols, p))) return rc;
+      const Layer *nx = L + 1 < n_layers ? &ctx->layers[L + 1] : nullptr;
+      if ((rc = run_linear(ctx, {{&ly.down, ctx->proj}}, cols, p, false,
+                           {nx ? wref(nx->q) : WRef{nullptr, 0}, nx ? wref(nx->k) : WRef{nullptr, 0},
+                            nx ? wref(nx->v) : WRef{nullptr, 0}})))
+        return rc;
     }
     // ---- per_layer_input_gate over the post-FFN norm-residual (the residual itself)
     {
@@ -953,7 +1002,10 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       p.g1 = ly.ln_post_ffn;
       p.hidden_out = ctx->res[cur ^ 1];
       p.eps = eps;
-      if ((rc = run_linear(ctx, {{&ly.pleg, ctx->pleg_out}}, cols, p))) return rc;
+      const Layer *nx = L + 1 < n_layers ? &ctx->layers[L + 1] : nullptr;
+      if ((rc = run_linear(ctx, {{&ly.pleg, ctx->pleg_out}}, cols, p, false,
+                           {nx ? wref(nx->o) : WRef{nullptr, 0}})))
+        return rc;
       cur ^= 1;
     }
     // ---- per_layer_projection over gelu(gate) * the layer's per-layer input row
@@ -964,7 +1016,10 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       p.up = ctx->ple_in;
       p.ld_up = ctx->ple_cols;
       p.up_off = L * PD;
-      if ((rc = run_linear(ctx, {{&ly.plep, ctx->proj}}, cols, p))) return rc;
+      const Layer *nx = L + 1 < n_layers ? &ctx->layers[L + 1] : nullptr;
+      if ((rc = run_linear(ctx, {{&ly.plep, ctx->proj}}, cols, p, false,
+                           {nx ? wref(nx->gate) : WRef{nullptr, 0}, nx ? wref(nx->up) : WRef{nullptr, 0}})))
+        return rc;
     }
   }
   if (head) {
@@ -1052,6 +1107,12 @@ static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos,
 static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
   CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)cols * 4, cudaMemcpyDeviceToHost, ctx->st));
   CK(cudaStreamSynchronize(ctx->st));
+  if (device_error_take() > 0) {
+    // A block that gave up may have left its column's finished-block count behind.
+    cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 4, ctx->st);
+    cudaStreamSynchronize(ctx->st);
+    return fail(ctx, G4_ERR_TIMEOUT, "a bounded device wait gave up (a bulk copy never completed)");
+  }
   for (int i = 0; i < cols; i++) out[i] = ctx->h_tok[i];
   return G4_OK;
 }
@@ -1145,8 +1206,11 @@ extern "C" int g4_step_stage(g4_ctx *ctx, int32_t B, const int32_t *seqs, const 
   if (!ctx || !seqs || !tokens || !positions) return fail(ctx, G4_ERR_INVALID, "g4_step_stage: null argument");
   if (B < 1 || B > ctx->maxc || B > ctx->head_cols) return fail(ctx, G4_ERR_INVALID, "batch %d too wide", B);
   int rc;
-  for (int i = 0; i < B; i++)
+  for (int i = 0; i < B; i++) {
     if ((rc = check_seq_pos(ctx, seqs[i], positions[i], 1))) return rc;
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == seqs[i]) return fail(ctx, G4_ERR_INVALID, "sequence %d appears twice in one batch", seqs[i]);
+  }
   CK(cudaSetDevice(ctx->dev));
   if ((rc = stage(ctx, B, seqs, positions, tokens, true))) return rc;
   CK(cudaStreamSynchronize(ctx->st));
@@ -1211,6 +1275,12 @@ extern "C" int g4_read_logits(g4_ctx *ctx, int32_t col, float *out, int32_t n) {
     if (e_ != cudaSuccess) return fail(nullptr, G4_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
   } while (0)
 
+static int device_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
 extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, float in_scale,
                            float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
                            int32_t *acc_out, void *stream) {
@@ -1220,10 +1290,9 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
   if (N < 1 || K < span || K % span != 0 || cols < 1)
     return fail(nullptr, G4_ERR_INVALID, "qgemv-%dbit needs K a multiple of %d, got %d (N %d, cols %d)", bits, span, K, N, cols);
   if (in_scale == 0.0f && cols != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "the f32 path takes one column");
-  int rpw, ppr;
-  if (!gemv_geometry(bits, K, N, &rpw, &ppr)) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
-  if (in_scale != 0.0f && (size_t)8 * K > 56 * 1024) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  if ((size_t)K * bits / 8 > 4096 || (size_t)8 * K > 64 * 1024) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
   cudaStream_t st = (cudaStream_t)stream;
+  const int sms = device_sms();
   for (int c0 = 0; c0 < cols; c0 += 8) {
     GemvArgs a;
     memset(&a, 0, sizeof(a));
@@ -1231,8 +1300,6 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
     a.alpha = 1.0f;
     a.K = K;
     a.cols = std::min(8, cols - c0);
-    a.rpw = rpw;
-    a.ppr = ppr;
     a.nseg = 1;
     a.seg[0].w = (const uint8_t *)wq;
     a.seg[0].s = (const uint16_t *)scales;
@@ -1243,8 +1310,8 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
     a.seg[0].out_scale = out_scale;
     a.src = x + (size_t)c0 * K;
     a.ld_src = K;
-    int blocks = (N + 8 * rpw - 1) / (8 * rpw);
-    OPCK(launch_gemv(a, bits, blocks, st, true));
+    gemv_stream_partition(a, 2 * sms);
+    OPCK(launch_gemv(a, bits, st, true));
   }
   OPCK(cudaGetLastError());
   return G4_OK;
@@ -1258,9 +1325,9 @@ extern "C" int g4_op_qgemv_gelu(const void *wq, const void *scales, const float 
   if ((bits != 4 && bits != 8) || N < 1 || K < span || K % span || cols < 1)
     return fail(nullptr, G4_ERR_INVALID, "bad qgemv-gelu shape");
   if (in_scale == 0.0f && cols != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "the f32 path takes one column");
-  int rpw, ppr;
-  if (!gemv_geometry(bits, K, N, &rpw, &ppr)) return fail(nullptr, G4_ERR_UNSUPPORTED, "K too wide");
+  if ((size_t)K * bits / 8 > 4096 || (size_t)8 * K > 64 * 1024) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
   cudaStream_t st = (cudaStream_t)stream;
+  const int sms = device_sms();
   for (int c0 = 0; c0 < cols; c0 += 8) {
     GemvArgs a;
     memset(&a, 0, sizeof(a));
@@ -1268,8 +1335,6 @@ extern "C" int g4_op_qgemv_gelu(const void *wq, const void *scales, const float 
     a.alpha = 1.0f;
     a.K = K;
     a.cols = std::min(8, cols - c0);
-    a.rpw = rpw;
-    a.ppr = ppr;
     a.nseg = 1;
     a.seg[0].w = (const uint8_t *)wq;
     a.seg[0].s = (const uint16_t *)scales;
@@ -1282,8 +1347,8 @@ extern "C" int g4_op_qgemv_gelu(const void *wq, const void *scales, const float 
     a.up = up + (size_t)c0 * up_stride;
     a.ld_up = up_stride;
     a.up_off = up_offset;
-    int blocks = (N + 8 * rpw - 1) / (8 * rpw);
-    OPCK(launch_gemv(a, bits, blocks, st, false));
+    gemv_stream_partition(a, 2 * sms);
+    OPCK(launch_gemv(a, bits, st, true));
   }
   return G4_OK;
 }

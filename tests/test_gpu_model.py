@@ -147,6 +147,11 @@ def test_invalid_calls(pkg, tiny):
         ctx.prefill(0, np.ones(200, np.int32), 0, True)
     with pytest.raises(pkg.G4Error, match="unknown tensor"):
         ctx.download("model.language_model.layers.99.mlp.up_proj.weight")
+    # A decode step holds one new position per sequence (its attention writes that row itself).
+    with pytest.raises(pkg.G4Error, match="twice"):
+        ctx.decode_batch([0, 0], [1, 2], [0, 0])
+    with pytest.raises(pkg.G4Error, match="twice"):
+        ctx.step_stage([1, 1], [1, 2], [0, 0])
     ctx.close()
 
 
