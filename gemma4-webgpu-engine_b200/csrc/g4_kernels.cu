@@ -72,63 +72,115 @@ __device__ __forceinline__ float4 f4_gelu_mul(float4 g, float4 u) {
                      __fmul_rn(g4_gelu(g.z), u.z), __fmul_rn(g4_gelu(g.w), u.w));
 }
 
+// Norm gains are weights: a CTA reads its chunks of them before the dependency wait.
+struct ProGains {
+  float4 g1[2], g2[2];
+};
+template <int PRO>
+__device__ __forceinline__ void prologue_gains(const GemvArgs &a, ProGains &pg) {
+  if (PRO != PRO_NORM && PRO != PRO_JOIN && PRO != PRO_NORMRES) return;
+  const int t = threadIdx.x, nc = a.K >> 2;
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+    if (t + 256 * i < nc) {
+      pg.g1[i] = reinterpret_cast<const float4 *>(a.g1)[t + 256 * i];
+      if (PRO == PRO_JOIN) pg.g2[i] = reinterpret_cast<const float4 *>(a.g2)[t + 256 * i];
+    }
+}
+
 // Compute column c's activation vector through the prologue and store its int8 codes.
-// Returns this thread's share of the code sum.
-template <int BITS>
-__device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, int c, float in_scale,
-                                                 uint8_t *codes, float *red, bool write_hidden) {
+// Returns this thread's share of the code sum. Every global load of a prologue is issued
+// before any of its results is used, so the prologue costs one round trip to L2.
+template <int BITS, int PRO>
+__device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, const ProGains &pg, int c,
+                                                 float in_scale, uint8_t *codes, float *red,
+                                                 bool write_hidden) {
   const int t = threadIdx.x;
   const int K = a.K;
   const int nc = K >> 2;
-  const float in_r = __fdiv_rn(1.0f, in_scale);
   int xs = 0;
-  if (a.pro == PRO_X || a.pro == PRO_GELU) {
+  if (PRO == PRO_CODES) {
+    // K <= 16384: at most four 16-byte pieces per thread.
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.src_codes + (size_t)c * a.ld_codes);
+    const int n16 = K >> 4;
+    uint4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (t + 256 * i < n16) v[i] = src[t + 256 * i];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (t + 256 * i < n16) {
+        reinterpret_cast<uint4 *>(codes)[t + 256 * i] = v[i];
+        xs = dp4a_ss(v[i].x, 0x01010101, xs);
+        xs = dp4a_ss(v[i].y, 0x01010101, xs);
+        xs = dp4a_ss(v[i].z, 0x01010101, xs);
+        xs = dp4a_ss(v[i].w, 0x01010101, xs);
+      }
+    return xs;
+  }
+  const float in_r = __fdiv_rn(1.0f, in_scale);
+  if (PRO == PRO_X || PRO == PRO_GELU) {
+    // K <= 8192: at most eight vec4 chunks per thread, loaded four at a time.
     const float4 *src = reinterpret_cast<const float4 *>(a.src + (size_t)c * a.ld_src);
-    const float4 *up = a.pro == PRO_GELU
+    const float4 *up = PRO == PRO_GELU
                            ? reinterpret_cast<const float4 *>(a.up + (size_t)c * a.ld_up + a.up_off)
                            : nullptr;
-    for (int ch = t; ch < nc; ch += 256) {
-      float4 x = src[ch];
-      if (a.pro == PRO_GELU) x = f4_gelu_mul(x, up[ch]);
-      xs += ChunkPro::store<BITS>(codes, ch, x, in_scale, in_r);
+#pragma unroll 1
+    for (int i0 = 0; i0 < 8 && t + 256 * i0 < nc; i0 += 4) {
+      float4 xv[4], uv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (t + 256 * (i0 + i) < nc) {
+          xv[i] = src[t + 256 * (i0 + i)];
+          if (up) uv[i] = up[t + 256 * (i0 + i)];
+        }
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (t + 256 * (i0 + i) < nc) {
+          const float4 x = up ? f4_gelu_mul(xv[i], uv[i]) : xv[i];
+          xs += ChunkPro::store<BITS>(codes, t + 256 * (i0 + i), x, in_scale, in_r);
+        }
     }
     return xs;
   }
   // Norm prologues: K <= 2048, so each thread owns at most two vec4 chunks (t, t + 256).
   const float4 *src = reinterpret_cast<const float4 *>(a.src + (size_t)c * a.ld_src);
-  const float4 *g1 = reinterpret_cast<const float4 *>(a.g1);
-  float4 sv[2];
+  const float4 *res = PRO != PRO_NORM ? reinterpret_cast<const float4 *>(a.res + (size_t)c * a.ld_res)
+                                        : nullptr;
+  float4 sv[2], rv[2];
   int cnt = 0;
 #pragma unroll
   for (int i = 0; i < 2; i++)
-    if (t + 256 * i < nc) sv[cnt++] = src[t + 256 * i];
+    if (t + 256 * i < nc) {
+      sv[i] = src[t + 256 * i];
+      if (res) rv[i] = res[t + 256 * i];
+      cnt = i + 1;
+    }
   float inv1 = rms_inv(block_sumsq256_regs<2>(sv, cnt, red), K, a.eps);
   float4 xv[2];
-  if (a.pro == PRO_NORM) {
+  if (PRO == PRO_NORM) {
 #pragma unroll
     for (int i = 0; i < 2; i++)
-      if (i < cnt) xv[i] = f4_norm_apply(sv[i], inv1, g1[t + 256 * i]);
+      if (i < cnt) xv[i] = f4_norm_apply(sv[i], inv1, pg.g1[i]);
   } else {
-    const float4 *res = reinterpret_cast<const float4 *>(a.res + (size_t)c * a.ld_res);
     float4 h[2];
 #pragma unroll
     for (int i = 0; i < 2; i++)
       if (i < cnt) {
-        h[i] = f4_add(res[t + 256 * i], f4_norm_apply(sv[i], inv1, g1[t + 256 * i]));
-        if (a.pro == PRO_JOIN) h[i] = f4_scale(h[i], a.alpha);
+        h[i] = f4_add(rv[i], f4_norm_apply(sv[i], inv1, pg.g1[i]));
+        if (PRO == PRO_JOIN) h[i] = f4_scale(h[i], a.alpha);
         if (write_hidden)
           reinterpret_cast<float4 *>(a.hidden_out + (size_t)c * a.ld_res)[t + 256 * i] = h[i];
       }
-    if (a.pro == PRO_NORMRES) {
+    if (PRO == PRO_NORMRES) {
 #pragma unroll
       for (int i = 0; i < 2; i++)
         if (i < cnt) xv[i] = h[i];
     } else {
       float inv2 = rms_inv(block_sumsq256_regs<2>(h, cnt, red), K, a.eps);
-      const float4 *g2 = reinterpret_cast<const float4 *>(a.g2);
 #pragma unroll
       for (int i = 0; i < 2; i++)
-        if (i < cnt) xv[i] = f4_norm_apply(h[i], inv2, g2[t + 256 * i]);
+        if (i < cnt) xv[i] = f4_norm_apply(h[i], inv2, pg.g2[i]);
     }
   }
 #pragma unroll
@@ -262,35 +314,71 @@ __device__ __forceinline__ void l2_prefetch_share(const void *p, uint64_t bytes,
   }
 }
 
-template <int BITS, int COLS, int RS>
-__global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
+// Shared memory of one streaming-GEMV CTA: the ring, then the barriers, the column sums, the
+// reduction and argmax scratch, the row scales of the CTA's slice (per sub-slice), the y rows
+// an EPI_GELU_CODES epilogue keeps, and the activation codes.
+struct GsLayout {
+  int bars, xsum, red, cand_v, cand_i, scales, ybuf, codes, total;
+};
+__host__ __device__ __forceinline__ GsLayout gs_layout(int ring, int cols, int max_rows, int nsub,
+                                                       bool keep_y, int K) {
+  GsLayout l;
+  l.bars = ring;
+  l.xsum = l.bars + GS_MAX_STAGES * 8;
+  l.red = l.xsum + 8 * 4;
+  l.cand_v = l.red + 8 * 4;
+  l.cand_i = l.cand_v + 8 * cols * 4;
+  l.scales = l.cand_i + 8 * cols * 4;
+  l.ybuf = l.scales + nsub * max_rows * 4;
+  l.codes = (l.ybuf + (keep_y ? nsub * cols * max_rows * 4 : 0) + 15) & ~15;
+  l.total = l.codes + cols * K;
+  return l;
+}
+
+// Resident CTAs per SM the register allocation is bounded for.
+#ifndef G4_GEMV_MIN_BLOCKS
+#define G4_GEMV_MIN_BLOCKS 2
+#endif
+
+template <int BITS, int COLS, int RS, int PRO, int EPI>
+__global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  const int ring_bytes = a.ring_bytes;
+  const bool pair = a.pair != 0;
+  const int nsub = pair ? 2 : 1;
+  constexpr bool keep_y = EPI == EPI_GELU_CODES;
+  const GsLayout lay = gs_layout(ring_bytes, COLS, a.max_rows, nsub, keep_y, a.K);
   uint8_t *ring = smem;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + GS_RING);
-  int *xsum = reinterpret_cast<int *>(bars + GS_MAX_STAGES);
-  float *red = reinterpret_cast<float *>(xsum + 8);
-  float *cand_v = red + 8;
-  int *cand_i = reinterpret_cast<int *>(cand_v + 8 * COLS);
-  uint8_t *codes = reinterpret_cast<uint8_t *>(cand_i + 8 * COLS);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + lay.bars);
+  int *xsum = reinterpret_cast<int *>(smem + lay.xsum);
+  float *red = reinterpret_cast<float *>(smem + lay.red);
+  float *cand_v = reinterpret_cast<float *>(smem + lay.cand_v);
+  int *cand_i = reinterpret_cast<int *>(smem + lay.cand_i);
+  float *rscale = reinterpret_cast<float *>(smem + lay.scales);
+  float *ybuf = reinterpret_cast<float *>(smem + lay.ybuf);
+  uint8_t *codes = smem + lay.codes;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int bid = blockIdx.x;
   int s = 0;
-  if (a.nseg > 1 && bid >= a.seg[1].block_begin) s = 1;
-  if (a.nseg > 2 && bid >= a.seg[2].block_begin) s = 2;
+  if (!pair && a.nseg > 1 && bid >= a.seg[1].block_begin) s = 1;
+  if (!pair && a.nseg > 2 && bid >= a.seg[2].block_begin) s = 2;
   const GemvSeg sg = a.seg[s];
-  const int nb = (s + 1 < a.nseg ? a.seg[s + 1].block_begin : a.n_blocks_total) - sg.block_begin;
-  const int ib = bid - sg.block_begin;
+  const int nb = pair ? a.n_blocks_total
+                      : (s + 1 < a.nseg ? a.seg[s + 1].block_begin : a.n_blocks_total) - sg.block_begin;
+  const int ib = pair ? bid : bid - sg.block_begin;
   const int r0 = (int)(((long long)sg.N * ib) / nb);
   const int r1 = (int)(((long long)sg.N * (ib + 1)) / nb);
   const int K = a.K;
   const int row_bytes = K * BITS / 8;
   const int vb = row_bytes / RS;                 // bytes per virtual row
-  const int svrows = gs_stage_vrows(vb);         // virtual rows per stage
-  const int srows = svrows / RS;                 // real rows per stage
+  int srows = gs_stage_vrows(vb) / RS;           // real rows per stage
+  if (srows > a.max_rows) srows = a.max_rows;    // a chunk never spans two sub-slices
+  if (srows * row_bytes > ring_bytes) srows = ring_bytes / row_bytes;
   const int stage_bytes = srows * row_bytes;
-  int nstages = GS_RING / stage_bytes;
+  int nstages = ring_bytes / stage_bytes;
   if (nstages > GS_MAX_STAGES) nstages = GS_MAX_STAGES;
-  const int nchunks = (r1 - r0 + srows - 1) / srows;
+  const int nch1 = (r1 - r0 + srows - 1) / srows;   // chunks per sub-slice
+  const int nchunks = nsub * nch1;
 
   if (t == 0) {
     for (int i = 0; i < nstages; i++) mbar_init(&bars[i], 1);
@@ -300,32 +388,33 @@ __global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
   __syncthreads();
   auto issue = [&](int c) {
     const int st = c % nstages;
-    const int cr0 = r0 + c * srows;
+    const int sub = c / nch1;
+    const int cr0 = r0 + (c - sub * nch1) * srows;
     const int rows = min(srows, r1 - cr0);
     const uint32_t bytes = (uint32_t)(rows * row_bytes);
     mbar_expect_tx(&bars[st], bytes);
-    bulk_g2s(ring + st * stage_bytes, sg.w + (size_t)cr0 * row_bytes, bytes, &bars[st]);
+    bulk_g2s(ring + st * stage_bytes, a.seg[pair ? sub : s].w + (size_t)cr0 * row_bytes, bytes, &bars[st]);
   };
   if (t == 0)
     for (int c = 0; c < nchunks && c < nstages; c++) issue(c);
   if (t == 32)
     for (int i = 0; i < 4; i++) l2_prefetch_share(a.prefetch[i], a.prefetch_bytes[i], bid, gridDim.x);
+  // Row scales and norm gains are weights too: read them before the wait.
+  for (int i = t; i < nsub * (r1 - r0); i += 256) {
+    const int sub = i / (r1 - r0);
+    rscale[sub * a.max_rows + i - sub * (r1 - r0)] =
+        f16_bits_to_f32(__ldg(a.seg[pair ? sub : s].s + r0 + i - sub * (r1 - r0)));
+  }
+  ProGains pg;
+  prologue_gains<PRO>(a, pg);
   grid_launch_dependents();
   grid_wait();
 
-  int xs_local[COLS];
-#pragma unroll
-  for (int c = 0; c < COLS; c++) {
-    xs_local[c] = 0;
-    if (c < a.cols)
-      xs_local[c] = gemv_prologue_col<BITS>(a, c, sg.in_scale, codes + c * K, red,
-                                            bid == 0 && a.hidden_out != nullptr);
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < COLS; c++) {
-    int v = warp_sum_int(xs_local[c]);
-    if (lane == 0 && c < a.cols) atomicAdd(&xsum[c], v);
+#pragma unroll 1
+  for (int c = 0; c < a.cols; c++) {
+    const int v = warp_sum_int(gemv_prologue_col<BITS, PRO>(a, pg, c, sg.in_scale, codes + c * K, red,
+                                                       bid == 0 && a.hidden_out != nullptr));
+    if (lane == 0) atomicAdd(&xsum[c], v);
   }
   __syncthreads();
 
@@ -336,7 +425,8 @@ __global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
     best_v[c] = -FLT_MAX;
     best_i[c] = 0x7fffffff;
   }
-  const float out_r = sg.out_scale != 0.0f ? __fdiv_rn(1.0f, sg.out_scale) : 0.0f;
+  const float out_r0 = sg.out_scale != 0.0f ? __fdiv_rn(1.0f, sg.out_scale) : 0.0f;
+  const float out_r1 = pair && a.seg[1].out_scale != 0.0f ? __fdiv_rn(1.0f, a.seg[1].out_scale) : 0.0f;
   for (int ch = 0; ch < nchunks; ch++) {
     const int st = ch % nstages;
     const bool ok = mbar_wait(&bars[st], (uint32_t)((ch / nstages) & 1));
@@ -351,9 +441,12 @@ __global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
       __syncthreads();
       return;
     }
-    const int cr0 = r0 + ch * srows;
+    const int sub = ch / nch1;
+    const int cr0 = r0 + (ch - sub * nch1) * srows;
     const int vrows = min(srows, r1 - cr0) * RS;
     const uint8_t *sw = ring + st * stage_bytes;
+    const float out_scale = sub ? a.seg[1].out_scale : sg.out_scale;
+    const float out_r = sub ? out_r1 : out_r0;
     // Each warp takes groups of four virtual rows; the four dot products run as independent
     // chains and close with one transposed reduction, after which lanes 0, 8, 16 and 24 hold
     // the four totals; the parts of a split row are then added and its lanes finish the rows
@@ -434,15 +527,17 @@ __global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
       const int vr = g0 + my_vrow;
       if ((lane & (8 * RS - 1)) == 0 && vr < vrows) {
         const int row = cr0 + vr / RS;
-        const float wscale = f16_bits_to_f32(__ldg(sg.s + row));
+        const float wscale = rscale[sub * a.max_rows + row - r0];
 #pragma unroll
         for (int c = 0; c < COLS; c++) {
           if (c < a.cols) {
             const int exact = BITS == 4 ? acc[0][c] - 8 * xsum[c] : acc[0][c];
             float y = __fmul_rn(__fmul_rn(sg.in_scale, wscale), (float)exact);
-            y = srq_out_r(y, sg.out_scale, out_r);
+            y = srq_out_r(y, out_scale, out_r);
             if (sg.acc_out) sg.acc_out[(size_t)c * sg.N + row] = exact;
-            if (a.head) {
+            if (keep_y) {
+              ybuf[(sub * COLS + c) * a.max_rows + row - r0] = y;
+            } else if (EPI == EPI_HEAD) {
               if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
               if (a.logits) a.logits[(size_t)c * a.ld_logits + row] = y;
               if (y > best_v[c] || (y == best_v[c] && row < best_i[c])) {
@@ -459,7 +554,24 @@ __global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
     __syncthreads();
     if (t == 0 && ch + nstages < nchunks) issue(ch + nstages);
   }
-  if (a.head) {
+  if constexpr (keep_y) {
+    // h = gelu(y0) * u (gelu-mul, src/kernels/geluMul.ts:67-115), snapped to the next linear's
+    // input codes exactly as its own prologue would (src/kernels/qgemv.ts:371-400, 624-626).
+    const int rows = r1 - r0;
+    const float cr = __fdiv_rn(1.0f, a.codes_scale);
+    for (int i = t; i < rows * COLS; i += 256) {
+      const int c = i / rows, r = i - c * rows;
+      if (c < a.cols) {
+        const float g = ybuf[c * a.max_rows + r];
+        const float u = pair ? ybuf[(COLS + c) * a.max_rows + r]
+                             : a.epi_up[(size_t)c * a.epi_ld_up + a.epi_up_off + r0 + r];
+        const float h = __fmul_rn(g4_gelu(g), u);
+        a.codes_out[(size_t)c * a.codes_ld + code_pos(r0 + r, a.codes_bits)] =
+            (uint8_t)(srq_code_r(h, a.codes_scale, cr) & 255);
+      }
+    }
+  }
+  if constexpr (EPI == EPI_HEAD) {
 #pragma unroll
     for (int c = 0; c < COLS; c++) {
       // The candidates sit in lanes 0, 8, 16, 24 of each warp; every other lane carries -FLT_MAX.
@@ -496,6 +608,14 @@ __global__ void __launch_bounds__(256) k_qgemv_stream(const GemvArgs a) {
 }
 
 int gemv_stream_partition(GemvArgs &a, int sms) {
+  if (a.pair) {
+    // Every CTA owns the same rows of both segments.
+    const int nb = a.seg[0].N < sms ? a.seg[0].N : sms;
+    a.seg[0].block_begin = 0;
+    a.seg[1].block_begin = 0;
+    a.n_blocks_total = nb;
+    return nb;
+  }
   long long total = 0;
   for (int i = 0; i < a.nseg; i++) total += a.seg[i].N;
   int target = (int)(total < sms ? total : sms);
@@ -511,23 +631,59 @@ int gemv_stream_partition(GemvArgs &a, int sms) {
   return begin;
 }
 
-template <int BITS, int COLS, int RS>
-static cudaError_t launch_stream_t(const GemvArgs &a, cudaStream_t st, bool pdl) {
-  const size_t smem = GS_RING + GS_MAX_STAGES * 8 + 16 * 4 + 8 * COLS * 8 + (size_t)COLS * a.K;
-  auto k = k_qgemv_stream<BITS, COLS, RS>;
+template <int BITS, int COLS, int RS, int PRO, int EPI>
+static cudaError_t launch_stream_t(const GemvArgs &a0, cudaStream_t st, bool pdl) {
+  // The ring holds the slice a CTA owns (both sub-slices for a pair) when that fits in GS_RING
+  // (then the whole slice is requested before the dependency wait), else GS_RING. A small ring
+  // lets the next launch's CTAs sit on the SM beside this one's and start their copies early.
+  GemvArgs a = a0;
+  const int row_bytes = a.K * BITS / 8;
+  const int nsub = a.pair ? 2 : 1;
+  int max_rows = 1;
+  if (a.pair) {
+    max_rows = (a.seg[0].N + a.n_blocks_total - 1) / a.n_blocks_total;
+  } else {
+    for (int i = 0; i < a.nseg; i++) {
+      const int nb = (i + 1 < a.nseg ? a.seg[i + 1].block_begin : a.n_blocks_total) - a.seg[i].block_begin;
+      max_rows = std::max(max_rows, (a.seg[i].N + nb - 1) / nb);
+    }
+  }
+  const long long slice = (long long)nsub * max_rows * row_bytes;
+  a.ring_bytes = slice < GS_RING ? (int)((slice + 127) & ~127LL) : GS_RING;
+#ifdef G4_GEMV_FULL_RING
+  a.ring_bytes = GS_RING;
+#endif
+  if (a.ring_bytes < row_bytes) a.ring_bytes = (row_bytes + 127) & ~127;
+  a.max_rows = max_rows;
+  const GsLayout lay = gs_layout(a.ring_bytes, COLS, max_rows, nsub, EPI == EPI_GELU_CODES, a.K);
+  if (lay.total > 200 * 1024) return cudaErrorInvalidConfiguration;
+  auto k = k_qgemv_stream<BITS, COLS, RS, PRO, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr_set = true;
   }
-  return launch_k(k, dim3(a.n_blocks_total), dim3(256), smem, st, pdl, a);
+  return launch_k(k, dim3(a.n_blocks_total), dim3(256), (size_t)lay.total, st, pdl, a);
 }
 
-template <int BITS, int COLS>
-static cudaError_t launch_stream_c(const GemvArgs &a, int rs, cudaStream_t st, bool pdl) {
-  if (rs == 1) return launch_stream_t<BITS, COLS, 1>(a, st, pdl);
-  if (rs == 2) return launch_stream_t<BITS, COLS, 2>(a, st, pdl);
-  return launch_stream_t<BITS, COLS, 4>(a, st, pdl);
+// Each (prologue, epilogue) pair is its own kernel: a launch runs a short straight path, which
+// matters because every launch starts with a cold instruction cache. One column or up to eight.
+template <int BITS, int PRO, int EPI>
+static cudaError_t launch_stream_b(const GemvArgs &a, int rs, cudaStream_t st, bool pdl) {
+  if (a.cols == 1) {
+    if (rs == 1) return launch_stream_t<BITS, 1, 1, PRO, EPI>(a, st, pdl);
+    if (rs == 2) return launch_stream_t<BITS, 1, 2, PRO, EPI>(a, st, pdl);
+    return launch_stream_t<BITS, 1, 4, PRO, EPI>(a, st, pdl);
+  }
+  if (rs == 1) return launch_stream_t<BITS, 8, 1, PRO, EPI>(a, st, pdl);
+  if (rs == 2) return launch_stream_t<BITS, 8, 2, PRO, EPI>(a, st, pdl);
+  return launch_stream_t<BITS, 8, 4, PRO, EPI>(a, st, pdl);
+}
+
+template <int PRO, int EPI>
+static cudaError_t launch_stream_pe(const GemvArgs &a, int bits, int rs, cudaStream_t st, bool pdl) {
+  return bits == 4 ? launch_stream_b<4, PRO, EPI>(a, rs, st, pdl) : launch_stream_b<8, PRO, EPI>(a, rs, st, pdl);
 }
 
 cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, bool pdl) {
@@ -535,17 +691,24 @@ cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, boo
   const int rs = gs_row_split(row_bytes);
   if (row_bytes % 16 != 0 || row_bytes % rs != 0 || row_bytes / rs > 1024 || (row_bytes / rs) % 16 != 0)
     return cudaErrorInvalidConfiguration;
-  const int c = a.cols;
-  if (bits == 4) {
-    if (c <= 1) return launch_stream_c<4, 1>(a, rs, st, pdl);
-    if (c <= 2) return launch_stream_c<4, 2>(a, rs, st, pdl);
-    if (c <= 4) return launch_stream_c<4, 4>(a, rs, st, pdl);
-    if (c <= 8) return launch_stream_c<4, 8>(a, rs, st, pdl);
-  } else if (bits == 8) {
-    if (c <= 1) return launch_stream_c<8, 1>(a, rs, st, pdl);
-    if (c <= 2) return launch_stream_c<8, 2>(a, rs, st, pdl);
-    if (c <= 4) return launch_stream_c<8, 4>(a, rs, st, pdl);
-    if (c <= 8) return launch_stream_c<8, 8>(a, rs, st, pdl);
+  if (a.cols < 1 || a.cols > 8 || (bits != 4 && bits != 8)) return cudaErrorInvalidConfiguration;
+  const int epi = a.head ? EPI_HEAD : a.epi;
+  if (epi == EPI_Y) {
+    switch (a.pro) {
+      case PRO_X: return launch_stream_pe<PRO_X, EPI_Y>(a, bits, rs, st, pdl);
+      case PRO_NORM: return launch_stream_pe<PRO_NORM, EPI_Y>(a, bits, rs, st, pdl);
+      case PRO_JOIN: return launch_stream_pe<PRO_JOIN, EPI_Y>(a, bits, rs, st, pdl);
+      case PRO_NORMRES: return launch_stream_pe<PRO_NORMRES, EPI_Y>(a, bits, rs, st, pdl);
+      case PRO_GELU: return launch_stream_pe<PRO_GELU, EPI_Y>(a, bits, rs, st, pdl);
+      case PRO_CODES: return launch_stream_pe<PRO_CODES, EPI_Y>(a, bits, rs, st, pdl);
+    }
+  } else if (epi == EPI_GELU_CODES) {
+    if (a.pro == PRO_JOIN) return launch_stream_pe<PRO_JOIN, EPI_GELU_CODES>(a, bits, rs, st, pdl);
+    if (a.pro == PRO_NORMRES) return launch_stream_pe<PRO_NORMRES, EPI_GELU_CODES>(a, bits, rs, st, pdl);
+  } else if (epi == EPI_HEAD) {
+    if (a.pro == PRO_JOIN) return launch_stream_pe<PRO_JOIN, EPI_HEAD>(a, bits, rs, st, pdl);
+    if (a.pro == PRO_NORM) return launch_stream_pe<PRO_NORM, EPI_HEAD>(a, bits, rs, st, pdl);
+    if (a.pro == PRO_X) return launch_stream_pe<PRO_X, EPI_HEAD>(a, bits, rs, st, pdl);
   }
   return cudaErrorInvalidConfiguration;
 }
@@ -1378,6 +1541,7 @@ static cudaError_t launch_attn_decode_t(const AttnDec &a, cudaStream_t st, bool 
   if (!attr_set) {
     cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)attn_decode_smem<HD>());
+    cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr_set = true;
   }
   return launch_k(k_attn_decode<HD>, dim3(a.cols, a.max_blocks), dim3(256), attn_decode_smem<HD>(),

@@ -13,7 +13,24 @@ enum Prologue : int {
   PRO_JOIN = 2,     // h = (res + norm(src) * g1) * alpha -> hidden_out; x = norm(h) * g2
   PRO_NORMRES = 3,  // h = res + norm(src) * g1 -> hidden_out; x = h
   PRO_GELU = 4,     // x = gelu(src) * up[up_off + k]
+  PRO_CODES = 5,    // the int8 codes themselves, precomputed by the producing launch
 };
+
+// Epilogues of the streaming GEMV.
+enum Epilogue : int {
+  EPI_Y = 0,           // y rows to seg.y
+  EPI_GELU_CODES = 1,  // h = gelu(y0) * (pair ? y1 : epi_up[epi_up_off + r]), stored as the
+                       // next linear's int8 codes (codes_scale, codes_bits layout)
+  EPI_HEAD = 2,        // lm_head: softcap, logits, per-CTA argmax partials (set through `head`)
+};
+
+// Byte offset of activation element k inside a column's code vector. int8 weights read codes in
+// order; int4 weights read each 8-element group as [x0 x2 x4 x6 | x1 x3 x5 x7] (even and odd
+// nibbles of a packed word).
+__host__ __device__ __forceinline__ int code_pos(int k, int bits) {
+  if (bits == 8) return k;
+  return (k & ~7) + 2 * ((k >> 2) & 1) + 4 * (k & 1) + ((k >> 1) & 1);
+}
 
 struct GemvSeg {
   const uint8_t *w;    // packed codes, row-major [N, K * bits / 8]
@@ -43,6 +60,14 @@ struct GemvArgs {
   float *part_val; int32_t *part_idx; int n_blocks_total;
   // Weights of later steps to pull into L2 while this launch runs (split across its CTAs).
   const void *prefetch[4]; uint64_t prefetch_bytes[4];
+  // Set by launch_gemv_stream: shared-memory ring bytes and the most rows any CTA owns.
+  int ring_bytes; int max_rows;
+  // pair: seg[0] and seg[1] have the same N and every CTA owns the same rows of both.
+  int pair;
+  int epi;
+  const float *epi_up; int epi_ld_up; int epi_up_off;
+  uint8_t *codes_out; int codes_ld; float codes_scale; int codes_bits;
+  const uint8_t *src_codes; int ld_codes;   // PRO_CODES
 };
 
 // The streaming GEMV: one CTA per SM (or fewer), each streaming a contiguous row slice of one

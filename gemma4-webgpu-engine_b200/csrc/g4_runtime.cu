@@ -89,6 +89,9 @@ struct g4_ctx {
   float *part_o, *part_m, *part_l;
   int att_blocks_sliding = 0, att_blocks_global = 0;
   int32_t *att_count = nullptr;     // finished attention blocks per column (decode steps)
+  uint8_t *codes_mlp = nullptr;     // down_proj input codes [maxc][ffn_max]
+  uint8_t *codes_ple = nullptr;     // per_layer_projection input codes [maxc][PD]
+  int ffn_max = 0;
   float *logits = nullptr;
   float *head_pv = nullptr;
   int32_t *head_pi = nullptr;
@@ -422,6 +425,9 @@ static int alloc_runtime(g4_ctx *ctx) {
   if ((rc = take(&ctx->part_o, (size_t)maxc * mb * nh * ghd))) return rc;
   if ((rc = take(&ctx->part_m, (size_t)maxc * mb * nh))) return rc;
   if ((rc = take(&ctx->part_l, (size_t)maxc * mb * nh))) return rc;
+  ctx->ffn_max = (ffn + 15) & ~15;
+  CK(cudaMalloc(&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
+  CK(cudaMalloc(&ctx->codes_ple, (size_t)maxc * ctx->PD));
   CK(cudaMalloc(&ctx->att_count, (size_t)maxc * 4));
   CK(cudaMemset(ctx->att_count, 0, (size_t)maxc * 4));
   ctx->head_cols = std::min(maxc, std::max(ctx->cfg.max_seqs, 1));
@@ -505,6 +511,8 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   for (float *p : fs) cudaFree(p);
   cudaFree(ctx->head_pi);
   cudaFree(ctx->att_count);
+  cudaFree(ctx->codes_mlp);
+  cudaFree(ctx->codes_ple);
   cudaFree(ctx->d_step);
   cudaFree(ctx->d_tok_out);
   for (int i = 0; i < g4_ctx::kStageSlots; i++) {
@@ -796,6 +804,9 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
     if (a.res) a.res += (size_t)c0 * a.ld_res;
     if (a.hidden_out) a.hidden_out += (size_t)c0 * a.ld_res;
     if (a.up) a.up += (size_t)c0 * a.ld_up;
+    if (a.epi_up) a.epi_up += (size_t)c0 * a.epi_ld_up;
+    if (a.codes_out) a.codes_out += (size_t)c0 * a.codes_ld;
+    if (a.src_codes) a.src_codes += (size_t)c0 * a.ld_codes;
     if (head) {
       a.head = 1;
       a.logits = ctx->logits + (size_t)c0 * ctx->V;
@@ -961,9 +972,24 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       p.ld_src = qrows;
       if ((rc = run_linear(ctx, {{&ly.o, ctx->proj}}, cols, p, false, {wref(ly.down)}))) return rc;
     }
+    // gelu(gate) * up is formed once, by the gate/up launch (each CTA owns the same rows of
+    // both), and handed to down_proj as its int8 codes; likewise gelu(pleg) * per-layer input
+    // for per_layer_projection. Needs calibrated scales on all three linears.
+    const bool mlp_codes = ly.gate.N == ly.up.N && ly.gate.bits == ly.up.bits &&
+                           ly.gate.in_scale != 0.0f && ly.gate.in_scale == ly.up.in_scale &&
+                           ly.down.in_scale != 0.0f && ly.down.K <= ctx->ffn_max;
+    const bool ple_codes = ly.pleg.in_scale != 0.0f && ly.plep.in_scale != 0.0f && ly.plep.K == PD;
     // ---- gate, up with the post-attention join fused in (alpha 1)
     {
       GemvArgs p = pro_args(PRO_JOIN);
+      if (mlp_codes) {
+        p.pair = 1;
+        p.epi = EPI_GELU_CODES;
+        p.codes_out = ctx->codes_mlp;
+        p.codes_ld = ctx->ffn_max;
+        p.codes_scale = ly.down.in_scale;
+        p.codes_bits = ly.down.bits;
+      }
       p.src = ctx->proj;
       p.ld_src = H;
       p.res = ctx->res[cur];
@@ -978,14 +1004,20 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
         return rc;
       cur ^= 1;
     }
-    // ---- down_proj over gelu(gate) * up (the fused gelu prologue)
+    // ---- down_proj over gelu(gate) * up (codes from the gate/up launch, or the gelu prologue)
     {
-      GemvArgs p = pro_args(PRO_GELU);
+      GemvArgs p = pro_args(mlp_codes ? PRO_CODES : PRO_GELU);
       p.src = ctx->gate;
       p.ld_src = ly.gate.N;
       p.up = ctx->up;
       p.ld_up = ly.up.N;
       p.up_off = 0;
+      if (mlp_codes) {
+        p.src = nullptr;
+        p.up = nullptr;
+        p.src_codes = ctx->codes_mlp;
+        p.ld_codes = ctx->ffn_max;
+      }
       const Layer *nx = L + 1 < n_layers ? &ctx->layers[L + 1] : nullptr;
       if ((rc = run_linear(ctx, {{&ly.down, ctx->proj}}, cols, p, false,
                            {nx ? wref(nx->q) : WRef{nullptr, 0}, nx ? wref(nx->k) : WRef{nullptr, 0},
@@ -1002,6 +1034,16 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       p.g1 = ly.ln_post_ffn;
       p.hidden_out = ctx->res[cur ^ 1];
       p.eps = eps;
+      if (ple_codes) {
+        p.epi = EPI_GELU_CODES;
+        p.epi_up = ctx->ple_in;
+        p.epi_ld_up = ctx->ple_cols;
+        p.epi_up_off = L * PD;
+        p.codes_out = ctx->codes_ple;
+        p.codes_ld = PD;
+        p.codes_scale = ly.plep.in_scale;
+        p.codes_bits = ly.plep.bits;
+      }
       const Layer *nx = L + 1 < n_layers ? &ctx->layers[L + 1] : nullptr;
       if ((rc = run_linear(ctx, {{&ly.pleg, ctx->pleg_out}}, cols, p, false,
                            {nx ? wref(nx->o) : WRef{nullptr, 0}})))
@@ -1010,12 +1052,18 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     }
     // ---- per_layer_projection over gelu(gate) * the layer's per-layer input row
     {
-      GemvArgs p = pro_args(PRO_GELU);
+      GemvArgs p = pro_args(ple_codes ? PRO_CODES : PRO_GELU);
       p.src = ctx->pleg_out;
       p.ld_src = PD;
       p.up = ctx->ple_in;
       p.ld_up = ctx->ple_cols;
       p.up_off = L * PD;
+      if (ple_codes) {
+        p.src = nullptr;
+        p.up = nullptr;
+        p.src_codes = ctx->codes_ple;
+        p.ld_codes = PD;
+      }
       const Layer *nx = L + 1 < n_layers ? &ctx->layers[L + 1] : nullptr;
       if ((rc = run_linear(ctx, {{&ly.plep, ctx->proj}}, cols, p, false,
                            {nx ? wref(nx->gate) : WRef{nullptr, 0}, nx ? wref(nx->up) : WRef{nullptr, 0}})))
