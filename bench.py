@@ -66,6 +66,9 @@ def token_bytes(ctx_len: int) -> dict:
 
 GEMV_N, GEMV_K = 6144, 1536
 GEMV_BYTES = GEMV_N * GEMV_K // 2 + 2 * GEMV_N + GEMV_K + 2 * GEMV_N  # W + scales + x(int8) + y(f16)
+# dram__bytes_read.sum + dram__bytes_write.sum of one config-1 GEMV launch, from the ncu capture
+# summarised in profiles/qgemv_stream_config1.md (None until captured).
+GEMV_TRAFFIC = None
 
 
 def load_peaks() -> dict:
@@ -245,6 +248,33 @@ def measure_gemv(pkg, torch, copies: int, iters: int) -> dict:
             "timing": "cuda graph of launches" if graph is not None else "eager launches"}
 
 
+def run_gemv_only(pkg, torch, args, world, rank) -> None:
+    """Config 1 as its own line: GB/s of the GEMV over 64 distinct weight copies, each launch
+    chained to the previous one (programmatic dependent launch inside one CUDA graph)."""
+    peaks = load_peaks()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        g = measure_gemv(pkg, torch, copies=64, iters=64 * max(args.steps, 10))
+    if world > 1:
+        t = torch.tensor([g["seconds_per_launch"]], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        g["seconds_per_launch"] = float(t.item())
+        g["gbs"] = GEMV_BYTES / g["seconds_per_launch"] / 1e9
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": "quant GEMV HBM GB/s (config 1, int4 x int8, 6144 x 1536)", "value": world * g["gbs"],
+        "unit": "GB/s", "n_gpus": world, "steps": max(args.steps, 10), "warmup": args.warmup,
+        "ms_per_step": 64 * g["seconds_per_launch"] * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4xint8 (int32 acc)", "data": "synthetic (seeded)",
+        "config": {"workload": "config 1: 64 distinct 6144x1536 int4 weight copies (302 MB > L2), one graph",
+                   "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": g["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": g["gbs"] / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC,
+                     "peak_source": peaks["source"], "us_per_launch": g["seconds_per_launch"] * 1e6},
+        "gpu_launches": 64 * max(args.steps, 10), "clocks": clocks.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -254,6 +284,8 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=24)
+    ap.add_argument("--only-gemv", action="store_true",
+                    help="BASELINE config 1 alone: the int4 x int8 GEMV [6144 x 1536] line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
@@ -273,6 +305,9 @@ def main():
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
     pkg = entry.load_package()
+    if args.only_gemv:
+        run_gemv_only(pkg, torch, args, world, rank)
+        return
     engine = pkg.engine
     B = args.batch
     total_steps = args.warmup + args.steps
@@ -355,7 +390,7 @@ def main():
         "token_hbm_gbs": tb["total"] * B * args.steps / dev_s / 1e9 if B == 1 else None,
         "roofline": {"bound": "hbm", "kernel": "qgemv-4bit 6144x1536 (config 1)",
                      "achieved": gemv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": gemv["gbs"] / peaks["hbm_gbs"], "traffic": None,
+                     "frac": gemv["gbs"] / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC,
                      "peak_source": peaks["source"], "bytes_per_launch": GEMV_BYTES,
                      "us_per_launch": gemv["seconds_per_launch"] * 1e6, "timing": gemv["timing"]},
         "clocks": clocks.summary(),

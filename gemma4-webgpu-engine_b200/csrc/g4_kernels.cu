@@ -94,7 +94,8 @@ __device__ __forceinline__ void prologue_gains(const GemvArgs &a, ProGains &pg) 
 template <int BITS, int PRO>
 __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, const ProGains &pg, int c,
                                                  float in_scale, uint8_t *codes, float *red,
-                                                 bool write_hidden) {
+                                                 bool write_hidden, float in_scale2 = 0.0f,
+                                                 uint8_t *codes2 = nullptr, int *xs2 = nullptr) {
   const int t = threadIdx.x;
   const int K = a.K;
   const int nc = K >> 2;
@@ -186,6 +187,15 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, const ProGai
 #pragma unroll
   for (int i = 0; i < 2; i++)
     if (i < cnt) xs += ChunkPro::store<BITS>(codes, t + 256 * i, xv[i], in_scale, in_r);
+  if (codes2) {
+    // A second linear on the same input with its own input scale (the gate/up pair).
+    const float in_r2 = __fdiv_rn(1.0f, in_scale2);
+    int x2 = 0;
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+      if (i < cnt) x2 += ChunkPro::store<BITS>(codes2, t + 256 * i, xv[i], in_scale2, in_r2);
+    *xs2 = x2;
+  }
   return xs;
 }
 
@@ -325,13 +335,13 @@ __host__ __device__ __forceinline__ GsLayout gs_layout(int ring, int cols, int m
   GsLayout l;
   l.bars = ring;
   l.xsum = l.bars + GS_MAX_STAGES * 8;
-  l.red = l.xsum + 8 * 4;
+  l.red = l.xsum + 16 * 4;
   l.cand_v = l.red + 8 * 4;
   l.cand_i = l.cand_v + 8 * cols * 4;
   l.scales = l.cand_i + 8 * cols * 4;
   l.ybuf = l.scales + nsub * max_rows * 4;
   l.codes = (l.ybuf + (keep_y ? nsub * cols * max_rows * 4 : 0) + 15) & ~15;
-  l.total = l.codes + cols * K;
+  l.total = l.codes + nsub * cols * K;
   return l;
 }
 
@@ -344,8 +354,9 @@ template <int BITS, int COLS, int RS, int PRO, int EPI>
 __global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int ring_bytes = a.ring_bytes;
-  const bool pair = a.pair != 0;
-  const int nsub = pair ? 2 : 1;
+  // gate/up: both sub-slices of one CTA, each with its own input codes.
+  constexpr bool pair = EPI == EPI_GELU_CODES && PRO == PRO_JOIN;
+  constexpr int nsub = pair ? 2 : 1;
   constexpr bool keep_y = EPI == EPI_GELU_CODES;
   const GsLayout lay = gs_layout(ring_bytes, COLS, a.max_rows, nsub, keep_y, a.K);
   uint8_t *ring = smem;
@@ -384,7 +395,7 @@ __global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const 
     for (int i = 0; i < nstages; i++) mbar_init(&bars[i], 1);
     mbar_fence_init();
   }
-  if (t < 8) xsum[t] = 0;
+  if (t < 16) xsum[t] = 0;
   __syncthreads();
   auto issue = [&](int c) {
     const int st = c % nstages;
@@ -412,9 +423,15 @@ __global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const 
 
 #pragma unroll 1
   for (int c = 0; c < a.cols; c++) {
-    const int v = warp_sum_int(gemv_prologue_col<BITS, PRO>(a, pg, c, sg.in_scale, codes + c * K, red,
-                                                       bid == 0 && a.hidden_out != nullptr));
+    int x2 = 0;
+    const int v = warp_sum_int(gemv_prologue_col<BITS, PRO>(
+        a, pg, c, sg.in_scale, codes + c * K, red, bid == 0 && a.hidden_out != nullptr,
+        pair ? a.seg[1].in_scale : 0.0f, pair ? codes + (COLS + c) * K : nullptr, &x2));
     if (lane == 0) atomicAdd(&xsum[c], v);
+    if (pair) {
+      x2 = warp_sum_int(x2);
+      if (lane == 0) atomicAdd(&xsum[8 + c], x2);
+    }
   }
   __syncthreads();
 
@@ -447,6 +464,8 @@ __global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const 
     const uint8_t *sw = ring + st * stage_bytes;
     const float out_scale = sub ? a.seg[1].out_scale : sg.out_scale;
     const float out_r = sub ? out_r1 : out_r0;
+    const float in_scale = sub ? a.seg[1].in_scale : sg.in_scale;
+    const uint8_t *ccodes = codes + sub * COLS * K;
     // Each warp takes groups of four virtual rows; the four dot products run as independent
     // chains and close with one transposed reduction, after which lanes 0, 8, 16 and 24 hold
     // the four totals; the parts of a split row are then added and its lanes finish the rows
@@ -475,11 +494,11 @@ __global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const 
 #pragma unroll
           for (int j = 0; j < NX; j++) {
             if (BITS == 4) {
-              const uint4 *xp = reinterpret_cast<const uint4 *>(codes + c * K + 2 * koff[j]);
+              const uint4 *xp = reinterpret_cast<const uint4 *>(ccodes + c * K + 2 * koff[j]);
               xa[j] = xp[0];
               xb[j] = xp[1];
             } else {
-              xa[j] = *reinterpret_cast<const uint4 *>(codes + c * K + koff[j]);
+              xa[j] = *reinterpret_cast<const uint4 *>(ccodes + c * K + koff[j]);
             }
           }
 #pragma unroll
@@ -531,8 +550,8 @@ __global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const 
 #pragma unroll
         for (int c = 0; c < COLS; c++) {
           if (c < a.cols) {
-            const int exact = BITS == 4 ? acc[0][c] - 8 * xsum[c] : acc[0][c];
-            float y = __fmul_rn(__fmul_rn(sg.in_scale, wscale), (float)exact);
+            const int exact = BITS == 4 ? acc[0][c] - 8 * xsum[sub * 8 + c] : acc[0][c];
+            float y = __fmul_rn(__fmul_rn(in_scale, wscale), (float)exact);
             y = srq_out_r(y, out_scale, out_r);
             if (sg.acc_out) sg.acc_out[(size_t)c * sg.N + row] = exact;
             if (keep_y) {
@@ -638,9 +657,9 @@ static cudaError_t launch_stream_t(const GemvArgs &a0, cudaStream_t st, bool pdl
   // lets the next launch's CTAs sit on the SM beside this one's and start their copies early.
   GemvArgs a = a0;
   const int row_bytes = a.K * BITS / 8;
-  const int nsub = a.pair ? 2 : 1;
+  const int nsub = (EPI == EPI_GELU_CODES && PRO == PRO_JOIN) ? 2 : 1;
   int max_rows = 1;
-  if (a.pair) {
+  if (nsub == 2) {
     max_rows = (a.seg[0].N + a.n_blocks_total - 1) / a.n_blocks_total;
   } else {
     for (int i = 0; i < a.nseg; i++) {
@@ -703,8 +722,11 @@ cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, boo
       case PRO_CODES: return launch_stream_pe<PRO_CODES, EPI_Y>(a, bits, rs, st, pdl);
     }
   } else if (epi == EPI_GELU_CODES) {
-    if (a.pro == PRO_JOIN) return launch_stream_pe<PRO_JOIN, EPI_GELU_CODES>(a, bits, rs, st, pdl);
-    if (a.pro == PRO_NORMRES) return launch_stream_pe<PRO_NORMRES, EPI_GELU_CODES>(a, bits, rs, st, pdl);
+    // join: the gate/up pair; norm-residual: one linear times the per-layer input row.
+    if (a.pro == PRO_JOIN && a.pair && a.nseg == 2 && a.seg[0].N == a.seg[1].N)
+      return launch_stream_pe<PRO_JOIN, EPI_GELU_CODES>(a, bits, rs, st, pdl);
+    if (a.pro == PRO_NORMRES && !a.pair)
+      return launch_stream_pe<PRO_NORMRES, EPI_GELU_CODES>(a, bits, rs, st, pdl);
   } else if (epi == EPI_HEAD) {
     if (a.pro == PRO_JOIN) return launch_stream_pe<PRO_JOIN, EPI_HEAD>(a, bits, rs, st, pdl);
     if (a.pro == PRO_NORM) return launch_stream_pe<PRO_NORM, EPI_HEAD>(a, bits, rs, st, pdl);

@@ -976,7 +976,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     // both), and handed to down_proj as its int8 codes; likewise gelu(pleg) * per-layer input
     // for per_layer_projection. Needs calibrated scales on all three linears.
     const bool mlp_codes = ly.gate.N == ly.up.N && ly.gate.bits == ly.up.bits &&
-                           ly.gate.in_scale != 0.0f && ly.gate.in_scale == ly.up.in_scale &&
+                           ly.gate.in_scale != 0.0f && ly.up.in_scale != 0.0f &&
                            ly.down.in_scale != 0.0f && ly.down.K <= ctx->ffn_max;
     const bool ple_codes = ly.pleg.in_scale != 0.0f && ly.plep.in_scale != 0.0f && ly.plep.K == PD;
     // ---- gate, up with the post-attention join fused in (alpha 1)
