@@ -42,7 +42,7 @@ class Config(C.Structure):
     _fields_ = [
         ("arch", Arch), ("max_seqs", C.c_int32), ("max_context", C.c_int32),
         ("max_step_columns", C.c_int32), ("use_graphs", C.c_int32),
-        ("ple_slice_bytes", C.c_uint64),
+        ("ple_slice_bytes", C.c_uint64), ("gemm_min_columns", C.c_int32),
     ]
 
 
@@ -76,6 +76,7 @@ SIGNATURES = {
     "g4_ctx_stream": (_vp, [_vp]),
     "g4_last_launches": (C.c_int, [_vp, _i32p]),
     "g4_op_qgemv": (C.c_int, [_vp, _vp, _vp, _f, _f, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "g4_op_qgemm": (C.c_int, [_vp, _vp, _vp, _f, _f, _i32, _i32, _i32, _i32, _vp, _vp]),
     "g4_op_qgemv_gelu": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _f, _f, _i32, _i32, _i32, _i32,
                                    _vp, _vp]),
     "g4_op_rms_norm": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _f, _vp]),

@@ -15,7 +15,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libgemma4_cuda.so"
-SOURCES = ["g4_kernels.cu", "g4_runtime.cu", "g4_noalloc.cu"]
+SOURCES = ["g4_kernels.cu", "g4_gemm.cu", "g4_runtime.cu", "g4_noalloc.cu"]
 HEADERS = ["g4_device.cuh", "g4_kernels.cuh"]
 
 NVCC_FLAGS = [
@@ -43,14 +43,17 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not needs_build():
         return LIB
     LIB_DIR.mkdir(exist_ok=True)
-    objs = []
-    for src in SOURCES:
+    objs, procs = [], []
+    for src in SOURCES:   # the translation units compile in parallel
         obj = LIB_DIR / (Path(src).stem + ".o")
         cmd = [_nvcc(), *NVCC_FLAGS, "-c", str(CSRC / src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        procs.append((subprocess.Popen(cmd), cmd))
         objs.append(str(obj))
+    failed = [cmd for p, cmd in procs if p.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [_nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", str(tmp)]
     if verbose:

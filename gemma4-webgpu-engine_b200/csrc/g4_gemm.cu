@@ -1,0 +1,398 @@
+// Tensor-core quantized linear for many columns (prefill chunks, batched decode): the qgemm
+// column contract of src/kernels/qgemm.ts:76-110, 490-552 (every token column is exactly the
+// qgemv of src/kernels/qgemv.ts:1131-1176) computed with tcgen05 int8 MMA.
+//
+// D[128 weight rows][BN tokens] = A[128][K] * B[BN][K]^T, int8 x int8 -> int32 in TMEM.
+//   A: weight codes as signed int8. int8 weights arrive by TMA straight into the 128-byte
+//      swizzled K-major layout the MMA reads; int4 weights arrive packed (TMA, no swizzle) and
+//      four unpack warps write them as (u - 8) into that layout.
+//   B: the activation codes of BN tokens (k_quantize wrote them, plain K order), TMA, swizzled.
+// The int32 accumulators are exact, so the epilogue y = srqOut((inScale * scale[r]) * f32(acc))
+// gives the GEMV's bits.
+//
+// Warps: 0 issues TMA, 1 owns TMEM and issues the MMAs (one thread), 2-5 unpack and then run the
+// epilogue (warp w reads TMEM lanes 32 (w % 4) .. + 31). Every mbarrier wait is bounded; a wait
+// that gives up raises g4_gemm_error, the copies and MMAs already issued are waited for (bounded),
+// and the TMEM is released on every path.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <mutex>
+
+#include "g4_device.cuh"
+#include "g4_kernels.cuh"
+
+namespace g4 {
+
+__device__ int g4_gemm_error;
+
+int gemm_error_take() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g4_gemm_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g4_gemm_error, &zero, sizeof(int));
+  return v;
+}
+
+// ------------------------------------------------------------------ tensor maps (host)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_u8(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  if (((uintptr_t)base & 15) || (row_stride & 15) || box_inner * 1u > 256 || box_outer > 256) return -2;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+                  elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+// ------------------------------------------------------------------ device helpers
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart
+// (start >> 4, leading offset 1, stride offset 1024 >> 4, descriptor version 1, layout 2).
+__device__ __forceinline__ uint64_t sw128_desc(const void *p) {
+  const uint32_t a = smem_u32(p);
+  return (uint64_t)((a >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::i8: D s32, A s8, B s8, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+      "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Eight packed int4 weights (code i at bits 4i) to eight signed int8 (u - 8), in K order.
+__device__ __forceinline__ uint2 unpack8(uint32_t w) {
+  const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+  uint32_t a = __byte_perm(lo, hi, 0x5140), b = __byte_perm(lo, hi, 0x7362);
+  // u - 8 in two's complement: flip bit 3, then copy bit 3 into the high nibble.
+  a ^= 0x08080808u;
+  b ^= 0x08080808u;
+  a |= (a & 0x08080808u) * 0x1Eu;
+  b |= (b & 0x08080808u) * 0x1Eu;
+  return make_uint2(a, b);
+}
+
+constexpr int GM_BM = 128;       // weight rows per tile (MMA M)
+constexpr int GM_BK = 128;       // K per stage: one 128-byte swizzle atom of int8
+
+template <int BN>
+struct GemmShape {
+  static constexpr int STAGES = BN >= 256 ? 3 : 4;
+  static constexpr int A_BYTES = GM_BM * GM_BK;          // 16 KB
+  static constexpr int B_BYTES = BN * GM_BK;
+  static constexpr int P_BYTES = GM_BM * GM_BK / 2;      // packed int4 staging, 8 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SMEM = 1024 + BAR_OFF + (3 * STAGES + 2) * 8 + 64 + 4 * 32 * 8;
+};
+
+template <int BITS, int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    k_qgemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+               const GemmArgs a) {
+  using S = GemmShape<BN>;
+  constexpr int NS = S::STAGES;
+  extern __shared__ __align__(1024) uint8_t gsm_raw[];
+  uint8_t *gsm = gsm_raw + ((1024 - (smem_u32(gsm_raw) & 1023)) & 1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(gsm + S::BAR_OFF);
+  uint64_t *aready = full + NS;
+  uint64_t *empty = aready + NS;
+  uint64_t *accf = empty + NS;
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 2);
+  int *flags = reinterpret_cast<int *>(tslot + 2);         // [0]: error seen
+  float *cand_v = reinterpret_cast<float *>(flags + 14);   // [4 warps][32] head candidates
+  int *cand_i = reinterpret_cast<int *>(cand_v + 4 * 32);
+  auto A = [&](int s) { return gsm + s * S::STAGE_BYTES; };
+  auto B = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES; };
+  auto P = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES + S::B_BYTES; };
+
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int n0 = blockIdx.x * GM_BM, m0 = blockIdx.y * BN;
+  const int KT = a.K / GM_BK;
+
+  if (t == 0) {
+    for (int s = 0; s < NS; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&aready[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    mbar_fence_init();
+    flags[0] = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  grid_launch_dependents();
+  grid_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer: weights and codes of stage kt, once the MMAs of kt - NS have read the slot.
+      const uint32_t wbytes = BITS == 4 ? S::P_BYTES : S::A_BYTES;
+      int issued = 0;
+      for (int kt = 0; kt < KT; kt++) {
+        const int s = kt % NS;
+        if (kt >= NS && !mbar_wait(&empty[s], (uint32_t)((kt / NS - 1) & 1))) {
+          atomicExch(&g4_gemm_error, 1);
+          flags[0] = 1;
+          break;
+        }
+        mbar_expect_tx(&full[s], wbytes + S::B_BYTES);
+        if (BITS == 4)
+          tma_load_2d(P(s), &tmW, kt * (GM_BK / 2), n0, &full[s]);
+        else
+          tma_load_2d(A(s), &tmW, kt * GM_BK, n0, &full[s]);
+        tma_load_2d(B(s), &tmX, kt * GM_BK, m0, &full[s]);
+        issued = kt + 1;
+      }
+      // Every copy issued lands before the CTA can leave (the last NS are the ones not yet
+      // known to be consumed).
+      for (int kt = issued - NS < 0 ? 0 : issued - NS; kt < issued; kt++)
+        mbar_wait(&full[kt % NS], (uint32_t)((kt / NS) & 1));
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_i8(BN);
+      for (int kt = 0; kt < KT; kt++) {
+        const int s = kt % NS;
+        uint64_t *ready = BITS == 4 ? &aready[s] : &full[s];
+        if (!mbar_wait(ready, (uint32_t)((kt / NS) & 1))) {
+          atomicExch(&g4_gemm_error, 1);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(A(s)), bd = sw128_desc(B(s));
+#pragma unroll
+        for (int kk = 0; kk < GM_BK / 32; kk++)
+          mma_i8(tmem, ad + 2 * kk, bd + 2 * kk, IDESC, (kt | kk) != 0 ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      mma_commit(accf);   // after the last MMA issued (or at once, if none was)
+    }
+  } else {
+    const int tu = t - 64;   // 0..127
+    if (BITS == 4) {
+      for (int kt = 0; kt < KT; kt++) {
+        const int s = kt % NS;
+        if (!mbar_wait(&full[s], (uint32_t)((kt / NS) & 1))) {
+          atomicExch(&g4_gemm_error, 1);
+          flags[0] = 1;
+          break;
+        }
+        const uint8_t *p = P(s);
+        uint8_t *dst = A(s);
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+          const int idx = tu + 128 * it;   // (row, 16-element chunk)
+          const int row = idx >> 3, ch = idx & 7;
+          const uint2 pk = *reinterpret_cast<const uint2 *>(p + row * 64 + ch * 8);
+          const uint2 lo = unpack8(pk.x), hi = unpack8(pk.y);
+          *reinterpret_cast<uint4 *>(dst + (row >> 3) * 1024 + (row & 7) * 128 + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aready[s]);
+      }
+    }
+    // ---- epilogue
+    const bool ok = mbar_wait(accf, 0);
+    if (!ok) {
+      atomicExch(&g4_gemm_error, 1);
+      mbar_wait(accf, 0);
+    }
+    tc_fence_after();
+    const int q = warp & 3;
+    const int row = n0 + 32 * q + lane;
+    const bool row_ok = row < a.N;
+    const float wscale = row_ok ? f16_bits_to_f32(a.s[row]) : 0.0f;
+    const float sc = __fmul_rn(a.in_scale, wscale);
+    const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t acc[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
+      // After a failed wait nothing is stored; the named barriers below still run in step.
+      const bool store = ok && !flags[0];
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        const int tok = m0 + c0 + j;
+        float y = __fmul_rn(sc, (float)(int)acc[j]);
+        y = srq_out_r(y, a.out_scale, out_r);
+        if (EPI == EPI_HEAD) {
+          if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
+          if (store && a.logits && row_ok && tok < a.M) a.logits[(size_t)tok * a.ld_logits + row] = y;
+          // Greatest value, lowest row on ties, across the warp's 32 rows.
+          float bv = row_ok ? y : -FLT_MAX;
+          int bi = row_ok ? row : 0x7fffffff;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+              bv = ov;
+              bi = oi;
+            }
+          }
+          if (lane == j) {
+            cand_v[q * 32 + j] = bv;
+            cand_i[q * 32 + j] = bi;
+          }
+        } else {
+          if (store && row_ok && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
+        }
+      }
+      if (EPI == EPI_HEAD) {
+        // The four warps' candidates for these 32 tokens: warp q == 0's lane j closes token j.
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (q == 0) {
+          float bv = cand_v[lane];
+          int bi = cand_i[lane];
+#pragma unroll
+          for (int w2 = 1; w2 < 4; w2++) {
+            const float ov = cand_v[w2 * 32 + lane];
+            const int oi = cand_i[w2 * 32 + lane];
+            if (ov > bv || (ov == bv && oi < bi)) {
+              bv = ov;
+              bi = oi;
+            }
+          }
+          const int tok = m0 + c0 + lane;
+          if (store && tok < a.M) {
+            a.part_val[(size_t)tok * a.n_parts + blockIdx.x] = bv;
+            a.part_idx[(size_t)tok * a.n_parts + blockIdx.x] = bi;
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+  }
+}
+
+template <int BITS, int BN, int EPI>
+static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                 cudaStream_t st, bool pdl) {
+  auto k = k_qgemm_tc<BITS, BN, EPI>;
+  const int smem = GemmShape<BN>::SMEM;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + BN - 1) / BN);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr1[1];
+  attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr1[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr1;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
+}
+
+template <int BITS, int EPI>
+static cudaError_t launch_gemm_b(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                 int bn, cudaStream_t st, bool pdl) {
+  if (bn == 64) return launch_gemm_t<BITS, 64, EPI>(tmW, tmX, a, st, pdl);
+  if (bn == 128) return launch_gemm_t<BITS, 128, EPI>(tmW, tmX, a, st, pdl);
+  if (bn == 256) return launch_gemm_t<BITS, 256, EPI>(tmW, tmX, a, st, pdl);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a, int bits,
+                         int bn, cudaStream_t st, bool pdl) {
+  if (a.K % GM_BK != 0 || a.K < GM_BK || a.N < 1 || a.M < 1) return cudaErrorInvalidValue;
+  if (bits == 4) {
+    if (a.head) return launch_gemm_b<4, EPI_HEAD>(tmW, tmX, a, bn, st, pdl);
+    return launch_gemm_b<4, EPI_Y>(tmW, tmX, a, bn, st, pdl);
+  }
+  if (bits == 8) {
+    if (a.head) return launch_gemm_b<8, EPI_HEAD>(tmW, tmX, a, bn, st, pdl);
+    return launch_gemm_b<8, EPI_Y>(tmW, tmX, a, bn, st, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+int gemm_tile_rows() { return GM_BM; }
+
+}  // namespace g4

@@ -199,6 +199,35 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, const ProGai
   return xs;
 }
 
+// Activation codes for the tensor-core path (one CTA per column, plain K order).
+template <int PRO>
+__global__ void __launch_bounds__(256) k_quantize(const GemvArgs a, uint8_t *codes, int ld, float s1,
+                                                  uint8_t *codes2, float s2) {
+  __shared__ float red[8];
+  ProGains pg;
+  prologue_gains<PRO>(a, pg);
+  grid_launch_dependents();
+  grid_wait();
+  const int c = blockIdx.x;
+  int x2 = 0;
+  gemv_prologue_col<8, PRO>(a, pg, c, s1, codes + (size_t)c * ld, red, a.hidden_out != nullptr, s2,
+                            codes2 ? codes2 + (size_t)c * ld : nullptr, &x2);
+}
+
+cudaError_t launch_quantize(const GemvArgs &a, uint8_t *codes, int ld, float s1, uint8_t *codes2,
+                           float s2, cudaStream_t st, bool pdl) {
+  if (a.cols < 1 || (a.K & 15) || s1 == 0.0f || (codes2 && s2 == 0.0f)) return cudaErrorInvalidValue;
+  const dim3 g(a.cols), b(256);
+  switch (a.pro) {
+    case PRO_X: return launch_k(k_quantize<PRO_X>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
+    case PRO_NORM: return launch_k(k_quantize<PRO_NORM>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
+    case PRO_JOIN: return launch_k(k_quantize<PRO_JOIN>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
+    case PRO_NORMRES: return launch_k(k_quantize<PRO_NORMRES>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
+    case PRO_GELU: return launch_k(k_quantize<PRO_GELU>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
+  }
+  return cudaErrorInvalidValue;
+}
+
 // The f32 path of an uncalibrated site (in_scale == 0, src/kernels/qgemv.ts:666-675), one column:
 // lane l accumulates the row's 16-byte chunks l, l + 32, ... in k order with fused multiply-adds,
 // the lanes close with the butterfly, y = srqOut((1 * scale) * sum).
@@ -257,45 +286,6 @@ __global__ void __launch_bounds__(256) k_gemv_f32(const GemvArgs a) {
 // =====================================================================================
 
 __device__ int g4_dev_error;
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_fence_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.b32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait on an mbarrier phase: false once the iteration limit is reached.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  for (int i = 0; i < (1 << 22); i++)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-__device__ __forceinline__ void l2_prefetch(const void *p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 constexpr int GS_RING = 96 * 1024;   // shared-memory ring per CTA
 constexpr int GS_MAX_STAGES = 8;

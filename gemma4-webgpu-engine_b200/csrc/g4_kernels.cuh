@@ -1,6 +1,7 @@
 // g4_kernels.cuh -- launch interface of the sm_100a kernels (internal to libgemma4_cuda.so).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -132,6 +133,32 @@ struct AttnArgs {
   float *out;                        // [cols, heads * hd]
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
+
+// Activation codes for the tensor-core path: one CTA per column runs the GEMV prologue `a.pro`
+// (norm / join / norm-residual / gelu / x) once and writes the column's int8 codes in K order
+// for in_scale s1 (and s2 into codes2 when non-null); a.hidden_out, when set, gets the join.
+cudaError_t launch_quantize(const GemvArgs &a, uint8_t *codes, int ld, float s1, uint8_t *codes2,
+                           float s2, cudaStream_t st, bool pdl);
+
+// Tensor-core quantized linear (g4_gemm.cu): y[M tokens][ld_y] rows < N, from weights (tensor
+// map tmW: int4 packed [N][K/2] box 64 x 128, or int8 [N][K] box 128 x 128 swizzled) and the
+// activation codes (tmX: int8 [tokens][K] box 128 x bn swizzled). K a multiple of 128; bn 64,
+// 128 or 256. head: softcap, logits and per-128-row argmax partials [token][n_parts].
+struct GemmArgs {
+  int N, K, M;
+  const uint16_t *s;
+  float in_scale, out_scale;
+  float *y; int ld_y;
+  int head; float softcap;
+  float *logits; int ld_logits;
+  float *part_val; int32_t *part_idx; int n_parts;
+};
+int make_tmap_u8(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
+                 uint64_t row_stride, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a, int bits,
+                         int bn, cudaStream_t st, bool pdl);
+int gemm_error_take();
+int gemm_tile_rows();
 
 // Decode attention in one launch (every column a distinct sequence at one new position): the
 // q-norm-rope of all heads, the K/V row of the new position (producer layers: k != nullptr),

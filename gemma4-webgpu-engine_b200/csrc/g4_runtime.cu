@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -32,7 +33,18 @@ struct Linear {
   int N = 0, K = 0, bits = 4;
   float in_scale = 0, out_scale = 0;
   std::string module;
+  CUtensorMap tmw;          // TMA view of w for the tensor-core path (has_tm)
+  bool has_tm = false;
 };
+
+// The tensor map the tensor-core linear loads weights through: int4 packed rows (box 64 bytes x
+// 128 rows, unpacked on chip) or int8 rows (box 128 x 128, 128-byte swizzle). Needs K % 128 == 0.
+static void linear_tmap(Linear &l) {
+  l.has_tm = false;
+  if (!l.w || l.K % 128 != 0 || (l.bits != 4 && l.bits != 8)) return;
+  const uint64_t rb = (uint64_t)l.K * l.bits / 8;
+  l.has_tm = make_tmap_u8(&l.tmw, l.w, rb, (uint64_t)l.N, rb, l.bits == 4 ? 64 : 128, 128, l.bits == 8) == 0;
+}
 
 struct Layer {
   int hd = 256;
@@ -89,6 +101,18 @@ struct g4_ctx {
   float *part_o, *part_m, *part_l;
   int att_blocks_sliding = 0, att_blocks_global = 0;
   int32_t *att_count = nullptr;     // finished attention blocks per column (decode steps)
+  // Tensor-core path: activation codes (three input scales at most per launch group), their
+  // TMA views by (buffer, K, tile columns), lm_head argmax partials, and the column threshold.
+  uint8_t *gq[3] = {nullptr, nullptr, nullptr};
+  int gq_ld = 0, gq_rows = 0;
+  std::map<std::tuple<int, int, int>, CUtensorMap> tmx;
+  float *gpv = nullptr;
+  int32_t *gpi = nullptr;
+  int gparts = 0, gemm_min_cols = 16;
+  // The argmax partials the head of the step being recorded wrote.
+  float *cur_pv = nullptr;
+  int32_t *cur_pi = nullptr;
+  int cur_parts = 0;
   uint8_t *codes_mlp = nullptr;     // down_proj input codes [maxc][ffn_max]
   uint8_t *codes_ple = nullptr;     // per_layer_projection input codes [maxc][PD]
   int ffn_max = 0;
@@ -182,6 +206,7 @@ extern "C" int g4_config_default(g4_config *cfg) {
   cfg->max_step_columns = 64;
   cfg->use_graphs = 1;
   cfg->ple_slice_bytes = 0;
+  cfg->gemm_min_columns = 16;
   return G4_OK;
 }
 
@@ -339,6 +364,10 @@ static int alloc_weights(g4_ctx *ctx) {
   ctx->lm.K = H;
   ctx->lm.bits = 4;
   ctx->lm.module = "lm_head";
+  for (Layer &ly : ctx->layers)
+    for (Linear *l : {&ly.q, &ly.k, &ly.v, &ly.o, &ly.gate, &ly.up, &ly.down, &ly.pleg, &ly.plep})
+      linear_tmap(*l);
+  linear_tmap(ctx->lm);
   // The PLE code table: one buffer or vocab-row slices (src/tableSplit.ts:125-215).
   const uint64_t row_bytes = (uint64_t)ctx->ple_cols / 2;
   const uint64_t total = row_bytes * V;
@@ -425,6 +454,16 @@ static int alloc_runtime(g4_ctx *ctx) {
   if ((rc = take(&ctx->part_o, (size_t)maxc * mb * nh * ghd))) return rc;
   if ((rc = take(&ctx->part_m, (size_t)maxc * mb * nh))) return rc;
   if ((rc = take(&ctx->part_l, (size_t)maxc * mb * nh))) return rc;
+  ctx->gq_ld = (int)((std::max<size_t>({(size_t)ctx->H, ffn, nh * ghd}) + 127) & ~(size_t)127);
+  ctx->gq_rows = std::max(maxc, 256);
+  for (int i = 0; i < 3; i++) {
+    CK(cudaMalloc(&ctx->gq[i], (size_t)ctx->gq_rows * ctx->gq_ld));
+    CK(cudaMemset(ctx->gq[i], 0, (size_t)ctx->gq_rows * ctx->gq_ld));
+  }
+  ctx->gparts = (int)((a.vocab_size + 127) / 128);
+  CK(cudaMalloc(&ctx->gpv, (size_t)maxc * ctx->gparts * 4));
+  CK(cudaMalloc(&ctx->gpi, (size_t)maxc * ctx->gparts * 4));
+  ctx->gemm_min_cols = ctx->cfg.gemm_min_columns > 0 ? ctx->cfg.gemm_min_columns : 16;
   ctx->ffn_max = (ffn + 15) & ~15;
   CK(cudaMalloc(&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
   CK(cudaMalloc(&ctx->codes_ple, (size_t)maxc * ctx->PD));
@@ -512,6 +551,9 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   cudaFree(ctx->head_pi);
   cudaFree(ctx->att_count);
   cudaFree(ctx->codes_mlp);
+  for (int i = 0; i < 3; i++) cudaFree(ctx->gq[i]);
+  cudaFree(ctx->gpv);
+  cudaFree(ctx->gpi);
   cudaFree(ctx->codes_ple);
   cudaFree(ctx->d_step);
   cudaFree(ctx->d_tok_out);
@@ -774,8 +816,83 @@ static WRef wref(const Linear &l) {
 
 // One quantized linear launch (or several, 8 columns each) with a fused prologue, streaming its
 // weights; `prefetch` names weights of later launches to pull into L2 meanwhile.
+static const CUtensorMap *codes_tmap(g4_ctx *ctx, int buf, int K, int bn) {
+  auto key = std::make_tuple(buf, K, bn);
+  auto it = ctx->tmx.find(key);
+  if (it != ctx->tmx.end()) return &it->second;
+  CUtensorMap m;
+  if (make_tmap_u8(&m, ctx->gq[buf], (uint64_t)K, (uint64_t)ctx->gq_rows, (uint64_t)ctx->gq_ld, 128, bn, true))
+    return nullptr;
+  return &(ctx->tmx[key] = m);
+}
+
+// The tensor-core path of a linear launch group: the prologue runs once per column into int8
+// codes (one code vector per distinct input scale), then one tcgen05 GEMM per segment.
+static bool gemm_eligible(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, const GemvArgs &p) {
+  if (cols < ctx->gemm_min_cols || p.pro == PRO_CODES || p.epi != EPI_Y || p.pair) return false;
+  for (auto &sg : segs)
+    if (!sg.lin->has_tm || sg.lin->in_scale == 0.0f || sg.lin->K % 128 != 0) return false;
+  return true;
+}
+
+static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs q, bool head) {
+  const int K = segs.begin()->lin->K;
+  float sc[3];
+  int nsc = 0, which[3];
+  int i = 0;
+  for (auto &sg : segs) {
+    int j = 0;
+    while (j < nsc && sc[j] != sg.lin->in_scale) j++;
+    if (j == nsc) sc[nsc++] = sg.lin->in_scale;
+    which[i++] = j;
+  }
+  q.K = K;
+  q.cols = cols;
+  CK(launch_quantize(q, ctx->gq[0], ctx->gq_ld, sc[0], nsc > 1 ? ctx->gq[1] : nullptr, nsc > 1 ? sc[1] : 0.0f,
+                     ctx->st, true));
+  ctx->launches++;
+  if (nsc > 2) {
+    q.hidden_out = nullptr;
+    CK(launch_quantize(q, ctx->gq[2], ctx->gq_ld, sc[2], nullptr, 0.0f, ctx->st, true));
+    ctx->launches++;
+  }
+  const int bn = cols <= 64 ? 64 : (cols <= 128 ? 128 : 256);
+  i = 0;
+  for (auto &sg : segs) {
+    const Linear &l = *sg.lin;
+    const CUtensorMap *tx = codes_tmap(ctx, which[i++], K, bn);
+    if (!tx) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
+    GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.N = l.N;
+    g.K = K;
+    g.M = cols;
+    g.s = l.s;
+    g.in_scale = l.in_scale;
+    g.out_scale = l.out_scale;
+    g.y = sg.y;
+    g.ld_y = l.N;
+    if (head) {
+      g.head = 1;
+      g.softcap = q.softcap;
+      g.logits = ctx->logits;
+      g.ld_logits = ctx->V;
+      g.part_val = ctx->gpv;
+      g.part_idx = ctx->gpi;
+      g.n_parts = (l.N + gemm_tile_rows() - 1) / gemm_tile_rows();
+      ctx->cur_pv = ctx->gpv;
+      ctx->cur_pi = ctx->gpi;
+      ctx->cur_parts = g.n_parts;
+    }
+    CK(launch_qgemm(l.tmw, *tx, g, l.bits, bn, ctx->st, true));
+    ctx->launches++;
+  }
+  return G4_OK;
+}
+
 static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs proto,
                       bool head = false, std::initializer_list<WRef> prefetch = {}) {
+  if (gemm_eligible(ctx, segs, cols, proto)) return run_linear_gemm(ctx, segs, cols, proto, head);
   const Linear *l0 = segs.begin()->lin;
   for (int c0 = 0; c0 < cols; c0 += 8) {
     GemvArgs a = proto;
@@ -814,6 +931,9 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
       a.part_val = ctx->head_pv + (size_t)c0 * blocks;
       a.part_idx = ctx->head_pi + (size_t)c0 * blocks;
       ctx->head_blocks = blocks;
+      ctx->cur_pv = ctx->head_pv;
+      ctx->cur_pi = ctx->head_pi;
+      ctx->cur_parts = blocks;
     }
     CK(launch_gemv(a, l0->bits, ctx->st, true));
     ctx->launches++;
@@ -975,10 +1095,11 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     // gelu(gate) * up is formed once, by the gate/up launch (each CTA owns the same rows of
     // both), and handed to down_proj as its int8 codes; likewise gelu(pleg) * per-layer input
     // for per_layer_projection. Needs calibrated scales on all three linears.
-    const bool mlp_codes = ly.gate.N == ly.up.N && ly.gate.bits == ly.up.bits &&
+    const bool gemm_step = cols >= ctx->gemm_min_cols;
+    const bool mlp_codes = !gemm_step && ly.gate.N == ly.up.N && ly.gate.bits == ly.up.bits &&
                            ly.gate.in_scale != 0.0f && ly.up.in_scale != 0.0f &&
                            ly.down.in_scale != 0.0f && ly.down.K <= ctx->ffn_max;
-    const bool ple_codes = ly.pleg.in_scale != 0.0f && ly.plep.in_scale != 0.0f && ly.plep.K == PD;
+    const bool ple_codes = !gemm_step && ly.pleg.in_scale != 0.0f && ly.plep.in_scale != 0.0f && ly.plep.K == PD;
     // ---- gate, up with the post-attention join fused in (alpha 1)
     {
       GemvArgs p = pro_args(PRO_JOIN);
@@ -1084,7 +1205,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     p.eps = eps;
     p.softcap = a.final_softcap;
     if ((rc = run_linear(ctx, {{&ctx->lm, nullptr}}, cols, p, true))) return rc;
-    CK(launch_argmax_final(ctx->head_pv, ctx->head_pi, ctx->head_blocks, cols, d_tok,
+    CK(launch_argmax_final(ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, cols, d_tok,
                            ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
     ctx->launches++;
     if (advance) {
@@ -1155,7 +1276,7 @@ static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos,
 static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
   CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)cols * 4, cudaMemcpyDeviceToHost, ctx->st));
   CK(cudaStreamSynchronize(ctx->st));
-  if (device_error_take() > 0) {
+  if (device_error_take() > 0 || gemm_error_take() > 0) {
     // A block that gave up may have left its column's finished-block count behind.
     cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 4, ctx->st);
     cudaStreamSynchronize(ctx->st);
@@ -1361,6 +1482,59 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
     gemv_stream_partition(a, 2 * sms);
     OPCK(launch_gemv(a, bits, st, true));
   }
+  OPCK(cudaGetLastError());
+  return G4_OK;
+}
+
+extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, float in_scale,
+                           float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
+                           void *stream) {
+  if (!wq || !scales || !x || !y) return fail(nullptr, G4_ERR_INVALID, "g4_op_qgemm: null pointer");
+  if (bits != 4 && bits != 8) return fail(nullptr, G4_ERR_INVALID, "bits must be 4 or 8");
+  const int span = bits == 4 ? 256 : 128;
+  if (N < 1 || K < span || K % span != 0 || cols < 1)
+    return fail(nullptr, G4_ERR_INVALID, "qgemm-%dbit needs K a multiple of %d, got %d (N %d, cols %d)", bits, span, K, N, cols);
+  if (in_scale == 0.0f) return fail(nullptr, G4_ERR_UNSUPPORTED, "the tensor-core path needs a calibrated site");
+  if (K > 8192) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int rows = std::max(cols, 256);
+  uint8_t *codes = nullptr;
+  OPCK(cudaMallocAsync(&codes, (size_t)rows * K, st));
+  OPCK(cudaMemsetAsync(codes, 0, (size_t)rows * K, st));
+  GemvArgs q;
+  memset(&q, 0, sizeof(q));
+  q.pro = PRO_X;
+  q.alpha = 1.0f;
+  q.K = K;
+  q.cols = cols;
+  q.src = x;
+  q.ld_src = K;
+  cudaError_t e = launch_quantize(q, codes, K, in_scale, nullptr, 0.0f, st, false);
+  CUtensorMap tw, tx;
+  const int bn = cols <= 64 ? 64 : (cols <= 128 ? 128 : 256);
+  const uint64_t rb = (uint64_t)K * bits / 8;
+  int rc = G4_OK;
+  if (e == cudaSuccess) {
+    if (make_tmap_u8(&tw, wq, rb, (uint64_t)N, rb, bits == 4 ? 64 : 128, 128, bits == 8) ||
+        make_tmap_u8(&tx, codes, (uint64_t)K, (uint64_t)rows, (uint64_t)K, 128, bn, true)) {
+      rc = fail(nullptr, G4_ERR_CUDA, "tensor map encoding failed");
+    } else {
+      GemmArgs g;
+      memset(&g, 0, sizeof(g));
+      g.N = N;
+      g.K = K;
+      g.M = cols;
+      g.s = (const uint16_t *)scales;
+      g.in_scale = in_scale;
+      g.out_scale = out_scale;
+      g.y = y;
+      g.ld_y = N;
+      e = launch_qgemm(tw, tx, g, bits, bn, st, false);
+    }
+  }
+  cudaFreeAsync(codes, st);
+  if (rc) return rc;
+  OPCK(e);
   OPCK(cudaGetLastError());
   return G4_OK;
 }

@@ -20,7 +20,7 @@ class Context:
 
     def __init__(self, device: int = 0, max_seqs: int = 1, max_context: int = 2048,
                  max_step_columns: int = 64, use_graphs: bool = True, ple_slice_bytes: int = 0,
-                 arch: _abi.Arch | None = None):
+                 arch: _abi.Arch | None = None, gemm_min_columns: int = 16):
         lib = _abi.load()
         cfg = _abi.config_default()
         if arch is not None:
@@ -30,6 +30,7 @@ class Context:
         cfg.max_step_columns = max_step_columns
         cfg.use_graphs = 1 if use_graphs else 0
         cfg.ple_slice_bytes = ple_slice_bytes
+        cfg.gemm_min_columns = gemm_min_columns
         h = C.c_void_p()
         _abi.check(lib.g4_ctx_create(device, C.byref(cfg), C.byref(h)))
         self.lib = lib

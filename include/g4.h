@@ -95,9 +95,12 @@ typedef struct g4_config {
   int32_t max_step_columns;  /* widest step: a prefill chunk or a decode batch */
   int32_t use_graphs;        /* 1: record decode steps into CUDA graphs (default) */
   uint64_t ple_slice_bytes;  /* 0: PLE table is one buffer; else the vocab-row slice cap */
+  int32_t gemm_min_columns;  /* steps this wide or wider run their linears on the tcgen05 int8
+                                GEMM (prefill chunks, batched decode); 0: 16 */
 } g4_config;
 
-/* Defaults: g4_arch_default, max_seqs 1, max_context 2048, max_step_columns 64, graphs on. */
+/* Defaults: g4_arch_default, max_seqs 1, max_context 2048, max_step_columns 64, graphs on,
+ * gemm_min_columns 16. */
 int g4_config_default(g4_config *cfg);
 
 /*
@@ -237,6 +240,17 @@ int g4_last_launches(const g4_ctx *ctx, int32_t *launches);
 int g4_op_qgemv(const void *wq, const void *scales, const float *x, float in_scale,
                 float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
                 int32_t *acc_out, void *stream);
+
+/*
+ * The prefill / batched form (qgemm-4bit, src/kernels/qgemm.ts:76-110, 490-552, 565-636: every
+ * column is exactly the qgemv of that column) on the tensor cores: the columns are snapped to
+ * int8 codes once, then a tcgen05 int8 GEMM accumulates exact int32 in tensor memory. Same
+ * arguments and results as g4_op_qgemv on a calibrated site (in_scale != 0); K a multiple of
+ * 128 (and of 256 for 4-bit). Allocates its code scratch stream-ordered (cudaMallocAsync).
+ */
+int g4_op_qgemm(const void *wq, const void *scales, const float *x, float in_scale,
+                float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
+                void *stream);
 
 /* The fused gelu prologue build (qgemv-Nbit-gelu, src/kernels/qgemv.ts:371-400): the GEMV over
  * gelu_tanh(gate) * up[up_offset..], snapped by in_scale. gate/up: f32 [cols, K]. */

@@ -119,6 +119,45 @@ def test_batch_matches_single(pkg, O, tiny):
     ctx.close()
 
 
+def test_batched_decode_tensor_core_path(pkg, O, tiny):
+    """B = 20 reaches gemm_min_columns: every calibrated linear of the step runs as the column
+    quantize + tcgen05 int8 GEMM, and the lm_head GEMM reduces argmax partials per 128-row tile.
+    Tokens equal the oracle's, sequence by sequence, with ragged contexts."""
+    a, om = tiny
+    ctx = make_ctx(pkg, a, max_seqs=20, max_step_columns=32)
+    B = 20
+    prompts = [O.synth_prompt(SEED + 40 + b, 3 + (b % 7), a.vocab_size) for b in range(B)]
+    toks = [ctx.prefill(b, prompts[b], 0, True) for b in range(B)]
+    pos = [len(p) for p in prompts]
+    for step in range(3):
+        out = ctx.decode_batch(np.arange(B), toks, pos)
+        for b in range(B):
+            ref, _ = om.generate(prompts[b], step + 2, 128)
+            assert out[b] == ref[step + 1], (step, b)
+        toks = list(out)
+        pos = [p + 1 for p in pos]
+    ctx.close()
+
+
+def test_prefill_tensor_core_chunks(pkg, O, tiny):
+    """A 100-token prompt in 64-column chunks (64 + 35 producer-only columns on the tensor-core
+    path, then the last position on the GEMV path) generates the oracle's tokens; the same
+    prompt with the tensor-core path switched off gives the same logits bit for bit."""
+    a, om = tiny
+    prompt = O.synth_prompt(SEED + 7, 100, a.vocab_size)
+    want, _ = om.generate(prompt, 4, 128)
+    logits = []
+    for gmin in (16, 1 << 20):
+        ctx = make_ctx(pkg, a, max_step_columns=64, gemm_min_columns=gmin)
+        got = [ctx.prefill(0, prompt, 0, True)]
+        logits.append(ctx.logits(0).copy())
+        for i in range(1, 4):
+            got.append(ctx.decode_ahead(0, len(prompt) + i - 1))
+        assert got == list(want), gmin
+        ctx.close()
+    np.testing.assert_array_equal(logits[0].view(np.uint32), logits[1].view(np.uint32))
+
+
 def test_prefill_chunking_and_sliced_table(pkg, O, tiny):
     a, om = tiny
     prompt = O.synth_prompt(SEED + 3, 40, a.vocab_size)

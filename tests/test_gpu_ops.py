@@ -78,6 +78,26 @@ def test_qgemv_exact(cuda, lib, O, bits, N, K, cols):
     np.testing.assert_array_equal(host(dy).view(np.uint32), y_ref.view(np.uint32))
 
 
+@pytest.mark.parametrize("bits,N,K,cols,out_s", [
+    (4, 6144, 1536, 64, 0.0625), (4, 1000, 1536, 100, 0.0), (4, 1536, 6144, 300, 0.0625),
+    (4, 262, 2048, 17, 0.0), (4, 2048, 1536, 129, 0.0625), (8, 256, 1536, 20, 0.0625),
+    (8, 1536, 256, 200, 0.0), (8, 300, 1536, 64, 0.0625),
+])
+def test_qgemm_tensor_core_matches_qgemv(cuda, lib, O, bits, N, K, cols, out_s):
+    """The tcgen05 int8 GEMM (prefill / batched decode) is column-for-column the qgemv of the
+    oracle (src/kernels/qgemm.ts:532-552 contract): y bit-identical, including ragged N (a partial
+    128-row tile), ragged columns (partial token tiles) and K 6144 (48 pipeline stages)."""
+    wq = RNG.integers(0, 256, N * K * bits // 8, dtype=np.uint8)
+    sc = f16_scales(N)
+    x = x_on_grid(cols, K, 0.02)
+    in_s, out_s = np.float32(0.02), np.float32(out_s)
+    y_ref, _ = O.qgemv(wq, sc, x, in_s, out_s, bits, N, K, cols)
+    dy = cuda.full((cols, N), np.nan, dtype=cuda.float32, device="cuda")
+    call(lib, "g4_op_qgemm", p(dev(cuda, wq)), p(dev(cuda, sc)), p(dev(cuda, x)), in_s, out_s, bits,
+         N, K, cols, p(dy), None)
+    np.testing.assert_array_equal(host(dy).view(np.uint32), y_ref.view(np.uint32))
+
+
 def test_qgemv_baseline_config1_fp16(cuda, lib, O):
     """x int8 codes U[-127,127] at static scale 0.02, W int4 U[-8,7] packed 8
     per u32, f16 row scales U[1e-3,1e-2]; int32 accumulators exact, fp16 output within 1e-2."""
