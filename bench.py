@@ -6,9 +6,11 @@ the device-resident decode chain (each step's token stays on the device and feed
 step); `e2e` is the same through the public C ABI (g4_decode: host token in, host token out,
 copies inside the timed region). `roofline` is the quantized GEMV (BASELINE config 1 shape,
 6144 x 1536 int4 x int8) timed live over weight copies larger than L2. `--batch 64` runs the
-batched-decode variant (config 4 shape at its contexts).
+batched-decode variant; with `--ctx-lo 128 --ctx-hi 4096` it is BASELINE config 4 (ragged
+contexts); `--workload prefill` is config 3 (2048-token prefill); `--only-gemv` is config 1.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+                  [--ctx-lo L --ctx-hi H] [--workload decode|prefill] [--only-gemv]
 
 Under torchrun each rank is an independent replica on its own GPU (weak scaling, no
 collectives on the data path); rank 0 prints one JSON line.
@@ -275,6 +277,82 @@ def run_gemv_only(pkg, torch, args, world, rank) -> None:
         "gpu_launches": 64 * max(args.steps, 10), "clocks": clocks.summary()}), flush=True)
 
 
+def run_prefill(pkg, torch, args, world, rank, dev) -> None:
+    """prefill of `--tokens` random ids with the KV-sharing exit (positions
+    0..n-2 run the producer layers only, the last position all layers and the head). One chunk:
+    the projections run as tcgen05 int8 GEMMs over all n-1 columns. Each step rewinds the KV
+    (src/kv.ts:247-254) and prefills again; the ids go host->device and the token comes back
+    inside the timed region."""
+    n = args.tokens
+    ctx = pkg.engine.Context(device=dev, max_seqs=1, max_context=n + 8, max_step_columns=n)
+    ctx.init_random(SEED)
+    prompt = np.array(pkg.plan.synth_prompt(SEED + 7919 * rank, n), np.int32)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    for _ in range(args.warmup):
+        ctx.kv_truncate(0, 0)
+        ctx.prefill(0, prompt, 0, True)
+    torch.cuda.synchronize()
+    launches = ctx.launches()
+    steps = max(1, args.steps // 20)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.perf_counter()
+    with ClockSampler(dev) as clocks:
+        torch.cuda.nvtx.range_push("timed")
+        e0.record(stream)
+        for _ in range(steps):
+            ctx.kv_truncate(0, 0)
+            ctx.prefill(0, prompt, 0, True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+    wall = time.perf_counter() - h0
+    dev_s = max(e0.elapsed_time(e1) / 1e3, 1e-9)
+    if world > 1:
+        t = torch.tensor([dev_s, wall], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dev_s, wall = float(t[0]), float(t[1])
+    # Algorithmic int8 ops: 2 x producer-layer linear parameters x (n - 1) columns plus the
+    # last position through all layers and the lm_head.
+    H, PD, V = 1536, 256, 262144
+    prod_params = mlp = 0
+    for L in range(35):
+        hd = 512 if L in {4, 9, 14, 19, 24, 29, 34} else 256
+        p = 8 * hd * H + H * 8 * hd + 3 * 6144 * H + 2 * PD * H + (2 * hd * H if L < 15 else 0)
+        mlp += p
+        if L < 15:
+            prod_params += p
+    ops = 2 * prod_params * (n - 1) + 2 * (mlp + V * H)
+    peaks = load_peaks()
+    int8_peak = 2 * peaks.get("bf16_tflops", 1590.0)
+    achieved = ops * steps / dev_s / 1e12
+    ctx.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": "prefill tokens/s (config 3, 2048-token prompt, KV-sharing exit)",
+        "value": world * n * steps / dev_s, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * dev_s / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8 (int32 acc) / f32",
+        "data": "synthetic (seeded random-init Gemma-4-E2B shape)",
+        "config": {"workload": f"config 3: prefill of {n} random ids, producer layers for 0..{n - 2}, "
+                               "all layers + head for the last", "global_batch": world,
+                   "seq_len": n, "parallelism": f"replicas x{world}", "l2": "weights exceed L2"},
+        "e2e": {"value": world * n * steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 4 * n,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": launches * steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
+                     "frac": achieved / int8_peak, "traffic": None,
+                     "peak_source": "2 x measured dense bf16 (int8 tensor rate)",
+                     "ops_per_step": ops, "kernel": "whole prefill (int8 GEMMs + attention + rest)"},
+        "clocks": clocks.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -286,6 +364,11 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=24)
     ap.add_argument("--only-gemv", action="store_true",
                     help="BASELINE config 1 alone: the int4 x int8 GEMV [6144 x 1536] line")
+    ap.add_argument("--ctx-lo", type=int, default=PROMPT,
+                    help="prompt lengths uniform in [ctx-lo, ctx-hi] per sequence (seeded)")
+    ap.add_argument("--ctx-hi", type=int, default=PROMPT)
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--tokens", type=int, default=2048, help="prefill workload: prompt length")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
@@ -308,18 +391,28 @@ def main():
     if args.only_gemv:
         run_gemv_only(pkg, torch, args, world, rank)
         return
+    if args.workload == "prefill":
+        run_prefill(pkg, torch, args, world, rank, dev)
+        return
     engine = pkg.engine
     B = args.batch
     total_steps = args.warmup + args.steps
-    max_ctx = PROMPT + total_steps + 8
-    ctx = engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=max(B, 64))
+    rng = np.random.default_rng(SEED + 1000 * rank)
+    lens = ([args.ctx_lo] * B if args.ctx_lo == args.ctx_hi
+            else [int(v) for v in rng.integers(args.ctx_lo, args.ctx_hi + 1, B)])
+    max_ctx = max(lens) + total_steps + 8
+    chunk = max(B, 512 if max(lens) > 256 else 64)
+    ctx = engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=chunk)
     ctx.init_random(SEED)
-    prompts = [np.array(pkg.plan.synth_prompt(SEED + b, PROMPT), np.int32) for b in range(B)]
+    prompts = [np.array(pkg.plan.synth_prompt(SEED + b + 7919 * rank, lens[b]), np.int32) for b in range(B)]
+    torch.cuda.synchronize()
+    p0 = time.perf_counter()
     first = [ctx.prefill(b, prompts[b], 0, True) for b in range(B)]
     torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - p0
 
     # ---- device-resident decode chain (value)
-    ctx.step_stage(np.arange(B), first, [PROMPT] * B)
+    ctx.step_stage(np.arange(B), first, lens)
     stream = torch.cuda.ExternalStream(ctx.stream())
     for _ in range(args.warmup):
         ctx.step_run_device(B)
@@ -330,11 +423,13 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
+        torch.cuda.nvtx.range_push("timed")   # profilers can keep to the timed steps
         e0.record(stream)
         for _ in range(args.steps):
             ctx.step_run_device(B)
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     dev_s = e0.elapsed_time(e1) / 1e3
     if world > 1:
         t = torch.tensor([dev_s], device="cuda")
@@ -345,8 +440,7 @@ def main():
     # ---- end to end through the C ABI: host token in, host token out, every step, over the
     # same positions (the KV rows past the prompt are rewound, src/kv.ts:247-254)
     for b in range(B):
-        ctx.kv_truncate(b, PROMPT)
-    pos_now = PROMPT
+        ctx.kv_truncate(b, lens[b])
     prev = [int(t) for t in first]
     if world > 1:
         torch.distributed.barrier()
@@ -357,9 +451,9 @@ def main():
     e2.record(stream)
     for i in range(args.steps):
         if B == 1:
-            prev = [ctx.decode(0, prev[0], pos_now + i)]
+            prev = [ctx.decode(0, prev[0], lens[0] + i)]
         else:
-            prev = list(ctx.decode_batch(np.arange(B), prev, [pos_now + i] * B))
+            prev = list(ctx.decode_batch(np.arange(B), prev, [lens[b] + i for b in range(B)]))
     e3.record(stream)
     torch.cuda.synchronize()
     e2e_s = max(e2.elapsed_time(e3) / 1e3, time.perf_counter() - h0)
@@ -371,23 +465,31 @@ def main():
     # ---- roofline of the dominant kernel (quant GEMV, config 1 shape)
     gemv = measure_gemv(pkg, torch, copies=64, iters=640)
     peaks = load_peaks()
-    ctx_mid = PROMPT + args.warmup + args.steps // 2
-    tb = token_bytes(ctx_mid)
+    mids = [lens[b] + args.warmup + args.steps // 2 for b in range(B)]
+    tb = token_bytes(mids[0])
+    step_bytes = tb["weights"] + tb["scales"] + sum(token_bytes(m)["kv"] for m in mids)
     value = world * B * args.steps / dev_s
+    if B == 1 and args.ctx_lo == args.ctx_hi == PROMPT:
+        workload = (f"config 2: B=1 greedy decode after a {PROMPT}-token prompt, contexts "
+                    f"{PROMPT}..{PROMPT + total_steps}")
+    else:
+        workload = (f"B={B} greedy decode per replica, prompt lengths "
+                    f"{'U[%d,%d]' % (args.ctx_lo, args.ctx_hi) if args.ctx_lo != args.ctx_hi else args.ctx_lo}"
+                    f" (seeded), {total_steps} steps")
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dev_s / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int4xint8 (int32 acc) / f32", "data": "synthetic (seeded random-init Gemma-4-E2B shape)",
-        "config": {"workload": f"config {'2' if B == 1 else '4-shape'}: B={B} greedy decode after a "
-                               f"{PROMPT}-token prompt, contexts {PROMPT}..{PROMPT + total_steps}",
-                   "global_batch": world * B, "seq_len": PROMPT, "parallelism": f"replicas x{world}",
-                   "l2": "weights (0.93 GB per token) exceed L2 every step"},
+        "config": {"workload": workload,
+                   "global_batch": world * B, "seq_len": max(lens), "parallelism": f"replicas x{world}",
+                   "l2": "weights (0.93 GB per step) exceed L2 every step"},
         "e2e": {"value": world * B * args.steps / e2e_s, "unit": "tokens/s",
                 "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B},
         "gpu_launches": launches_per_step * args.steps,
-        "token_bytes": tb["total"],
-        "token_hbm_gbs": tb["total"] * B * args.steps / dev_s / 1e9 if B == 1 else None,
+        "step_bytes": step_bytes,
+        "step_hbm_gbs": step_bytes * args.steps / dev_s / 1e9,
+        "prefill_tokens_per_s": sum(lens) / prefill_s,
         "roofline": {"bound": "hbm", "kernel": "qgemv-4bit 6144x1536 (config 1)",
                      "achieved": gemv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": gemv["gbs"] / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC,

@@ -1023,6 +1023,7 @@ __global__ void __launch_bounds__(256) k_attn_blocks(const AttnArgs a) {
   float *ss = qs + NH * HD;           // [NH][64]
   float *ps = ss + NH * ATT_BLK;      // [NH][64]
   float *ms = ps + NH * ATT_BLK;      // [NH]
+  float *vs = ms + 4 * NH;            // [64][HD]: the block's V rows (16-byte aligned)
   grid_launch_dependents();
   grid_wait();
   const int c = blockIdx.x, bi = blockIdx.y, t = threadIdx.x;
@@ -1037,6 +1038,13 @@ __global__ void __launch_bounds__(256) k_attn_blocks(const AttnArgs a) {
 
   const float4 *qsrc = reinterpret_cast<const float4 *>(a.qr + (size_t)c * NH * HD);
   for (int i = t; i < NH * NC; i += 256) reinterpret_cast<float4 *>(qs)[i] = qsrc[i];
+  // V rows j0..j1 into shared memory: independent loads, consumed after the scores.
+  {
+    const int nrow = j1 - j0 + 1;
+    const float4 *vsrc = reinterpret_cast<const float4 *>(V + (size_t)j0 * HD);
+    float4 *vdst = reinterpret_cast<float4 *>(vs + (size_t)(j0 - b * ATT_BLK) * HD);
+    for (int i = t; i < nrow * NC; i += 256) vdst[i] = vsrc[i];
+  }
   __syncthreads();
 
   // Scores: thread (jl, m) with m = t & 3 computes accumulator m of position jl for all heads.
@@ -1095,9 +1103,10 @@ __global__ void __launch_bounds__(256) k_attn_blocks(const AttnArgs a) {
       o[hh] = make_float4(0.f, 0.f, 0.f, 0.f);
       l[hh] = 0.0f;
     }
+#pragma unroll 4
     for (int j = j0; j <= j1; j++) {
-      const float4 v4 = reinterpret_cast<const float4 *>(V + (size_t)j * HD)[dc];
       const int jl = j - b * ATT_BLK;
+      const float4 v4 = reinterpret_cast<const float4 *>(vs + (size_t)jl * HD)[dc];
 #pragma unroll
       for (int hh = 0; hh < HPG; hh++) {
         const float pj = ps[(hg * HPG + hh) * ATT_BLK + jl];
@@ -1154,7 +1163,13 @@ __global__ void __launch_bounds__(256) k_attn_merge(const AttnArgs a) {
 
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl) {
   if (a.heads != 8) return cudaErrorInvalidValue;
-  size_t smem = ((size_t)8 * a.hd + 8 * ATT_BLK * 2 + 8) * 4;
+  size_t smem = ((size_t)8 * a.hd + 8 * ATT_BLK * 2 + 32 + (size_t)ATT_BLK * a.hd) * 4;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_attn_blocks<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_attn_blocks<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
   dim3 g1(a.cols, a.max_blocks), g2(a.cols, 8);
   cudaError_t e;
   if (a.hd == 256) {

@@ -131,6 +131,7 @@ struct g4_ctx {
   int32_t *h_tok = nullptr;    // pinned token outputs
   uint64_t other_bytes = 0;
   std::map<GraphKey, cudaGraphExec_t> graphs;
+  std::map<GraphKey, int> graph_launches;   // kernels in each graph
   int sms = 148;
   int launches = 0;
   int last_cols = 0;
@@ -1236,11 +1237,13 @@ static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance
     CK(cudaGraphInstantiate(&ex, g, 0));
     cudaGraphDestroy(g);
     ctx->graphs[key] = ex;
+    ctx->graph_launches[key] = launches;
     ctx->launches = launches;
     // The eager run already advanced the step; the graph serves the next calls.
     return G4_OK;
   }
   CK(cudaGraphLaunch(it->second, ctx->st));
+  ctx->launches = ctx->graph_launches[key];
   return G4_OK;
 }
 
@@ -1300,16 +1303,20 @@ extern "C" int g4_prefill(g4_ctx *ctx, int32_t seq, const int32_t *ids, int32_t 
   // need all layers only for their KV (which only producers write), so they run as the
   // producer-only chunk (src/plan.ts:160-192, 812-824).
   int body = is_last ? n - 1 : n;
+  int launches = 0;
   for (int c0 = 0; c0 < body; c0 += ctx->maxc) {
     int cols = std::min(ctx->maxc, body - c0);
     for (int i = 0; i < cols; i++) ps[i] = start_pos + c0 + i;
     if ((rc = stage(ctx, cols, sq.data(), ps.data(), ids + c0, true))) return rc;
     if ((rc = record_step(ctx, cols, nl_prod, false))) return rc;
+    launches += ctx->launches;
   }
+  ctx->launches = launches;
   if (is_last) {
     ps[0] = start_pos + n - 1;
     if ((rc = stage(ctx, 1, sq.data(), ps.data(), ids + n - 1, true))) return rc;
     if ((rc = run_step(ctx, 1, nl_all, true))) return rc;
+    ctx->launches += launches;
     int32_t tok;
     if ((rc = fetch_tokens(ctx, 1, &tok))) return rc;
     if (out_token) *out_token = tok;
