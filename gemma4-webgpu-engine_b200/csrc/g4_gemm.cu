@@ -171,7 +171,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int n0 = blockIdx.x * GM_BM, m0 = blockIdx.y * BN;
-  const int KT = a.K / GM_BK;
+  // This CTA's K tiles: split blockIdx.z of a.splits (an even share, at least one tile).
+  const int KTALL = a.K / GM_BK;
+  const int kt_begin = (int)(((long long)KTALL * blockIdx.z) / gridDim.z);
+  const int KT = (int)(((long long)KTALL * (blockIdx.z + 1)) / gridDim.z) - kt_begin;
 
   if (t == 0) {
     for (int s = 0; s < NS; s++) {
@@ -209,11 +212,12 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         mbar_expect_tx(&full[s], wbytes + S::B_BYTES);
+        const int kg = kt_begin + kt;
         if (BITS == 4)
-          tma_load_2d(P(s), &tmW, kt * (GM_BK / 2), n0, &full[s]);
+          tma_load_2d(P(s), &tmW, kg * (GM_BK / 2), n0, &full[s]);
         else
-          tma_load_2d(A(s), &tmW, kt * GM_BK, n0, &full[s]);
-        tma_load_2d(B(s), &tmX, kt * GM_BK, m0, &full[s]);
+          tma_load_2d(A(s), &tmW, kg * GM_BK, n0, &full[s]);
+        tma_load_2d(B(s), &tmX, kg * GM_BK, m0, &full[s]);
         issued = kt + 1;
       }
       // Every copy issued lands before the CTA can leave (the last NS are the ones not yet
@@ -280,10 +284,48 @@ __global__ void __launch_bounds__(192, 1)
     const float wscale = row_ok ? f16_bits_to_f32(a.s[row]) : 0.0f;
     const float sc = __fmul_rn(a.in_scale, wscale);
     const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
+    bool last = true;
+    if (gridDim.z > 1) {
+      // Split K: add this CTA's partial into the workspace; the tile's last split finishes.
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
+        if (ok && !flags[0] && row_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            const int tok = m0 + c0 + j;
+            if (tok < a.M) atomicAdd(a.acc_ws + (size_t)tok * a.ld_ws + row, (int)acc[j]);
+          }
+        }
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      int *cnt = a.tile_cnt + blockIdx.y * gridDim.x + blockIdx.x;
+      if (t == 64) flags[1] = atomicAdd(cnt, 1) == (int)gridDim.z - 1;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      last = flags[1] != 0;
+      if (last) {
+        __threadfence();
+        if (t == 64) *cnt = 0;
+      }
+    }
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN && last; c0 += 32) {
       uint32_t acc[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
+      if (gridDim.z > 1) {
+        // The tile's full sums, read back (all 32 loads in flight together), then the workspace
+        // is cleared for the next launch.
+        int32_t *wp = a.acc_ws + (size_t)(m0 + c0) * a.ld_ws + row;
+        const int nt = min(32, a.M - (m0 + c0));
+#pragma unroll
+        for (int j = 0; j < 32; j++) acc[j] = (row_ok && j < nt) ? (uint32_t)__ldcg(wp + (size_t)j * a.ld_ws) : 0u;
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (row_ok && j < nt) wp[(size_t)j * a.ld_ws] = 0;
+      } else {
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
+      }
       // After a failed wait nothing is stored; the named barriers below still run in step.
       const bool store = ok && !flags[0];
 #pragma unroll
@@ -358,7 +400,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX,
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + BN - 1) / BN);
+  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + BN - 1) / BN, a.splits > 1 ? a.splits : 1);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -382,6 +424,8 @@ static cudaError_t launch_gemm_b(const CUtensorMap &tmW, const CUtensorMap &tmX,
 cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a, int bits,
                          int bn, cudaStream_t st, bool pdl) {
   if (a.K % GM_BK != 0 || a.K < GM_BK || a.N < 1 || a.M < 1) return cudaErrorInvalidValue;
+  if (a.splits > 1 && (a.head || !a.acc_ws || !a.tile_cnt || a.splits > a.K / GM_BK || a.ld_ws < a.N))
+    return cudaErrorInvalidValue;
   if (bits == 4) {
     if (a.head) return launch_gemm_b<4, EPI_HEAD>(tmW, tmX, a, bn, st, pdl);
     return launch_gemm_b<4, EPI_Y>(tmW, tmX, a, bn, st, pdl);

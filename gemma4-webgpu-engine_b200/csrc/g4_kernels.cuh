@@ -152,6 +152,9 @@ struct GemmArgs {
   int head; float softcap;
   float *logits; int ld_logits;
   float *part_val; int32_t *part_idx; int n_parts;
+  // Split K (splits > 1): each CTA adds its exact int32 partial into acc_ws[token][ld_ws] (zero on
+  // entry, left zero), and the last of a tile's splits to finish (tile_cnt) runs the epilogue.
+  int splits; int32_t *acc_ws; int ld_ws; int32_t *tile_cnt;
 };
 int make_tmap_u8(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
                  uint64_t row_stride, uint32_t box_inner, uint32_t box_outer, bool swizzle128);

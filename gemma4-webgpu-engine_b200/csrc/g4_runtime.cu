@@ -108,6 +108,9 @@ struct g4_ctx {
   std::map<std::tuple<int, int, int>, CUtensorMap> tmx;
   float *gpv = nullptr;
   int32_t *gpi = nullptr;
+  int32_t *gacc = nullptr, *gcnt = nullptr;   // split-K workspace [maxc][gacc_ld] and tile counts
+  int gacc_ld = 0;
+  bool gemm_split = false;
   int gparts = 0, gemm_min_cols = 16;
   // The argmax partials the head of the step being recorded wrote.
   float *cur_pv = nullptr;
@@ -461,6 +464,11 @@ static int alloc_runtime(g4_ctx *ctx) {
     CK(cudaMalloc(&ctx->gq[i], (size_t)ctx->gq_rows * ctx->gq_ld));
     CK(cudaMemset(ctx->gq[i], 0, (size_t)ctx->gq_rows * ctx->gq_ld));
   }
+  ctx->gacc_ld = ctx->gq_ld;
+  CK(cudaMalloc(&ctx->gacc, (size_t)maxc * ctx->gacc_ld * 4));
+  CK(cudaMemset(ctx->gacc, 0, (size_t)maxc * ctx->gacc_ld * 4));
+  CK(cudaMalloc(&ctx->gcnt, 8192 * 4));
+  CK(cudaMemset(ctx->gcnt, 0, 8192 * 4));
   ctx->gparts = (int)((a.vocab_size + 127) / 128);
   CK(cudaMalloc(&ctx->gpv, (size_t)maxc * ctx->gparts * 4));
   CK(cudaMalloc(&ctx->gpi, (size_t)maxc * ctx->gparts * 4));
@@ -555,6 +563,8 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   for (int i = 0; i < 3; i++) cudaFree(ctx->gq[i]);
   cudaFree(ctx->gpv);
   cudaFree(ctx->gpi);
+  cudaFree(ctx->gacc);
+  cudaFree(ctx->gcnt);
   cudaFree(ctx->codes_ple);
   cudaFree(ctx->d_step);
   cudaFree(ctx->d_tok_out);
@@ -873,6 +883,19 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     g.out_scale = l.out_scale;
     g.y = sg.y;
     g.ld_y = l.N;
+    // Split K is available (exact int32 partials through a workspace) but off in the executor:
+    // measured on a B=64 step it cost more in atomics and the extra round trips than the added
+    // CTAs gained.
+    const int tiles = ((l.N + 127) / 128) * ((cols + bn - 1) / bn);
+    const int kts = K / 128;
+    if (ctx->gemm_split && !head && tiles < ctx->sms && l.N <= ctx->gacc_ld && tiles <= 8192) {
+      g.splits = std::min(kts, (ctx->sms + tiles - 1) / tiles);
+      if (g.splits > 1) {
+        g.acc_ws = ctx->gacc;
+        g.ld_ws = ctx->gacc_ld;
+        g.tile_cnt = ctx->gcnt;
+      }
+    }
     if (head) {
       g.head = 1;
       g.softcap = q.softcap;
@@ -1536,7 +1559,22 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
       g.out_scale = out_scale;
       g.y = y;
       g.ld_y = N;
-      e = launch_qgemm(tw, tx, g, bits, bn, st, false);
+      // The executor's rule: few tiles split K (exact int32 partials through a workspace).
+      const int tiles = ((N + 127) / 128) * ((cols + bn - 1) / bn);
+      const int sms = device_sms();
+      int32_t *ws = nullptr;
+      if (tiles < sms && tiles <= 8192) {
+        g.splits = std::min(K / 128, (sms + tiles - 1) / tiles);
+        if (g.splits > 1) {
+          e = cudaMallocAsync(&ws, ((size_t)cols * N + 8192) * 4, st);
+          if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, ((size_t)cols * N + 8192) * 4, st);
+          g.acc_ws = ws;
+          g.ld_ws = N;
+          g.tile_cnt = ws + (size_t)cols * N;
+        }
+      }
+      if (e == cudaSuccess) e = launch_qgemm(tw, tx, g, bits, bn, st, false);
+      if (ws) cudaFreeAsync(ws, st);
     }
   }
   cudaFreeAsync(codes, st);
