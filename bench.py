@@ -368,6 +368,9 @@ def main():
                     help="prompt lengths uniform in [ctx-lo, ctx-hi] per sequence (seeded)")
     ap.add_argument("--ctx-hi", type=int, default=PROMPT)
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--box", action="store_true",
+                    help="config 5: 512 sequences split over the replicas, 512-token prompts, "
+                         "the per-layer-embedding table in 128 MiB vocab-row slices")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill workload: prompt length")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -380,10 +383,8 @@ def main():
     import __graft_entry__ as entry
     world, rank, local = dist_env()
     if world > 1:
-        import datetime
         torch.cuda.set_device(local)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=torch.device("cuda", local))
+        entry.load_package().replicas.init_group(torch, "nccl", 300.0, torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
@@ -396,13 +397,20 @@ def main():
         return
     engine = pkg.engine
     B = args.batch
+    slice_bytes = 0
+    if args.box:
+        lo, hi = pkg.replicas.replica_slice(512, world, rank)
+        B = hi - lo
+        args.ctx_lo = args.ctx_hi = 512
+        slice_bytes = 128 << 20
     total_steps = args.warmup + args.steps
     rng = np.random.default_rng(SEED + 1000 * rank)
     lens = ([args.ctx_lo] * B if args.ctx_lo == args.ctx_hi
             else [int(v) for v in rng.integers(args.ctx_lo, args.ctx_hi + 1, B)])
     max_ctx = max(lens) + total_steps + 8
     chunk = max(B, 512 if max(lens) > 256 else 64)
-    ctx = engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=chunk)
+    ctx = engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=chunk,
+                         ple_slice_bytes=slice_bytes)
     ctx.init_random(SEED)
     prompts = [np.array(pkg.plan.synth_prompt(SEED + b + 7919 * rank, lens[b]), np.int32) for b in range(B)]
     torch.cuda.synchronize()
@@ -469,7 +477,10 @@ def main():
     tb = token_bytes(mids[0])
     step_bytes = tb["weights"] + tb["scales"] + sum(token_bytes(m)["kv"] for m in mids)
     value = world * B * args.steps / dev_s
-    if B == 1 and args.ctx_lo == args.ctx_hi == PROMPT:
+    if args.box:
+        workload = (f"config 5: 512 sequences over {world} replica(s) ({B} here), 512-token prompts, "
+                    f"{total_steps} greedy steps, PLE table in 128 MiB slices")
+    elif B == 1 and args.ctx_lo == args.ctx_hi == PROMPT:
         workload = (f"config 2: B=1 greedy decode after a {PROMPT}-token prompt, contexts "
                     f"{PROMPT}..{PROMPT + total_steps}")
     else:
