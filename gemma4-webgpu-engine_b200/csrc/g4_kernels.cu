@@ -888,9 +888,97 @@ k_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K
   }
 }
 
+// Many columns (prefill): warp w of a CTA keeps rows R (8 b + w) .. + R - 1 in registers (read once,
+// before the dependency wait) and walks the columns in tiles of 8 staged in shared memory. Each
+// (row, column) sum is the same per-lane chunk order and butterfly as k_dense_bf16.
+template <int MAXCH>
+__global__ void __launch_bounds__(256)
+k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K, int cols,
+                  float alpha) {
+  constexpr int R = MAXCH <= 6 ? 4 : 2, T = 8;
+  extern __shared__ __align__(16) float xs[];  // [T][K]
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int row0 = (blockIdx.x * 8 + warp) * R;
+  const int nch = K / 8;
+  uint4 wv[R][MAXCH];
+#pragma unroll
+  for (int r = 0; r < R; r++)
+#pragma unroll
+    for (int i = 0; i < MAXCH; i++) {
+      const int ch = lane + 32 * i;
+      wv[r][i] = (row0 + r < N && ch < nch) ? ldg_stream(w + (size_t)(row0 + r) * K + 8 * ch)
+                                            : make_uint4(0, 0, 0, 0);
+    }
+  grid_launch_dependents();
+  grid_wait();
+  for (int c0 = 0; c0 < cols; c0 += T) {
+    const int nc = min(T, cols - c0);
+    __syncthreads();
+    for (int i = t; i < nc * (K / 4); i += 256) {
+      const int c = i / (K / 4), k4 = i - c * (K / 4);
+      reinterpret_cast<float4 *>(xs + c * K)[k4] =
+          reinterpret_cast<const float4 *>(x + (size_t)(c0 + c) * ld_x)[k4];
+    }
+    __syncthreads();
+    float acc[R][T];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int c = 0; c < T; c++) acc[r][c] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXCH; i++) {
+      const int ch = lane + 32 * i;
+      if (ch < nch) {
+#pragma unroll
+        for (int c = 0; c < T; c++) {
+          if (c < nc) {
+            const float4 xa = reinterpret_cast<const float4 *>(xs + c * K + 8 * ch)[0];
+            const float4 xb = reinterpret_cast<const float4 *>(xs + c * K + 8 * ch)[1];
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+              const uint32_t ww[4] = {wv[r][i].x, wv[r][i].y, wv[r][i].z, wv[r][i].w};
+              float v = acc[r][c];
+#pragma unroll
+              for (int j = 0; j < 8; j++) {
+                const float wf = (j & 1) ? __uint_as_float(ww[j >> 1] & 0xffff0000u)
+                                         : __uint_as_float(ww[j >> 1] << 16);
+                v = fmaf(wf, xv[j], v);
+              }
+              acc[r][c] = v;
+            }
+          }
+        }
+      }
+    }
+    // Close the 32 sums; lane 8 r + c stores (row0 + r, column c0 + c).
+    float mine = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+      for (int c = 0; c < T; c++) {
+        const float sum = warp_sum_bfly(acc[r][c]);
+        if (lane == r * T + c) mine = sum;
+      }
+    const int r = lane / T, c = lane % T;
+    if (r < R && row0 + r < N && c < nc) y[(size_t)(c0 + c) * N + row0 + r] = __fmul_rn(alpha, mine);
+  }
+}
+
 cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K,
                               int cols, float alpha, cudaStream_t st, bool pdl) {
   if (K % 8 != 0 || K > 2048) return cudaErrorInvalidValue;
+  if (cols > 8) {
+    const size_t smem = (size_t)8 * K * 4;
+    if (K <= 1536) {
+      const dim3 grid((N + 31) / 32);
+      cudaFuncSetAttribute(k_dense_bf16_wide<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      return launch_k(k_dense_bf16_wide<6>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, N, K, cols, alpha);
+    }
+    const dim3 grid((N + 15) / 16);
+    cudaFuncSetAttribute(k_dense_bf16_wide<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    return launch_k(k_dense_bf16_wide<8>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, N, K, cols, alpha);
+  }
   cudaError_t e = cudaSuccess;
   for (int c0 = 0; c0 < cols && e == cudaSuccess; c0 += 8) {
     int nc = cols - c0 < 8 ? cols - c0 : 8;

@@ -989,7 +989,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
   ctx->launches++;
   CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, H, cols,
                        (float)std::pow((double)H, -0.5), ctx->st, true));
-  ctx->launches += (cols + 7) / 8;
+  ctx->launches += cols > 8 ? 1 : 1;
   CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, ctx->NL, PD,
                         eps, (float)0.7071067811865476, ctx->st, true));
   ctx->launches++;

@@ -294,8 +294,11 @@ def test_embed_gather_sliced(cuda, lib, O):
                                   O.embed_gather(codes_e, sc_e, ids, 1536, 1536, es).view(np.uint32))
 
 
-@pytest.mark.parametrize("N,K,cols", [(8960, 1536, 1), (1000, 1536, 3), (333, 256, 9)])
+@pytest.mark.parametrize("N,K,cols", [(8960, 1536, 1), (1000, 1536, 3), (333, 256, 9),
+                                      (8960, 1536, 70), (1000, 2048, 40), (130, 1536, 17)])
 def test_dense_bf16(cuda, lib, O, N, K, cols):
+    """One to eight columns: the per-launch kernel; more (prefill): the column-tiled kernel that
+    reads the weights once. Both keep the per-lane chunk order, so both are bit-exact."""
     w32 = RNG.uniform(-0.0442, 0.0442, N * K).astype(np.float32)
     w = (w32.view(np.uint32) >> 16).astype(np.uint16)
     x = RNG.normal(0, 1, cols * K).astype(np.float32)
