@@ -88,6 +88,7 @@ SIGNATURES = {
     "g4_op_kv_norm_rope_store": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32,
                                            _f, _vp]),
     "g4_op_attention": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "g4_op_attention_prefill": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
     "g4_op_attention_noalloc": (C.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                           _vp]),
     "g4_op_embed_gather": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _f, _i32, _i32, _vp]),

@@ -1249,6 +1249,217 @@ __global__ void __launch_bounds__(256) k_attn_merge(const AttnArgs a) {
   for (int d = 0; d < DPT; d++) out[t + 256 * d] = __fdiv_rn(O[d], L);
 }
 
+// Prefill attention (a chunk of consecutive positions of one sequence): CTA = QT consecutive
+// queries x 8 heads. It walks the 64-position blocks in ascending order, reading each block's K
+// (scores) and V (staged in shared memory) once for all QT x 8 (query, head) pairs, and folds each
+// block into a running (M, L, O) right away. Per (query, block) the arithmetic is k_attn_blocks'
+// (four-accumulator scores, block max, exp, ascending l and o chains) and the fold is
+// k_attn_merge's in the same ascending block order, so the result is bit-identical.
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
+  constexpr int NH = 8, NC = HD / 4, QT = 2048 / HD, NP = QT * NH;   // pairs per CTA
+  constexpr int G = 256 / NC, PPT = NP / G;                         // PV: pairs per thread
+  extern __shared__ __align__(16) float sm[];
+  float *qs = sm;                              // [QT][NH][HD]
+  float *vs = qs + NP * HD;                    // [64][HD]
+  float *ss = vs + ATT_BLK * HD;               // [NP][64] scores, then probabilities
+  float *mb = ss + NP * ATT_BLK;               // [NP] block max
+  float *lb = mb + NP;                         // [NP] block sum
+  float *RM = lb + NP;                         // [NP] running max
+  float *RL = RM + NP;                         // [NP] running sum
+  float *ea = RL + NP;                         // [NP]
+  float *ec = ea + NP;                         // [NP]
+  int *mode = reinterpret_cast<int *>(ec + NP);  // [NP] 0 skip, 1 copy, 2 fold
+  int *qp = mode + NP;                         // [QT] positions
+  int *qlo = qp + QT;                          // [QT] window start
+  grid_launch_dependents();
+  grid_wait();
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int c0 = blockIdx.x * QT;
+  const int nq = min(QT, a.cols - c0);
+  const int seq = a.refs.seq ? a.refs.seq[c0] : 0;
+  const float *K = a.cache + (size_t)seq * a.seq_stride;
+  const float *V = K + (size_t)a.max_ctx * HD;
+  if (t < QT) {
+    int p = -1, lo = 0, hi = -1;
+    if (t < nq) attn_range(a, c0 + t, &p, &lo, &hi);
+    qp[t] = t < nq ? hi : -1;
+    qlo[t] = t < nq ? lo : 1 << 30;
+  }
+  for (int i = t; i < NP; i += 256) {
+    RM[i] = -FLT_MAX;
+    RL[i] = 0.0f;
+  }
+  for (int i = t; i < nq * NH * NC; i += 256)
+    reinterpret_cast<float4 *>(qs)[i] = reinterpret_cast<const float4 *>(a.qr + (size_t)c0 * NH * HD)[i];
+  for (int i = nq * NH * NC + t; i < NP * NC; i += 256)
+    reinterpret_cast<float4 *>(qs)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  int ulo = 1 << 30, uhi = -1;
+#pragma unroll
+  for (int q = 0; q < QT; q++) {
+    ulo = min(ulo, qlo[q]);
+    uhi = max(uhi, qp[q]);
+  }
+  // PV thread: float4 chunk dc of pairs g * PPT .. + PPT - 1.
+  const int dc = t % NC, g = t / NC;
+  float4 O[PPT];
+#pragma unroll
+  for (int i = 0; i < PPT; i++) O[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int b = ulo / ATT_BLK; b * ATT_BLK <= uhi; b++) {
+    const int jb = b * ATT_BLK;
+    const int jlo = max(jb, ulo), jhi = min(jb + ATT_BLK - 1, uhi);
+    // V rows of the union range; rows outside it are zero (their probabilities are zero too).
+    for (int i = t; i < ATT_BLK * NC; i += 256) {
+      const int jl = i / NC, k4 = i - jl * NC, j = jb + jl;
+      reinterpret_cast<float4 *>(vs)[i] = (j >= jlo && j <= jhi)
+          ? reinterpret_cast<const float4 *>(V + (size_t)j * HD)[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // Scores: thread (jl, m) runs accumulator m of position jl for every (query, head) pair.
+    {
+      const int jl = t >> 2, m = t & 3, j = jb + jl;
+      const bool inr = j >= jlo && j <= jhi;
+      float acc[NP];
+#pragma unroll
+      for (int i = 0; i < NP; i++) acc[i] = 0.0f;
+      if (inr) {
+        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)j * HD);
+#pragma unroll 2
+        for (int cc = m; cc < NC; cc += 4) {
+          const float4 k4 = kr[cc];
+#pragma unroll
+          for (int i = 0; i < NP; i++) {
+            const float4 q4 = reinterpret_cast<const float4 *>(qs + i * HD)[cc];
+            float v = acc[i];
+            v = fmaf(q4.x, k4.x, v);
+            v = fmaf(q4.y, k4.y, v);
+            v = fmaf(q4.z, k4.z, v);
+            v = fmaf(q4.w, k4.w, v);
+            acc[i] = v;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < NP; i++) {
+        const float v1 = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 1));
+        const float v2 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, 2));
+        const int q = i / NH;
+        if (m == 0) ss[i * ATT_BLK + jl] = (j >= qlo[q] && j <= qp[q]) ? v2 : -FLT_MAX;
+      }
+    }
+    __syncthreads();
+    // Block max and probabilities per pair (warp w: pairs w, w + 8, ...).
+    for (int i = warp; i < NP; i += 8) {
+      const int q = i / NH;
+      const float s0 = ss[i * ATT_BLK + lane], s1 = ss[i * ATT_BLK + lane + 32];
+      float mx = fmaxf(s0, s1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const int ja = jb + lane, jc = ja + 32;
+      ss[i * ATT_BLK + lane] = (ja >= qlo[q] && ja <= qp[q]) ? g4_exp(__fsub_rn(s0, mx)) : 0.0f;
+      ss[i * ATT_BLK + lane + 32] = (jc >= qlo[q] && jc <= qp[q]) ? g4_exp(__fsub_rn(s1, mx)) : 0.0f;
+      if (lane == 0) mb[i] = mx;
+    }
+    __syncthreads();
+    // Weighted V of the block and its probability sum, ascending j (zeros outside a query's range).
+    float4 o[PPT];
+    float l[PPT];
+#pragma unroll
+    for (int i = 0; i < PPT; i++) {
+      o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      l[i] = 0.0f;
+    }
+#pragma unroll 4
+    for (int jl = jlo - jb; jl <= jhi - jb; jl++) {
+      const float4 v4 = reinterpret_cast<const float4 *>(vs + (size_t)jl * HD)[dc];
+#pragma unroll
+      for (int i = 0; i < PPT; i++) {
+        const float pj = ss[(g * PPT + i) * ATT_BLK + jl];
+        o[i].x = fmaf(pj, v4.x, o[i].x);
+        o[i].y = fmaf(pj, v4.y, o[i].y);
+        o[i].z = fmaf(pj, v4.z, o[i].z);
+        o[i].w = fmaf(pj, v4.w, o[i].w);
+        l[i] = __fadd_rn(l[i], pj);
+      }
+    }
+    if (dc == 0) {
+#pragma unroll
+      for (int i = 0; i < PPT; i++) lb[g * PPT + i] = l[i];
+    }
+    __syncthreads();
+    // The fold of this block into each pair's running (M, L): k_attn_merge's formula.
+    for (int i = t; i < NP; i += 256) {
+      const int q = i / NH;
+      const bool valid = jb <= qp[q] && jb + ATT_BLK - 1 >= qlo[q];
+      if (!valid) {
+        mode[i] = 0;
+      } else if (RM[i] == -FLT_MAX && RL[i] == 0.0f) {
+        mode[i] = 1;
+        RM[i] = mb[i];
+        RL[i] = lb[i];
+      } else {
+        mode[i] = 2;
+        const float Mn = fmaxf(RM[i], mb[i]);
+        const float e1 = g4_exp(__fsub_rn(RM[i], Mn)), e2 = g4_exp(__fsub_rn(mb[i], Mn));
+        RL[i] = __fadd_rn(__fmul_rn(RL[i], e1), __fmul_rn(lb[i], e2));
+        RM[i] = Mn;
+        ea[i] = e1;
+        ec[i] = e2;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < PPT; i++) {
+      const int pi = g * PPT + i, md = mode[pi];
+      if (md == 1) {
+        O[i] = o[i];
+      } else if (md == 2) {
+        const float e1 = ea[pi], e2 = ec[pi];
+        O[i].x = __fadd_rn(__fmul_rn(O[i].x, e1), __fmul_rn(o[i].x, e2));
+        O[i].y = __fadd_rn(__fmul_rn(O[i].y, e1), __fmul_rn(o[i].y, e2));
+        O[i].z = __fadd_rn(__fmul_rn(O[i].z, e1), __fmul_rn(o[i].z, e2));
+        O[i].w = __fadd_rn(__fmul_rn(O[i].w, e1), __fmul_rn(o[i].w, e2));
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < PPT; i++) {
+    const int pi = g * PPT + i, q = pi / NH, h = pi % NH;
+    if (q < nq) {
+      const float L = RL[pi];
+      float4 r;
+      r.x = __fdiv_rn(O[i].x, L);
+      r.y = __fdiv_rn(O[i].y, L);
+      r.z = __fdiv_rn(O[i].z, L);
+      r.w = __fdiv_rn(O[i].w, L);
+      reinterpret_cast<float4 *>(a.out + (size_t)(c0 + q) * NH * HD + (size_t)h * HD)[dc] = r;
+    }
+  }
+}
+
+template <int HD>
+static size_t attn_prefill_smem() {
+  constexpr int NP = (2048 / HD) * 8;
+  return ((size_t)NP * HD + (size_t)ATT_BLK * HD + (size_t)NP * ATT_BLK + 7 * NP + 2 * (2048 / HD)) * 4;
+}
+
+cudaError_t launch_attention_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
+  if (a.heads != 8 || a.kv_cap != 0) return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_attn_prefill<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_prefill_smem<256>());
+    cudaFuncSetAttribute(k_attn_prefill<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_prefill_smem<512>());
+    attr = true;
+  }
+  if (a.hd == 256)
+    return launch_k(k_attn_prefill<256>, dim3((a.cols + 7) / 8), dim3(256), attn_prefill_smem<256>(), st, pdl, a);
+  if (a.hd == 512)
+    return launch_k(k_attn_prefill<512>, dim3((a.cols + 3) / 4), dim3(256), attn_prefill_smem<512>(), st, pdl, a);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl) {
   if (a.heads != 8) return cudaErrorInvalidValue;
   size_t smem = ((size_t)8 * a.hd + 8 * ATT_BLK * 2 + 32 + (size_t)ATT_BLK * a.hd) * 4;

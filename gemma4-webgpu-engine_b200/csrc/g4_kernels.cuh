@@ -133,6 +133,9 @@ struct AttnArgs {
   float *out;                        // [cols, heads * hd]
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
+// The same attention for a prefill chunk (columns = consecutive positions of one sequence),
+// query-tiled: bit-identical to launch_attention on such a chunk.
+cudaError_t launch_attention_prefill(const AttnArgs &a, cudaStream_t st, bool pdl);
 
 // Activation codes for the tensor-core path: one CTA per column runs the GEMV prologue `a.pro`
 // (norm / join / norm-residual / gelu / x) once and writes the column's int8 codes in K order

@@ -1106,8 +1106,14 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       at.part_m = ctx->part_m;
       at.part_l = ctx->part_l;
       at.out = ctx->attn;
-      CK(launch_attention(at, ctx->st, true));
-      ctx->launches += 2;
+      if (cols > 1) {
+        // A prefill chunk: consecutive positions of one sequence, query-tiled.
+        CK(launch_attention_prefill(at, ctx->st, true));
+        ctx->launches++;
+      } else {
+        CK(launch_attention(at, ctx->st, true));
+        ctx->launches += 2;
+      }
     }
     // ---- o_proj
     {
@@ -1744,6 +1750,29 @@ extern "C" int g4_op_attention(const float *q, const float *cache, float *out, i
   cudaError_t e = launch_attention(a, st, false);
   cudaFreeAsync(scratch, st);
   OPCK(e);
+  return G4_OK;
+}
+
+extern "C" int g4_op_attention_prefill(const float *q, const float *cache, float *out, int32_t heads,
+                                       int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,
+                                       int32_t window, int32_t max_context, void *stream) {
+  if (!q || !cache || !out) return fail(nullptr, G4_ERR_INVALID, "g4_op_attention_prefill: null pointer");
+  if (heads != 8) return fail(nullptr, G4_ERR_UNSUPPORTED, "the attention kernel is built for 8 query heads");
+  if (head_dim != 256 && head_dim != 512) return fail(nullptr, G4_ERR_UNSUPPORTED, "head_dim 256 or 512");
+  if (q_count < 1 || q_start < 0 || kv_len < 1 || q_start + q_count > kv_len || kv_len > max_context)
+    return fail(nullptr, G4_ERR_INVALID, "attention: query positions extend past kv_len; store KV before attending");
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.cols = q_count;
+  a.heads = heads;
+  a.hd = head_dim;
+  a.window = window;
+  a.max_ctx = max_context;
+  a.qr = q;
+  a.cache = cache;
+  a.refs.pos_base = q_start;
+  a.out = out;
+  OPCK(launch_attention_prefill(a, (cudaStream_t)stream, false));
   return G4_OK;
 }
 

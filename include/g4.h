@@ -296,6 +296,14 @@ int g4_op_attention(const float *q, const float *cache, float *out, int32_t head
                     int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,
                     int32_t window, int32_t max_context, void *stream);
 
+/* The prefill form of the same attention (src/kernels/attention.ts:339-752 with q_count > 1): the
+ * queries are the consecutive positions q_start .. q_start + q_count - 1 of one sequence, tiled
+ * so each KV block is read once per query tile. Same arguments and bit-identical results as
+ * g4_op_attention; allocates nothing. */
+int g4_op_attention_prefill(const float *q, const float *cache, float *out, int32_t heads,
+                            int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,
+                            int32_t window, int32_t max_context, void *stream);
+
 /* embed-gather (int4 rows here) and ple-gather-4bit(-sliced) (src/kernels/embedGather.ts:
  * 176-261, 319-344, 547-577). codes: row-major int4; scales f16 [rows, groups]; ids int32
  * [slots]; dst f32 [slots, cols]. A sliced call writes only the slots whose id lies in

@@ -249,6 +249,28 @@ def test_attention(cuda, lib, O, hd, q_count, q_start, kv_len, window):
     assert cos >= 0.999 and np.max(np.abs(got - ref)) < 1e-4
 
 
+@pytest.mark.parametrize("hd,q_count,q_start,kv_len,window", [
+    (256, 300, 200, 500, 128), (256, 97, 0, 97, 512), (512, 130, 70, 200, 0), (512, 3, 5, 8, 0),
+    (256, 64, 640, 704, 512), (256, 33, 1000, 1033, 16),
+])
+def test_attention_prefill_tiled_matches(cuda, lib, O, hd, q_count, q_start, kv_len, window):
+    """The query-tiled prefill attention equals the per-(column, block) kernels bit for bit and
+    the oracle's mirror, across windows, tile edges and block boundaries."""
+    heads, max_ctx = 8, 1200
+    q = RNG.normal(0, 1, q_count * heads * hd).astype(np.float32)
+    cache = RNG.normal(0, 1, 2 * max_ctx * hd).astype(np.float32)
+    dq, dc = dev(cuda, q), dev(cuda, cache)
+    out_a = cuda.zeros(q_count * heads * hd, dtype=cuda.float32, device="cuda")
+    out_b = cuda.zeros(q_count * heads * hd, dtype=cuda.float32, device="cuda")
+    call(lib, "g4_op_attention", p(dq), p(dc), p(out_a), heads, hd, q_count, q_start, kv_len, window, max_ctx, None)
+    call(lib, "g4_op_attention_prefill", p(dq), p(dc), p(out_b), heads, hd, q_count, q_start, kv_len, window,
+         max_ctx, None)
+    a, b = host(out_a), host(out_b)
+    np.testing.assert_array_equal(b.view(np.uint32), a.view(np.uint32))
+    mirror = O.attention(q, cache, heads, hd, q_count, q_start, kv_len, window, max_ctx)
+    np.testing.assert_array_equal(b.view(np.uint32), mirror.view(np.uint32))
+
+
 def test_attention_scale_is_one(cuda, lib, O):
     """Trap 2 (src/kernels/attention.ts:11-18): the kernel matches scale 1.0 and not 1/sqrt(d)."""
     heads, hd, max_ctx, p_ = 8, 256, 256, 99
