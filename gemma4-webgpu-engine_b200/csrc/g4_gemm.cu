@@ -138,9 +138,11 @@ __device__ __forceinline__ uint2 unpack8(uint32_t w) {
 constexpr int GM_BM = 128;       // weight rows per tile (MMA M)
 constexpr int GM_BK = 128;       // K per stage: one 128-byte swizzle atom of int8
 
-template <int BN>
+// NSTAGE 0: the default depth (3 at BN 256, else 4, one CTA per SM); 2: two CTAs share an SM
+// (their epilogues overlap each other's main loops).
+template <int BN, int NSTAGE = 0>
 struct GemmShape {
-  static constexpr int STAGES = BN >= 256 ? 3 : 4;
+  static constexpr int STAGES = NSTAGE ? NSTAGE : (BN >= 256 ? 3 : 4);
   static constexpr int A_BYTES = GM_BM * GM_BK;          // 16 KB
   static constexpr int B_BYTES = BN * GM_BK;
   static constexpr int P_BYTES = GM_BM * GM_BK / 2;      // packed int4 staging, 8 KB
@@ -149,11 +151,11 @@ struct GemmShape {
   static constexpr int SMEM = 1024 + BAR_OFF + (3 * STAGES + 2) * 8 + 64 + 4 * 32 * 8;
 };
 
-template <int BITS, int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+template <int BITS, int BN, int EPI, int NSTAGE>
+__global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
     k_qgemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const GemmArgs a) {
-  using S = GemmShape<BN>;
+  using S = GemmShape<BN, NSTAGE>;
   constexpr int NS = S::STAGES;
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
   uint8_t *gsm = gsm_raw + ((1024 - (smem_u32(gsm_raw) & 1023)) & 1023);
@@ -389,11 +391,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-template <int BITS, int BN, int EPI>
+template <int BITS, int BN, int EPI, int NSTAGE = 0>
 static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  cudaStream_t st, bool pdl) {
-  auto k = k_qgemm_tc<BITS, BN, EPI>;
-  const int smem = GemmShape<BN>::SMEM;
+  auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE>;
+  const int smem = GemmShape<BN, NSTAGE>::SMEM;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -418,6 +420,7 @@ static cudaError_t launch_gemm_b(const CUtensorMap &tmW, const CUtensorMap &tmX,
   if (bn == 64) return launch_gemm_t<BITS, 64, EPI>(tmW, tmX, a, st, pdl);
   if (bn == 128) return launch_gemm_t<BITS, 128, EPI>(tmW, tmX, a, st, pdl);
   if (bn == 256) return launch_gemm_t<BITS, 256, EPI>(tmW, tmX, a, st, pdl);
+  if (bn == -128) return launch_gemm_t<BITS, 128, EPI, 2>(tmW, tmX, a, st, pdl);
   return cudaErrorInvalidValue;
 }
 

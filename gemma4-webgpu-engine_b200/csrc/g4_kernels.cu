@@ -1259,10 +1259,12 @@ template <int HD>
 __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
   constexpr int NH = 8, NC = HD / 4, QT = 2048 / HD, NP = QT * NH;   // pairs per CTA
   constexpr int G = 256 / NC, PPT = NP / G;                         // PV: pairs per thread
+  constexpr bool KSM = HD <= 256;              // K rows staged in shared memory too
   extern __shared__ __align__(16) float sm[];
   float *qs = sm;                              // [QT][NH][HD]
   float *vs = qs + NP * HD;                    // [64][HD]
-  float *ss = vs + ATT_BLK * HD;               // [NP][64] scores, then probabilities
+  float *ks = vs + ATT_BLK * HD;               // [64][HD] when KSM
+  float *ss = ks + (KSM ? ATT_BLK * HD : 0);   // [NP][64] scores, then probabilities
   float *mb = ss + NP * ATT_BLK;               // [NP] block max
   float *lb = mb + NP;                         // [NP] block sum
   float *RM = lb + NP;                         // [NP] running max
@@ -1313,9 +1315,14 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
     // V rows of the union range; rows outside it are zero (their probabilities are zero too).
     for (int i = t; i < ATT_BLK * NC; i += 256) {
       const int jl = i / NC, k4 = i - jl * NC, j = jb + jl;
-      reinterpret_cast<float4 *>(vs)[i] = (j >= jlo && j <= jhi)
-          ? reinterpret_cast<const float4 *>(V + (size_t)j * HD)[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool in = j >= jlo && j <= jhi;
+      reinterpret_cast<float4 *>(vs)[i] =
+          in ? reinterpret_cast<const float4 *>(V + (size_t)j * HD)[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (KSM)
+        reinterpret_cast<float4 *>(ks)[i] =
+            in ? reinterpret_cast<const float4 *>(K + (size_t)j * HD)[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    if (KSM) __syncthreads();
     // Scores: thread (jl, m) runs accumulator m of position jl for every (query, head) pair.
     {
       const int jl = t >> 2, m = t & 3, j = jb + jl;
@@ -1324,19 +1331,26 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
 #pragma unroll
       for (int i = 0; i < NP; i++) acc[i] = 0.0f;
       if (inr) {
-        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)j * HD);
-#pragma unroll 2
-        for (int cc = m; cc < NC; cc += 4) {
-          const float4 k4 = kr[cc];
+        const float4 *kr = reinterpret_cast<const float4 *>(KSM ? ks + (size_t)jl * HD : K + (size_t)j * HD);
+        constexpr int PER = NC / 4, BATCH = KSM ? 1 : 8;   // chunks per thread; global loads 8 at a time
+#pragma unroll 1
+        for (int i0 = 0; i0 < PER; i0 += BATCH) {
+          float4 kb[BATCH];
 #pragma unroll
-          for (int i = 0; i < NP; i++) {
-            const float4 q4 = reinterpret_cast<const float4 *>(qs + i * HD)[cc];
-            float v = acc[i];
-            v = fmaf(q4.x, k4.x, v);
-            v = fmaf(q4.y, k4.y, v);
-            v = fmaf(q4.z, k4.z, v);
-            v = fmaf(q4.w, k4.w, v);
-            acc[i] = v;
+          for (int u = 0; u < BATCH; u++) kb[u] = kr[m + 4 * (i0 + u)];
+#pragma unroll
+          for (int u = 0; u < BATCH; u++) {
+            const int cc = m + 4 * (i0 + u);
+#pragma unroll
+            for (int i = 0; i < NP; i++) {
+              const float4 q4 = reinterpret_cast<const float4 *>(qs + i * HD)[cc];
+              float v = acc[i];
+              v = fmaf(q4.x, kb[u].x, v);
+              v = fmaf(q4.y, kb[u].y, v);
+              v = fmaf(q4.z, kb[u].z, v);
+              v = fmaf(q4.w, kb[u].w, v);
+              acc[i] = v;
+            }
           }
         }
       }
@@ -1442,7 +1456,8 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
 template <int HD>
 static size_t attn_prefill_smem() {
   constexpr int NP = (2048 / HD) * 8;
-  return ((size_t)NP * HD + (size_t)ATT_BLK * HD + (size_t)NP * ATT_BLK + 7 * NP + 2 * (2048 / HD)) * 4;
+  return ((size_t)NP * HD + (size_t)ATT_BLK * HD * (HD <= 256 ? 2 : 1) + (size_t)NP * ATT_BLK + 7 * NP +
+          2 * (2048 / HD)) * 4;
 }
 
 cudaError_t launch_attention_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
