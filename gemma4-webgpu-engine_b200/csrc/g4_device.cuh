@@ -166,6 +166,28 @@ __device__ __forceinline__ float srq_out_r(float v, float s, float r) {
   return __fmul_rn(srq_q_r(v, s, r), s);
 }
 
+// ---------------------------------------------------------------------- tracing
+// Built with -DG4_TRACE (a diagnostic build, never the shipped library): block 0 of each traced
+// kernel records (kernel id, %globaltimer) right after its dependency wait, so consecutive
+// records give each launch's share of the live critical path. Off: the macro is empty.
+#ifdef G4_TRACE
+// g4_trace_buf / g4_trace_n are defined in the one translation unit that records (g4_kernels.cu).
+#define G4_TRACE_POINT(id)                                                                   \
+  do {                                                                                       \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) {       \
+      unsigned long long now;                                                                \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));                                \
+      const unsigned int slot = atomicAdd(&g4_trace_n, 1u);                                  \
+      if (slot < (1u << 15)) {                                                               \
+        g4_trace_buf[2 * slot] = (unsigned long long)(id);                                   \
+        g4_trace_buf[2 * slot + 1] = now;                                                    \
+      }                                                                                      \
+    }                                                                                        \
+  } while (0)
+#else
+#define G4_TRACE_POINT(id) do {} while (0)
+#endif
+
 // ---------------------------------------------------------------------- mbarriers, bulk copies
 #ifdef __CUDACC__
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

@@ -286,6 +286,10 @@ __global__ void __launch_bounds__(256) k_gemv_f32(const GemvArgs a) {
 // =====================================================================================
 
 __device__ int g4_dev_error;
+#ifdef G4_TRACE
+__device__ unsigned long long g4_trace_buf[1 << 16];
+__device__ unsigned int g4_trace_n;
+#endif
 
 constexpr int GS_RING = 96 * 1024;   // shared-memory ring per CTA
 constexpr int GS_MAX_STAGES = 8;
@@ -410,6 +414,7 @@ __global__ void __launch_bounds__(256, G4_GEMV_MIN_BLOCKS) k_qgemv_stream(const 
   prologue_gains<PRO>(a, pg);
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(1000 + BITS * 100 + PRO * 10 + EPI);
 
 #pragma unroll 1
   for (int c = 0; c < a.cols; c++) {
@@ -725,6 +730,18 @@ cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, boo
   return cudaErrorInvalidConfiguration;
 }
 
+#ifdef G4_TRACE
+int trace_take(unsigned long long *out, int max_records) {
+  unsigned int n = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&n, g4_trace_n, sizeof(n)) != cudaSuccess) return -1;
+  if (n > (1u << 15)) n = 1u << 15;
+  if ((int)n > max_records) n = (unsigned int)max_records;
+  if (n && cudaMemcpyFromSymbol(out, g4_trace_buf, (size_t)n * 16) != cudaSuccess) return -1;
+  cudaMemcpyToSymbol(g4_trace_n, &zero, sizeof(zero));
+  return (int)n;
+}
+#endif
+
 int device_error_take() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g4_dev_error, sizeof(int)) != cudaSuccess) return -1;
@@ -761,6 +778,7 @@ k_embed(const int32_t *tokens, const uint8_t *embed_w, const uint16_t *embed_s, 
         int ple_group, float *residual, float *ple_id) {
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(3001);
   const int c = blockIdx.y;
   const int w = blockIdx.x * 256 + threadIdx.x;
   const int hw = H / 8, pw = ple_cols / 8;
@@ -851,6 +869,7 @@ k_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K
   }
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(3002);
   for (int c = 0; c < cols; c++)
     for (int i = t; i < K / 4; i += 256)
       reinterpret_cast<float4 *>(xs + c * K)[i] = reinterpret_cast<const float4 *>(x + (size_t)c * ld_x)[i];
@@ -1005,6 +1024,7 @@ k_ple_combine(const float *proj, const float *identity, const float *gain, float
   __shared__ float red[8];
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(3003);
   const int c = blockIdx.x, g = blockIdx.y, t = threadIdx.x;
   const size_t base = (size_t)c * row_width + (size_t)g * group_dim;
   const float inv = rms_inv(block_sumsq256(proj + base, group_dim, red), group_dim, eps);
@@ -1586,21 +1606,25 @@ __device__ __forceinline__ void head_norm_rope_warp(const float *src, const floa
   }
 }
 
-template <int HD>
+template <int HD, int NHL>
 __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
+  // NHL query heads per CTA: 8 (one CTA per (column, block)) or 1 (grid z = head).
   constexpr int NH = 8;
   constexpr int NC = HD / 4;
-  constexpr int HPG = HD / 128;
+  constexpr int NOUT = NHL * NC;                       // float4 outputs of the PV step
+  constexpr int HPT = NOUT >= 256 ? NOUT / 256 : 1;    // heads per PV thread
+  constexpr int NCH = NOUT >= 256 ? 256 / NC : NHL;    // PV head groups
   extern __shared__ __align__(16) float sm[];
   float *vs = sm;                     // [64][HD]   (bulk copy destination)
-  float *qs = vs + ATT_BLK * HD;      // [NH][HD]
-  float *kc = qs + NH * HD;           // [HD]       K row of the new position
-  float *ss = kc + HD;                // [NH][64]
-  float *ps = ss + NH * ATT_BLK;      // [NH][64]
-  float *ms = ps + NH * ATT_BLK;      // [NH]
-  uint64_t *bar = reinterpret_cast<uint64_t *>(ms + NH);   // 8-byte aligned: offsets above are
+  float *qs = vs + ATT_BLK * HD;      // [NHL][HD]
+  float *kc = qs + NHL * HD;          // [HD]       K row of the new position
+  float *ss = kc + HD;                // [NHL][64]
+  float *ps = ss + NHL * ATT_BLK;     // [NHL][64]
+  float *ms = ps + NHL * ATT_BLK;     // [8]
+  uint64_t *bar = reinterpret_cast<uint64_t *>(ms + 8);    // 8-byte aligned: offsets above are
   int *flag = reinterpret_cast<int *>(bar + 1);            // multiples of 8 floats
   const int c = blockIdx.x, bi = blockIdx.y, t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int h0 = blockIdx.z * NHL;    // first head of this CTA
 
   grid_launch_dependents();
   if (t == 0) {
@@ -1609,7 +1633,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     // L2 prefetch of this block's rows from a possibly stale position (clamped in bounds).
     int p = a.refs.pos ? a.refs.pos[c] : a.refs.pos_base + c;
     int sq = a.refs.seq ? a.refs.seq[c] : 0;
-    if (p >= 0 && p < a.max_ctx && sq >= 0 && sq < a.max_seqs) {
+    if (p >= 0 && p < a.max_ctx && sq >= 0 && sq < a.max_seqs && blockIdx.z == 0) {
       const int lo = a.window > 0 ? max(0, p - a.window + 1) : 0;
       const int b = lo / ATT_BLK + bi;
       if (b * ATT_BLK <= p) {
@@ -1622,6 +1646,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     }
   }
   grid_wait();
+  G4_TRACE_POINT(2000 + HD);
   int p, lo, hi;
   {
     AttnArgs r;
@@ -1638,6 +1663,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
   float *K = a.cache + (size_t)seq * a.seq_stride;
   float *V = K + (size_t)a.max_ctx * HD;
   const bool cur = a.k != nullptr && j1 == p;     // this block writes and uses row p itself
+  const bool store_kv = cur && blockIdx.z == 0;   // one CTA of the block stores the new row
   const int jv1 = cur ? p - 1 : j1;
   const uint32_t vbytes = jv1 >= j0 ? (uint32_t)(jv1 - j0 + 1) * HD * 4 : 0u;
   __syncthreads();   // barrier initialised
@@ -1646,18 +1672,22 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     bulk_g2s(vs + (size_t)(j0 - b * ATT_BLK) * HD, V + (size_t)j0 * HD, vbytes, bar);
   }
 
-  // Query heads (warp h), then the new position's K (warp 0) and V (warp 1) rows.
+  // Query heads (warp w < NHL: head h0 + w), then the new position's K and V rows (the warps
+  // after them).
   {
     const float *ct = a.cos_tab + (size_t)p * (HD / 2);
     const float *stb = a.sin_tab + (size_t)p * (HD / 2);
-    head_norm_rope_warp<HD>(a.q + (size_t)c * a.q_ld + (size_t)w * HD, a.qgain, ct, stb, a.eps,
-                            qs + w * HD, nullptr, lane);
-    if (cur && w == 0)
+    if (w < NHL)
+      head_norm_rope_warp<HD>(a.q + (size_t)c * a.q_ld + (size_t)(h0 + w) * HD, a.qgain, ct, stb,
+                              a.eps, qs + w * HD, nullptr, lane);
+    constexpr int WK = NHL < 8 ? NHL : 0, WV = NHL < 7 ? NHL + 1 : 1;
+    if (cur && w == WK)
       head_norm_rope_warp<HD>(a.k + (size_t)c * HD, a.kgain, ct, stb, a.eps, kc,
-                              K + (size_t)p * HD, lane);
-    if (cur && w == 1)
+                              store_kv ? K + (size_t)p * HD : nullptr, lane);
+    if (cur && w == WV)
       head_norm_rope_warp<HD>(a.v + (size_t)c * HD, nullptr, nullptr, nullptr, a.eps,
-                              vs + (size_t)(p - b * ATT_BLK) * HD, V + (size_t)p * HD, lane);
+                              vs + (size_t)(p - b * ATT_BLK) * HD, store_kv ? V + (size_t)p * HD : nullptr,
+                              lane);
   }
   __syncthreads();
 
@@ -1666,9 +1696,9 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     const int jl = t >> 2, m = t & 3;
     const int j = b * ATT_BLK + jl;
     const bool valid = j >= j0 && j <= j1;
-    float acc[NH];
+    float acc[NHL];
 #pragma unroll
-    for (int h = 0; h < NH; h++) acc[h] = 0.0f;
+    for (int h = 0; h < NHL; h++) acc[h] = 0.0f;
     if (valid) {
       const float4 *kr = reinterpret_cast<const float4 *>(cur && j == p ? kc : K + (size_t)j * HD);
       constexpr int PER = NC / 4, BATCH = PER < 16 ? PER : 16;
@@ -1681,7 +1711,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
         for (int i = 0; i < BATCH; i++) {
           const int cc = m + 4 * (i0 + i);
 #pragma unroll
-          for (int h = 0; h < NH; h++) {
+          for (int h = 0; h < NHL; h++) {
             const float4 q4 = reinterpret_cast<const float4 *>(qs + h * HD)[cc];
             float v = acc[h];
             v = fmaf(q4.x, k4[i].x, v);
@@ -1694,14 +1724,14 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       }
     }
 #pragma unroll
-    for (int h = 0; h < NH; h++) {
+    for (int h = 0; h < NHL; h++) {
       float v1 = __fadd_rn(acc[h], __shfl_xor_sync(0xffffffffu, acc[h], 1));
       float v2 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, 2));
       if (m == 0) ss[h * ATT_BLK + jl] = valid ? v2 : -FLT_MAX;
     }
   }
   __syncthreads();
-  {
+  if (w < NHL) {
     const int h = w;
     float s0 = ss[h * ATT_BLK + lane], s1 = ss[h * ATT_BLK + lane + 32];
     float mx = fmaxf(s0, s1);
@@ -1722,80 +1752,92 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
   }
   __syncthreads();
   const int dc = t % NC, hg = t / NC;
-  float4 o[HPG];
-  float l[HPG];
+  const bool pv = hg < NCH;
+  float4 o[HPT];
+  float l[HPT];
 #pragma unroll
-  for (int hh = 0; hh < HPG; hh++) {
+  for (int hh = 0; hh < HPT; hh++) {
     o[hh] = make_float4(0.f, 0.f, 0.f, 0.f);
     l[hh] = 0.0f;
   }
+  if (pv) {
 #pragma unroll 4
-  for (int j = j0; j <= j1; j++) {
-    const int jl = j - b * ATT_BLK;
-    const float4 v4 = reinterpret_cast<const float4 *>(vs + (size_t)jl * HD)[dc];
+    for (int j = j0; j <= j1; j++) {
+      const int jl = j - b * ATT_BLK;
+      const float4 v4 = reinterpret_cast<const float4 *>(vs + (size_t)jl * HD)[dc];
 #pragma unroll
-    for (int hh = 0; hh < HPG; hh++) {
-      const float pj = ps[(hg * HPG + hh) * ATT_BLK + jl];
-      o[hh].x = fmaf(pj, v4.x, o[hh].x);
-      o[hh].y = fmaf(pj, v4.y, o[hh].y);
-      o[hh].z = fmaf(pj, v4.z, o[hh].z);
-      o[hh].w = fmaf(pj, v4.w, o[hh].w);
-      l[hh] = __fadd_rn(l[hh], pj);
+      for (int hh = 0; hh < HPT; hh++) {
+        const float pj = ps[(hg * HPT + hh) * ATT_BLK + jl];
+        o[hh].x = fmaf(pj, v4.x, o[hh].x);
+        o[hh].y = fmaf(pj, v4.y, o[hh].y);
+        o[hh].z = fmaf(pj, v4.z, o[hh].z);
+        o[hh].w = fmaf(pj, v4.w, o[hh].w);
+        l[hh] = __fadd_rn(l[hh], pj);
+      }
     }
   }
   if (nb == 1) {
+    if (pv) {
 #pragma unroll
-    for (int hh = 0; hh < HPG; hh++) {
-      const int h = hg * HPG + hh;
-      float4 r;
-      r.x = __fdiv_rn(o[hh].x, l[hh]);
-      r.y = __fdiv_rn(o[hh].y, l[hh]);
-      r.z = __fdiv_rn(o[hh].z, l[hh]);
-      r.w = __fdiv_rn(o[hh].w, l[hh]);
-      reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD + (size_t)h * HD)[dc] = r;
+      for (int hh = 0; hh < HPT; hh++) {
+        const int h = h0 + hg * HPT + hh;
+        float4 r;
+        r.x = __fdiv_rn(o[hh].x, l[hh]);
+        r.y = __fdiv_rn(o[hh].y, l[hh]);
+        r.z = __fdiv_rn(o[hh].z, l[hh]);
+        r.w = __fdiv_rn(o[hh].w, l[hh]);
+        reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD + (size_t)h * HD)[dc] = r;
+      }
     }
     return;
   }
+  if (pv) {
 #pragma unroll
-  for (int hh = 0; hh < HPG; hh++) {
-    const int h = hg * HPG + hh;
-    const size_t slot = ((size_t)c * a.max_blocks + bi) * NH + h;
-    reinterpret_cast<float4 *>(a.part_o + slot * HD)[dc] = o[hh];
-    if (dc == 0) {
-      a.part_m[slot] = ms[h];
-      a.part_l[slot] = l[hh];
+    for (int hh = 0; hh < HPT; hh++) {
+      const int hl = hg * HPT + hh, h = h0 + hl;
+      const size_t slot = ((size_t)c * a.max_blocks + bi) * NH + h;
+      reinterpret_cast<float4 *>(a.part_o + slot * HD)[dc] = o[hh];
+      if (dc == 0) {
+        a.part_m[slot] = ms[hl];
+        a.part_l[slot] = l[hh];
+      }
     }
   }
   __threadfence();
   __syncthreads();
-  if (t == 0) *flag = atomicAdd(a.counter + c, 1) == nb - 1;
+  int *cnt = a.counter + c * (NH / NHL) + blockIdx.z;
+  if (t == 0) *flag = atomicAdd(cnt, 1) == nb - 1;
   __syncthreads();
   if (!*flag) return;
   __threadfence();
-  // The merge, in k_attn_merge's order. Per head, M_k = max(m_0..m_k) is an exact prefix max,
-  // so lane k of warp h computes ea_k = exp(M_{k-1} - M_k), ec_k = exp(m_k - M_k) and
-  // l_k * ec_k in parallel; lane 0 then runs L_k = L_{k-1} * ea_k + l_k * ec_k. Each thread
-  // folds its vec4s of the partial outputs block after block with the same factors.
+  // The merge, in k_attn_merge's order, for this CTA's heads. Per head, M_k = max(m_0..m_k) is
+  // an exact prefix max, so lane k of warp hl computes ea_k = exp(M_{k-1} - M_k),
+  // ec_k = exp(m_k - M_k) and l_k * ec_k in parallel; lane 0 then runs
+  // L_k = L_{k-1} * ea_k + l_k * ec_k. Each thread folds its vec4s of the partial outputs block
+  // after block with the same factors.
   const size_t base = (size_t)c * a.max_blocks * NH;
-  float *fa = vs;                          // [nb][NH] ea_k  (vs is free after the PV loop)
-  float *fc = vs + (size_t)a.max_blocks * NH;      // [nb][NH] ec_k
-  float *fl = fc + (size_t)a.max_blocks * NH;      // [nb][NH] l_k * ec_k
-  float *Lh = fl + (size_t)a.max_blocks * NH;      // [NH] final L
-  constexpr int F = HD / 128;              // vec4s per thread per block: 8 * HD / 4 / 256
-  constexpr int KB = 16 / F;               // blocks loaded per round
+  float *fa = vs;                                  // [nb][8] ea_k  (vs is free after the PV loop)
+  float *fc = vs + (size_t)a.max_blocks * NH;      // [nb][8] ec_k
+  float *fl = fc + (size_t)a.max_blocks * NH;      // [nb][8] l_k * ec_k
+  float *Lh = fl + (size_t)a.max_blocks * NH;      // [8] final L
+  constexpr int NV = NHL * HD / 4;                 // float4 outputs of this CTA per block
+  constexpr int F = (NV + 255) / 256;              // per thread
+  constexpr int KB = F <= 2 ? 8 : 16 / F;          // blocks loaded per round
   float4 O[F];
   float4 nx[KB][F];
-  const float4 *po = reinterpret_cast<const float4 *>(a.part_o + base * HD);
+  const float4 *po = reinterpret_cast<const float4 *>(a.part_o + (base + h0) * HD);
 #pragma unroll
-  for (int i = 0; i < F; i++) O[i] = __ldcg(po + t + 256 * i);
+  for (int i = 0; i < F; i++)
+    if (t + 256 * i < NV) O[i] = __ldcg(po + t + 256 * i);
 #pragma unroll
   for (int kk = 0; kk < KB; kk++)
     if (1 + kk < nb) {
 #pragma unroll
-      for (int i = 0; i < F; i++) nx[kk][i] = __ldcg(po + (size_t)(1 + kk) * NH * HD / 4 + t + 256 * i);
+      for (int i = 0; i < F; i++)
+        if (t + 256 * i < NV) nx[kk][i] = __ldcg(po + (size_t)(1 + kk) * NH * HD / 4 + t + 256 * i);
     }
-  {
-    const int h = w;
+  if (w < NHL) {
+    const int h = h0 + w;
     float carry = -FLT_MAX, Lrun = 0.0f;
     for (int k0 = 0; k0 < nb; k0 += 32) {
       const int k = k0 + lane;
@@ -1803,9 +1845,9 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       const float lk = k < nb ? __ldcg(a.part_l + base + (size_t)k * NH + h) : 0.0f;
       float Mk = mk;   // inclusive prefix max within the chunk, then with the carry
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, Mk, o);
-        if (lane >= o) Mk = fmaxf(Mk, u);
+      for (int o2 = 1; o2 < 32; o2 <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, Mk, o2);
+        if (lane >= o2) Mk = fmaxf(Mk, u);
       }
       Mk = fmaxf(Mk, carry);
       float Mp = __shfl_up_sync(0xffffffffu, Mk, 1);
@@ -1814,10 +1856,10 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
         if (k == 0) {
           fl[h] = lk;
         } else {
-          const float ea = g4_exp(__fsub_rn(Mp, Mk)), ec = g4_exp(__fsub_rn(mk, Mk));
-          fa[k * NH + h] = ea;
-          fc[k * NH + h] = ec;
-          fl[k * NH + h] = __fmul_rn(lk, ec);
+          const float e1 = g4_exp(__fsub_rn(Mp, Mk)), e2 = g4_exp(__fsub_rn(mk, Mk));
+          fa[k * NH + h] = e1;
+          fc[k * NH + h] = e2;
+          fl[k * NH + h] = __fmul_rn(lk, e2);
         }
       }
       carry = __shfl_sync(0xffffffffu, Mk, 31);
@@ -1839,12 +1881,14 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       if (k < nb) {
 #pragma unroll
         for (int i = 0; i < F; i++) {
-          const int h = (4 * (t + 256 * i)) / HD;
-          const float ea = fa[k * NH + h], ec = fc[k * NH + h];
-          O[i].x = __fadd_rn(__fmul_rn(O[i].x, ea), __fmul_rn(nx[kk][i].x, ec));
-          O[i].y = __fadd_rn(__fmul_rn(O[i].y, ea), __fmul_rn(nx[kk][i].y, ec));
-          O[i].z = __fadd_rn(__fmul_rn(O[i].z, ea), __fmul_rn(nx[kk][i].z, ec));
-          O[i].w = __fadd_rn(__fmul_rn(O[i].w, ea), __fmul_rn(nx[kk][i].w, ec));
+          if (t + 256 * i < NV) {
+            const int h = h0 + (4 * (t + 256 * i)) / HD;
+            const float e1 = fa[k * NH + h], e2 = fc[k * NH + h];
+            O[i].x = __fadd_rn(__fmul_rn(O[i].x, e1), __fmul_rn(nx[kk][i].x, e2));
+            O[i].y = __fadd_rn(__fmul_rn(O[i].y, e1), __fmul_rn(nx[kk][i].y, e2));
+            O[i].z = __fadd_rn(__fmul_rn(O[i].z, e1), __fmul_rn(nx[kk][i].z, e2));
+            O[i].w = __fadd_rn(__fmul_rn(O[i].w, e1), __fmul_rn(nx[kk][i].w, e2));
+          }
         }
       }
     }
@@ -1854,46 +1898,52 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       if (k0 + KB + kk < nb) {
 #pragma unroll
         for (int i = 0; i < F; i++)
-          nx[kk][i] = __ldcg(po + (size_t)(k0 + KB + kk) * NH * HD / 4 + t + 256 * i);
+          if (t + 256 * i < NV)
+            nx[kk][i] = __ldcg(po + (size_t)(k0 + KB + kk) * NH * HD / 4 + t + 256 * i);
       }
   }
 #pragma unroll
   for (int i = 0; i < F; i++) {
-    const int h = (4 * (t + 256 * i)) / HD;
-    const float L = Lh[h];
-    float4 r;
-    r.x = __fdiv_rn(O[i].x, L);
-    r.y = __fdiv_rn(O[i].y, L);
-    r.z = __fdiv_rn(O[i].z, L);
-    r.w = __fdiv_rn(O[i].w, L);
-    reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD)[t + 256 * i] = r;
+    if (t + 256 * i < NV) {
+      const int h = h0 + (4 * (t + 256 * i)) / HD;
+      const float L = Lh[h];
+      float4 r;
+      r.x = __fdiv_rn(O[i].x, L);
+      r.y = __fdiv_rn(O[i].y, L);
+      r.z = __fdiv_rn(O[i].z, L);
+      r.w = __fdiv_rn(O[i].w, L);
+      reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD + (size_t)h0 * HD)[t + 256 * i] = r;
+    }
   }
-  if (t == 0) a.counter[c] = 0;
+  if (t == 0) *cnt = 0;
 }
 
-template <int HD>
+template <int HD, int NHL>
 static size_t attn_decode_smem() {
-  return ((size_t)ATT_BLK * HD + 8 * HD + HD + 2 * 8 * ATT_BLK + 8) * 4 + 16;
+  return ((size_t)ATT_BLK * HD + NHL * HD + HD + 2 * NHL * ATT_BLK + 8) * 4 + 16;
 }
 
-template <int HD>
+template <int HD, int NHL>
 static cudaError_t launch_attn_decode_t(const AttnDec &a, cudaStream_t st, bool pdl) {
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)attn_decode_smem<HD>());
-    cudaFuncSetAttribute(k_attn_decode<HD>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(k_attn_decode<HD, NHL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)attn_decode_smem<HD, NHL>());
+    cudaFuncSetAttribute(k_attn_decode<HD, NHL>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr_set = true;
   }
-  return launch_k(k_attn_decode<HD>, dim3(a.cols, a.max_blocks), dim3(256), attn_decode_smem<HD>(),
-                  st, pdl, a);
+  return launch_k(k_attn_decode<HD, NHL>, dim3(a.cols, a.max_blocks, 8 / NHL), dim3(256),
+                  attn_decode_smem<HD, NHL>(), st, pdl, a);
 }
 
 cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl) {
   // The merge keeps three factors per (block, head) in the 64-row V buffer.
   if ((size_t)3 * a.max_blocks * 8 + 8 > (size_t)ATT_BLK * a.hd) return cudaErrorInvalidValue;
-  if (a.hd == 256) return launch_attn_decode_t<256>(a, st, pdl);
-  if (a.hd == 512) return launch_attn_decode_t<512>(a, st, pdl);
+  // Few columns: one CTA per (column, block, head) spreads a latency-bound step over more SMs;
+  // a wide batch keeps all 8 heads of a block in one CTA (the V block is staged once for them).
+  const bool split = a.cols * a.max_blocks <= 64;
+  if (a.hd == 256) return split ? launch_attn_decode_t<256, 1>(a, st, pdl) : launch_attn_decode_t<256, 8>(a, st, pdl);
+  if (a.hd == 512) return split ? launch_attn_decode_t<512, 1>(a, st, pdl) : launch_attn_decode_t<512, 8>(a, st, pdl);
   return cudaErrorInvalidValue;
 }
 
@@ -1915,6 +1965,7 @@ k_argmax_final(const float *part_val, const int32_t *part_idx, int n_parts, int3
   __shared__ int si[8];
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(3004);
   const int c = blockIdx.x, t = threadIdx.x, lane = t & 31;
   float bv = -FLT_MAX;
   int bi = 0x7fffffff;
@@ -1949,6 +2000,7 @@ cudaError_t launch_argmax_final(const float *part_val, const int32_t *part_idx, 
 __global__ void k_advance(int32_t *pos, int cols) {
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(3005);
   int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c < cols) pos[c] += 1;
 }

@@ -78,6 +78,10 @@ int gemv_stream_partition(GemvArgs &a, int sms);
 cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, bool pdl);
 // Nonzero when a bounded device wait gave up since the last call (then cleared).
 int device_error_take();
+#ifdef G4_TRACE
+// Diagnostic build only: the (kernel id, time) records since the last call, then cleared.
+int trace_take(unsigned long long *out, int max_records);
+#endif
 
 // A quantized linear launch (the streaming kernel, or the f32 path when in_scale is 0).
 // Calibrated launches need gemv_stream_partition first.
@@ -179,7 +183,7 @@ struct AttnDec {
   float *cache; size_t seq_stride;   // this layer's (or its producer's) cache
   ColRefs refs;
   float *part_o; float *part_m; float *part_l;
-  int32_t *counter;                  // [cols]
+  int32_t *counter;                  // [cols][8]
   float *out;                        // [cols, 8 * hd]
   float eps;
 };

@@ -480,8 +480,8 @@ static int alloc_runtime(g4_ctx *ctx) {
   ctx->ffn_max = (ffn + 15) & ~15;
   CK(cudaMalloc(&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
   CK(cudaMalloc(&ctx->codes_ple, (size_t)maxc * ctx->PD));
-  CK(cudaMalloc(&ctx->att_count, (size_t)maxc * 4));
-  CK(cudaMemset(ctx->att_count, 0, (size_t)maxc * 4));
+  CK(cudaMalloc(&ctx->att_count, (size_t)maxc * 8 * 4));
+  CK(cudaMemset(ctx->att_count, 0, (size_t)maxc * 8 * 4));
   ctx->head_cols = std::min(maxc, std::max(ctx->cfg.max_seqs, 1));
   if ((rc = take(&ctx->logits, (size_t)ctx->head_cols * ctx->V))) return rc;
   CK(cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, ctx->dev));
@@ -548,6 +548,16 @@ extern "C" int g4_ctx_create(int cuda_device, const g4_config *cfg_in, g4_ctx **
 }
 
 extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
+#ifdef G4_TRACE
+  if (const char *path = getenv("G4_TRACE_FILE")) {
+    std::vector<unsigned long long> rec(2 << 15);
+    const int n = trace_take(rec.data(), 1 << 15);
+    if (FILE *f = fopen(path, "w")) {
+      for (int i = 0; i < n; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
+      fclose(f);
+    }
+  }
+#endif
   if (!ctx) return;
   cudaSetDevice(ctx->dev);
   if (ctx->st) cudaStreamSynchronize(ctx->st);
@@ -1316,7 +1326,7 @@ static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
   CK(cudaStreamSynchronize(ctx->st));
   if (device_error_take() > 0 || gemm_error_take() > 0) {
     // A block that gave up may have left its column's finished-block count behind.
-    cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 4, ctx->st);
+    cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 8 * 4, ctx->st);
     cudaStreamSynchronize(ctx->st);
     return fail(ctx, G4_ERR_TIMEOUT, "a bounded device wait gave up (a bulk copy never completed)");
   }
