@@ -21,6 +21,8 @@
 #include "../../include/g4.h"
 #include "g4_device.cuh"
 #include "g4_kernels.cuh"
+#include "g4_persist.cuh"
+#include "g4_gemv.cuh"
 
 using namespace g4;
 
@@ -120,6 +122,15 @@ struct g4_ctx {
   float *cur_pv = nullptr;
   int32_t *cur_pi = nullptr;
   int cur_parts = 0;
+  // Persistent B=1 decode: the phase list per advance flag (built from record_step in plan
+  // mode), its grid, and the grid-barrier words.
+  std::vector<PPhase> *plan = nullptr;    // plan mode: record_step appends phases here
+  bool plan_ok = true;
+  PPhase *d_plan[2] = {nullptr, nullptr};
+  int plan_n[2] = {0, 0};
+  int plan_state[2] = {0, 0};              // 0 not built, 1 built, -1 not eligible
+  int persist_grid = 0;
+  unsigned *pbar = nullptr;
   uint8_t *codes_mlp = nullptr;     // down_proj input codes [maxc][ffn_max]
   uint8_t *codes_ple = nullptr;     // per_layer_projection input codes [maxc][PD]
   int ffn_max = 0;
@@ -215,6 +226,7 @@ extern "C" int g4_config_default(g4_config *cfg) {
   cfg->use_graphs = 1;
   cfg->ple_slice_bytes = 0;
   cfg->gemm_min_columns = 16;
+  cfg->persistent_decode = 0;
   return G4_OK;
 }
 
@@ -477,6 +489,9 @@ static int alloc_runtime(g4_ctx *ctx) {
   CK(cudaMalloc(&ctx->gpv, (size_t)maxc * ctx->gparts * 4));
   CK(cudaMalloc(&ctx->gpi, (size_t)maxc * ctx->gparts * 4));
   ctx->gemm_min_cols = ctx->cfg.gemm_min_columns > 0 ? ctx->cfg.gemm_min_columns : 16;
+  CK(cudaMalloc(&ctx->pbar, 2 * sizeof(unsigned)));
+  CK(cudaMemset(ctx->pbar, 0, 2 * sizeof(unsigned)));
+  ctx->persist_grid = ctx->cfg.persistent_decode ? persist_max_grid(ctx->dev) : 0;
   ctx->ffn_max = (ffn + 15) & ~15;
   CK(cudaMalloc(&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
   CK(cudaMalloc(&ctx->codes_ple, (size_t)maxc * ctx->PD));
@@ -554,6 +569,8 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
     const int n = trace_take(rec.data(), 1 << 15);
     if (FILE *f = fopen(path, "w")) {
       for (int i = 0; i < n; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
+      const int m = persist_trace_take(rec.data(), 1 << 15);
+      for (int i = 0; i < m; i++) fprintf(f, "%llu %llu\n", 100000000ull + rec[2 * i], rec[2 * i + 1]);
       fclose(f);
     }
   }
@@ -579,6 +596,8 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   cudaFree(ctx->gpi);
   cudaFree(ctx->gacc);
   cudaFree(ctx->gcnt);
+  cudaFree(ctx->pbar);
+  for (int i = 0; i < 2; i++) cudaFree(ctx->d_plan[i]);
   cudaFree(ctx->codes_ple);
   cudaFree(ctx->d_step);
   cudaFree(ctx->d_tok_out);
@@ -710,6 +729,7 @@ extern "C" int g4_init_random(g4_ctx *ctx, uint64_t seed) {
   ctx->weights_ready = true;
   for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
   ctx->graphs.clear();
+  ctx->plan_state[0] = ctx->plan_state[1] = 0;
   return G4_OK;
 }
 
@@ -811,6 +831,7 @@ extern "C" int g4_set_scalar(g4_ctx *ctx, const char *name, float value) {
   *slot = value;
   for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
   ctx->graphs.clear();
+  ctx->plan_state[0] = ctx->plan_state[1] = 0;
   return G4_OK;
 }
 
@@ -930,8 +951,79 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   return G4_OK;
 }
 
+// Plan mode: the launch becomes one phase of the persistent decode kernel (one column), its rows
+// partitioned over the persistent grid; shapes the kernel does not cover mark the plan ineligible.
+static int plan_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs a, bool head) {
+  const Linear *l0 = segs.begin()->lin;
+  const int bits = l0->bits, K = l0->K, row_bytes = K * bits / 8;
+  const int rs = gs_row_split(row_bytes);
+  bool ok = cols == 1 && row_bytes <= persist_slot_bytes() && row_bytes % rs == 0 &&
+            row_bytes / rs <= 1024 && (row_bytes / rs) % 16 == 0 && K <= 6144;
+  a.K = K;
+  a.cols = 1;
+  a.nseg = 0;
+  for (auto &s : segs) {
+    GemvSeg &g = a.seg[a.nseg++];
+    g.w = s.lin->w;
+    g.s = s.lin->s;
+    g.y = s.y;
+    g.acc_out = nullptr;
+    g.N = s.lin->N;
+    g.in_scale = s.lin->in_scale;
+    g.out_scale = s.lin->out_scale;
+    ok = ok && s.lin->bits == bits && s.lin->K == K && s.lin->in_scale != 0.0f;
+  }
+  // The segments' CTA counts round up; shrink the target until they fit the persistent grid.
+  const int P = ctx->persist_grid;
+  for (int target = P; target > 0; target--) {
+    gemv_stream_partition(a, target);
+    if (a.n_blocks_total <= P) break;
+  }
+  int max_rows = 0;
+  for (int i = 0; i < a.nseg; i++) {
+    const int nb = a.pair ? a.n_blocks_total
+                          : (i + 1 < a.nseg ? a.seg[i + 1].block_begin : a.n_blocks_total) - a.seg[i].block_begin;
+    max_rows = std::max(max_rows, (a.seg[i].N + nb - 1) / nb);
+  }
+  PPhase ph;
+  memset(&ph, 0, sizeof(ph));
+  ph.kind = PK_GEMV;
+  ph.bits = bits;
+  ph.rs = rs;
+  const int pro = a.pro, epi = head ? EPI_HEAD : a.epi;
+  if (bits == 4 && pro == PRO_NORM && epi == EPI_Y) ph.variant = PV_Q0;
+  else if (bits == 4 && pro == PRO_JOIN && epi == EPI_Y) ph.variant = PV_QKV;
+  else if (bits == 4 && pro == PRO_X && epi == EPI_Y) ph.variant = PV_O1;
+  else if (bits == 4 && pro == PRO_JOIN && epi == EPI_GELU_CODES && a.pair) ph.variant = PV_GATEUP;
+  else if (bits == 4 && pro == PRO_CODES && epi == EPI_Y) ph.variant = PV_DOWN;
+  else if (bits == 8 && pro == PRO_NORMRES && epi == EPI_GELU_CODES && !a.pair) ph.variant = PV_PLEG;
+  else if (bits == 8 && pro == PRO_CODES && epi == EPI_Y) ph.variant = PV_PLEP;
+  else if (bits == 4 && pro == PRO_JOIN && epi == EPI_HEAD) ph.variant = PV_HEAD;
+  else ok = false;
+  if (epi == EPI_GELU_CODES) ok = ok && max_rows <= 64;
+  ok = ok && max_rows <= (a.pair ? persist_max_rows() / 2 : persist_max_rows());
+  for (int i = 0; i < 4; i++) a.prefetch_bytes[i] = 0;
+  if (head) {
+    a.head = 1;
+    a.logits = ctx->logits;
+    a.ld_logits = ctx->V;
+    a.part_val = ctx->head_pv;
+    a.part_idx = ctx->head_pi;
+    ok = ok && a.n_blocks_total <= ctx->head_blocks * ctx->head_cols;
+    ctx->cur_pv = ctx->head_pv;
+    ctx->cur_pi = ctx->head_pi;
+    ctx->cur_parts = a.n_blocks_total;
+  }
+  ph.g = a;
+  if (!ok) ctx->plan_ok = false;
+  ctx->plan->push_back(ph);
+  ctx->launches++;
+  return G4_OK;
+}
+
 static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs proto,
                       bool head = false, std::initializer_list<WRef> prefetch = {}) {
+  if (ctx->plan) return plan_linear(ctx, segs, cols, proto, head);
   if (gemm_eligible(ctx, segs, cols, proto)) return run_linear_gemm(ctx, segs, cols, proto, head);
   const Linear *l0 = segs.begin()->lin;
   for (int c0 = 0; c0 < cols; c0 += 8) {
@@ -999,16 +1091,34 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
   int32_t *d_seq = ctx->d_step, *d_pos = ctx->d_step + ctx->maxc, *d_tok = ctx->d_step + 2 * ctx->maxc;
   ctx->launches = 0;
   // ---- embed phase (planEmbed, src/plan.ts:727-736)
-  CK(launch_embed(d_tok, cols, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
-                  (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H,
-                  ctx->ple_cols, PD, ctx->res[0], ctx->ple_id, ctx->st, true));
-  ctx->launches++;
-  CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, H, cols,
-                       (float)std::pow((double)H, -0.5), ctx->st, true));
-  ctx->launches += cols > 8 ? 1 : 1;
-  CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, ctx->NL, PD,
-                        eps, (float)0.7071067811865476, ctx->st, true));
-  ctx->launches++;
+  if (ctx->plan) {
+    PPhase e;
+    memset(&e, 0, sizeof(e));
+    e.kind = PK_EMBED;
+    e.em = {d_tok, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
+            (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H, ctx->ple_cols, PD,
+            ctx->res[0], ctx->ple_id};
+    ctx->plan->push_back(e);
+    PPhase d;
+    memset(&d, 0, sizeof(d));
+    d.kind = PK_DENSE;
+    d.de = {ctx->plmp_w, ctx->res[0], ctx->ple_proj, ctx->ple_cols, H, (float)std::pow((double)H, -0.5)};
+    ctx->plan->push_back(d);
+    PPhase c;
+    memset(&c, 0, sizeof(c));
+    c.kind = PK_COMBINE;
+    c.co = {ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, ctx->NL, PD, eps, (float)0.7071067811865476};
+    ctx->plan->push_back(c);
+  } else {
+    CK(launch_embed(d_tok, cols, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
+                    (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H,
+                    ctx->ple_cols, PD, ctx->res[0], ctx->ple_id, ctx->st, true));
+    CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, H, cols,
+                         (float)std::pow((double)H, -0.5), ctx->st, true));
+    CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, ctx->NL, PD,
+                          eps, (float)0.7071067811865476, ctx->st, true));
+  }
+  ctx->launches += 3;
   int cur = 0;
   int rc;
   for (int L = 0; L < n_layers; L++) {
@@ -1071,7 +1181,16 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       ad.counter = ctx->att_count;
       ad.out = ctx->attn;
       ad.eps = eps;
-      CK(launch_attn_decode(ad, ctx->st, true));
+      if (ctx->plan) {
+        PPhase ph;
+        memset(&ph, 0, sizeof(ph));
+        ph.kind = PK_ATTN;
+        ph.at = ad;
+        if (cols != 1 || (hd != 256 && hd != 512)) ctx->plan_ok = false;
+        ctx->plan->push_back(ph);
+      } else {
+        CK(launch_attn_decode(ad, ctx->st, true));
+      }
       ctx->launches++;
     }
     // ---- attention prologue: q-norm-rope, kv-norm-rope-store (src/kernels/attnPrologue.ts)
@@ -1251,18 +1370,60 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     p.eps = eps;
     p.softcap = a.final_softcap;
     if ((rc = run_linear(ctx, {{&ctx->lm, nullptr}}, cols, p, true))) return rc;
-    CK(launch_argmax_final(ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, cols, d_tok,
-                           ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
-    ctx->launches++;
-    if (advance) {
-      CK(launch_advance(d_pos, cols, ctx->st, true));
-      ctx->launches++;
+    if (ctx->plan) {
+      PPhase m;
+      memset(&m, 0, sizeof(m));
+      m.kind = PK_ARGMAX;
+      m.am = {ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, d_tok, ctx->d_tok_out, ctx->d_val_out, d_pos,
+              advance ? 1 : 0};
+      ctx->plan->push_back(m);
+    } else {
+      CK(launch_argmax_final(ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, cols, d_tok,
+                             ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
+      if (advance) CK(launch_advance(d_pos, cols, ctx->st, true));
     }
+    ctx->launches += advance ? 2 : 1;
   }
   return G4_OK;
 }
 
+// The persistent decode step for one column: the phase list is built once per advance flag (from
+// record_step in plan mode) and launched as one cooperative kernel; 0 when not eligible.
+static int try_persist(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance, bool *done) {
+  *done = false;
+  if (cols != 1 || !head || n_layers != ctx->NL || ctx->persist_grid <= 0) return G4_OK;
+  const int k = advance ? 1 : 0;
+  if (ctx->plan_state[k] == 0) {
+    std::vector<PPhase> plan;
+    ctx->plan = &plan;
+    ctx->plan_ok = true;
+    int rc = record_step(ctx, cols, n_layers, head, advance);
+    ctx->plan = nullptr;
+    if (rc) return rc;
+    ctx->plan_state[k] = -1;
+    if (ctx->plan_ok && !plan.empty()) {
+      for (size_t i = 0; i + 1 < plan.size(); i++) plan[i].sync_after = 1;
+      cudaFree(ctx->d_plan[k]);
+      ctx->d_plan[k] = nullptr;
+      CK(cudaMalloc(&ctx->d_plan[k], plan.size() * sizeof(PPhase)));
+      CK(cudaMemcpyAsync(ctx->d_plan[k], plan.data(), plan.size() * sizeof(PPhase),
+                         cudaMemcpyHostToDevice, ctx->st));
+      CK(cudaStreamSynchronize(ctx->st));
+      ctx->plan_n[k] = (int)plan.size();
+      ctx->plan_state[k] = 1;
+    }
+  }
+  if (ctx->plan_state[k] != 1) return G4_OK;
+  CK(launch_decode_persist(ctx->d_plan[k], ctx->plan_n[k], ctx->pbar, ctx->persist_grid, ctx->st));
+  ctx->launches = 1;
+  *done = true;
+  return G4_OK;
+}
+
 static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false) {
+  bool done = false;
+  int prc = try_persist(ctx, cols, n_layers, head, advance, &done);
+  if (prc || done) return prc;
   if (!ctx->cfg.use_graphs) return record_step(ctx, cols, n_layers, head, advance);
   GraphKey key{cols, n_layers, head ? 1 : 0, advance ? 1 : 0};
   auto it = ctx->graphs.find(key);
@@ -1324,9 +1485,11 @@ static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos,
 static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
   CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)cols * 4, cudaMemcpyDeviceToHost, ctx->st));
   CK(cudaStreamSynchronize(ctx->st));
-  if (device_error_take() > 0 || gemm_error_take() > 0) {
-    // A block that gave up may have left its column's finished-block count behind.
+  if (device_error_take() > 0 || gemm_error_take() > 0 || persist_error_take() > 0) {
+    // A block that gave up may have left its column's finished-block count (or the persistent
+    // kernel its barrier words) behind.
     cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 8 * 4, ctx->st);
+    cudaMemsetAsync(ctx->pbar, 0, 2 * sizeof(unsigned), ctx->st);
     cudaStreamSynchronize(ctx->st);
     return fail(ctx, G4_ERR_TIMEOUT, "a bounded device wait gave up (a bulk copy never completed)");
   }

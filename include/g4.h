@@ -97,10 +97,13 @@ typedef struct g4_config {
   uint64_t ple_slice_bytes;  /* 0: PLE table is one buffer; else the vocab-row slice cap */
   int32_t gemm_min_columns;  /* steps this wide or wider run their linears on the tcgen05 int8
                                 GEMM (prefill chunks, batched decode); 0: 16 */
+  int32_t persistent_decode; /* 1: a one-column decode step runs as one persistent cooperative
+                                kernel (grid barriers between phases, bit-identical); 0 (default):
+                                one launch per kernel, chained by programmatic dependent launch */
 } g4_config;
 
 /* Defaults: g4_arch_default, max_seqs 1, max_context 2048, max_step_columns 64, graphs on,
- * gemm_min_columns 16. */
+ * gemm_min_columns 16, persistent_decode 0. */
 int g4_config_default(g4_config *cfg);
 
 /*
