@@ -1074,21 +1074,29 @@ __global__ void __launch_bounds__(256) k_attn_merge(const AttnArgs a) {
 }
 
 // Prefill attention (a chunk of consecutive positions of one sequence): CTA = QT consecutive
-// queries x 8 heads. It walks the 64-position blocks in ascending order, reading each block's K
-// (scores) and V (staged in shared memory) once for all QT x 8 (query, head) pairs, and folds each
-// block into a running (M, L, O) right away. Per (query, block) the arithmetic is k_attn_blocks'
-// (four-accumulator scores, block max, exp, ascending l and o chains) and the fold is
-// k_attn_merge's in the same ascending block order, so the result is bit-identical.
+// queries x 8 heads = NP (query, head) pairs. It walks the 64-position blocks in ascending order
+// and folds each block into a running (M, L, O) right away. Per (query, block) the arithmetic is
+// k_attn_blocks' (four-accumulator scores, block max, exp, ascending l and o chains) and the fold
+// is k_attn_merge's in the same ascending block order, so the result is bit-identical.
+//
+// Register micro-tiles keep the shared-memory traffic below the FMA rate: a score thread owns
+// accumulator m (chunks m, m + 4, ...) of PA pairs x 8 positions, loading PA q and 8 K vectors
+// per chunk for PA x 8 x 4 FMAs; a PV thread owns 8 pairs x 2 vec4 columns. K and V rows are
+// staged KVR at a time (all 64 at head dim 256, 32 at 512) in one padded buffer; the positions
+// of score group jg are jg, jg + 8, ... so the padded rows a warp reads fall in distinct banks.
 template <int HD>
-__global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
+__global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
   constexpr int NH = 8, NC = HD / 4, QT = 2048 / HD, NP = QT * NH;   // pairs per CTA
-  constexpr int G = 256 / NC, PPT = NP / G;                         // PV: pairs per thread
-  constexpr bool KSM = HD <= 256;              // K rows staged in shared memory too
+  constexpr int PA = NP / 8;                   // score micro-tile pairs (8 pair groups)
+  constexpr int KVR = HD <= 256 ? 64 : 32;     // K / V rows staged at a time
+  constexpr int LDK = HD + 4;                  // padded row (floats)
+  constexpr int PB = 8, DB = 2;                // PV micro-tile: pairs x vec4 columns
+  constexpr int NDG = NC / DB;                 // PV column groups
+  static_assert((NP / PB) * NDG == 256, "PV tiling covers the CTA");
   extern __shared__ __align__(16) float sm[];
-  float *qs = sm;                              // [QT][NH][HD]
-  float *vs = qs + NP * HD;                    // [64][HD]
-  float *ks = vs + ATT_BLK * HD;               // [64][HD] when KSM
-  float *ss = ks + (KSM ? ATT_BLK * HD : 0);   // [NP][64] scores, then probabilities
+  float *qs = sm;                              // [NP][HD]
+  float *kv = qs + NP * HD;                    // [KVR][LDK]
+  float *ss = kv + KVR * LDK;                  // [NP][64] scores, then probabilities
   float *mb = ss + NP * ATT_BLK;               // [NP] block max
   float *lb = mb + NP;                         // [NP] block sum
   float *RM = lb + NP;                         // [NP] running max
@@ -1100,7 +1108,7 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
   int *qlo = qp + QT;                          // [QT] window start
   grid_launch_dependents();
   grid_wait();
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int t = threadIdx.x;
   const int c0 = blockIdx.x * QT;
   const int nq = min(QT, a.cols - c0);
   const int seq = a.refs.seq ? a.refs.seq[c0] : 0;
@@ -1127,106 +1135,126 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
     ulo = min(ulo, qlo[q]);
     uhi = max(uhi, qp[q]);
   }
-  // PV thread: float4 chunk dc of pairs g * PPT .. + PPT - 1.
-  const int dc = t % NC, g = t / NC;
-  float4 O[PPT];
+  // Score thread: accumulator m, pair group pg (pairs pg*PA ..), position group jg.
+  const int m = t & 3, mt = t >> 2, pg = mt >> 3, jg = mt & 7;
+  // PV thread: pairs pb*PB .., vec4 columns dg + NDG * d.
+  const int pb = t / NDG, dg = t % NDG;
+  float4 O[PB][DB];
 #pragma unroll
-  for (int i = 0; i < PPT; i++) O[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < PB; i++)
+#pragma unroll
+    for (int d = 0; d < DB; d++) O[i][d] = make_float4(0.f, 0.f, 0.f, 0.f);
 
   for (int b = ulo / ATT_BLK; b * ATT_BLK <= uhi; b++) {
     const int jb = b * ATT_BLK;
     const int jlo = max(jb, ulo), jhi = min(jb + ATT_BLK - 1, uhi);
-    // V rows of the union range; rows outside it are zero (their probabilities are zero too).
-    for (int i = t; i < ATT_BLK * NC; i += 256) {
-      const int jl = i / NC, k4 = i - jl * NC, j = jb + jl;
-      const bool in = j >= jlo && j <= jhi;
-      reinterpret_cast<float4 *>(vs)[i] =
-          in ? reinterpret_cast<const float4 *>(V + (size_t)j * HD)[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (KSM)
-        reinterpret_cast<float4 *>(ks)[i] =
-            in ? reinterpret_cast<const float4 *>(K + (size_t)j * HD)[k4] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    if (KSM) __syncthreads();
-    // Scores: thread (jl, m) runs accumulator m of position jl for every (query, head) pair.
-    {
-      const int jl = t >> 2, m = t & 3, j = jb + jl;
-      const bool inr = j >= jlo && j <= jhi;
-      float acc[NP];
-#pragma unroll
-      for (int i = 0; i < NP; i++) acc[i] = 0.0f;
-      if (inr) {
-        const float4 *kr = reinterpret_cast<const float4 *>(KSM ? ks + (size_t)jl * HD : K + (size_t)j * HD);
-        constexpr int PER = NC / 4, BATCH = KSM ? 1 : 8;   // chunks per thread; global loads 8 at a time
+    // ---- scores, KVR rows of K at a time
 #pragma unroll 1
-        for (int i0 = 0; i0 < PER; i0 += BATCH) {
-          float4 kb[BATCH];
+    for (int r0 = 0; r0 < ATT_BLK; r0 += KVR) {
+      __syncthreads();   // the previous stage's rows are no longer read
+      for (int i = t; i < KVR * NC; i += 256) {
+        const int r = i / NC, k4 = i - r * NC, j = jb + r0 + r;
+        reinterpret_cast<float4 *>(kv + (size_t)r * LDK)[k4] =
+            (j >= jlo && j <= jhi) ? reinterpret_cast<const float4 *>(K + (size_t)j * HD)[k4]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      __syncthreads();
+      constexpr int JB = KVR / 8;               // this stage's positions per score thread
+      float acc[PA][JB];
 #pragma unroll
-          for (int u = 0; u < BATCH; u++) kb[u] = kr[m + 4 * (i0 + u)];
+      for (int x = 0; x < PA; x++)
 #pragma unroll
-          for (int u = 0; u < BATCH; u++) {
-            const int cc = m + 4 * (i0 + u);
+        for (int y = 0; y < JB; y++) acc[x][y] = 0.0f;
+#pragma unroll 2
+      for (int cc = m; cc < NC; cc += 4) {
+        float4 qv[PA], kk[JB];
 #pragma unroll
-            for (int i = 0; i < NP; i++) {
-              const float4 q4 = reinterpret_cast<const float4 *>(qs + i * HD)[cc];
-              float v = acc[i];
-              v = fmaf(q4.x, kb[u].x, v);
-              v = fmaf(q4.y, kb[u].y, v);
-              v = fmaf(q4.z, kb[u].z, v);
-              v = fmaf(q4.w, kb[u].w, v);
-              acc[i] = v;
-            }
+        for (int x = 0; x < PA; x++) qv[x] = reinterpret_cast<const float4 *>(qs + (size_t)(pg * PA + x) * HD)[cc];
+#pragma unroll
+        for (int y = 0; y < JB; y++) kk[y] = reinterpret_cast<const float4 *>(kv + (size_t)(jg + 8 * y) * LDK)[cc];
+#pragma unroll
+        for (int x = 0; x < PA; x++)
+#pragma unroll
+          for (int y = 0; y < JB; y++) {
+            float v = acc[x][y];
+            v = fmaf(qv[x].x, kk[y].x, v);
+            v = fmaf(qv[x].y, kk[y].y, v);
+            v = fmaf(qv[x].z, kk[y].z, v);
+            v = fmaf(qv[x].w, kk[y].w, v);
+            acc[x][y] = v;
           }
+      }
+#pragma unroll
+      for (int x = 0; x < PA; x++)
+#pragma unroll
+        for (int y = 0; y < JB; y++) {
+          const float v1 = __fadd_rn(acc[x][y], __shfl_xor_sync(0xffffffffu, acc[x][y], 1));
+          const float v2 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, 2));
+          const int pi = pg * PA + x, q = pi / NH, jl = r0 + jg + 8 * y, j = jb + jl;
+          if (m == 0) ss[pi * ATT_BLK + jl] = (j >= qlo[q] && j <= qp[q]) ? v2 : -FLT_MAX;
+        }
+    }
+    __syncthreads();
+    // ---- block max and probabilities per pair (warp w: pairs w, w + 8, ...)
+    {
+      const int lane = t & 31, warp = t >> 5;
+      for (int i = warp; i < NP; i += 8) {
+        const int q = i / NH;
+        const float s0 = ss[i * ATT_BLK + lane], s1 = ss[i * ATT_BLK + lane + 32];
+        float mx = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int ja = jb + lane, jc = ja + 32;
+        ss[i * ATT_BLK + lane] = (ja >= qlo[q] && ja <= qp[q]) ? g4_exp(__fsub_rn(s0, mx)) : 0.0f;
+        ss[i * ATT_BLK + lane + 32] = (jc >= qlo[q] && jc <= qp[q]) ? g4_exp(__fsub_rn(s1, mx)) : 0.0f;
+        if (lane == 0) mb[i] = mx;
+      }
+    }
+    // ---- weighted V and the probability sums, ascending j, KVR rows of V at a time
+    float4 o[PB][DB];
+    float l[PB];
+#pragma unroll
+    for (int i = 0; i < PB; i++) {
+      l[i] = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DB; d++) o[i][d] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll 1
+    for (int r0 = 0; r0 < ATT_BLK; r0 += KVR) {
+      __syncthreads();   // scores / the previous V stage are no longer read
+      const int slo = max(jlo - jb, r0), shi = min(jhi - jb, r0 + KVR - 1);
+      for (int i = t; i < KVR * NC; i += 256) {
+        const int r = i / NC, k4 = i - r * NC, jl = r0 + r;
+        reinterpret_cast<float4 *>(kv + (size_t)r * LDK)[k4] =
+            (jl >= slo && jl <= shi) ? reinterpret_cast<const float4 *>(V + (size_t)(jb + jl) * HD)[k4]
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      __syncthreads();
+#pragma unroll 2
+      for (int jl = slo; jl <= shi; jl++) {
+        float4 v4[DB];
+#pragma unroll
+        for (int d = 0; d < DB; d++) v4[d] = reinterpret_cast<const float4 *>(kv + (size_t)(jl - r0) * LDK)[dg + NDG * d];
+#pragma unroll
+        for (int i = 0; i < PB; i++) {
+          const float pj = ss[(pb * PB + i) * ATT_BLK + jl];
+#pragma unroll
+          for (int d = 0; d < DB; d++) {
+            o[i][d].x = fmaf(pj, v4[d].x, o[i][d].x);
+            o[i][d].y = fmaf(pj, v4[d].y, o[i][d].y);
+            o[i][d].z = fmaf(pj, v4[d].z, o[i][d].z);
+            o[i][d].w = fmaf(pj, v4[d].w, o[i][d].w);
+          }
+          l[i] = __fadd_rn(l[i], pj);
         }
       }
+    }
+    if (dg == 0) {
 #pragma unroll
-      for (int i = 0; i < NP; i++) {
-        const float v1 = __fadd_rn(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], 1));
-        const float v2 = __fadd_rn(v1, __shfl_xor_sync(0xffffffffu, v1, 2));
-        const int q = i / NH;
-        if (m == 0) ss[i * ATT_BLK + jl] = (j >= qlo[q] && j <= qp[q]) ? v2 : -FLT_MAX;
-      }
+      for (int i = 0; i < PB; i++) lb[pb * PB + i] = l[i];
     }
     __syncthreads();
-    // Block max and probabilities per pair (warp w: pairs w, w + 8, ...).
-    for (int i = warp; i < NP; i += 8) {
-      const int q = i / NH;
-      const float s0 = ss[i * ATT_BLK + lane], s1 = ss[i * ATT_BLK + lane + 32];
-      float mx = fmaxf(s0, s1);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const int ja = jb + lane, jc = ja + 32;
-      ss[i * ATT_BLK + lane] = (ja >= qlo[q] && ja <= qp[q]) ? g4_exp(__fsub_rn(s0, mx)) : 0.0f;
-      ss[i * ATT_BLK + lane + 32] = (jc >= qlo[q] && jc <= qp[q]) ? g4_exp(__fsub_rn(s1, mx)) : 0.0f;
-      if (lane == 0) mb[i] = mx;
-    }
-    __syncthreads();
-    // Weighted V of the block and its probability sum, ascending j (zeros outside a query's range).
-    float4 o[PPT];
-    float l[PPT];
-#pragma unroll
-    for (int i = 0; i < PPT; i++) {
-      o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      l[i] = 0.0f;
-    }
-#pragma unroll 4
-    for (int jl = jlo - jb; jl <= jhi - jb; jl++) {
-      const float4 v4 = reinterpret_cast<const float4 *>(vs + (size_t)jl * HD)[dc];
-#pragma unroll
-      for (int i = 0; i < PPT; i++) {
-        const float pj = ss[(g * PPT + i) * ATT_BLK + jl];
-        o[i].x = fmaf(pj, v4.x, o[i].x);
-        o[i].y = fmaf(pj, v4.y, o[i].y);
-        o[i].z = fmaf(pj, v4.z, o[i].z);
-        o[i].w = fmaf(pj, v4.w, o[i].w);
-        l[i] = __fadd_rn(l[i], pj);
-      }
-    }
-    if (dc == 0) {
-#pragma unroll
-      for (int i = 0; i < PPT; i++) lb[g * PPT + i] = l[i];
-    }
-    __syncthreads();
-    // The fold of this block into each pair's running (M, L): k_attn_merge's formula.
+    // ---- the fold of this block into each pair's running (M, L): k_attn_merge's formula
     for (int i = t; i < NP; i += 256) {
       const int q = i / NH;
       const bool valid = jb <= qp[q] && jb + ATT_BLK - 1 >= qlo[q];
@@ -1248,40 +1276,45 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
     }
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < PPT; i++) {
-      const int pi = g * PPT + i, md = mode[pi];
-      if (md == 1) {
-        O[i] = o[i];
-      } else if (md == 2) {
-        const float e1 = ea[pi], e2 = ec[pi];
-        O[i].x = __fadd_rn(__fmul_rn(O[i].x, e1), __fmul_rn(o[i].x, e2));
-        O[i].y = __fadd_rn(__fmul_rn(O[i].y, e1), __fmul_rn(o[i].y, e2));
-        O[i].z = __fadd_rn(__fmul_rn(O[i].z, e1), __fmul_rn(o[i].z, e2));
-        O[i].w = __fadd_rn(__fmul_rn(O[i].w, e1), __fmul_rn(o[i].w, e2));
+    for (int i = 0; i < PB; i++) {
+      const int pi = pb * PB + i, md = mode[pi];
+#pragma unroll
+      for (int d = 0; d < DB; d++) {
+        if (md == 1) {
+          O[i][d] = o[i][d];
+        } else if (md == 2) {
+          const float e1 = ea[pi], e2 = ec[pi];
+          O[i][d].x = __fadd_rn(__fmul_rn(O[i][d].x, e1), __fmul_rn(o[i][d].x, e2));
+          O[i][d].y = __fadd_rn(__fmul_rn(O[i][d].y, e1), __fmul_rn(o[i][d].y, e2));
+          O[i][d].z = __fadd_rn(__fmul_rn(O[i][d].z, e1), __fmul_rn(o[i][d].z, e2));
+          O[i][d].w = __fadd_rn(__fmul_rn(O[i][d].w, e1), __fmul_rn(o[i][d].w, e2));
+        }
       }
     }
-    __syncthreads();
   }
+  __syncthreads();
 #pragma unroll
-  for (int i = 0; i < PPT; i++) {
-    const int pi = g * PPT + i, q = pi / NH, h = pi % NH;
+  for (int i = 0; i < PB; i++) {
+    const int pi = pb * PB + i, q = pi / NH, h = pi % NH;
     if (q < nq) {
       const float L = RL[pi];
-      float4 r;
-      r.x = __fdiv_rn(O[i].x, L);
-      r.y = __fdiv_rn(O[i].y, L);
-      r.z = __fdiv_rn(O[i].z, L);
-      r.w = __fdiv_rn(O[i].w, L);
-      reinterpret_cast<float4 *>(a.out + (size_t)(c0 + q) * NH * HD + (size_t)h * HD)[dc] = r;
+#pragma unroll
+      for (int d = 0; d < DB; d++) {
+        float4 r;
+        r.x = __fdiv_rn(O[i][d].x, L);
+        r.y = __fdiv_rn(O[i][d].y, L);
+        r.z = __fdiv_rn(O[i][d].z, L);
+        r.w = __fdiv_rn(O[i][d].w, L);
+        reinterpret_cast<float4 *>(a.out + (size_t)(c0 + q) * NH * HD + (size_t)h * HD)[dg + NDG * d] = r;
+      }
     }
   }
 }
 
 template <int HD>
 static size_t attn_prefill_smem() {
-  constexpr int NP = (2048 / HD) * 8;
-  return ((size_t)NP * HD + (size_t)ATT_BLK * HD * (HD <= 256 ? 2 : 1) + (size_t)NP * ATT_BLK + 7 * NP +
-          2 * (2048 / HD)) * 4;
+  constexpr int NP = (2048 / HD) * 8, KVR = HD <= 256 ? 64 : 32;
+  return ((size_t)NP * HD + (size_t)KVR * (HD + 4) + (size_t)NP * ATT_BLK + 7 * NP + 2 * (2048 / HD)) * 4;
 }
 
 cudaError_t launch_attention_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
