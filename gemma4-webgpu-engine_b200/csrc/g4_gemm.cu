@@ -391,6 +391,254 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
   }
 }
 
+// Persistent form for many tiles (prefill): one CTA per SM loops over tiles (m-major order, so
+// the CTAs running at once share a token tile in L2). Warps: 0 TMA, 1 MMA + TMEM owner, 2-5 int4
+// unpack, 6-9 epilogue. Two TMEM accumulators of BN columns: the MMAs of tile i + 1 run while the
+// epilogue warps read tile i. Stage and accumulator barriers use running counters for their
+// phases; every wait is bounded.
+template <int BITS, int BN, int EPI>
+__global__ void __launch_bounds__(320, 1)
+    k_qgemm_persist(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                    const GemmArgs a) {
+  using S = GemmShape<BN, 4>;
+  constexpr int NS = S::STAGES;
+  extern __shared__ __align__(1024) uint8_t gsm_raw[];
+  uint8_t *gsm = gsm_raw + ((1024 - (smem_u32(gsm_raw) & 1023)) & 1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(gsm + S::BAR_OFF);
+  uint64_t *aready = full + NS;
+  uint64_t *empty = aready + NS;
+  uint64_t *acc_full = empty + NS;      // [2]
+  uint64_t *acc_empty = acc_full + 2;   // [2]
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  int *flags = reinterpret_cast<int *>(tslot + 2);
+  float *cand_v = reinterpret_cast<float *>(flags + 14);
+  int *cand_i = reinterpret_cast<int *>(cand_v + 4 * 32);
+  auto A = [&](int s) { return gsm + s * S::STAGE_BYTES; };
+  auto B = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES; };
+  auto P = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES + S::B_BYTES; };
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int KT = a.K / GM_BK;
+  const int n_tiles = (a.N + GM_BM - 1) / GM_BM, m_tiles = (a.M + BN - 1) / BN;
+  const int tiles = n_tiles * m_tiles;
+
+  if (t == 0) {
+    for (int s = 0; s < NS; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&aready[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_fence_init();
+    flags[0] = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  grid_launch_dependents();
+  grid_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t wbytes = BITS == 4 ? S::P_BYTES : S::A_BYTES;
+      uint32_t g = 0;
+      for (int tile = blockIdx.x; tile < tiles && !flags[0]; tile += gridDim.x) {
+        const int n0 = (tile % n_tiles) * GM_BM, m0 = (tile / n_tiles) * BN;
+        for (int kt = 0; kt < KT; kt++, g++) {
+          const int s = g % NS;
+          if (g >= (uint32_t)NS && !mbar_wait(&empty[s], ((g / NS) - 1) & 1)) {
+            atomicExch(&g4_gemm_error, 1);
+            flags[0] = 1;
+            break;
+          }
+          mbar_expect_tx(&full[s], wbytes + S::B_BYTES);
+          if (BITS == 4)
+            tma_load_2d(P(s), &tmW, kt * (GM_BK / 2), n0, &full[s]);
+          else
+            tma_load_2d(A(s), &tmW, kt * GM_BK, n0, &full[s]);
+          tma_load_2d(B(s), &tmX, kt * GM_BK, m0, &full[s]);
+        }
+      }
+      for (uint32_t q = g > (uint32_t)NS ? g - NS : 0; q < g; q++) mbar_wait(&full[q % NS], (q / NS) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_i8(BN);
+      uint32_t g = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < tiles && !flags[0]; tile += gridDim.x, lt++) {
+        const int b = lt & 1;
+        const uint32_t u = lt >> 1;
+        if (u >= 1 && !mbar_wait(&acc_empty[b], (u - 1) & 1)) {
+          atomicExch(&g4_gemm_error, 1);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int kt = 0; kt < KT; kt++, g++) {
+          const int s = g % NS;
+          uint64_t *ready = BITS == 4 ? &aready[s] : &full[s];
+          if (!mbar_wait(ready, (g / NS) & 1)) {
+            atomicExch(&g4_gemm_error, 1);
+            flags[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(A(s)), bd = sw128_desc(B(s));
+#pragma unroll
+          for (int kk = 0; kk < GM_BK / 32; kk++)
+            mma_i8(d, ad + 2 * kk, bd + 2 * kk, IDESC, (kt | kk) != 0 ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp < 6) {
+    if (BITS == 4) {
+      const int tu = t - 64;   // 0..127
+      const uint32_t total = (uint32_t)((tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * KT;
+      for (uint32_t g = 0; g < total && !flags[0]; g++) {
+        const int s = g % NS;
+        if (!mbar_wait(&full[s], (g / NS) & 1)) {
+          atomicExch(&g4_gemm_error, 1);
+          flags[0] = 1;
+          break;
+        }
+        const uint8_t *p = P(s);
+        uint8_t *dst = A(s);
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+          const int idx = tu + 128 * it;
+          const int row = idx >> 3, ch = idx & 7;
+          const uint2 pk = *reinterpret_cast<const uint2 *>(p + row * 64 + ch * 8);
+          const uint2 lo = unpack8(pk.x), hi = unpack8(pk.y);
+          *reinterpret_cast<uint4 *>(dst + (row >> 3) * 1024 + (row & 7) * 128 + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(lo.x, lo.y, hi.x, hi.y);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aready[s]);
+      }
+    }
+  } else {
+    // ---- epilogue warps 6-9: warp w reads TMEM lanes 32 (w % 4) .. + 31
+    const int q = warp & 3;
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, lt++) {
+      const int b = lt & 1;
+      const bool ok = !flags[0] && mbar_wait(&acc_full[b], (lt >> 1) & 1);
+      if (!ok) {
+        atomicExch(&g4_gemm_error, 1);
+        flags[0] = 1;
+        break;
+      }
+      tc_fence_after();
+      const int nt = tile % n_tiles, n0 = nt * GM_BM, m0 = (tile / n_tiles) * BN;
+      const int row = n0 + 32 * q + lane;
+      const bool row_ok = row < a.N;
+      const float wscale = row_ok ? f16_bits_to_f32(a.s[row]) : 0.0f;
+      const float sc = __fmul_rn(a.in_scale, wscale);
+      const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + (uint32_t)(b * BN) + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int tok = m0 + c0 + j;
+          float y = __fmul_rn(sc, (float)(int)acc[j]);
+          y = srq_out_r(y, a.out_scale, out_r);
+          if (EPI == EPI_HEAD) {
+            if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
+            if (a.logits && row_ok && tok < a.M) a.logits[(size_t)tok * a.ld_logits + row] = y;
+            float bv = row_ok ? y : -FLT_MAX;
+            int bi = row_ok ? row : 0x7fffffff;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+              const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+              if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+              }
+            }
+            if (lane == j) {
+              cand_v[q * 32 + j] = bv;
+              cand_i[q * 32 + j] = bi;
+            }
+          } else {
+            if (row_ok && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
+          }
+        }
+        if (EPI == EPI_HEAD) {
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (q == 0) {
+            float bv = cand_v[lane];
+            int bi = cand_i[lane];
+#pragma unroll
+            for (int w2 = 1; w2 < 4; w2++) {
+              const float ov = cand_v[w2 * 32 + lane];
+              const int oi = cand_i[w2 * 32 + lane];
+              if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+              }
+            }
+            const int tok = m0 + c0 + lane;
+            if (tok < a.M) {
+              a.part_val[(size_t)tok * a.n_parts + nt] = bv;
+              a.part_idx[(size_t)tok * a.n_parts + nt] = bi;
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+      }
+      // This accumulator may take the next tile's MMAs.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+  }
+}
+
+template <int BITS, int BN, int EPI>
+static cudaError_t launch_gemm_persist(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                       int grid, cudaStream_t st, bool pdl) {
+  auto k = k_qgemm_persist<BITS, BN, EPI>;
+  const int smem = GemmShape<BN, 4>::SMEM + 64;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(320);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr1[1];
+  attr1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr1[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr1;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
+}
+
 template <int BITS, int BN, int EPI, int NSTAGE = 0>
 static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  cudaStream_t st, bool pdl) {
@@ -421,6 +669,19 @@ static cudaError_t launch_gemm_b(const CUtensorMap &tmW, const CUtensorMap &tmX,
   if (bn == 128) return launch_gemm_t<BITS, 128, EPI>(tmW, tmX, a, st, pdl);
   if (bn == 256) return launch_gemm_t<BITS, 256, EPI>(tmW, tmX, a, st, pdl);
   if (bn == -128) return launch_gemm_t<BITS, 128, EPI, 2>(tmW, tmX, a, st, pdl);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_qgemm_persist(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                 int bits, int grid, cudaStream_t st, bool pdl) {
+  if (a.K % GM_BK != 0 || a.K < GM_BK || a.N < 1 || a.M < 1 || a.splits > 1 || grid < 1)
+    return cudaErrorInvalidValue;
+  if (bits == 4)
+    return a.head ? launch_gemm_persist<4, 128, EPI_HEAD>(tmW, tmX, a, grid, st, pdl)
+                  : launch_gemm_persist<4, 128, EPI_Y>(tmW, tmX, a, grid, st, pdl);
+  if (bits == 8)
+    return a.head ? launch_gemm_persist<8, 128, EPI_HEAD>(tmW, tmX, a, grid, st, pdl)
+                  : launch_gemm_persist<8, 128, EPI_Y>(tmW, tmX, a, grid, st, pdl);
   return cudaErrorInvalidValue;
 }
 

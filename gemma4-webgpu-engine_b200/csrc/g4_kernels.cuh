@@ -167,6 +167,10 @@ int make_tmap_u8(CUtensorMap *m, const void *base, uint64_t inner, uint64_t oute
                  uint64_t row_stride, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a, int bits,
                          int bn, cudaStream_t st, bool pdl);
+// Persistent form (one CTA per SM looping over 128 x 128 tiles, two TMEM accumulators so the
+// epilogue overlaps the next tile's MMAs): tmX with box rows 128; no split K.
+cudaError_t launch_qgemm_persist(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                 int bits, int grid, cudaStream_t st, bool pdl);
 int gemm_error_take();
 int gemm_tile_rows();
 

@@ -114,6 +114,7 @@ struct g4_ctx {
   int32_t *gacc = nullptr, *gcnt = nullptr;   // split-K workspace [maxc][gacc_ld] and tile counts
   int gacc_ld = 0;
   bool gemm_split = false;
+  bool gemm_persist = false;
   // Token tile of steps wider than 128 columns: 128 columns at two CTAs per SM (-128), measured
   // 10% faster on a 2048-token prefill than 256-column tiles at one CTA per SM.
   int gemm_wide_bn = -128;
@@ -945,7 +946,17 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
       ctx->cur_pi = ctx->gpi;
       ctx->cur_parts = g.n_parts;
     }
-    CK(launch_qgemm(l.tmw, *tx, g, l.bits, bn, ctx->st, true));
+    // The persistent tile loop (epilogue overlapping the next tile's MMAs) measured 6% slower on a
+    // 2048-token prefill than two per-tile CTAs per SM (tail imbalance, twice the DRAM reads), so
+    // the executor keeps the per-tile kernel; g4_op_qgemm uses the loop for wide calls.
+    const int tiles128 = ((l.N + 127) / 128) * ((cols + 127) / 128);
+    if (ctx->gemm_persist && !head && g.splits <= 1 && tiles128 > ctx->sms) {
+      const CUtensorMap *tx128 = codes_tmap(ctx, which[i - 1], K, 128);
+      if (!tx128) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
+      CK(launch_qgemm_persist(l.tmw, *tx128, g, l.bits, std::min(tiles128, ctx->sms), ctx->st, true));
+    } else {
+      CK(launch_qgemm(l.tmw, *tx, g, l.bits, bn, ctx->st, true));
+    }
     ctx->launches++;
   }
   return G4_OK;
@@ -1726,8 +1737,10 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
   q.ld_src = K;
   cudaError_t e = launch_quantize(q, codes, K, in_scale, nullptr, 0.0f, st, false);
   CUtensorMap tw, tx;
-  // Token tiles: 64, 128, 128 at two CTAs per SM (up to 256 columns), 256.
-  const int bn = cols <= 64 ? 64 : (cols <= 128 ? 128 : (cols <= 256 ? -128 : 256));
+  // Token tiles: 64, 128, 128 at two CTAs per SM (up to 256 columns), then the persistent tile
+  // loop (128-column tiles).
+  const bool persist = cols > 256;
+  const int bn = cols <= 64 ? 64 : (cols <= 128 ? 128 : -128);
   const int bnv = bn < 0 ? -bn : bn;
   const uint64_t rb = (uint64_t)K * bits / 8;
   int rc = G4_OK;
@@ -1760,7 +1773,12 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
           g.tile_cnt = ws + (size_t)cols * N;
         }
       }
-      if (e == cudaSuccess) e = launch_qgemm(tw, tx, g, bits, bn, st, false);
+      if (e == cudaSuccess) {
+        if (persist && g.splits <= 1)
+          e = launch_qgemm_persist(tw, tx, g, bits, std::min(tiles, sms), st, false);
+        else
+          e = launch_qgemm(tw, tx, g, bits, bn, st, false);
+      }
       if (ws) cudaFreeAsync(ws, st);
     }
   }
