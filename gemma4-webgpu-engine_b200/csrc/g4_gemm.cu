@@ -25,6 +25,19 @@
 namespace g4 {
 
 __device__ int g4_gemm_error;
+#ifdef G4_TRACE
+__device__ unsigned long long g4_trace_buf[1 << 16];
+__device__ unsigned int g4_trace_n;
+int gemm_trace_take(unsigned long long *out, int max_records) {
+  unsigned int n = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&n, g4_trace_n, sizeof(n)) != cudaSuccess) return -1;
+  if (n > (1u << 15)) n = 1u << 15;
+  if ((int)n > max_records) n = (unsigned int)max_records;
+  if (n && cudaMemcpyFromSymbol(out, g4_trace_buf, (size_t)n * 16) != cudaSuccess) return -1;
+  cudaMemcpyToSymbol(g4_trace_n, &zero, sizeof(zero));
+  return (int)n;
+}
+#endif
 
 int gemm_error_take() {
   int v = 0, zero = 0;
@@ -142,7 +155,7 @@ constexpr int GM_BK = 128;       // K per stage: one 128-byte swizzle atom of in
 // (their epilogues overlap each other's main loops).
 template <int BN, int NSTAGE = 0>
 struct GemmShape {
-  static constexpr int STAGES = NSTAGE ? NSTAGE : (BN >= 256 ? 3 : 4);
+  static constexpr int STAGES = NSTAGE ? NSTAGE : (BN >= 256 ? 3 : (BN <= 64 ? 6 : 4));
   static constexpr int A_BYTES = GM_BM * GM_BK;          // 16 KB
   static constexpr int B_BYTES = BN * GM_BK;
   static constexpr int P_BYTES = GM_BM * GM_BK / 2;      // packed int4 staging, 8 KB
@@ -200,6 +213,7 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
   const uint32_t tmem = *tslot;
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(5000 + BITS * 100 + (BN == 64 ? 1 : 2));
 
   if (warp == 0) {
     if (lane == 0) {

@@ -10,6 +10,11 @@
 
 namespace g4 {
 
+#ifdef G4_TRACE
+__device__ unsigned long long g4_trace_buf[1 << 16];
+__device__ unsigned int g4_trace_n;
+#endif
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
                             cudaStream_t st, bool pdl, Args... args) {
@@ -48,6 +53,7 @@ __global__ void __launch_bounds__(256) k_quantize(const GemvArgs a, uint8_t *cod
   prologue_gains<PRO>(a, pg);
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(4000 + PRO);
   const int c = blockIdx.x;
   int x2 = 0;
   gemv_prologue_col<8, PRO>(a, pg, c, s1, codes + (size_t)c * ld, red, a.hidden_out != nullptr, s2,
@@ -126,10 +132,6 @@ __global__ void __launch_bounds__(256) k_gemv_f32(const GemvArgs a) {
 // =====================================================================================
 
 __device__ int g4_dev_error;
-#ifdef G4_TRACE
-__device__ unsigned long long g4_trace_buf[1 << 16];
-__device__ unsigned int g4_trace_n;
-#endif
 
 // Shared memory of one streaming-GEMV CTA: the ring, then the barriers, the column sums, the
 // reduction and argmax scratch, the row scales of the CTA's slice (per sub-slice), the y rows
@@ -1108,6 +1110,7 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
   int *qlo = qp + QT;                          // [QT] window start
   grid_launch_dependents();
   grid_wait();
+  G4_TRACE_POINT(2100 + HD);
   const int t = threadIdx.x;
   const int c0 = blockIdx.x * QT;
   const int nq = min(QT, a.cols - c0);

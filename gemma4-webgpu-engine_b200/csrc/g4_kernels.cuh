@@ -81,6 +81,7 @@ int device_error_take();
 #ifdef G4_TRACE
 // Diagnostic build only: the (kernel id, time) records since the last call, then cleared.
 int trace_take(unsigned long long *out, int max_records);
+int gemm_trace_take(unsigned long long *out, int max_records);
 #endif
 
 // A quantized linear launch (the streaming kernel, or the f32 path when in_scale is 0).

@@ -572,6 +572,8 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
       for (int i = 0; i < n; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
       const int m = persist_trace_take(rec.data(), 1 << 15);
       for (int i = 0; i < m; i++) fprintf(f, "%llu %llu\n", 100000000ull + rec[2 * i], rec[2 * i + 1]);
+      const int gm = gemm_trace_take(rec.data(), 1 << 15);
+      for (int i = 0; i < gm; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
       fclose(f);
     }
   }
@@ -926,7 +928,10 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     // CTAs gained.
     const int tiles = ((l.N + 127) / 128) * ((cols + std::abs(bn) - 1) / std::abs(bn));
     const int kts = K / 128;
-    if (ctx->gemm_split && !head && tiles < ctx->sms && l.N <= ctx->gacc_ld && tiles <= 8192) {
+    // Split K where a launch has very few tiles and a long K loop (the down projection of a
+    // decode batch: 12 tiles x 48 K stages): there the added CTAs outweigh the workspace traffic.
+    const bool few_long = tiles <= 24 && kts >= 16;
+    if ((ctx->gemm_split || few_long) && !head && tiles < ctx->sms && l.N <= ctx->gacc_ld && tiles <= 8192) {
       g.splits = std::min(kts, (ctx->sms + tiles - 1) / tiles);
       if (g.splits > 1) {
         g.acc_ws = ctx->gacc;
