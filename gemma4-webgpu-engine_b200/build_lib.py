@@ -39,14 +39,21 @@ def needs_build() -> bool:
     return any(d.stat().st_mtime > t for d in deps if d.exists())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not needs_build():
+TRACE_LIB = LIB_DIR / "trace" / "libgemma4_cuda.so"
+
+
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
+    """Build the library (or, with trace=True, the diagnostic build with kernel time stamps
+    into lib/trace/, which the `trace` module reads; never the library the package loads)."""
+    out = TRACE_LIB if trace else LIB
+    if not force and not trace and not needs_build():
         return LIB
-    LIB_DIR.mkdir(exist_ok=True)
+    out.parent.mkdir(parents=True, exist_ok=True)
     objs, procs = [], []
+    extra = ["-DG4_TRACE"] if trace else []
     for src in SOURCES:   # the translation units compile in parallel
-        obj = LIB_DIR / (Path(src).stem + ".o")
-        cmd = [_nvcc(), *NVCC_FLAGS, "-c", str(CSRC / src), "-o", str(obj)]
+        obj = out.parent / (Path(src).stem + ".o")
+        cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-c", str(CSRC / src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
         procs.append((subprocess.Popen(cmd), cmd))
@@ -54,17 +61,16 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     failed = [cmd for p, cmd in procs if p.wait() != 0]
     if failed:
         raise subprocess.CalledProcessError(1, failed[0])
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = out.with_suffix(".so.tmp")
     cmd = [_nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", str(tmp)]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
+    os.replace(tmp, out)
     for o in objs:
         Path(o).unlink(missing_ok=True)
-    return LIB
+    return out
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose=True)
-    print(LIB)
+    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))

@@ -563,6 +563,17 @@ extern "C" int g4_ctx_create(int cuda_device, const g4_config *cfg_in, g4_ctx **
   return G4_OK;
 }
 
+#ifdef G4_TRACE
+// Diagnostic builds only (not part of include/g4.h): drop the records so far.
+extern "C" int g4_trace_reset(void) {
+  unsigned long long dummy[2];
+  trace_take(dummy, 0);
+  gemm_trace_take(dummy, 0);
+  persist_trace_take(dummy, 0);
+  return 0;
+}
+#endif
+
 extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
 #ifdef G4_TRACE
   if (const char *path = getenv("G4_TRACE_FILE")) {

@@ -1,0 +1,115 @@
+"""Live critical-path shares of decode steps, from the diagnostic build.
+
+`python gemma4-webgpu-engine_b200/build_lib.py --trace` builds lib/trace/libgemma4_cuda.so, in
+which block 0 of every step kernel stamps %globaltimer right after its programmatic-dependency
+wait. Consecutive stamps then measure each launch's share of the live critical path (its own
+work after the wait plus the release of the next launch), which a profiler replaying launches
+one by one cannot show. Usage, on a GPU:
+
+  python gemma4-webgpu-engine_b200/build_lib.py --trace
+  python gemma4-webgpu-engine_b200/trace.py [--batch B] [--ctx-lo L --ctx-hi H] [--steps K]
+
+The product library never contains the stamps (the macro is empty without G4_TRACE).
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+import os
+import sys
+import tempfile
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+# Kernel ids written by G4_TRACE_POINT (csrc/*.cu).
+_PRO = {0: "x", 1: "norm", 2: "join", 3: "normres", 4: "gelu", 5: "codes"}
+_EPI = {0: "y", 1: "gelu-codes", 2: "head"}
+_FIXED = {3001: "embed", 3002: "dense (per-layer inputs)", 3003: "per-layer combine",
+          3004: "argmax", 3005: "advance", 2256: "attention hd256", 2512: "attention hd512",
+          2356: "prefill attention hd256", 2612: "prefill attention hd512",
+          5401: "gemm int4 64 tok", 5402: "gemm int4 128 tok", 5801: "gemm int8 64 tok",
+          5802: "gemm int8 128 tok"}
+
+
+def kernel_name(i: int) -> str:
+    # GEMV launches stamp three times: after the wait, after the prologue, after the main loop.
+    if 101000 <= i < 102000:
+        return kernel_name(i - 100000) + " [main loop]"
+    if 201000 <= i < 202000:
+        return kernel_name(i - 200000) + " [epilogue + release]"
+    if 1000 <= i < 2000:
+        bits, pro, epi = (i - 1000) // 100, (i // 10) % 10, i % 10
+        return f"gemv int{bits} {_PRO.get(pro, pro)} -> {_EPI.get(epi, epi)} [prologue]"
+    if i in _FIXED:
+        return _FIXED[i]
+    if 4000 <= i < 4010:
+        return f"quantize ({_PRO.get(i - 4000, i)})"
+    return str(i)
+
+
+def summarize(records, steps: int, step_marker: int = 3001):
+    """Per-kernel (launches, total us, us per launch) over the last `steps` steps."""
+    rec = sorted(records, key=lambda r: r[1])
+    starts = [i for i, (k, _) in enumerate(rec) if k == step_marker]
+    if len(starts) >= steps:
+        rec = rec[starts[-steps]:]
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for (k, ta), (_, tb) in zip(rec, rec[1:]):
+        d = (tb - ta) / 1000.0
+        if d > 5000.0:   # a host gap between steps
+            continue
+        agg[kernel_name(k)][0] += 1
+        agg[kernel_name(k)][1] += d
+    return agg
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx-lo", type=int, default=128)
+    ap.add_argument("--ctx-hi", type=int, default=128)
+    ap.add_argument("--steps", type=int, default=10)
+    args = ap.parse_args()
+    import numpy as np
+    import __graft_entry__ as entry
+    pkg = entry.load_package()
+    lib_path = Path(pkg.__file__).resolve().parent / "lib" / "trace" / "libgemma4_cuda.so"
+    if not lib_path.exists():
+        raise SystemExit(f"{lib_path} missing: run build_lib.py --trace first")
+    out = Path(tempfile.mkdtemp()) / "trace.txt"
+    os.environ["G4_TRACE_FILE"] = str(out)
+    pkg._abi.load(lib_path)
+    import torch
+    B = args.batch
+    rng = np.random.default_rng(0x6E6D6134)
+    lens = ([args.ctx_lo] * B if args.ctx_lo == args.ctx_hi
+            else [int(v) for v in rng.integers(args.ctx_lo, args.ctx_hi + 1, B)])
+    ctx = pkg.engine.Context(device=0, max_seqs=B, max_context=max(lens) + args.steps + 16,
+                             max_step_columns=max(B, 512 if max(lens) > 256 else 64))
+    ctx.init_random(0x6E6D6134)
+    first = [ctx.prefill(b, np.array(pkg.plan.synth_prompt(0x6E6D6134 + b, lens[b]), np.int32), 0, True)
+             for b in range(B)]
+    ctx.step_stage(np.arange(B), first, lens)
+    for _ in range(2):
+        ctx.step_run_device(B)
+    torch.cuda.synchronize()
+    pkg._abi.load().g4_trace_reset()   # keep only the measured steps
+    for _ in range(args.steps):
+        ctx.step_run_device(B)
+    torch.cuda.synchronize()
+    ctx.close()   # writes the records
+    rec = [tuple(map(int, line.split())) for line in open(out)]
+    rec = [r for r in rec if r[0] < 100000000]
+    agg = summarize(rec, args.steps)
+    tot = sum(v[1] for v in agg.values())
+    print(f"B={B}, prompt lengths {args.ctx_lo}..{args.ctx_hi}, last {args.steps} steps: "
+          f"{tot / args.steps:.1f} us per step on the critical path")
+    print(f"{'kernel':34s} {'launches':>8s} {'us/launch':>10s} {'share':>7s}")
+    for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1]):
+        print(f"{k:34s} {n:8d} {t / n:10.2f} {100 * t / tot:6.1f}%")
+
+
+if __name__ == "__main__":
+    main()
