@@ -372,6 +372,8 @@ def main():
                     help="config 5: 512 sequences split over the replicas, 512-token prompts, "
                          "the per-layer-embedding table in 128 MiB vocab-row slices")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill workload: prompt length")
+    ap.add_argument("--gemm-split-k", type=int, default=0, choices=[0, 1, 2],
+                    help="g4_config.gemm_split_k: 0 cluster, 1 none, 2 workspace")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
@@ -410,7 +412,7 @@ def main():
     max_ctx = max(lens) + total_steps + 8
     chunk = max(B, 512 if max(lens) > 256 else 64)
     ctx = engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=chunk,
-                         ple_slice_bytes=slice_bytes)
+                         ple_slice_bytes=slice_bytes, gemm_split_k=args.gemm_split_k)
     ctx.init_random(SEED)
     prompts = [np.array(pkg.plan.synth_prompt(SEED + b + 7919 * rank, lens[b]), np.int32) for b in range(B)]
     torch.cuda.synchronize()

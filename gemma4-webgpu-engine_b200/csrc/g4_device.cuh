@@ -184,8 +184,22 @@ __device__ __forceinline__ float srq_out_r(float v, float s, float r) {
       }                                                                                      \
     }                                                                                        \
   } while (0)
+// The same record from the thread of block 0 that reaches the call (the call site picks it).
+#define G4_TRACE_POINT_T(id)                                                                 \
+  do {                                                                                       \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {                             \
+      unsigned long long now;                                                                \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));                                \
+      const unsigned int slot = atomicAdd(&g4_trace_n, 1u);                                  \
+      if (slot < (1u << 15)) {                                                               \
+        g4_trace_buf[2 * slot] = (unsigned long long)(id);                                   \
+        g4_trace_buf[2 * slot + 1] = now;                                                    \
+      }                                                                                      \
+    }                                                                                        \
+  } while (0)
 #else
 #define G4_TRACE_POINT(id) do {} while (0)
+#define G4_TRACE_POINT_T(id) do {} while (0)
 #endif
 
 // ---------------------------------------------------------------------- mbarriers, bulk copies

@@ -136,6 +136,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Every thread of every CTA in the cluster (the warp-divergent form: the role branches rejoin here).
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The 32-bit word at this CTA's shared address `p`, read from cluster CTA `rank`'s copy.
+__device__ __forceinline__ int ld_dsmem(const void *p, uint32_t rank) {
+  uint32_t remote;
+  int v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(remote));
+  return v;
+}
+
 // Eight packed int4 weights (code i at bits 4i) to eight signed int8 (u - 8), in K order.
 __device__ __forceinline__ uint2 unpack8(uint32_t w) {
   const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
@@ -164,7 +183,11 @@ struct GemmShape {
   static constexpr int SMEM = 1024 + BAR_OFF + (3 * STAGES + 2) * 8 + 64 + 4 * 32 * 8;
 };
 
-template <int BITS, int BN, int EPI, int NSTAGE>
+// CLU: K split over a thread-block cluster along z (gridDim.z = the cluster size). Every CTA
+// accumulates its K range in TMEM and parks the int32 partial in its own shared memory; after a
+// cluster barrier each CTA sums all partials of its share of the tile's token columns through
+// distributed shared memory (exact integer adds, fixed rank order) and runs the epilogue on it.
+template <int BITS, int BN, int EPI, int NSTAGE, bool CLU>
 __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
     k_qgemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const GemmArgs a) {
@@ -213,7 +236,7 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
   const uint32_t tmem = *tslot;
   grid_launch_dependents();
   grid_wait();
-  G4_TRACE_POINT(5000 + BITS * 100 + (BN == 64 ? 1 : 2));
+  G4_TRACE_POINT(5000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU ? 10 : 0));
 
   if (warp == 0) {
     if (lane == 0) {
@@ -294,6 +317,7 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
       mbar_wait(accf, 0);
     }
     tc_fence_after();
+    if (t == 64) G4_TRACE_POINT_T(205000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU ? 10 : 0));
     const int q = warp & 3;
     const int row = n0 + 32 * q + lane;
     const bool row_ok = row < a.N;
@@ -301,7 +325,19 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
     const float sc = __fmul_rn(a.in_scale, wscale);
     const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
     bool last = true;
-    if (gridDim.z > 1) {
+    if (CLU) {
+      // Park the partial, int32 [BN tokens][128 rows], over the stage buffers (every MMA that
+      // read them has completed).
+      int32_t *pbuf = reinterpret_cast<int32_t *>(gsm);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
+#pragma unroll
+        for (int j = 0; j < 32; j++) pbuf[(c0 + j) * GM_BM + 32 * q + lane] = (int)acc[j];
+      }
+      last = false;   // reduced and stored after the cluster barrier below
+    } else if (gridDim.z > 1) {
       // Split K: add this CTA's partial into the workspace; the tile's last split finishes.
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -396,6 +432,33 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
     }
+  }
+  if (CLU) {
+    cluster_sync_all();   // every CTA of the cluster has parked its partial
+    if (warp >= 2) {
+      const int q = warp & 3;
+      const int row = n0 + 32 * q + lane;
+      const bool row_ok = row < a.N;
+      const float wscale = row_ok ? f16_bits_to_f32(a.s[row]) : 0.0f;
+      const float sc = __fmul_rn(a.in_scale, wscale);
+      const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
+      const int nr = (int)gridDim.z, me = (int)cluster_rank();
+      const int per = (BN + nr - 1) / nr;
+      const int tl_end = min(BN, (me + 1) * per);
+      const int32_t *mine = reinterpret_cast<const int32_t *>(gsm) + 32 * q + lane;
+      const bool store = !flags[0] && g4_gemm_error == 0;
+#pragma unroll 1
+      for (int tl = me * per; tl < tl_end; tl++) {
+        int sum = 0;
+#pragma unroll 1
+        for (int r = 0; r < nr; r++) sum += ld_dsmem(mine + tl * GM_BM, (uint32_t)r);
+        const int tok = m0 + tl;
+        float y = __fmul_rn(sc, (float)sum);
+        y = srq_out_r(y, a.out_scale, out_r);
+        if (store && row_ok && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
+      }
+    }
+    cluster_sync_all();   // no CTA leaves while another still reads its partial
   }
   tc_fence_before();
   __syncthreads();
@@ -656,7 +719,7 @@ static cudaError_t launch_gemm_persist(const CUtensorMap &tmW, const CUtensorMap
 template <int BITS, int BN, int EPI, int NSTAGE = 0>
 static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  cudaStream_t st, bool pdl) {
-  auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE>;
+  auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE, false>;
   const int smem = GemmShape<BN, NSTAGE>::SMEM;
   static bool attr = false;
   if (!attr) {
@@ -674,6 +737,44 @@ static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX,
   cfg.attrs = attr1;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
+}
+
+template <int BITS>
+static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                         cudaStream_t st, bool pdl) {
+  auto k = k_qgemm_tc<BITS, 64, EPI_Y, 0, true>;
+  const int smem = GemmShape<64, 0>::SMEM;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + 63) / 64, a.splits);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = a.splits;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
+}
+
+cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                 int bits, cudaStream_t st, bool pdl) {
+  if (a.K % GM_BK != 0 || a.N < 1 || a.M < 1 || a.head || a.splits < 2 || a.splits > 8 ||
+      a.splits > a.K / GM_BK)
+    return cudaErrorInvalidValue;
+  if (bits == 4) return launch_gemm_cluster_t<4>(tmW, tmX, a, st, pdl);
+  if (bits == 8) return launch_gemm_cluster_t<8>(tmW, tmX, a, st, pdl);
+  return cudaErrorInvalidValue;
 }
 
 template <int BITS, int EPI>

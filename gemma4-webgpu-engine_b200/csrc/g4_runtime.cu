@@ -113,7 +113,7 @@ struct g4_ctx {
   int32_t *gpi = nullptr;
   int32_t *gacc = nullptr, *gcnt = nullptr;   // split-K workspace [maxc][gacc_ld] and tile counts
   int gacc_ld = 0;
-  bool gemm_split = false;
+  int gemm_split_k = 0;   // g4_config::gemm_split_k
   bool gemm_persist = false;
   // Token tile of steps wider than 128 columns: 128 columns at two CTAs per SM (-128), measured
   // 10% faster on a 2048-token prefill than 256-column tiles at one CTA per SM.
@@ -228,6 +228,7 @@ extern "C" int g4_config_default(g4_config *cfg) {
   cfg->ple_slice_bytes = 0;
   cfg->gemm_min_columns = 16;
   cfg->persistent_decode = 0;
+  cfg->gemm_split_k = 0;
   return G4_OK;
 }
 
@@ -490,6 +491,7 @@ static int alloc_runtime(g4_ctx *ctx) {
   CK(cudaMalloc(&ctx->gpv, (size_t)maxc * ctx->gparts * 4));
   CK(cudaMalloc(&ctx->gpi, (size_t)maxc * ctx->gparts * 4));
   ctx->gemm_min_cols = ctx->cfg.gemm_min_columns > 0 ? ctx->cfg.gemm_min_columns : 16;
+  ctx->gemm_split_k = ctx->cfg.gemm_split_k;
   CK(cudaMalloc(&ctx->pbar, 2 * sizeof(unsigned)));
   CK(cudaMemset(ctx->pbar, 0, 2 * sizeof(unsigned)));
   ctx->persist_grid = ctx->cfg.persistent_decode ? persist_max_grid(ctx->dev) : 0;
@@ -934,15 +936,25 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     g.out_scale = l.out_scale;
     g.y = sg.y;
     g.ld_y = l.N;
-    // Split K is available (exact int32 partials through a workspace) but off in the executor:
-    // measured on a B=64 step it cost more in atomics and the extra round trips than the added
-    // CTAs gained.
     const int tiles = ((l.N + 127) / 128) * ((cols + std::abs(bn) - 1) / std::abs(bn));
     const int kts = K / 128;
-    // Split K where a launch has very few tiles and a long K loop (the down projection of a
-    // decode batch: 12 tiles x 48 K stages): there the added CTAs outweigh the workspace traffic.
+    if (ctx->gemm_split_k == 0 && !head && bn == 64 && tiles < ctx->sms) {
+      // A launch of fewer tiles than SMs (a decode batch: 2 to 48 tiles) splits K over a cluster
+      // of 2, 4 or 8 CTAs per tile, as many as the SMs hold, each with at least one K stage.
+      int splits = 1;
+      while (splits < 8 && 2 * splits * tiles <= ctx->sms && 2 * splits <= kts) splits *= 2;
+      if (splits > 1) {
+        g.splits = splits;
+        CK(launch_qgemm_cluster(l.tmw, *tx, g, l.bits, ctx->st, true));
+        ctx->launches++;
+        continue;
+      }
+    }
+    // The workspace form (int32 atomics into a global buffer, the tile's last split finishes)
+    // pays only where a launch has very few tiles and a long K loop (the down projection of a
+    // decode batch: 12 tiles x 48 K stages).
     const bool few_long = tiles <= 24 && kts >= 16;
-    if ((ctx->gemm_split || few_long) && !head && tiles < ctx->sms && l.N <= ctx->gacc_ld && tiles <= 8192) {
+    if (ctx->gemm_split_k == 2 && few_long && !head && tiles < ctx->sms && l.N <= ctx->gacc_ld && tiles <= 8192) {
       g.splits = std::min(kts, (ctx->sms + tiles - 1) / tiles);
       if (g.splits > 1) {
         g.acc_ws = ctx->gacc;
@@ -1775,11 +1787,20 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
       g.out_scale = out_scale;
       g.y = y;
       g.ld_y = N;
-      // The executor's rule: few tiles split K (exact int32 partials through a workspace).
+      // The executor's rule: fewer tiles than SMs split K, over a thread-block cluster for
+      // 64-token tiles, else through an int32 workspace (both exact).
       const int tiles = ((N + 127) / 128) * ((cols + bnv - 1) / bnv);
       const int sms = device_sms();
       int32_t *ws = nullptr;
-      if (tiles < sms && tiles <= 8192) {
+      bool cluster = false;
+      if (bn == 64 && tiles < sms) {
+        int splits = 1;
+        while (splits < 8 && 2 * splits * tiles <= sms && 2 * splits <= K / 128) splits *= 2;
+        if (splits > 1) {
+          g.splits = splits;
+          cluster = true;
+        }
+      } else if (tiles < sms && tiles <= 8192) {
         g.splits = std::min(K / 128, (sms + tiles - 1) / tiles);
         if (g.splits > 1) {
           e = cudaMallocAsync(&ws, ((size_t)cols * N + 8192) * 4, st);
@@ -1790,7 +1811,9 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
         }
       }
       if (e == cudaSuccess) {
-        if (persist && g.splits <= 1)
+        if (cluster)
+          e = launch_qgemm_cluster(tw, tx, g, bits, st, false);
+        else if (persist && g.splits <= 1)
           e = launch_qgemm_persist(tw, tx, g, bits, std::min(tiles, sms), st, false);
         else
           e = launch_qgemm(tw, tx, g, bits, bn, st, false);

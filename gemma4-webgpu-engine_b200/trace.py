@@ -30,7 +30,8 @@ _FIXED = {3001: "embed", 3002: "dense (per-layer inputs)", 3003: "per-layer comb
           3004: "argmax", 3005: "advance", 2256: "attention hd256", 2512: "attention hd512",
           2356: "prefill attention hd256", 2612: "prefill attention hd512",
           5401: "gemm int4 64 tok", 5402: "gemm int4 128 tok", 5801: "gemm int8 64 tok",
-          5802: "gemm int8 128 tok"}
+          5802: "gemm int8 128 tok", 5411: "gemm int4 64 tok, cluster split",
+          5811: "gemm int8 64 tok, cluster split"}
 
 
 def kernel_name(i: int) -> str:
@@ -38,6 +39,9 @@ def kernel_name(i: int) -> str:
     if 101000 <= i < 102000:
         return kernel_name(i - 100000) + " [main loop]"
     if 201000 <= i < 202000:
+        return kernel_name(i - 200000) + " [epilogue + release]"
+    # GEMM launches stamp after the wait and when the accumulator is complete.
+    if 205000 <= i < 206000:
         return kernel_name(i - 200000) + " [epilogue + release]"
     if 1000 <= i < 2000:
         bits, pro, epi = (i - 1000) // 100, (i // 10) % 10, i % 10
@@ -71,6 +75,7 @@ def main() -> None:
     ap.add_argument("--ctx-lo", type=int, default=128)
     ap.add_argument("--ctx-hi", type=int, default=128)
     ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--gemm-split-k", type=int, default=0, choices=[0, 1, 2])
     args = ap.parse_args()
     import numpy as np
     import __graft_entry__ as entry
@@ -87,7 +92,8 @@ def main() -> None:
     lens = ([args.ctx_lo] * B if args.ctx_lo == args.ctx_hi
             else [int(v) for v in rng.integers(args.ctx_lo, args.ctx_hi + 1, B)])
     ctx = pkg.engine.Context(device=0, max_seqs=B, max_context=max(lens) + args.steps + 16,
-                             max_step_columns=max(B, 512 if max(lens) > 256 else 64))
+                             max_step_columns=max(B, 512 if max(lens) > 256 else 64),
+                             gemm_split_k=args.gemm_split_k)
     ctx.init_random(0x6E6D6134)
     first = [ctx.prefill(b, np.array(pkg.plan.synth_prompt(0x6E6D6134 + b, lens[b]), np.int32), 0, True)
              for b in range(B)]

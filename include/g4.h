@@ -100,10 +100,14 @@ typedef struct g4_config {
   int32_t persistent_decode; /* 1: a one-column decode step runs as one persistent cooperative
                                 kernel (grid barriers between phases, bit-identical); 0 (default):
                                 one launch per kernel, chained by programmatic dependent launch */
+  int32_t gemm_split_k;      /* K split of tensor-core launches with fewer tiles than SMs (all
+                                bit-identical): 0 (default) over a thread-block cluster, partials
+                                summed in distributed shared memory; 1 never; 2 through a global
+                                int32 workspace, only for launches of few tiles and long K */
 } g4_config;
 
 /* Defaults: g4_arch_default, max_seqs 1, max_context 2048, max_step_columns 64, graphs on,
- * gemm_min_columns 16, persistent_decode 0. */
+ * gemm_min_columns 16, persistent_decode 0, gemm_split_k 0. */
 int g4_config_default(g4_config *cfg);
 
 /*
