@@ -197,6 +197,15 @@ __device__ __forceinline__ float srq_out_r(float v, float s, float r) {
       }                                                                                      \
     }                                                                                        \
   } while (0)
+// A record with a given time stamp, from whichever thread calls it.
+#define G4_TRACE_REC(id, when)                                                               \
+  do {                                                                                       \
+    const unsigned int slot = atomicAdd(&g4_trace_n, 1u);                                    \
+    if (slot < (1u << 15)) {                                                                 \
+      g4_trace_buf[2 * slot] = (unsigned long long)(id);                                     \
+      g4_trace_buf[2 * slot + 1] = (when);                                                   \
+    }                                                                                        \
+  } while (0)
 #else
 #define G4_TRACE_POINT(id) do {} while (0)
 #define G4_TRACE_POINT_T(id) do {} while (0)

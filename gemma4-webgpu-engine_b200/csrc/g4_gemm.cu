@@ -28,6 +28,15 @@ __device__ int g4_gemm_error;
 #ifdef G4_TRACE
 __device__ unsigned long long g4_trace_buf[1 << 16];
 __device__ unsigned int g4_trace_n;
+// Per launch: the latest accumulator-complete time over the CTAs, and the CTAs finished so far
+// (the last one records both, then clears them for the next launch).
+__device__ unsigned long long g4_gemm_accmax;
+__device__ unsigned int g4_gemm_done;
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long now;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+  return now;
+}
 int gemm_trace_take(unsigned long long *out, int max_records) {
   unsigned int n = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&n, g4_trace_n, sizeof(n)) != cudaSuccess) return -1;
@@ -146,12 +155,17 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// The 32-bit word at this CTA's shared address `p`, read from cluster CTA `rank`'s copy.
-__device__ __forceinline__ int ld_dsmem(const void *p, uint32_t rank) {
+// This CTA's shared address `p` mapped to cluster CTA `rank`'s copy, and a 32-bit load from it.
+__device__ __forceinline__ uint32_t map_dsmem(const void *p, uint32_t rank) {
   uint32_t remote;
-  int v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
-  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(remote));
+  return remote;
+}
+__device__ __forceinline__ int4 ld_dsmem_v4(uint32_t remote) {
+  int4 v;
+  asm volatile("ld.shared::cluster.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(remote));
   return v;
 }
 
@@ -183,11 +197,11 @@ struct GemmShape {
   static constexpr int SMEM = 1024 + BAR_OFF + (3 * STAGES + 2) * 8 + 64 + 4 * 32 * 8;
 };
 
-// CLU: K split over a thread-block cluster along z (gridDim.z = the cluster size). Every CTA
+// CLU > 1: K split over a thread-block cluster of CLU CTAs along z (gridDim.z == CLU). Every CTA
 // accumulates its K range in TMEM and parks the int32 partial in its own shared memory; after a
 // cluster barrier each CTA sums all partials of its share of the tile's token columns through
 // distributed shared memory (exact integer adds, fixed rank order) and runs the epilogue on it.
-template <int BITS, int BN, int EPI, int NSTAGE, bool CLU>
+template <int BITS, int BN, int EPI, int NSTAGE, int CLU>
 __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
     k_qgemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const GemmArgs a) {
@@ -201,8 +215,6 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
   uint64_t *accf = empty + NS;
   uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 2);
   int *flags = reinterpret_cast<int *>(tslot + 2);         // [0]: error seen
-  float *cand_v = reinterpret_cast<float *>(flags + 14);   // [4 warps][32] head candidates
-  int *cand_i = reinterpret_cast<int *>(cand_v + 4 * 32);
   auto A = [&](int s) { return gsm + s * S::STAGE_BYTES; };
   auto B = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES; };
   auto P = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES + S::B_BYTES; };
@@ -236,7 +248,7 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
   const uint32_t tmem = *tslot;
   grid_launch_dependents();
   grid_wait();
-  G4_TRACE_POINT(5000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU ? 10 : 0));
+  G4_TRACE_POINT(5000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU > 1 ? 10 : 0));
 
   if (warp == 0) {
     if (lane == 0) {
@@ -317,7 +329,12 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
       mbar_wait(accf, 0);
     }
     tc_fence_after();
-    if (t == 64) G4_TRACE_POINT_T(205000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU ? 10 : 0));
+#ifdef G4_TRACE
+    if (t == 64) {
+      G4_TRACE_POINT_T(205000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU > 1 ? 10 : 0));
+      atomicMax(&g4_gemm_accmax, gtimer());
+    }
+#endif
     const int q = warp & 3;
     const int row = n0 + 32 * q + lane;
     const bool row_ok = row < a.N;
@@ -325,7 +342,7 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
     const float sc = __fmul_rn(a.in_scale, wscale);
     const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
     bool last = true;
-    if (CLU) {
+    if (CLU > 1) {
       // Park the partial, int32 [BN tokens][128 rows], over the stage buffers (every MMA that
       // read them has completed).
       int32_t *pbuf = reinterpret_cast<int32_t *>(gsm);
@@ -362,6 +379,65 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
         if (t == 64) *cnt = 0;
       }
     }
+    if constexpr (EPI == EPI_HEAD) {
+      // Through shared memory (the stage buffers, free once every MMA completed): the int32 sums
+      // parked as [BN tokens][128 rows], then each thread's row of logits for every token (a
+      // short loop, 8 tokens in flight), then per token the greatest value over the tile's rows,
+      // lowest row on ties, scanned by 128 / BN threads per token in bank-rotated order.
+      int32_t *ab = reinterpret_cast<int32_t *>(gsm);
+      float *yb = reinterpret_cast<float *>(gsm);
+      const bool store = ok && !flags[0];
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
+#pragma unroll
+        for (int j = 0; j < 32; j++) ab[(c0 + j) * GM_BM + 32 * q + lane] = (int)acc[j];
+      }
+#pragma unroll 8
+      for (int j = 0; j < BN; j++) {
+        const int slot = j * GM_BM + 32 * q + lane;
+        float y = __fmul_rn(sc, (float)ab[slot]);
+        y = srq_out_r(y, a.out_scale, out_r);
+        if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
+        const int tok = m0 + j;
+        if (store && a.logits && row_ok && tok < a.M) a.logits[(size_t)tok * a.ld_logits + row] = y;
+        yb[slot] = y;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      constexpr int TPT = BN <= GM_BM ? GM_BM / BN : 1;   // threads per token
+      constexpr int R = GM_BM / TPT;                       // rows each scans
+      const int u = t - 64;
+#pragma unroll 1
+      for (int j = TPT > 1 ? u / TPT : u; j < BN; j += 128 / TPT) {
+        const int h = TPT > 1 ? u % TPT : 0;
+        float bv = -FLT_MAX;
+        int bi = 0x7fffffff;
+#pragma unroll 8
+        for (int i = 0; i < R; i++) {
+          const int r = h * R + ((i + u) & (R - 1));
+          const float v = yb[j * GM_BM + r];
+          if (n0 + r < a.N && (v > bv || (v == bv && n0 + r < bi))) {
+            bv = v;
+            bi = n0 + r;
+          }
+        }
+        if (TPT == 2) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, 1);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, 1);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        const int tok = m0 + j;
+        if (h == 0 && store && tok < a.M) {
+          a.part_val[(size_t)tok * a.n_parts + blockIdx.x] = bv;
+          a.part_idx[(size_t)tok * a.n_parts + blockIdx.x] = bi;
+        }
+      }
+      last = false;
+    }
 #pragma unroll 1
     for (int c0 = 0; c0 < BN && last; c0 += 32) {
       uint32_t acc[32];
@@ -378,84 +454,61 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
       } else {
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, acc);
       }
-      // After a failed wait nothing is stored; the named barriers below still run in step.
+      // After a failed wait nothing is stored.
       const bool store = ok && !flags[0];
 #pragma unroll
       for (int j = 0; j < 32; j++) {
         const int tok = m0 + c0 + j;
         float y = __fmul_rn(sc, (float)(int)acc[j]);
         y = srq_out_r(y, a.out_scale, out_r);
-        if (EPI == EPI_HEAD) {
-          if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
-          if (store && a.logits && row_ok && tok < a.M) a.logits[(size_t)tok * a.ld_logits + row] = y;
-          // Greatest value, lowest row on ties, across the warp's 32 rows.
-          float bv = row_ok ? y : -FLT_MAX;
-          int bi = row_ok ? row : 0x7fffffff;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-              bv = ov;
-              bi = oi;
-            }
-          }
-          if (lane == j) {
-            cand_v[q * 32 + j] = bv;
-            cand_i[q * 32 + j] = bi;
-          }
-        } else {
-          if (store && row_ok && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
-        }
-      }
-      if (EPI == EPI_HEAD) {
-        // The four warps' candidates for these 32 tokens: warp q == 0's lane j closes token j.
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (q == 0) {
-          float bv = cand_v[lane];
-          int bi = cand_i[lane];
-#pragma unroll
-          for (int w2 = 1; w2 < 4; w2++) {
-            const float ov = cand_v[w2 * 32 + lane];
-            const int oi = cand_i[w2 * 32 + lane];
-            if (ov > bv || (ov == bv && oi < bi)) {
-              bv = ov;
-              bi = oi;
-            }
-          }
-          const int tok = m0 + c0 + lane;
-          if (store && tok < a.M) {
-            a.part_val[(size_t)tok * a.n_parts + blockIdx.x] = bv;
-            a.part_idx[(size_t)tok * a.n_parts + blockIdx.x] = bi;
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (store && row_ok && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
       }
     }
   }
-  if (CLU) {
+  if constexpr (CLU > 1) {
     cluster_sync_all();   // every CTA of the cluster has parked its partial
     if (warp >= 2) {
-      const int q = warp & 3;
-      const int row = n0 + 32 * q + lane;
-      const bool row_ok = row < a.N;
-      const float wscale = row_ok ? f16_bits_to_f32(a.s[row]) : 0.0f;
-      const float sc = __fmul_rn(a.in_scale, wscale);
+      // This CTA's share: PER token columns. Thread u takes rows 4g..4g+3 (g = u % 32) of the
+      // tokens u / 32 + 4i, 16-byte loads from every rank's partial, all in flight together.
+      constexpr int PER = BN / CLU;
+      constexpr int ITEMS = PER / 4;
+      const int u = t - 64, g = u & 31, jb = u >> 5;
+      const int t0 = (int)cluster_rank() * PER;
       const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
-      const int nr = (int)gridDim.z, me = (int)cluster_rank();
-      const int per = (BN + nr - 1) / nr;
-      const int tl_end = min(BN, (me + 1) * per);
-      const int32_t *mine = reinterpret_cast<const int32_t *>(gsm) + 32 * q + lane;
+      float sc[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int row = n0 + 4 * g + e;
+        sc[e] = row < a.N ? __fmul_rn(a.in_scale, f16_bits_to_f32(a.s[row])) : 0.0f;
+      }
+      const int32_t *mine = reinterpret_cast<const int32_t *>(gsm) + t0 * GM_BM + 4 * g;
       const bool store = !flags[0] && g4_gemm_error == 0;
-#pragma unroll 1
-      for (int tl = me * per; tl < tl_end; tl++) {
-        int sum = 0;
-#pragma unroll 1
-        for (int r = 0; r < nr; r++) sum += ld_dsmem(mine + tl * GM_BM, (uint32_t)r);
-        const int tok = m0 + tl;
-        float y = __fmul_rn(sc, (float)sum);
-        y = srq_out_r(y, a.out_scale, out_r);
-        if (store && row_ok && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
+      int4 v[CLU][ITEMS];
+#pragma unroll
+      for (int r = 0; r < CLU; r++) {
+        const uint32_t base = map_dsmem(mine, (uint32_t)r);
+#pragma unroll
+        for (int it = 0; it < ITEMS; it++) v[r][it] = ld_dsmem_v4(base + (uint32_t)((jb + 4 * it) * GM_BM * 4));
+      }
+#pragma unroll
+      for (int it = 0; it < ITEMS; it++) {
+        int4 sum = v[0][it];
+#pragma unroll
+        for (int r = 1; r < CLU; r++) {
+          sum.x += v[r][it].x;
+          sum.y += v[r][it].y;
+          sum.z += v[r][it].z;
+          sum.w += v[r][it].w;
+        }
+        const int tok = m0 + t0 + jb + 4 * it;
+        const int sv[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int row = n0 + 4 * g + e;
+          float y = __fmul_rn(sc[e], (float)sv[e]);
+          y = srq_out_r(y, a.out_scale, out_r);
+          if (store && row < a.N && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
+        }
       }
     }
     cluster_sync_all();   // no CTA leaves while another still reads its partial
@@ -466,6 +519,19 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
   }
+#ifdef G4_TRACE
+  if (t == 64) {
+    const int id = 5000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU > 1 ? 10 : 0);
+    G4_TRACE_POINT_T(300000 + id);
+    __threadfence();
+    const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(&g4_gemm_done, 1u) == total - 1) {
+      G4_TRACE_REC(500000 + id, atomicExch(&g4_gemm_accmax, 0ull));
+      G4_TRACE_REC(400000 + id, gtimer());
+      g4_gemm_done = 0;
+    }
+  }
+#endif
 }
 
 // Persistent form for many tiles (prefill): one CTA per SM loops over tiles (m-major order, so
@@ -719,7 +785,7 @@ static cudaError_t launch_gemm_persist(const CUtensorMap &tmW, const CUtensorMap
 template <int BITS, int BN, int EPI, int NSTAGE = 0>
 static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  cudaStream_t st, bool pdl) {
-  auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE, false>;
+  auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE, 0>;
   const int smem = GemmShape<BN, NSTAGE>::SMEM;
   static bool attr = false;
   if (!attr) {
@@ -739,10 +805,10 @@ static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX,
   return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
 }
 
-template <int BITS>
+template <int BITS, int CLU>
 static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                          cudaStream_t st, bool pdl) {
-  auto k = k_qgemm_tc<BITS, 64, EPI_Y, 0, true>;
+  auto k = k_qgemm_tc<BITS, 64, EPI_Y, 0, CLU>;
   const int smem = GemmShape<64, 0>::SMEM;
   static bool attr = false;
   if (!attr) {
@@ -751,7 +817,7 @@ static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorM
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + 63) / 64, a.splits);
+  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + 63) / 64, CLU);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -759,7 +825,7 @@ static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorM
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 1;
   at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = a.splits;
+  at[0].val.clusterDim.z = CLU;
   at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
@@ -769,12 +835,18 @@ static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorM
 
 cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  int bits, cudaStream_t st, bool pdl) {
-  if (a.K % GM_BK != 0 || a.N < 1 || a.M < 1 || a.head || a.splits < 2 || a.splits > 8 ||
-      a.splits > a.K / GM_BK)
+  if (a.K % GM_BK != 0 || a.N < 1 || a.M < 1 || a.head || a.splits > a.K / GM_BK ||
+      (bits != 4 && bits != 8))
     return cudaErrorInvalidValue;
-  if (bits == 4) return launch_gemm_cluster_t<4>(tmW, tmX, a, st, pdl);
-  if (bits == 8) return launch_gemm_cluster_t<8>(tmW, tmX, a, st, pdl);
-  return cudaErrorInvalidValue;
+  switch (a.splits * 10 + bits) {
+    case 24: return launch_gemm_cluster_t<4, 2>(tmW, tmX, a, st, pdl);
+    case 44: return launch_gemm_cluster_t<4, 4>(tmW, tmX, a, st, pdl);
+    case 84: return launch_gemm_cluster_t<4, 8>(tmW, tmX, a, st, pdl);
+    case 28: return launch_gemm_cluster_t<8, 2>(tmW, tmX, a, st, pdl);
+    case 48: return launch_gemm_cluster_t<8, 4>(tmW, tmX, a, st, pdl);
+    case 88: return launch_gemm_cluster_t<8, 8>(tmW, tmX, a, st, pdl);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 template <int BITS, int EPI>

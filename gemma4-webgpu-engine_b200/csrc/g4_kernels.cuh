@@ -172,7 +172,7 @@ cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const G
 // epilogue overlaps the next tile's MMAs): tmX with box rows 128; no split K.
 cudaError_t launch_qgemm_persist(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  int bits, int grid, cudaStream_t st, bool pdl);
-// K split over a thread-block cluster of a.splits (2..8) CTAs per 128-row x 64-token tile: the
+// K split over a thread-block cluster of a.splits (2, 4 or 8) CTAs per 128-row x 64-token tile: the
 // int32 partials are reduced through distributed shared memory, no workspace. tmX: box rows 64.
 cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  int bits, cudaStream_t st, bool pdl);

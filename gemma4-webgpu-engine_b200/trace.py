@@ -34,18 +34,27 @@ _FIXED = {3001: "embed", 3002: "dense (per-layer inputs)", 3003: "per-layer comb
           5811: "gemm int8 64 tok, cluster split"}
 
 
+# GEMM records (id + offset): block 0's accumulator complete, block 0 done, the last CTA done,
+# the latest accumulator-complete time over all CTAs (written by the last CTA).
+_GEMM_PHASE = {0: "[block 0 main loop]", 200000: "[block 0 epilogue]", 300000: "[after block 0 done]",
+               400000: "[last CTA done -> next]", 500000: "[after the last accumulator]"}
+
+
+def _gemv_name(i: int) -> str:
+    bits, pro, epi = (i - 1000) // 100, (i // 10) % 10, i % 10
+    return f"gemv int{bits} {_PRO.get(pro, pro)} -> {_EPI.get(epi, epi)}"
+
+
 def kernel_name(i: int) -> str:
     # GEMV launches stamp three times: after the wait, after the prologue, after the main loop.
-    if 101000 <= i < 102000:
-        return kernel_name(i - 100000) + " [main loop]"
-    if 201000 <= i < 202000:
-        return kernel_name(i - 200000) + " [epilogue + release]"
-    # GEMM launches stamp after the wait and when the accumulator is complete.
-    if 205000 <= i < 206000:
-        return kernel_name(i - 200000) + " [epilogue + release]"
     if 1000 <= i < 2000:
-        bits, pro, epi = (i - 1000) // 100, (i // 10) % 10, i % 10
-        return f"gemv int{bits} {_PRO.get(pro, pro)} -> {_EPI.get(epi, epi)} [prologue]"
+        return _gemv_name(i) + " [prologue]"
+    if 101000 <= i < 102000:
+        return _gemv_name(i - 100000) + " [main loop]"
+    if 201000 <= i < 202000:
+        return _gemv_name(i - 200000) + " [epilogue + release]"
+    if (i % 100000) // 1000 == 5 and i // 100000 in (0, 2, 3, 4, 5) and i % 100000 in _FIXED:
+        return _FIXED[i % 100000] + " " + _GEMM_PHASE[i - i % 100000]
     if i in _FIXED:
         return _FIXED[i]
     if 4000 <= i < 4010:

@@ -152,7 +152,8 @@ def test_batch_matches_single(pkg, O, tiny):
 def test_batched_decode_tensor_core_path(pkg, O, tiny):
     """B = 20 reaches gemm_min_columns: every calibrated linear of the step runs as the column
     quantize + tcgen05 int8 GEMM, and the lm_head GEMM reduces argmax partials per 128-row tile.
-    Tokens equal the oracle's, sequence by sequence, with ragged contexts."""
+    Tokens equal the oracle's, sequence by sequence, with ragged contexts; the head GEMM's
+    softcapped logits are bit-identical to the oracle's."""
     a, om = tiny
     ctx = make_ctx(pkg, a, max_seqs=20, max_step_columns=32)
     B = 20
@@ -161,6 +162,10 @@ def test_batched_decode_tensor_core_path(pkg, O, tiny):
     pos = [len(p) for p in prompts]
     for step in range(3):
         out = ctx.decode_batch(np.arange(B), toks, pos)
+        if step == 0:
+            for b in (0, 7, B - 1):
+                _, want_logits = oracle_run(O, om, prompts[b], 2)
+                np.testing.assert_array_equal(ctx.logits(b).view(np.uint32), want_logits[1].view(np.uint32))
         for b in range(B):
             ref, _ = om.generate(prompts[b], step + 2, 128)
             assert out[b] == ref[step + 1], (step, b)
