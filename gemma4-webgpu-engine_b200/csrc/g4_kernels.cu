@@ -1364,7 +1364,9 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl) {
 // (c, bi) of a column:
 //   * before the dependency wait, pulls its K and V rows into L2 (a prefetch only: the
 //     position read there may be stale, which costs nothing but a wasted prefetch);
-//   * requests its V rows (all but the new position) as one bulk copy into shared memory;
+//   * requests its V rows (all but the new position) as bulk copies into shared memory: the
+//     whole block at once (per-head CTAs), or in two 32-row halves through one half-size buffer
+//     (8-head CTAs, so that two CTAs fit an SM at head dim 512);
 //   * normalises and rotates the 8 query heads itself (warp h: head h; the sum of squares
 //     follows block_sumsq256's chunk order exactly), and, in the block holding the new position
 //     of a producer layer, the K row (gain, rotation) and V row (weightless norm), which it
@@ -1382,21 +1384,24 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
   constexpr int NOUT = NHL * NC;                       // float4 outputs of the PV step
   constexpr int HPT = NOUT >= 256 ? NOUT / 256 : 1;    // heads per PV thread
   constexpr int NCH = NOUT >= 256 ? 256 / NC : NHL;    // PV head groups
+  constexpr int VH = NHL == 8 ? 2 : 1;                 // V staging phases
+  constexpr int VROWS = ATT_BLK / VH;
   extern __shared__ __align__(16) float sm[];
-  float *vs = sm;                     // [64][HD]   (bulk copy destination)
-  float *qs = vs + ATT_BLK * HD;      // [NHL][HD]
+  float *vs = sm;                     // [VROWS][HD] (bulk copy destination)
+  float *qs = vs + VROWS * HD;        // [NHL][HD]
   float *kc = qs + NHL * HD;          // [HD]       K row of the new position
-  float *ss = kc + HD;                // [NHL][64]
+  float *vn = kc + HD;                // [HD]       V row of the new position
+  float *ss = vn + HD;                // [NHL][64]
   float *ps = ss + NHL * ATT_BLK;     // [NHL][64]
   float *ms = ps + NHL * ATT_BLK;     // [8]
-  uint64_t *bar = reinterpret_cast<uint64_t *>(ms + 8);    // 8-byte aligned: offsets above are
-  int *flag = reinterpret_cast<int *>(bar + 1);            // multiples of 8 floats
+  uint64_t *bar = reinterpret_cast<uint64_t *>(ms + 8);    // [VH], 8-byte aligned: offsets above
+  int *flag = reinterpret_cast<int *>(bar + VH);           // are multiples of 8 floats
   const int c = blockIdx.x, bi = blockIdx.y, t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int h0 = blockIdx.z * NHL;    // first head of this CTA
 
   grid_launch_dependents();
   if (t == 0) {
-    mbar_init(bar, 1);
+    for (int i = 0; i < VH; i++) mbar_init(&bar[i], 1);
     mbar_fence_init();
     // L2 prefetch of this block's rows from a possibly stale position (clamped in bounds).
     int p = a.refs.pos ? a.refs.pos[c] : a.refs.pos_base + c;
@@ -1433,12 +1438,30 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
   const bool cur = a.k != nullptr && j1 == p;     // this block writes and uses row p itself
   const bool store_kv = cur && blockIdx.z == 0;   // one CTA of the block stores the new row
   const int jv1 = cur ? p - 1 : j1;
-  const uint32_t vbytes = jv1 >= j0 ? (uint32_t)(jv1 - j0 + 1) * HD * 4 : 0u;
-  __syncthreads();   // barrier initialised
-  if (t == 0 && vbytes) {
-    mbar_expect_tx(bar, vbytes);
-    bulk_g2s(vs + (size_t)(j0 - b * ATT_BLK) * HD, V + (size_t)j0 * HD, vbytes, bar);
-  }
+  // Staging phase ph covers rows [b * 64 + ph * VROWS, + VROWS) of [j0, jv1].
+  auto vfirst = [&](int ph) { return max(j0, b * ATT_BLK + ph * VROWS); };
+  auto vbytes = [&](int ph) {
+    const int r1 = min(jv1, b * ATT_BLK + ph * VROWS + VROWS - 1);
+    return r1 >= vfirst(ph) ? (uint32_t)(r1 - vfirst(ph) + 1) * HD * 4 : 0u;
+  };
+  auto vissue = [&](int ph) {
+    const uint32_t nbytes = vbytes(ph);
+    if (nbytes) {
+      mbar_expect_tx(&bar[ph], nbytes);
+      bulk_g2s(vs + (size_t)(vfirst(ph) - b * ATT_BLK - ph * VROWS) * HD, V + (size_t)vfirst(ph) * HD,
+               nbytes, &bar[ph]);
+    }
+  };
+  // Bounded wait on phase ph's copy; on a timeout the error flag is raised, the copy is waited
+  // for once more (bounded), and the block finishes with whatever arrived.
+  auto vwait = [&](int ph) {
+    if (vbytes(ph) && !mbar_wait(&bar[ph], 0)) {
+      if (t == 0) atomicExch(&g4_dev_error, 2);
+      mbar_wait(&bar[ph], 0);
+    }
+  };
+  __syncthreads();   // barriers initialised
+  if (t == 0) vissue(0);
 
   // Query heads (warp w < NHL: head h0 + w), then the new position's K and V rows (the warps
   // after them).
@@ -1453,9 +1476,8 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       head_norm_rope_warp<HD>(a.k + (size_t)c * HD, a.kgain, ct, stb, a.eps, kc,
                               store_kv ? K + (size_t)p * HD : nullptr, lane);
     if (cur && w == WV)
-      head_norm_rope_warp<HD>(a.v + (size_t)c * HD, nullptr, nullptr, nullptr, a.eps,
-                              vs + (size_t)(p - b * ATT_BLK) * HD, store_kv ? V + (size_t)p * HD : nullptr,
-                              lane);
+      head_norm_rope_warp<HD>(a.v + (size_t)c * HD, nullptr, nullptr, nullptr, a.eps, vn,
+                              store_kv ? V + (size_t)p * HD : nullptr, lane);
   }
   __syncthreads();
 
@@ -1510,14 +1532,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     ps[h * ATT_BLK + lane + 32] = (jb >= j0 && jb <= j1) ? g4_exp(__fsub_rn(s1, mx)) : 0.0f;
     if (lane == 0) ms[h] = mx;
   }
-  // V rows: bounded wait on the bulk copy; on a timeout the error flag is raised, the copy is
-  // waited for once more (bounded), and the block finishes with whatever arrived.
-  if (vbytes) {
-    if (!mbar_wait(bar, 0)) {
-      if (t == 0) atomicExch(&g4_dev_error, 2);
-      mbar_wait(bar, 0);
-    }
-  }
+  vwait(0);
   __syncthreads();
   const int dc = t % NC, hg = t / NC;
   const bool pv = hg < NCH;
@@ -1528,19 +1543,30 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     o[hh] = make_float4(0.f, 0.f, 0.f, 0.f);
     l[hh] = 0.0f;
   }
-  if (pv) {
+#pragma unroll 1
+  for (int ph = 0; ph < VH; ph++) {
+    if (ph > 0) {
+      __syncthreads();   // every thread is done with the previous phase's rows
+      if (t == 0) vissue(ph);
+      vwait(ph);
+    }
+    const int r0 = b * ATT_BLK + ph * VROWS;
+    const int ja = max(j0, r0), jb = min(j1, r0 + VROWS - 1);
+    if (pv) {
 #pragma unroll 4
-    for (int j = j0; j <= j1; j++) {
-      const int jl = j - b * ATT_BLK;
-      const float4 v4 = reinterpret_cast<const float4 *>(vs + (size_t)jl * HD)[dc];
+      for (int j = ja; j <= jb; j++) {
+        const int jl = j - b * ATT_BLK;
+        const float *vrow = cur && j == p ? vn : vs + (size_t)(j - r0) * HD;
+        const float4 v4 = reinterpret_cast<const float4 *>(vrow)[dc];
 #pragma unroll
-      for (int hh = 0; hh < HPT; hh++) {
-        const float pj = ps[(hg * HPT + hh) * ATT_BLK + jl];
-        o[hh].x = fmaf(pj, v4.x, o[hh].x);
-        o[hh].y = fmaf(pj, v4.y, o[hh].y);
-        o[hh].z = fmaf(pj, v4.z, o[hh].z);
-        o[hh].w = fmaf(pj, v4.w, o[hh].w);
-        l[hh] = __fadd_rn(l[hh], pj);
+        for (int hh = 0; hh < HPT; hh++) {
+          const float pj = ps[(hg * HPT + hh) * ATT_BLK + jl];
+          o[hh].x = fmaf(pj, v4.x, o[hh].x);
+          o[hh].y = fmaf(pj, v4.y, o[hh].y);
+          o[hh].z = fmaf(pj, v4.z, o[hh].z);
+          o[hh].w = fmaf(pj, v4.w, o[hh].w);
+          l[hh] = __fadd_rn(l[hh], pj);
+        }
       }
     }
   }
@@ -1688,7 +1714,8 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
 
 template <int HD, int NHL>
 static size_t attn_decode_smem() {
-  return ((size_t)ATT_BLK * HD + NHL * HD + HD + 2 * NHL * ATT_BLK + 8) * 4 + 16;
+  constexpr int VROWS = NHL == 8 ? ATT_BLK / 2 : ATT_BLK;
+  return ((size_t)VROWS * HD + NHL * HD + 2 * HD + 2 * NHL * ATT_BLK + 8) * 4 + 32;
 }
 
 template <int HD, int NHL>
@@ -1705,8 +1732,8 @@ static cudaError_t launch_attn_decode_t(const AttnDec &a, cudaStream_t st, bool 
 }
 
 cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl) {
-  // The merge keeps three factors per (block, head) in the 64-row V buffer.
-  if ((size_t)3 * a.max_blocks * 8 + 8 > (size_t)ATT_BLK * a.hd) return cudaErrorInvalidValue;
+  // The merge keeps three factors per (block, head) in the (32- or 64-row) V buffer.
+  if ((size_t)3 * a.max_blocks * 8 + 8 > (size_t)(ATT_BLK / 2) * a.hd) return cudaErrorInvalidValue;
   // Few columns: one CTA per (column, block, head) spreads a latency-bound step over more SMs;
   // a wide batch keeps all 8 heads of a block in one CTA (the V block is staged once for them).
   const bool split = a.cols * a.max_blocks <= 64;
