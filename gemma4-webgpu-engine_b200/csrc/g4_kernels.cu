@@ -60,16 +60,33 @@ __global__ void __launch_bounds__(256) k_quantize(const GemvArgs a, uint8_t *cod
                             codes2 ? codes2 + (size_t)c * ld : nullptr, &x2);
 }
 
+// The elementwise prologues (x, gelu(x) * u) need no per-column reduction: grid (column, chunk
+// block), one vec4 chunk per thread, so a wide column (down_proj's 6144) spreads over many SMs.
+template <int PRO>
+__global__ void __launch_bounds__(256) k_quantize_elem(const GemvArgs a, uint8_t *codes, int ld, float s1,
+                                                       uint8_t *codes2, float s2) {
+  grid_launch_dependents();
+  grid_wait();
+  G4_TRACE_POINT(4000 + PRO);
+  const int c = blockIdx.x, ch = blockIdx.y * 256 + threadIdx.x;
+  if (ch >= (a.K >> 2)) return;
+  float4 x = reinterpret_cast<const float4 *>(a.src + (size_t)c * a.ld_src)[ch];
+  if (PRO == PRO_GELU)
+    x = f4_gelu_mul(x, reinterpret_cast<const float4 *>(a.up + (size_t)c * a.ld_up + a.up_off)[ch]);
+  ChunkPro::store<8>(codes + (size_t)c * ld, ch, x, s1, __fdiv_rn(1.0f, s1));
+  if (codes2) ChunkPro::store<8>(codes2 + (size_t)c * ld, ch, x, s2, __fdiv_rn(1.0f, s2));
+}
+
 cudaError_t launch_quantize(const GemvArgs &a, uint8_t *codes, int ld, float s1, uint8_t *codes2,
                            float s2, cudaStream_t st, bool pdl) {
   if (a.cols < 1 || (a.K & 15) || s1 == 0.0f || (codes2 && s2 == 0.0f)) return cudaErrorInvalidValue;
-  const dim3 g(a.cols), b(256);
+  const dim3 g(a.cols), b(256), ge(a.cols, ((a.K >> 2) + 255) / 256);
   switch (a.pro) {
-    case PRO_X: return launch_k(k_quantize<PRO_X>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
+    case PRO_X: return launch_k(k_quantize_elem<PRO_X>, ge, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
     case PRO_NORM: return launch_k(k_quantize<PRO_NORM>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
     case PRO_JOIN: return launch_k(k_quantize<PRO_JOIN>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
     case PRO_NORMRES: return launch_k(k_quantize<PRO_NORMRES>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
-    case PRO_GELU: return launch_k(k_quantize<PRO_GELU>, g, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
+    case PRO_GELU: return launch_k(k_quantize_elem<PRO_GELU>, ge, b, 0, st, pdl, a, codes, ld, s1, codes2, s2);
   }
   return cudaErrorInvalidValue;
 }

@@ -2042,9 +2042,8 @@ extern "C" int g4_op_softcap_argmax(const float *logits, float *capped, int32_t 
   OPCK(cudaMallocAsync((void **)&pv, (size_t)parts * 8, st));
   int32_t *pi = (int32_t *)(pv + parts);
   cudaError_t e = launch_softcap_partials(logits, capped, n, cap, pv, pi, parts, st);
-  float *val = nullptr;
+  // token[0] = index, token[1] = the value's bits.
   if (e == cudaSuccess) e = launch_argmax_final(pv, pi, parts, 1, nullptr, token, (float *)(token + 1), st, false);
-  (void)val;
   cudaFreeAsync(pv, st);
   OPCK(e);
   return G4_OK;
