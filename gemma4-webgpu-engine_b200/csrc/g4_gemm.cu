@@ -32,6 +32,8 @@ __device__ unsigned int g4_trace_n;
 // (the last one records both, then clears them for the next launch).
 __device__ unsigned long long g4_gemm_accmax;
 __device__ unsigned int g4_gemm_done;
+// The latest CTA start and the latest return from the dependency wait over the launch's CTAs.
+__device__ unsigned long long g4_gemm_entrymax, g4_gemm_waitmax;
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long now;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
@@ -219,6 +221,9 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
   auto B = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES; };
   auto P = [&](int s) { return gsm + s * S::STAGE_BYTES + S::A_BYTES + S::B_BYTES; };
 
+#ifdef G4_TRACE
+  const unsigned long long t_entry = gtimer();
+#endif
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int n0 = blockIdx.x * GM_BM, m0 = blockIdx.y * BN;
   // This CTA's K tiles: split blockIdx.z of a.splits (an even share, at least one tile).
@@ -247,13 +252,38 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
   tc_fence_after();
   const uint32_t tmem = *tslot;
   grid_launch_dependents();
+  // The producer requests the first stages' weights before the dependency wait (weights never
+  // depend on the previous kernel), so their fetch overlaps that kernel's tail.
+  const uint32_t wbytes = BITS == 4 ? S::P_BYTES : S::A_BYTES;
+  const int npre = KT < NS ? KT : NS;
+  auto load_w = [&](int kt) {
+    const int s = kt % NS, kg = kt_begin + kt;
+    if (BITS == 4)
+      tma_load_2d(P(s), &tmW, kg * (GM_BK / 2), n0, &full[s]);
+    else
+      tma_load_2d(A(s), &tmW, kg * GM_BK, n0, &full[s]);
+  };
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+    for (int kt = 0; kt < npre; kt++) {
+      mbar_expect_tx(&full[kt], wbytes + S::B_BYTES);
+      load_w(kt);
+    }
+  }
   grid_wait();
   G4_TRACE_POINT(5000 + BITS * 100 + (BN == 64 ? 1 : 2) + (CLU > 1 ? 10 : 0));
+#ifdef G4_TRACE
+  if (t == 64) {
+    atomicMax(&g4_gemm_entrymax, t_entry);
+    atomicMax(&g4_gemm_waitmax, gtimer());
+  }
+#endif
 
   if (warp == 0) {
     if (lane == 0) {
-      // Producer: weights and codes of stage kt, once the MMAs of kt - NS have read the slot.
-      const uint32_t wbytes = BITS == 4 ? S::P_BYTES : S::A_BYTES;
+      // Producer: codes of the prefetched stages, then weights and codes of stage kt once the
+      // MMAs of kt - NS have read the slot.
       int issued = 0;
       for (int kt = 0; kt < KT; kt++) {
         const int s = kt % NS;
@@ -262,13 +292,11 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
           flags[0] = 1;
           break;
         }
-        mbar_expect_tx(&full[s], wbytes + S::B_BYTES);
-        const int kg = kt_begin + kt;
-        if (BITS == 4)
-          tma_load_2d(P(s), &tmW, kg * (GM_BK / 2), n0, &full[s]);
-        else
-          tma_load_2d(A(s), &tmW, kg * GM_BK, n0, &full[s]);
-        tma_load_2d(B(s), &tmX, kg * GM_BK, m0, &full[s]);
+        if (kt >= npre) {
+          mbar_expect_tx(&full[s], wbytes + S::B_BYTES);
+          load_w(kt);
+        }
+        tma_load_2d(B(s), &tmX, (kt_begin + kt) * GM_BK, m0, &full[s]);
         issued = kt + 1;
       }
       // Every copy issued lands before the CTA can leave (the last NS are the ones not yet
@@ -527,6 +555,8 @@ __global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
     const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
     if (atomicAdd(&g4_gemm_done, 1u) == total - 1) {
       G4_TRACE_REC(500000 + id, atomicExch(&g4_gemm_accmax, 0ull));
+      G4_TRACE_REC(600000 + id, atomicExch(&g4_gemm_entrymax, 0ull));
+      G4_TRACE_REC(700000 + id, atomicExch(&g4_gemm_waitmax, 0ull));
       G4_TRACE_REC(400000 + id, gtimer());
       g4_gemm_done = 0;
     }

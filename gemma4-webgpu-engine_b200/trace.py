@@ -37,7 +37,8 @@ _FIXED = {3001: "embed", 3002: "dense (per-layer inputs)", 3003: "per-layer comb
 # GEMM records (id + offset): block 0's accumulator complete, block 0 done, the last CTA done,
 # the latest accumulator-complete time over all CTAs (written by the last CTA).
 _GEMM_PHASE = {0: "[block 0 main loop]", 200000: "[block 0 epilogue]", 300000: "[after block 0 done]",
-               400000: "[last CTA done -> next]", 500000: "[after the last accumulator]"}
+               400000: "[last CTA done -> next]", 500000: "[after the last accumulator]",
+               600000: "[after the last CTA start]", 700000: "[after the last dependency wait]"}
 
 
 def _gemv_name(i: int) -> str:
@@ -53,7 +54,7 @@ def kernel_name(i: int) -> str:
         return _gemv_name(i - 100000) + " [main loop]"
     if 201000 <= i < 202000:
         return _gemv_name(i - 200000) + " [epilogue + release]"
-    if (i % 100000) // 1000 == 5 and i // 100000 in (0, 2, 3, 4, 5) and i % 100000 in _FIXED:
+    if (i % 100000) // 1000 == 5 and i // 100000 in (0, 2, 3, 4, 5, 6, 7) and i % 100000 in _FIXED:
         return _FIXED[i % 100000] + " " + _GEMM_PHASE[i - i % 100000]
     if i in _FIXED:
         return _FIXED[i]
