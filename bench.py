@@ -298,7 +298,6 @@ def run_prefill(pkg, torch, args, world, rank, dev) -> None:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    h0 = time.perf_counter()
     with ClockSampler(dev) as clocks:
         torch.cuda.nvtx.range_push("timed")
         e0.record(stream)
@@ -308,6 +307,16 @@ def run_prefill(pkg, torch, args, world, rank, dev) -> None:
         e1.record(stream)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
+    # End to end (host ids in, host token out) on its own clock, without the sampler's
+    # nvidia-smi processes starting inside the timed region.
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    for _ in range(steps):
+        ctx.kv_truncate(0, 0)
+        ctx.prefill(0, prompt, 0, True)
+    torch.cuda.synchronize()
     wall = time.perf_counter() - h0
     dev_s = max(e0.elapsed_time(e1) / 1e3, 1e-9)
     if world > 1:
