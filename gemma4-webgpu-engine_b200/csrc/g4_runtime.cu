@@ -138,7 +138,9 @@ struct g4_ctx {
   float *logits = nullptr;
   float *head_pv = nullptr;
   int32_t *head_pi = nullptr;
-  int head_blocks = 0;
+  int head_blocks = 0;   // CTAs of the last recorded GEMV head launch
+  int head_cap = 0;      // argmax partials allocated per head column
+  int gemv_target = 0;   // CTAs a GEMV launch is partitioned for (two per SM)
   int32_t *d_step = nullptr;   // [3][maxc]: seq, pos, token
   int32_t *d_tok_out = nullptr;
   float *d_val_out = nullptr;
@@ -503,9 +505,13 @@ static int alloc_runtime(g4_ctx *ctx) {
   ctx->head_cols = std::min(maxc, std::max(ctx->cfg.max_seqs, 1));
   if ((rc = take(&ctx->logits, (size_t)ctx->head_cols * ctx->V))) return rc;
   CK(cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, ctx->dev));
-  ctx->head_blocks = std::min(2 * ctx->sms, ctx->V);
-  if ((rc = take(&ctx->head_pv, (size_t)ctx->head_cols * ctx->head_blocks))) return rc;
-  CK(cudaMalloc(&ctx->head_pi, (size_t)ctx->head_cols * ctx->head_blocks * 4));
+  ctx->gemv_target = 2 * ctx->sms;
+  // A GEMV launch has at most gemv_target CTAs (gemv_stream_partition), each writing one argmax
+  // partial per column in the head.
+  ctx->head_cap = std::min(ctx->gemv_target, ctx->V);
+  ctx->head_blocks = ctx->head_cap;
+  if ((rc = take(&ctx->head_pv, (size_t)ctx->head_cols * ctx->head_cap))) return rc;
+  CK(cudaMalloc(&ctx->head_pi, (size_t)ctx->head_cols * ctx->head_cap * 4));
   CK(cudaMalloc(&ctx->d_step, (size_t)3 * maxc * 4));
   CK(cudaMemset(ctx->d_step, 0, (size_t)3 * maxc * 4));
   CK(cudaMalloc(&ctx->d_tok_out, (size_t)maxc * 4));
@@ -1048,7 +1054,7 @@ static int plan_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, G
     a.ld_logits = ctx->V;
     a.part_val = ctx->head_pv;
     a.part_idx = ctx->head_pi;
-    ok = ok && a.n_blocks_total <= ctx->head_blocks * ctx->head_cols;
+    ok = ok && a.n_blocks_total <= ctx->head_cap * ctx->head_cols;
     ctx->cur_pv = ctx->head_pv;
     ctx->cur_pi = ctx->head_pi;
     ctx->cur_parts = a.n_blocks_total;
@@ -1080,7 +1086,7 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
       g.in_scale = s.lin->in_scale;
       g.out_scale = s.lin->out_scale;
     }
-    const int blocks = gemv_stream_partition(a, 2 * ctx->sms);
+    const int blocks = gemv_stream_partition(a, ctx->gemv_target);
     int np = 0;
     if (c0 == 0)
       for (auto &w : prefetch)
@@ -1096,6 +1102,9 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
     if (a.codes_out) a.codes_out += (size_t)c0 * a.codes_ld;
     if (a.src_codes) a.src_codes += (size_t)c0 * a.ld_codes;
     if (head) {
+      if (blocks > ctx->head_cap || c0 + a.cols > ctx->head_cols)
+        return fail(ctx, G4_ERR_STATE, "head launch of %d CTAs x %d columns exceeds its partial buffers (%d x %d)",
+                    blocks, c0 + a.cols, ctx->head_cap, ctx->head_cols);
       a.head = 1;
       a.logits = ctx->logits + (size_t)c0 * ctx->V;
       a.ld_logits = ctx->V;

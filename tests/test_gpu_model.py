@@ -174,6 +174,26 @@ def test_batched_decode_tensor_core_path(pkg, O, tiny):
     ctx.close()
 
 
+def test_batched_decode_split_k_modes_identical(pkg, O, tiny):
+    """The three K-split forms of few-tile tensor-core launches (thread-block cluster with a
+    distributed-shared-memory sum, none, int32 workspace) give the same logits bit for bit."""
+    a, om = tiny
+    B = 24
+    prompts = [O.synth_prompt(SEED + 70 + b, 4 + (b % 5), a.vocab_size) for b in range(B)]
+    runs = []
+    for mode in (0, 1, 2):
+        ctx = make_ctx(pkg, a, max_seqs=B, max_step_columns=32, gemm_split_k=mode)
+        toks = [ctx.prefill(b, prompts[b], 0, True) for b in range(B)]
+        pos = [len(p) for p in prompts]
+        out = ctx.decode_batch(np.arange(B), toks, pos)
+        runs.append((list(out), [ctx.logits(b).copy() for b in (0, 11, B - 1)]))
+        ctx.close()
+    for toks, logits in runs[1:]:
+        assert toks == runs[0][0]
+        for la, lb in zip(logits, runs[0][1]):
+            np.testing.assert_array_equal(la.view(np.uint32), lb.view(np.uint32))
+
+
 def test_prefill_tensor_core_chunks(pkg, O, tiny):
     """A 100-token prompt in 64-column chunks (64 + 35 producer-only columns on the tensor-core
     path, then the last position on the GEMV path) generates the oracle's tokens; the same
