@@ -186,8 +186,8 @@ __device__ __forceinline__ uint2 unpack8(uint32_t w) {
 constexpr int GM_BM = 128;       // weight rows per tile (MMA M)
 constexpr int GM_BK = 128;       // K per stage: one 128-byte swizzle atom of int8
 
-// NSTAGE 0: the default depth (3 at BN 256, else 4, one CTA per SM); 2: two CTAs share an SM
-// (their epilogues overlap each other's main loops).
+// NSTAGE 0: the default depth (3 at BN 256, 6 at BN 64, else 4, one CTA per SM); 2 (BN 128) or
+// 3 (BN 64): two CTAs share an SM (their epilogues overlap each other's main loops).
 template <int BN, int NSTAGE = 0>
 struct GemmShape {
   static constexpr int STAGES = NSTAGE ? NSTAGE : (BN >= 256 ? 3 : (BN <= 64 ? 6 : 4));
@@ -204,7 +204,7 @@ struct GemmShape {
 // cluster barrier each CTA sums all partials of its share of the tile's token columns through
 // distributed shared memory (exact integer adds, fixed rank order) and runs the epilogue on it.
 template <int BITS, int BN, int EPI, int NSTAGE, int CLU>
-__global__ void __launch_bounds__(192, NSTAGE == 2 ? 2 : 1)
+__global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
     k_qgemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                const GemmArgs a) {
   using S = GemmShape<BN, NSTAGE>;
@@ -886,6 +886,7 @@ static cudaError_t launch_gemm_b(const CUtensorMap &tmW, const CUtensorMap &tmX,
   if (bn == 128) return launch_gemm_t<BITS, 128, EPI>(tmW, tmX, a, st, pdl);
   if (bn == 256) return launch_gemm_t<BITS, 256, EPI>(tmW, tmX, a, st, pdl);
   if (bn == -128) return launch_gemm_t<BITS, 128, EPI, 2>(tmW, tmX, a, st, pdl);
+  if (bn == -64) return launch_gemm_t<BITS, 64, EPI, 3>(tmW, tmX, a, st, pdl);
   return cudaErrorInvalidValue;
 }
 

@@ -989,7 +989,10 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
       if (!tx128) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
       CK(launch_qgemm_persist(l.tmw, *tx128, g, l.bits, std::min(tiles128, ctx->sms), ctx->st, true));
     } else {
-      CK(launch_qgemm(l.tmw, *tx, g, l.bits, bn, ctx->st, true));
+      // Many 64-token tiles (the lm_head of a decode batch: 2,048): three stages, two CTAs per SM,
+      // so one CTA's epilogue runs beside the other's main loop.
+      const int bn_l = bn == 64 && tiles >= 2 * ctx->sms ? -64 : bn;
+      CK(launch_qgemm(l.tmw, *tx, g, l.bits, bn_l, ctx->st, true));
     }
     ctx->launches++;
   }
@@ -1825,7 +1828,7 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
         else if (persist && g.splits <= 1)
           e = launch_qgemm_persist(tw, tx, g, bits, std::min(tiles, sms), st, false);
         else
-          e = launch_qgemm(tw, tx, g, bits, bn, st, false);
+          e = launch_qgemm(tw, tx, g, bits, bn == 64 && tiles >= 2 * sms ? -64 : bn, st, false);
       }
       if (ws) cudaFreeAsync(ws, st);
     }

@@ -82,13 +82,15 @@ def test_qgemv_exact(cuda, lib, O, bits, N, K, cols):
     (4, 6144, 1536, 64, 0.0625), (4, 1000, 1536, 100, 0.0), (4, 1536, 6144, 300, 0.0625),
     (4, 262, 2048, 17, 0.0), (4, 2048, 1536, 129, 0.0625), (8, 256, 1536, 20, 0.0625),
     (8, 1536, 256, 200, 0.0), (8, 300, 1536, 64, 0.0625), (4, 1536, 6144, 64, 0.0625),
-    (4, 2048, 256, 33, 0.0), (8, 1536, 256, 64, 0.0625),
+    (4, 2048, 256, 33, 0.0), (8, 1536, 256, 64, 0.0625), (4, 40000, 256, 40, 0.0625),
+    (8, 38100, 256, 64, 0.0),
 ])
 def test_qgemm_tensor_core_matches_qgemv(cuda, lib, O, bits, N, K, cols, out_s):
     """The tcgen05 int8 GEMM (prefill / batched decode) is column-for-column the qgemv of the
     oracle (src/kernels/qgemm.ts:532-552 contract): y bit-identical, including ragged N (a partial
     128-row tile), ragged columns (partial token tiles), K 6144 (48 pipeline stages) and the K
-    splits of few-tile launches (64-token tiles: clusters of 2, 4 or 8 CTAs; wider: workspace)."""
+    splits of few-tile launches (64-token tiles: clusters of 2, 4 or 8 CTAs; wider: workspace)
+    and the three-stage, two-CTAs-per-SM form of many-tile 64-token launches."""
     wq = RNG.integers(0, 256, N * K * bits // 8, dtype=np.uint8)
     sc = f16_scales(N)
     x = x_on_grid(cols, K, 0.02)
