@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <float.h>
+#include <string.h>
 #include <mutex>
 
 #include "g4_device.cuh"
@@ -205,8 +206,7 @@ struct GemmShape {
 // distributed shared memory (exact integer adds, fixed rank order) and runs the epilogue on it.
 template <int BITS, int BN, int EPI, int NSTAGE, int CLU>
 __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
-    k_qgemm_tc(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-               const GemmArgs a) {
+    k_qgemm_tc(const __grid_constant__ GemmMaps maps, const GemmArgs a) {
   using S = GemmShape<BN, NSTAGE>;
   constexpr int NS = S::STAGES;
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
@@ -225,7 +225,18 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
   const unsigned long long t_entry = gtimer();
 #endif
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int n0 = blockIdx.x * GM_BM, m0 = blockIdx.y * BN;
+  // This CTA's segment (a multi-segment launch) and its tile within it.
+  int sg = 0;
+  for (int i = 1; i < a.nseg; i++)
+    if ((int)blockIdx.x >= a.tile_begin[i]) sg = i;
+  const int gN = sg ? a.more[sg - 1].N : a.N;
+  const uint16_t *gS = sg ? a.more[sg - 1].s : a.s;
+  const float gIn = sg ? a.more[sg - 1].in_scale : a.in_scale;
+  const float gOut = sg ? a.more[sg - 1].out_scale : a.out_scale;
+  float *const gY = sg ? a.more[sg - 1].y : a.y;
+  const int gLdY = sg ? a.more[sg - 1].ld_y : a.ld_y;
+  const CUtensorMap *tmW = &maps.w[sg], *tmX = &maps.x[sg];
+  const int n0 = ((int)blockIdx.x - (sg ? a.tile_begin[sg] : 0)) * GM_BM, m0 = blockIdx.y * BN;
   // This CTA's K tiles: split blockIdx.z of a.splits (an even share, at least one tile).
   const int KTALL = a.K / GM_BK;
   const int kt_begin = (int)(((long long)KTALL * blockIdx.z) / gridDim.z);
@@ -259,13 +270,13 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
   auto load_w = [&](int kt) {
     const int s = kt % NS, kg = kt_begin + kt;
     if (BITS == 4)
-      tma_load_2d(P(s), &tmW, kg * (GM_BK / 2), n0, &full[s]);
+      tma_load_2d(P(s), tmW, kg * (GM_BK / 2), n0, &full[s]);
     else
-      tma_load_2d(A(s), &tmW, kg * GM_BK, n0, &full[s]);
+      tma_load_2d(A(s), tmW, kg * GM_BK, n0, &full[s]);
   };
   if (warp == 0 && lane == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmW)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmX)) : "memory");
     for (int kt = 0; kt < npre; kt++) {
       mbar_expect_tx(&full[kt], wbytes + S::B_BYTES);
       load_w(kt);
@@ -296,7 +307,7 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
           mbar_expect_tx(&full[s], wbytes + S::B_BYTES);
           load_w(kt);
         }
-        tma_load_2d(B(s), &tmX, (kt_begin + kt) * GM_BK, m0, &full[s]);
+        tma_load_2d(B(s), tmX, (kt_begin + kt) * GM_BK, m0, &full[s]);
         issued = kt + 1;
       }
       // Every copy issued lands before the CTA can leave (the last NS are the ones not yet
@@ -365,10 +376,10 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
 #endif
     const int q = warp & 3;
     const int row = n0 + 32 * q + lane;
-    const bool row_ok = row < a.N;
-    const float wscale = row_ok ? f16_bits_to_f32(a.s[row]) : 0.0f;
-    const float sc = __fmul_rn(a.in_scale, wscale);
-    const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
+    const bool row_ok = row < gN;
+    const float wscale = row_ok ? f16_bits_to_f32(gS[row]) : 0.0f;
+    const float sc = __fmul_rn(gIn, wscale);
+    const float out_r = gOut != 0.0f ? __fdiv_rn(1.0f, gOut) : 0.0f;
     bool last = true;
     if (CLU > 1) {
       // Park the partial, int32 [BN tokens][128 rows], over the stage buffers (every MMA that
@@ -426,7 +437,7 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
       for (int j = 0; j < BN; j++) {
         const int slot = j * GM_BM + 32 * q + lane;
         float y = __fmul_rn(sc, (float)ab[slot]);
-        y = srq_out_r(y, a.out_scale, out_r);
+        y = srq_out_r(y, gOut, out_r);
         if (a.softcap != 0.0f) y = __fmul_rn(g4_tanh(__fdiv_rn(y, a.softcap)), a.softcap);
         const int tok = m0 + j;
         if (store && a.logits && row_ok && tok < a.M) a.logits[(size_t)tok * a.ld_logits + row] = y;
@@ -445,7 +456,7 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
         for (int i = 0; i < R; i++) {
           const int r = h * R + ((i + u) & (R - 1));
           const float v = yb[j * GM_BM + r];
-          if (n0 + r < a.N && (v > bv || (v == bv && n0 + r < bi))) {
+          if (n0 + r < gN && (v > bv || (v == bv && n0 + r < bi))) {
             bv = v;
             bi = n0 + r;
           }
@@ -488,8 +499,8 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
       for (int j = 0; j < 32; j++) {
         const int tok = m0 + c0 + j;
         float y = __fmul_rn(sc, (float)(int)acc[j]);
-        y = srq_out_r(y, a.out_scale, out_r);
-        if (store && row_ok && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
+        y = srq_out_r(y, gOut, out_r);
+        if (store && row_ok && tok < a.M) gY[(size_t)tok * gLdY + row] = y;
       }
     }
   }
@@ -502,12 +513,12 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
       constexpr int ITEMS = PER / 4;
       const int u = t - 64, g = u & 31, jb = u >> 5;
       const int t0 = (int)cluster_rank() * PER;
-      const float out_r = a.out_scale != 0.0f ? __fdiv_rn(1.0f, a.out_scale) : 0.0f;
+      const float out_r = gOut != 0.0f ? __fdiv_rn(1.0f, gOut) : 0.0f;
       float sc[4];
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         const int row = n0 + 4 * g + e;
-        sc[e] = row < a.N ? __fmul_rn(a.in_scale, f16_bits_to_f32(a.s[row])) : 0.0f;
+        sc[e] = row < gN ? __fmul_rn(gIn, f16_bits_to_f32(gS[row])) : 0.0f;
       }
       const int32_t *mine = reinterpret_cast<const int32_t *>(gsm) + t0 * GM_BM + 4 * g;
       const bool store = !flags[0] && g4_gemm_error == 0;
@@ -534,8 +545,8 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
         for (int e = 0; e < 4; e++) {
           const int row = n0 + 4 * g + e;
           float y = __fmul_rn(sc[e], (float)sv[e]);
-          y = srq_out_r(y, a.out_scale, out_r);
-          if (store && row < a.N && tok < a.M) a.y[(size_t)tok * a.ld_y + row] = y;
+          y = srq_out_r(y, gOut, out_r);
+          if (store && row < gN && tok < a.M) gY[(size_t)tok * gLdY + row] = y;
         }
       }
     }
@@ -812,9 +823,20 @@ static cudaError_t launch_gemm_persist(const CUtensorMap &tmW, const CUtensorMap
   return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
 }
 
+// Tiles along x: the segments' 128-row tiles end to end.
+static int gemm_x_tiles(const GemmArgs &a) {
+  return a.nseg > 1 ? a.tile_begin[a.nseg] : (a.N + GM_BM - 1) / GM_BM;
+}
+static GemmMaps one_map(const CUtensorMap &tmW, const CUtensorMap &tmX) {
+  GemmMaps m;
+  memset(&m, 0, sizeof(m));
+  m.w[0] = tmW;
+  m.x[0] = tmX;
+  return m;
+}
+
 template <int BITS, int BN, int EPI, int NSTAGE = 0>
-static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
-                                 cudaStream_t st, bool pdl) {
+static cudaError_t launch_gemm_t(const GemmMaps &maps, const GemmArgs &a, cudaStream_t st, bool pdl) {
   auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE, 0>;
   const int smem = GemmShape<BN, NSTAGE>::SMEM;
   static bool attr = false;
@@ -823,7 +845,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX,
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + BN - 1) / BN, a.splits > 1 ? a.splits : 1);
+  cfg.gridDim = dim3(gemm_x_tiles(a), (a.M + BN - 1) / BN, a.splits > 1 ? a.splits : 1);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -832,12 +854,11 @@ static cudaError_t launch_gemm_t(const CUtensorMap &tmW, const CUtensorMap &tmX,
   attr1[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr1;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
+  return cudaLaunchKernelEx(&cfg, k, maps, a);
 }
 
 template <int BITS, int CLU>
-static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
-                                         cudaStream_t st, bool pdl) {
+static cudaError_t launch_gemm_cluster_t(const GemmMaps &maps, const GemmArgs &a, cudaStream_t st, bool pdl) {
   auto k = k_qgemm_tc<BITS, 64, EPI_Y, 0, CLU>;
   const int smem = GemmShape<64, 0>::SMEM;
   static bool attr = false;
@@ -847,7 +868,7 @@ static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorM
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + GM_BM - 1) / GM_BM, (a.M + 63) / 64, CLU);
+  cfg.gridDim = dim3(gemm_x_tiles(a), (a.M + 63) / 64, CLU);
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -860,33 +881,52 @@ static cudaError_t launch_gemm_cluster_t(const CUtensorMap &tmW, const CUtensorM
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, k, tmW, tmX, a);
+  return cudaLaunchKernelEx(&cfg, k, maps, a);
 }
 
-cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
-                                 int bits, cudaStream_t st, bool pdl) {
+static cudaError_t launch_cluster_maps(const GemmMaps &m, const GemmArgs &a, int bits, cudaStream_t st, bool pdl) {
   if (a.K % GM_BK != 0 || a.N < 1 || a.M < 1 || a.head || a.splits > a.K / GM_BK ||
       (bits != 4 && bits != 8))
     return cudaErrorInvalidValue;
   switch (a.splits * 10 + bits) {
-    case 24: return launch_gemm_cluster_t<4, 2>(tmW, tmX, a, st, pdl);
-    case 44: return launch_gemm_cluster_t<4, 4>(tmW, tmX, a, st, pdl);
-    case 84: return launch_gemm_cluster_t<4, 8>(tmW, tmX, a, st, pdl);
-    case 28: return launch_gemm_cluster_t<8, 2>(tmW, tmX, a, st, pdl);
-    case 48: return launch_gemm_cluster_t<8, 4>(tmW, tmX, a, st, pdl);
-    case 88: return launch_gemm_cluster_t<8, 8>(tmW, tmX, a, st, pdl);
+    case 24: return launch_gemm_cluster_t<4, 2>(m, a, st, pdl);
+    case 44: return launch_gemm_cluster_t<4, 4>(m, a, st, pdl);
+    case 84: return launch_gemm_cluster_t<4, 8>(m, a, st, pdl);
+    case 28: return launch_gemm_cluster_t<8, 2>(m, a, st, pdl);
+    case 48: return launch_gemm_cluster_t<8, 4>(m, a, st, pdl);
+    case 88: return launch_gemm_cluster_t<8, 8>(m, a, st, pdl);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
+                                 int bits, cudaStream_t st, bool pdl) {
+  if (a.nseg > 1) return cudaErrorInvalidValue;
+  return launch_cluster_maps(one_map(tmW, tmX), a, bits, st, pdl);
+}
+
+cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, cudaStream_t st, bool pdl) {
+  if (a.nseg < 2 || a.nseg > 3 || a.head || a.M > 64 || a.tile_begin[0] != 0) return cudaErrorInvalidValue;
+  for (int i = 0; i < a.nseg; i++) {
+    const int n = i ? a.more[i - 1].N : a.N;
+    if (n < 1 || a.tile_begin[i + 1] - a.tile_begin[i] != (n + GM_BM - 1) / GM_BM) return cudaErrorInvalidValue;
+  }
+  if (a.splits > 1) return launch_cluster_maps(m, a, bits, st, pdl);
+  if (a.K % GM_BK != 0 || a.K < GM_BK) return cudaErrorInvalidValue;
+  if (bits == 4) return launch_gemm_t<4, 64, EPI_Y>(m, a, st, pdl);
+  if (bits == 8) return launch_gemm_t<8, 64, EPI_Y>(m, a, st, pdl);
+  return cudaErrorInvalidValue;
 }
 
 template <int BITS, int EPI>
 static cudaError_t launch_gemm_b(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  int bn, cudaStream_t st, bool pdl) {
-  if (bn == 64) return launch_gemm_t<BITS, 64, EPI>(tmW, tmX, a, st, pdl);
-  if (bn == 128) return launch_gemm_t<BITS, 128, EPI>(tmW, tmX, a, st, pdl);
-  if (bn == 256) return launch_gemm_t<BITS, 256, EPI>(tmW, tmX, a, st, pdl);
-  if (bn == -128) return launch_gemm_t<BITS, 128, EPI, 2>(tmW, tmX, a, st, pdl);
-  if (bn == -64) return launch_gemm_t<BITS, 64, EPI, 3>(tmW, tmX, a, st, pdl);
+  const GemmMaps m = one_map(tmW, tmX);
+  if (bn == 64) return launch_gemm_t<BITS, 64, EPI>(m, a, st, pdl);
+  if (bn == 128) return launch_gemm_t<BITS, 128, EPI>(m, a, st, pdl);
+  if (bn == 256) return launch_gemm_t<BITS, 256, EPI>(m, a, st, pdl);
+  if (bn == -128) return launch_gemm_t<BITS, 128, EPI, 2>(m, a, st, pdl);
+  if (bn == -64) return launch_gemm_t<BITS, 64, EPI, 3>(m, a, st, pdl);
   return cudaErrorInvalidValue;
 }
 
@@ -905,7 +945,7 @@ cudaError_t launch_qgemm_persist(const CUtensorMap &tmW, const CUtensorMap &tmX,
 
 cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a, int bits,
                          int bn, cudaStream_t st, bool pdl) {
-  if (a.K % GM_BK != 0 || a.K < GM_BK || a.N < 1 || a.M < 1) return cudaErrorInvalidValue;
+  if (a.K % GM_BK != 0 || a.K < GM_BK || a.N < 1 || a.M < 1 || a.nseg > 1) return cudaErrorInvalidValue;
   if (a.splits > 1 && (a.head || !a.acc_ws || !a.tile_cnt || a.splits > a.K / GM_BK || a.ld_ws < a.N))
     return cudaErrorInvalidValue;
   if (bits == 4) {

@@ -163,6 +163,16 @@ struct GemmArgs {
   // Split K (splits > 1): each CTA adds its exact int32 partial into acc_ws[token][ld_ws] (zero on
   // entry, left zero), and the last of a tile's splits to finish (tile_cnt) runs the epilogue.
   int splits; int32_t *acc_ws; int ld_ws; int32_t *tile_cnt;
+  // Several linears over the same codes width in one launch (nseg > 1, no head, no workspace
+  // split): blockIdx.x in [tile_begin[i], tile_begin[i + 1]) is a 128-row tile of segment i,
+  // with tensor maps GemmMaps::w[i] / x[i]. Segment 0 is N, s, in_scale, out_scale, y, ld_y
+  // above; segments 1 and 2 are more[0], more[1].
+  int nseg; int tile_begin[4];
+  struct Seg { int N; const uint16_t *s; float in_scale, out_scale; float *y; int ld_y; } more[2];
+};
+struct GemmMaps {
+  CUtensorMap w[3];   // weights of each segment
+  CUtensorMap x[3];   // activation codes each segment reads
 };
 int make_tmap_u8(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
                  uint64_t row_stride, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
@@ -176,6 +186,8 @@ cudaError_t launch_qgemm_persist(const CUtensorMap &tmW, const CUtensorMap &tmX,
 // int32 partials are reduced through distributed shared memory, no workspace. tmX: box rows 64.
 cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  int bits, cudaStream_t st, bool pdl);
+// One launch over a.nseg segments (maps m.w[i], m.x[i]); a.splits 2/4/8 splits K over a cluster.
+cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, cudaStream_t st, bool pdl);
 int gemm_error_take();
 int gemm_tile_rows();
 

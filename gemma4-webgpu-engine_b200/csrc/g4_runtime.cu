@@ -927,6 +927,49 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   // Token tile: 64 or 128 columns; wider steps use 128-column tiles at two CTAs per SM (one
   // CTA's epilogue runs while the other's MMAs do), or 256-column tiles one per SM.
   const int bn = cols <= 64 ? 64 : (cols <= 128 ? 128 : ctx->gemm_wide_bn);
+  const int nseg = (int)segs.size();
+  bool same_bits = true;
+  for (auto &sg : segs) same_bits = same_bits && sg.lin->bits == segs.begin()->lin->bits;
+  if (nseg > 1 && nseg <= 3 && !head && bn == 64 && same_bits && ctx->gemm_split_k != 2) {
+    // A decode batch's q/k/v or gate/up: one launch, the segments' tiles end to end along x, each
+    // CTA with its segment's weight and code tensor maps; few tiles split K over a cluster.
+    GemmMaps m;
+    memset(&m, 0, sizeof(m));
+    GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    int tb = 0, si = 0;
+    for (auto &sg : segs) {
+      const Linear &l = *sg.lin;
+      const CUtensorMap *tx = codes_tmap(ctx, which[si], K, 64);
+      if (!tx) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
+      m.w[si] = l.tmw;
+      m.x[si] = *tx;
+      if (si == 0) {
+        g.N = l.N;
+        g.s = l.s;
+        g.in_scale = l.in_scale;
+        g.out_scale = l.out_scale;
+        g.y = sg.y;
+        g.ld_y = l.N;
+      } else {
+        g.more[si - 1] = {l.N, l.s, l.in_scale, l.out_scale, sg.y, l.N};
+      }
+      g.tile_begin[si] = tb;
+      tb += (l.N + 127) / 128;
+      si++;
+    }
+    g.tile_begin[nseg] = tb;
+    g.nseg = nseg;
+    g.K = K;
+    g.M = cols;
+    int splits = 1;
+    if (ctx->gemm_split_k == 0)
+      while (splits < 8 && 2 * splits * tb <= ctx->sms && 2 * splits <= K / 128) splits *= 2;
+    g.splits = splits;
+    CK(launch_qgemm_multi(m, g, segs.begin()->lin->bits, ctx->st, true));
+    ctx->launches++;
+    return G4_OK;
+  }
   i = 0;
   for (auto &sg : segs) {
     const Linear &l = *sg.lin;
