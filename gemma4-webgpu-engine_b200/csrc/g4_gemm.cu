@@ -857,10 +857,12 @@ static cudaError_t launch_gemm_t(const GemmMaps &maps, const GemmArgs &a, cudaSt
   return cudaLaunchKernelEx(&cfg, k, maps, a);
 }
 
-template <int BITS, int CLU>
+// NSTAGE 0: six stages, one CTA per SM; 3: three stages, two CTAs per SM (launches of more CTAs
+// than SMs).
+template <int BITS, int CLU, int NSTAGE>
 static cudaError_t launch_gemm_cluster_t(const GemmMaps &maps, const GemmArgs &a, cudaStream_t st, bool pdl) {
-  auto k = k_qgemm_tc<BITS, 64, EPI_Y, 0, CLU>;
-  const int smem = GemmShape<64, 0>::SMEM;
+  auto k = k_qgemm_tc<BITS, 64, EPI_Y, NSTAGE, CLU>;
+  const int smem = GemmShape<64, NSTAGE>::SMEM;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -888,13 +890,23 @@ static cudaError_t launch_cluster_maps(const GemmMaps &m, const GemmArgs &a, int
   if (a.K % GM_BK != 0 || a.N < 1 || a.M < 1 || a.head || a.splits > a.K / GM_BK ||
       (bits != 4 && bits != 8))
     return cudaErrorInvalidValue;
-  switch (a.splits * 10 + bits) {
-    case 24: return launch_gemm_cluster_t<4, 2>(m, a, st, pdl);
-    case 44: return launch_gemm_cluster_t<4, 4>(m, a, st, pdl);
-    case 84: return launch_gemm_cluster_t<4, 8>(m, a, st, pdl);
-    case 28: return launch_gemm_cluster_t<8, 2>(m, a, st, pdl);
-    case 48: return launch_gemm_cluster_t<8, 4>(m, a, st, pdl);
-    case 88: return launch_gemm_cluster_t<8, 8>(m, a, st, pdl);
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool two = gemm_x_tiles(a) * a.splits > sms;
+  switch (a.splits * 100 + bits * 10 + (two ? 1 : 0)) {
+    case 240: return launch_gemm_cluster_t<4, 2, 0>(m, a, st, pdl);
+    case 440: return launch_gemm_cluster_t<4, 4, 0>(m, a, st, pdl);
+    case 840: return launch_gemm_cluster_t<4, 8, 0>(m, a, st, pdl);
+    case 280: return launch_gemm_cluster_t<8, 2, 0>(m, a, st, pdl);
+    case 480: return launch_gemm_cluster_t<8, 4, 0>(m, a, st, pdl);
+    case 880: return launch_gemm_cluster_t<8, 8, 0>(m, a, st, pdl);
+    case 241: return launch_gemm_cluster_t<4, 2, 3>(m, a, st, pdl);
+    case 441: return launch_gemm_cluster_t<4, 4, 3>(m, a, st, pdl);
+    case 841: return launch_gemm_cluster_t<4, 8, 3>(m, a, st, pdl);
+    case 281: return launch_gemm_cluster_t<8, 2, 3>(m, a, st, pdl);
+    case 481: return launch_gemm_cluster_t<8, 4, 3>(m, a, st, pdl);
+    case 881: return launch_gemm_cluster_t<8, 8, 3>(m, a, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
