@@ -741,15 +741,22 @@ k_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K
   }
 }
 
-// Many columns (prefill): warp w of a CTA keeps rows R (8 b + w) .. + R - 1 in registers (read once,
-// before the dependency wait) and walks the columns in tiles of 8 staged in shared memory. Each
-// (row, column) sum is the same per-lane chunk order and butterfly as k_dense_bf16.
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Many columns (prefill, wide batches): warp w of a CTA keeps rows R (8 b + w) .. + R - 1 in
+// registers (read once, before the dependency wait) and walks the columns in tiles of 8 staged
+// in shared memory, double-buffered: the next tile's copy (cp.async) runs under this tile's
+// FMAs. Each (row, column) sum is the same per-lane chunk order and butterfly as k_dense_bf16.
 template <int MAXCH>
 __global__ void __launch_bounds__(256)
 k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K, int cols,
                   float alpha) {
   constexpr int R = MAXCH <= 6 ? 4 : 2, T = 8;
-  extern __shared__ __align__(16) float xs[];  // [T][K]
+  extern __shared__ __align__(16) float xs_both[];  // [2][T][K]
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int row0 = (blockIdx.x * 8 + warp) * R;
   const int nch = K / 8;
@@ -764,14 +771,23 @@ k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int N, 
     }
   grid_launch_dependents();
   grid_wait();
-  for (int c0 = 0; c0 < cols; c0 += T) {
+  G4_TRACE_POINT(3002);
+  auto stage = [&](int c0) {   // request tile c0 into buffer (c0 / T) & 1
+    float *dst = xs_both + ((c0 / T) & 1) * T * K;
     const int nc = min(T, cols - c0);
-    __syncthreads();
     for (int i = t; i < nc * (K / 4); i += 256) {
       const int c = i / (K / 4), k4 = i - c * (K / 4);
-      reinterpret_cast<float4 *>(xs + c * K)[k4] =
-          reinterpret_cast<const float4 *>(x + (size_t)(c0 + c) * ld_x)[k4];
+      cp_async16(dst + c * K + 4 * k4, x + (size_t)(c0 + c) * ld_x + 4 * k4);
     }
+    cp_async_commit();
+  };
+  stage(0);
+  for (int c0 = 0; c0 < cols; c0 += T) {
+    const int nc = min(T, cols - c0);
+    const float *xs = xs_both + ((c0 / T) & 1) * T * K;
+    if (c0 + T < cols) stage(c0 + T);
+    else cp_async_commit();   // an empty group keeps the wait below uniform
+    cp_async_wait_1();        // this tile's copies (all but the newest group) have landed
     __syncthreads();
     float acc[R][T];
 #pragma unroll
@@ -815,6 +831,7 @@ k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int N, 
       }
     const int r = lane / T, c = lane % T;
     if (r < R && row0 + r < N && c < nc) y[(size_t)(c0 + c) * N + row0 + r] = __fmul_rn(alpha, mine);
+    __syncthreads();   // the next iteration's copy overwrites the buffer read here
   }
 }
 
@@ -822,14 +839,14 @@ cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float
                               int cols, float alpha, cudaStream_t st, bool pdl) {
   if (K % 8 != 0 || K > 2048) return cudaErrorInvalidValue;
   if (cols > 8) {
-    const size_t smem = (size_t)8 * K * 4;
+    const size_t smem = (size_t)2 * 8 * K * 4;   // two tiles of 8 columns
     if (K <= 1536) {
       const dim3 grid((N + 31) / 32);
-      cudaFuncSetAttribute(k_dense_bf16_wide<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      cudaFuncSetAttribute(k_dense_bf16_wide<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
       return launch_k(k_dense_bf16_wide<6>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, N, K, cols, alpha);
     }
     const dim3 grid((N + 15) / 16);
-    cudaFuncSetAttribute(k_dense_bf16_wide<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    cudaFuncSetAttribute(k_dense_bf16_wide<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
     return launch_k(k_dense_bf16_wide<8>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, N, K, cols, alpha);
   }
   cudaError_t e = cudaSuccess;
