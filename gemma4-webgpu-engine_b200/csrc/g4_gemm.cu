@@ -918,7 +918,7 @@ cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX,
 }
 
 cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, cudaStream_t st, bool pdl) {
-  if (a.nseg < 2 || a.nseg > 3 || a.head || a.M > 64 || a.tile_begin[0] != 0) return cudaErrorInvalidValue;
+  if (a.nseg < 2 || a.nseg > 3 || a.head || a.tile_begin[0] != 0) return cudaErrorInvalidValue;
   for (int i = 0; i < a.nseg; i++) {
     const int n = i ? a.more[i - 1].N : a.N;
     if (n < 1 || a.tile_begin[i + 1] - a.tile_begin[i] != (n + GM_BM - 1) / GM_BM) return cudaErrorInvalidValue;

@@ -926,7 +926,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   }
   // Token tile: 64 or 128 columns; wider steps use 128-column tiles at two CTAs per SM (one
   // CTA's epilogue runs while the other's MMAs do), or 256-column tiles one per SM.
-  const int bn = cols <= 64 ? 64 : (cols <= 128 ? 128 : ctx->gemm_wide_bn);
+  const int bn = cols <= 64 || cols > 128 && cols <= 512 ? 64 : (cols <= 128 ? 128 : ctx->gemm_wide_bn);
   const int nseg = (int)segs.size();
   bool same_bits = true;
   for (auto &sg : segs) same_bits = same_bits && sg.lin->bits == segs.begin()->lin->bits;
