@@ -893,7 +893,7 @@ static cudaError_t launch_cluster_maps(const GemmMaps &m, const GemmArgs &a, int
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const bool two = gemm_x_tiles(a) * a.splits > sms;
+  const bool two = gemm_x_tiles(a) * ((a.M + 63) / 64) * a.splits > sms;
   switch (a.splits * 100 + bits * 10 + (two ? 1 : 0)) {
     case 240: return launch_gemm_cluster_t<4, 2, 0>(m, a, st, pdl);
     case 440: return launch_gemm_cluster_t<4, 4, 0>(m, a, st, pdl);
@@ -925,8 +925,13 @@ cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, c
   }
   if (a.splits > 1) return launch_cluster_maps(m, a, bits, st, pdl);
   if (a.K % GM_BK != 0 || a.K < GM_BK) return cudaErrorInvalidValue;
-  if (bits == 4) return launch_gemm_t<4, 64, EPI_Y>(m, a, st, pdl);
-  if (bits == 8) return launch_gemm_t<8, 64, EPI_Y>(m, a, st, pdl);
+  // More CTAs than SMs: three stages, two CTAs per SM.
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool two = gemm_x_tiles(a) * ((a.M + 63) / 64) > sms;
+  if (bits == 4) return two ? launch_gemm_t<4, 64, EPI_Y, 3>(m, a, st, pdl) : launch_gemm_t<4, 64, EPI_Y>(m, a, st, pdl);
+  if (bits == 8) return two ? launch_gemm_t<8, 64, EPI_Y, 3>(m, a, st, pdl) : launch_gemm_t<8, 64, EPI_Y>(m, a, st, pdl);
   return cudaErrorInvalidValue;
 }
 

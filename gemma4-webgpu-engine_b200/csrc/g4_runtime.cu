@@ -990,9 +990,9 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     const int kts = K / 128;
     if (ctx->gemm_split_k == 0 && !head && bn == 64 && tiles < ctx->sms) {
       // A launch of fewer tiles than SMs (a decode batch: 2 to 48 tiles) splits K over a cluster
-      // of 2, 4 or 8 CTAs per tile, as many as the SMs hold, each with at least one K stage.
+      // of 2, 4 or 8 CTAs per tile, as many as two per SM hold, each with at least one K stage.
       int splits = 1;
-      while (splits < 8 && 2 * splits * tiles <= ctx->sms && 2 * splits <= kts) splits *= 2;
+      while (splits < 8 && 2 * splits * tiles <= 2 * ctx->sms && 2 * splits <= kts) splits *= 2;
       if (splits > 1) {
         g.splits = splits;
         CK(launch_qgemm_cluster(l.tmw, *tx, g, l.bits, ctx->st, true));
