@@ -962,10 +962,12 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     g.nseg = nseg;
     g.K = K;
     g.M = cols;
-    // Up to two CTAs per SM (the cluster kernel drops to three stages past one per SM).
+    // Up to two CTAs per SM over all (row, token) tiles (the cluster kernel drops to three
+    // stages past one per SM).
+    const int all_tiles = tb * ((cols + 63) / 64);
     int splits = 1;
     if (ctx->gemm_split_k == 0)
-      while (splits < 8 && 2 * splits * tb <= 2 * ctx->sms && 2 * splits <= K / 128) splits *= 2;
+      while (splits < 8 && 2 * splits * all_tiles <= 2 * ctx->sms && 2 * splits <= K / 128) splits *= 2;
     g.splits = splits;
     CK(launch_qgemm_multi(m, g, segs.begin()->lin->bits, ctx->st, true));
     ctx->launches++;
