@@ -926,7 +926,15 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   }
   // Token tile: 64 or 128 columns; wider steps use 128-column tiles at two CTAs per SM (one
   // CTA's epilogue runs while the other's MMAs do), or 256-column tiles one per SM.
-  const int bn = cols <= 64 || cols > 128 && cols <= 512 ? 64 : (cols <= 128 ? 128 : ctx->gemm_wide_bn);
+  int bn = cols <= 64 || cols > 128 && cols <= 512 ? 64 : (cols <= 128 ? 128 : ctx->gemm_wide_bn);
+  if (cols > 128 && bn == 64) {
+    // 129-512 columns: 64-token tiles where the launch is small enough to split K or to merge
+    // segments; a group with two SMs' worth of 64-token tiles or more (a box step's gate/up)
+    // keeps 128-token tiles, which unpack each weight tile for twice the tokens.
+    int xt = 0;
+    for (auto &sg : segs) xt += (sg.lin->N + 127) / 128;
+    if (xt * ((cols + 63) / 64) >= 2 * ctx->sms) bn = ctx->gemm_wide_bn;
+  }
   const int nseg = (int)segs.size();
   bool same_bits = true;
   for (auto &sg : segs) same_bits = same_bits && sg.lin->bits == segs.begin()->lin->bits;
