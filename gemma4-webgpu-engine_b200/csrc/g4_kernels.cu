@@ -688,7 +688,7 @@ cudaError_t launch_embed_op(const uint8_t *codes, const uint16_t *scales, const 
 
 template <int COLS>
 __global__ void __launch_bounds__(256)
-k_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K, int cols,
+k_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int ld_y, int N, int K, int cols,
              float alpha) {
   extern __shared__ __align__(16) float xs[];  // [COLS][K]
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -737,7 +737,7 @@ k_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K
 #pragma unroll
   for (int c = 0; c < COLS; c++) {
     float sum = warp_sum_bfly(acc[c]);
-    if (lane == 0 && c < cols) y[(size_t)c * N + row] = __fmul_rn(alpha, sum);
+    if (lane == 0 && c < cols) y[(size_t)c * ld_y + row] = __fmul_rn(alpha, sum);
   }
 }
 
@@ -753,7 +753,7 @@ __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_
 // FMAs. Each (row, column) sum is the same per-lane chunk order and butterfly as k_dense_bf16.
 template <int MAXCH>
 __global__ void __launch_bounds__(256)
-k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K, int cols,
+k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int ld_y, int N, int K, int cols,
                   float alpha) {
   constexpr int R = MAXCH <= 6 ? 4 : 2, T = 8;
   extern __shared__ __align__(16) float xs_both[];  // [2][T][K]
@@ -830,12 +830,12 @@ k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int N, 
         if (lane == r * T + c) mine = sum;
       }
     const int r = lane / T, c = lane % T;
-    if (r < R && row0 + r < N && c < nc) y[(size_t)(c0 + c) * N + row0 + r] = __fmul_rn(alpha, mine);
+    if (r < R && row0 + r < N && c < nc) y[(size_t)(c0 + c) * ld_y + row0 + r] = __fmul_rn(alpha, mine);
     __syncthreads();   // the next iteration's copy overwrites the buffer read here
   }
 }
 
-cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K,
+cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int ld_y, int N, int K,
                               int cols, float alpha, cudaStream_t st, bool pdl) {
   if (K % 8 != 0 || K > 2048) return cudaErrorInvalidValue;
   if (cols > 8) {
@@ -843,11 +843,11 @@ cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float
     if (K <= 1536) {
       const dim3 grid((N + 31) / 32);
       cudaFuncSetAttribute(k_dense_bf16_wide<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
-      return launch_k(k_dense_bf16_wide<6>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, N, K, cols, alpha);
+      return launch_k(k_dense_bf16_wide<6>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, ld_y, N, K, cols, alpha);
     }
     const dim3 grid((N + 15) / 16);
     cudaFuncSetAttribute(k_dense_bf16_wide<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
-    return launch_k(k_dense_bf16_wide<8>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, N, K, cols, alpha);
+    return launch_k(k_dense_bf16_wide<8>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, ld_y, N, K, cols, alpha);
   }
   cudaError_t e = cudaSuccess;
   for (int c0 = 0; c0 < cols && e == cudaSuccess; c0 += 8) {
@@ -855,13 +855,13 @@ cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float
     size_t smem = (size_t)nc * K * 4;
     dim3 grid((N + 7) / 8);
     const float *xc = x + (size_t)c0 * ld_x;
-    float *yc = y + (size_t)c0 * N;
-    if (nc <= 1) e = launch_k(k_dense_bf16<1>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, N, K, nc, alpha);
-    else if (nc <= 2) e = launch_k(k_dense_bf16<2>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, N, K, nc, alpha);
-    else if (nc <= 4) e = launch_k(k_dense_bf16<4>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, N, K, nc, alpha);
+    float *yc = y + (size_t)c0 * ld_y;
+    if (nc <= 1) e = launch_k(k_dense_bf16<1>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, ld_y, N, K, nc, alpha);
+    else if (nc <= 2) e = launch_k(k_dense_bf16<2>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, ld_y, N, K, nc, alpha);
+    else if (nc <= 4) e = launch_k(k_dense_bf16<4>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, ld_y, N, K, nc, alpha);
     else {
       cudaFuncSetAttribute(k_dense_bf16<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-      e = launch_k(k_dense_bf16<8>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, N, K, nc, alpha);
+      e = launch_k(k_dense_bf16<8>, grid, dim3(256), smem, st, pdl, w, xc, ld_x, yc, ld_y, N, K, nc, alpha);
     }
   }
   return e;
@@ -890,10 +890,10 @@ k_ple_combine(const float *proj, const float *identity, const float *gain, float
 }
 
 cudaError_t launch_ple_combine(const float *proj, const float *identity, const float *gain,
-                               float *out, int cols, int groups, int group_dim, float eps,
+                               float *out, int cols, int groups, int group_dim, int row_width, float eps,
                                float scale, cudaStream_t st, bool pdl) {
   return launch_k(k_ple_combine, dim3(cols, groups), dim3(256), 0, st, pdl, proj, identity, gain,
-                  out, groups * group_dim, group_dim, eps, scale);
+                  out, row_width, group_dim, eps, scale);
 }
 
 // =====================================================================================

@@ -104,11 +104,11 @@ cudaError_t launch_embed_op(const uint8_t *codes, const uint16_t *scales, const 
                             float *dst, int slots, int cols, int group, float out_scale,
                             int slice_start, int slice_rows, cudaStream_t st, bool pdl);
 
-cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int N, int K,
+cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float *y, int ld_y, int N, int K,
                               int cols, float alpha, cudaStream_t st, bool pdl);
 
 cudaError_t launch_ple_combine(const float *proj, const float *identity, const float *gain,
-                               float *out, int cols, int groups, int group_dim, float eps,
+                               float *out, int cols, int groups, int group_dim, int row_width, float eps,
                                float scale, cudaStream_t st, bool pdl);
 
 struct AttnPro {

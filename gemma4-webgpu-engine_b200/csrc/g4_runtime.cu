@@ -1218,10 +1218,12 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     CK(launch_embed(d_tok, cols, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
                     (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H,
                     ctx->ple_cols, PD, ctx->res[0], ctx->ple_id, ctx->st, true));
-    CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, H, cols,
+    // Per-layer inputs of the layers this step runs (rows are layer-major): a prefill chunk's
+    // producer-only columns need the first n_layers groups only.
+    CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, n_layers * PD, H, cols,
                          (float)std::pow((double)H, -0.5), ctx->st, true));
-    CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, ctx->NL, PD,
-                          eps, (float)0.7071067811865476, ctx->st, true));
+    CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, n_layers, PD,
+                          ctx->ple_cols, eps, (float)0.7071067811865476, ctx->st, true));
   }
   ctx->launches += 3;
   int cur = 0;
@@ -2095,7 +2097,7 @@ extern "C" int g4_op_dense_bf16(const void *w, const float *x, float *y, int32_t
                                 int32_t cols, float alpha, void *stream) {
   if (!w || !x || !y || N < 1 || cols < 1) return fail(nullptr, G4_ERR_INVALID, "g4_op_dense_bf16: bad argument");
   if (K % 8 != 0 || K > 2048) return fail(nullptr, G4_ERR_UNSUPPORTED, "dense K %d (multiple of 8 up to 2048)", K);
-  OPCK(launch_dense_bf16((const uint16_t *)w, x, K, y, N, K, cols, alpha, (cudaStream_t)stream, false));
+  OPCK(launch_dense_bf16((const uint16_t *)w, x, K, y, N, N, K, cols, alpha, (cudaStream_t)stream, false));
   return G4_OK;
 }
 
