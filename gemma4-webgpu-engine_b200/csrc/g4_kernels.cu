@@ -1146,7 +1146,8 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
   grid_wait();
   G4_TRACE_POINT(2100 + HD);
   const int t = threadIdx.x;
-  const int c0 = blockIdx.x * QT;
+  // The last query tiles of a chunk see the most keys: they start first (longest work first).
+  const int c0 = ((int)gridDim.x - 1 - (int)blockIdx.x) * QT;
   const int nq = min(QT, a.cols - c0);
   const int seq = a.refs.seq ? a.refs.seq[c0] : 0;
   const float *K = a.cache + (size_t)seq * a.seq_stride;
