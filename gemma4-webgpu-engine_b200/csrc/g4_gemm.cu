@@ -917,14 +917,20 @@ cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX,
   return launch_cluster_maps(one_map(tmW, tmX), a, bits, st, pdl);
 }
 
-cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, cudaStream_t st, bool pdl) {
+cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, int bn, cudaStream_t st, bool pdl) {
   if (a.nseg < 2 || a.nseg > 3 || a.head || a.tile_begin[0] != 0) return cudaErrorInvalidValue;
   for (int i = 0; i < a.nseg; i++) {
     const int n = i ? a.more[i - 1].N : a.N;
     if (n < 1 || a.tile_begin[i + 1] - a.tile_begin[i] != (n + GM_BM - 1) / GM_BM) return cudaErrorInvalidValue;
   }
-  if (a.splits > 1) return launch_cluster_maps(m, a, bits, st, pdl);
+  if (bn != 64 && bn != -128) return cudaErrorInvalidValue;
+  if (a.splits > 1) return bn == 64 ? launch_cluster_maps(m, a, bits, st, pdl) : cudaErrorInvalidValue;
   if (a.K % GM_BK != 0 || a.K < GM_BK) return cudaErrorInvalidValue;
+  if (bn == -128) {
+    if (bits == 4) return launch_gemm_t<4, 128, EPI_Y, 2>(m, a, st, pdl);
+    if (bits == 8) return launch_gemm_t<8, 128, EPI_Y, 2>(m, a, st, pdl);
+    return cudaErrorInvalidValue;
+  }
   // More CTAs than SMs: three stages, two CTAs per SM.
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);

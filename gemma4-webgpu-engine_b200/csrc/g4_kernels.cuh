@@ -186,8 +186,9 @@ cudaError_t launch_qgemm_persist(const CUtensorMap &tmW, const CUtensorMap &tmX,
 // int32 partials are reduced through distributed shared memory, no workspace. tmX: box rows 64.
 cudaError_t launch_qgemm_cluster(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a,
                                  int bits, cudaStream_t st, bool pdl);
-// One launch over a.nseg segments (maps m.w[i], m.x[i]); a.splits 2/4/8 splits K over a cluster.
-cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, cudaStream_t st, bool pdl);
+// One launch over a.nseg segments (maps m.w[i], m.x[i]); token tile bn 64 (a.splits 2/4/8 splits
+// K over a cluster) or -128 (128-token tiles, two CTAs per SM, no split).
+cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, int bn, cudaStream_t st, bool pdl);
 int gemm_error_take();
 int gemm_tile_rows();
 

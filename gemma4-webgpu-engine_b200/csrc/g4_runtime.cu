@@ -938,9 +938,9 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   const int nseg = (int)segs.size();
   bool same_bits = true;
   for (auto &sg : segs) same_bits = same_bits && sg.lin->bits == segs.begin()->lin->bits;
-  if (nseg > 1 && nseg <= 3 && !head && bn == 64 && same_bits && ctx->gemm_split_k != 2) {
-    // A decode batch's q/k/v or gate/up: one launch, the segments' tiles end to end along x, each
-    // CTA with its segment's weight and code tensor maps; few tiles split K over a cluster.
+  if (nseg > 1 && nseg <= 3 && !head && (bn == 64 || bn == -128) && same_bits && ctx->gemm_split_k != 2) {
+    // q/k/v or gate/up: one launch, the segments' tiles end to end along x, each CTA with its
+    // segment's weight and code tensor maps; with 64-token tiles, few tiles split K over a cluster.
     GemmMaps m;
     memset(&m, 0, sizeof(m));
     GemmArgs g;
@@ -948,7 +948,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     int tb = 0, si = 0;
     for (auto &sg : segs) {
       const Linear &l = *sg.lin;
-      const CUtensorMap *tx = codes_tmap(ctx, which[si], K, 64);
+      const CUtensorMap *tx = codes_tmap(ctx, which[si], K, bn < 0 ? -bn : bn);
       if (!tx) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
       m.w[si] = l.tmw;
       m.x[si] = *tx;
@@ -974,10 +974,10 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     // stages past one per SM).
     const int all_tiles = tb * ((cols + 63) / 64);
     int splits = 1;
-    if (ctx->gemm_split_k == 0)
+    if (ctx->gemm_split_k == 0 && bn == 64)
       while (splits < 8 && 2 * splits * all_tiles <= 2 * ctx->sms && 2 * splits <= K / 128) splits *= 2;
     g.splits = splits;
-    CK(launch_qgemm_multi(m, g, segs.begin()->lin->bits, ctx->st, true));
+    CK(launch_qgemm_multi(m, g, segs.begin()->lin->bits, bn, ctx->st, true));
     ctx->launches++;
     return G4_OK;
   }

@@ -194,19 +194,21 @@ def test_batched_decode_split_k_modes_identical(pkg, O, tiny):
             np.testing.assert_array_equal(la.view(np.uint32), lb.view(np.uint32))
 
 
-@pytest.mark.parametrize("n,chunk", [(100, 64), (200, 256)])
+@pytest.mark.parametrize("n,chunk", [(100, 64), (200, 256), (600, 1024)])
 def test_prefill_tensor_core_chunks(pkg, O, tiny, n, chunk):
     """A 100-token prompt in 64-column chunks (64 + 35 producer-only columns on the tensor-core
-    path, then the last position on the GEMV path), and a 200-token prompt in one 199-column
-    chunk (64-token tiles, multi-segment launches over several token tiles), generate the
-    oracle's tokens; the same prompt with the tensor-core path switched off gives the same
-    logits bit for bit."""
+    path, then the last position on the GEMV path), a 200-token prompt in one 199-column chunk
+    (64-token tiles, multi-segment launches over several token tiles) and a 600-token prompt in
+    one 599-column chunk (128-token tiles at two CTAs per SM, multi-segment q/k/v and gate/up)
+    generate the oracle's tokens; the same prompt with the tensor-core path switched off gives
+    the same logits bit for bit."""
     a, om = tiny
+    max_ctx = 1024 if n > 256 else 256
     prompt = O.synth_prompt(SEED + 7, n, a.vocab_size)
-    want, _ = om.generate(prompt, 4, 256)
+    want, _ = om.generate(prompt, 4, max_ctx)
     logits = []
     for gmin in (16, 1 << 20):
-        ctx = make_ctx(pkg, a, max_step_columns=chunk, max_context=256, gemm_min_columns=gmin)
+        ctx = make_ctx(pkg, a, max_step_columns=chunk, max_context=max_ctx, gemm_min_columns=gmin)
         got = [ctx.prefill(0, prompt, 0, True)]
         logits.append(ctx.logits(0).copy())
         for i in range(1, 4):
