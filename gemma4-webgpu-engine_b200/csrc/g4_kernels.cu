@@ -772,20 +772,23 @@ k_dense_bf16_wide(const uint16_t *w, const float *x, int ld_x, float *y, int ld_
   grid_launch_dependents();
   grid_wait();
   G4_TRACE_POINT(3002);
+  // This CTA's columns: grid.y splits them into ranges of whole tiles.
+  const int span = ((cols + (int)gridDim.y - 1) / (int)gridDim.y + T - 1) / T * T;
+  const int c_begin = (int)blockIdx.y * span, c_end = min(cols, c_begin + span);
   auto stage = [&](int c0) {   // request tile c0 into buffer (c0 / T) & 1
     float *dst = xs_both + ((c0 / T) & 1) * T * K;
-    const int nc = min(T, cols - c0);
+    const int nc = min(T, c_end - c0);
     for (int i = t; i < nc * (K / 4); i += 256) {
       const int c = i / (K / 4), k4 = i - c * (K / 4);
       cp_async16(dst + c * K + 4 * k4, x + (size_t)(c0 + c) * ld_x + 4 * k4);
     }
     cp_async_commit();
   };
-  stage(0);
-  for (int c0 = 0; c0 < cols; c0 += T) {
-    const int nc = min(T, cols - c0);
+  if (c_begin < c_end) stage(c_begin);
+  for (int c0 = c_begin; c0 < c_end; c0 += T) {
+    const int nc = min(T, c_end - c0);
     const float *xs = xs_both + ((c0 / T) & 1) * T * K;
-    if (c0 + T < cols) stage(c0 + T);
+    if (c0 + T < c_end) stage(c0 + T);
     else cp_async_commit();   // an empty group keeps the wait below uniform
     cp_async_wait_1();        // this tile's copies (all but the newest group) have landed
     __syncthreads();
@@ -840,12 +843,28 @@ cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float
   if (K % 8 != 0 || K > 2048) return cudaErrorInvalidValue;
   if (cols > 8) {
     const size_t smem = (size_t)2 * 8 * K * 4;   // two tiles of 8 columns
+    // Column ranges along grid.y: the split (up to 16, at least two tiles each) that fills the
+    // SMs' waves best (one CTA per SM).
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int row_ctas = K <= 1536 ? (N + 31) / 32 : (N + 15) / 16;
+    int gy = 1;
+    double best = 0.0;
+    for (int y = 1; y <= 16 && (y == 1 || cols / y >= 16); y++) {
+      const int ctas = row_ctas * y, waves = (ctas + sms - 1) / sms;
+      const double eff = (double)ctas / ((double)waves * sms) - 0.01 * y;   // small cost per split
+      if (eff > best) {
+        best = eff;
+        gy = y;
+      }
+    }
     if (K <= 1536) {
-      const dim3 grid((N + 31) / 32);
+      const dim3 grid((N + 31) / 32, gy);
       cudaFuncSetAttribute(k_dense_bf16_wide<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
       return launch_k(k_dense_bf16_wide<6>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, ld_y, N, K, cols, alpha);
     }
-    const dim3 grid((N + 15) / 16);
+    const dim3 grid((N + 15) / 16, gy);
     cudaFuncSetAttribute(k_dense_bf16_wide<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
     return launch_k(k_dense_bf16_wide<8>, grid, dim3(256), smem, st, pdl, w, x, ld_x, y, ld_y, N, K, cols, alpha);
   }

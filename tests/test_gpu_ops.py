@@ -321,7 +321,8 @@ def test_embed_gather_sliced(cuda, lib, O):
 
 
 @pytest.mark.parametrize("N,K,cols", [(8960, 1536, 1), (1000, 1536, 3), (333, 256, 9),
-                                      (8960, 1536, 70), (1000, 2048, 40), (130, 1536, 17)])
+                                      (8960, 1536, 70), (1000, 2048, 40), (130, 1536, 17),
+                                      (300, 1536, 100)])
 def test_dense_bf16(cuda, lib, O, N, K, cols):
     """One to eight columns: the per-launch kernel; more (prefill): the column-tiled kernel that
     reads the weights once. Both keep the per-lane chunk order, so both are bit-exact."""
