@@ -966,8 +966,44 @@ __global__ void __launch_bounds__(256) k_attn_prologue(const AttnPro a) {
   }
 }
 
+// The same prologue at head dim 256 / 512 with one warp per (column, role) row (eight rows per
+// CTA, no block barriers): head_norm_rope_warp's sum of squares follows block_sumsq256's order,
+// so the results are the block kernel's bit for bit.
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_prologue_w(const AttnPro a) {
+  grid_launch_dependents();
+  grid_wait();
+  const int lane = threadIdx.x & 31;
+  const int roles = a.heads + (a.k ? 2 : 0);
+  const int gw = (int)blockIdx.x * 8 + (int)(threadIdx.x >> 5);
+  if (gw >= a.cols * roles) return;
+  const int c = gw / roles, role = gw - c * roles;
+  const int tab = a.tab_row ? a.tab_row[c] : c / a.rows_per_col_tab;
+  const float *ct = a.cos_tab + (size_t)tab * (HD / 2);
+  const float *stb = a.sin_tab + (size_t)tab * (HD / 2);
+  if (role < a.heads) {
+    head_norm_rope_warp<HD>(a.q + (size_t)c * a.q_ld + (size_t)role * HD, a.qgain, ct, stb, a.eps,
+                            a.qr + (size_t)c * a.heads * HD + (size_t)role * HD, nullptr, lane);
+    return;
+  }
+  const int seq = a.refs.seq ? a.refs.seq[c] : 0;
+  const int cpos = a.refs.pos ? a.refs.pos[c] : a.refs.pos_base + c;
+  float *kbase = a.cache + (size_t)seq * a.seq_stride;
+  if (role == a.heads)
+    head_norm_rope_warp<HD>(a.k + (size_t)c * a.kv_ld, a.kgain, ct, stb, a.eps, kbase + (size_t)cpos * HD,
+                            nullptr, lane);
+  else
+    head_norm_rope_warp<HD>(a.v + (size_t)c * a.kv_ld, nullptr, nullptr, nullptr, a.eps,
+                            kbase + (size_t)a.max_ctx * HD + (size_t)cpos * HD, nullptr, lane);
+}
+
 cudaError_t launch_attn_prologue(const AttnPro &a, cudaStream_t st, bool pdl) {
   int roles = a.heads + (a.k ? 2 : 0);
+  if ((a.hd == 256 || a.hd == 512) && (!a.k || a.cache)) {
+    const dim3 grid((a.cols * roles + 7) / 8);
+    if (a.hd == 256) return launch_k(k_attn_prologue_w<256>, grid, dim3(256), 0, st, pdl, a);
+    return launch_k(k_attn_prologue_w<512>, grid, dim3(256), 0, st, pdl, a);
+  }
   return launch_k(k_attn_prologue, dim3(a.cols, roles), dim3(256), (size_t)a.hd * 4, st, pdl, a);
 }
 
