@@ -68,8 +68,8 @@ def token_bytes(ctx_len: int) -> dict:
 
 GEMV_N, GEMV_K = 6144, 1536
 GEMV_BYTES = GEMV_N * GEMV_K // 2 + 2 * GEMV_N + GEMV_K + 2 * GEMV_N  # W + scales + x(int8) + y(f16)
-# dram__bytes_read.sum + dram__bytes_write.sum of one config-1 GEMV launch, from the ncu capture
-# summarised in profiles/qgemv_stream_config1.md.
+# dram__bytes_read.sum + dram__bytes_write.sum of one config-1 GEMV launch, from an ncu capture
+# of this kernel on the config-1 shape (the weights cross DRAM once).
 GEMV_TRAFFIC = 4_793_856
 
 

@@ -1,6 +1,6 @@
 """ctypes binding of include/g4.h (libgemma4_cuda.so).
 
-This is the Python twin of the N-API addon a TypeScript host would bind (INTEGRATION.md): every
+This is the Python twin of the N-API addon a TypeScript host would bind: every
 declaration of g4.h, with status codes turned into exceptions that carry g4_last_error's text.
 """
 from __future__ import annotations

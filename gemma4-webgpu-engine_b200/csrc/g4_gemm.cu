@@ -805,11 +805,10 @@ static cudaError_t launch_gemm_persist(const CUtensorMap &tmW, const CUtensorMap
                                        int grid, cudaStream_t st, bool pdl) {
   auto k = k_qgemm_persist<BITS, BN, EPI>;
   const int smem = GemmShape<BN, 4>::SMEM + 64;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  attr([&] {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  });
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(320);
@@ -839,11 +838,10 @@ template <int BITS, int BN, int EPI, int NSTAGE = 0>
 static cudaError_t launch_gemm_t(const GemmMaps &maps, const GemmArgs &a, cudaStream_t st, bool pdl) {
   auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE, 0>;
   const int smem = GemmShape<BN, NSTAGE>::SMEM;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  attr([&] {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  });
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gemm_x_tiles(a), (a.M + BN - 1) / BN, a.splits > 1 ? a.splits : 1);
   cfg.blockDim = dim3(192);
@@ -863,12 +861,11 @@ template <int BITS, int CLU, int NSTAGE>
 static cudaError_t launch_gemm_cluster_t(const GemmMaps &maps, const GemmArgs &a, cudaStream_t st, bool pdl) {
   auto k = k_qgemm_tc<BITS, 64, EPI_Y, NSTAGE, CLU>;
   const int smem = GemmShape<64, NSTAGE>::SMEM;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  attr([&] {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
-    attr = true;
-  }
+  });
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gemm_x_tiles(a), (a.M + 63) / 64, CLU);
   cfg.blockDim = dim3(192);

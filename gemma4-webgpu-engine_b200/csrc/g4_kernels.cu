@@ -506,12 +506,11 @@ static cudaError_t launch_stream_t(const GemvArgs &a0, cudaStream_t st, bool pdl
   const GsLayout lay = gs_layout(a.ring_bytes, COLS, max_rows, nsub, EPI == EPI_GELU_CODES, a.K);
   if (lay.total > 200 * 1024) return cudaErrorInvalidConfiguration;
   auto k = k_qgemv_stream<BITS, COLS, RS, PRO, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static DeviceOnce attr_set;
+  attr_set([&] {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr_set = true;
-  }
+  });
   return launch_k(k, dim3(a.n_blocks_total), dim3(256), (size_t)lay.total, st, pdl, a);
 }
 
@@ -1412,12 +1411,11 @@ static size_t attn_prefill_smem() {
 
 cudaError_t launch_attention_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
   if (a.heads != 8 || a.kv_cap != 0) return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  attr([&] {
     cudaFuncSetAttribute(k_attn_prefill<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_prefill_smem<256>());
     cudaFuncSetAttribute(k_attn_prefill<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_prefill_smem<512>());
-    attr = true;
-  }
+  });
   if (a.hd == 256)
     return launch_k(k_attn_prefill<256>, dim3((a.cols + 7) / 8), dim3(256), attn_prefill_smem<256>(), st, pdl, a);
   if (a.hd == 512)
@@ -1428,12 +1426,11 @@ cudaError_t launch_attention_prefill(const AttnArgs &a, cudaStream_t st, bool pd
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl) {
   if (a.heads != 8) return cudaErrorInvalidValue;
   size_t smem = ((size_t)8 * a.hd + 8 * ATT_BLK * 2 + 32 + (size_t)ATT_BLK * a.hd) * 4;
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  attr([&] {
     cudaFuncSetAttribute(k_attn_blocks<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k_attn_blocks<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  });
   dim3 g1(a.cols, a.max_blocks), g2(a.cols, 8);
   cudaError_t e;
   if (a.hd == 256) {
@@ -1810,13 +1807,12 @@ static size_t attn_decode_smem() {
 
 template <int HD, int NHL>
 static cudaError_t launch_attn_decode_t(const AttnDec &a, cudaStream_t st, bool pdl) {
-  static bool attr_set = false;
-  if (!attr_set) {
+  static DeviceOnce attr_set;
+  attr_set([&] {
     cudaFuncSetAttribute(k_attn_decode<HD, NHL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)attn_decode_smem<HD, NHL>());
     cudaFuncSetAttribute(k_attn_decode<HD, NHL>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr_set = true;
-  }
+  });
   return launch_k(k_attn_decode<HD, NHL>, dim3(a.cols, a.max_blocks, 8 / NHL), dim3(256),
                   attn_decode_smem<HD, NHL>(), st, pdl, a);
 }

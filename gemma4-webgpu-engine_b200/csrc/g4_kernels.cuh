@@ -5,7 +5,33 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 namespace g4 {
+
+// Runs a set-up function once per (call site, CUDA device). Function attributes such as the
+// dynamic shared-memory limit belong to the device that is current when they are set, so a
+// process that drives several devices must set them on each. Thread-safe; device ordinals past
+// 63 run the set-up on every call.
+struct DeviceOnce {
+  std::atomic<uint64_t> done{0};
+  std::mutex m;
+  template <class F>
+  void operator()(F &&f) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+      f();
+      return;
+    }
+    const uint64_t bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return;
+    std::lock_guard<std::mutex> g(m);
+    if (done.load(std::memory_order_relaxed) & bit) return;
+    f();
+    done.fetch_or(bit, std::memory_order_release);
+  }
+};
 
 // Activation prologue a quantized linear applies before snapping its input to int8 codes.
 enum Prologue : int {

@@ -32,13 +32,11 @@ static __device__ __align__(256) float g4_attention_scratch[kScratchFloats];
 
 constexpr int kMaxDevices = 64;
 
-struct DeviceScratch {
-  std::once_flag once;
-  float *ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
-
-DeviceScratch g_scratch[kMaxDevices];
+// The array's device address per device. Only a successful lookup is kept: a lookup that fails
+// (for instance a first call made while the stream is being captured and the module is not yet
+// loaded) leaves the slot empty, and the next call tries again.
+std::mutex g_scratch_mutex;
+float *g_scratch[kMaxDevices] = {};
 
 int set_error(int code, const char *fmt, ...) {
   char buf[512];
@@ -52,24 +50,47 @@ int set_error(int code, const char *fmt, ...) {
 
 }  // namespace
 
-// The device address of the scratch array on `device`, looked up once per device with that
-// device current. Host code must never pass &g4_attention_scratch itself to a kernel: on the host
-// that name is only a stand-in, not a device address.
+// The device address of the scratch array on `device`, looked up with that device current (the
+// caller has made it current). Host code must never pass &g4_attention_scratch itself to a
+// kernel: on the host that name is only a stand-in, not a device address.
 static int scratch_for(int device, float **out) {
   if (device < 0 || device >= kMaxDevices)
     return set_error(G4_ERR_UNSUPPORTED, "device ordinal %d outside the %d supported", device, kMaxDevices);
-  DeviceScratch &s = g_scratch[device];
-  std::call_once(s.once, [&] {
-    s.err = cudaSetDevice(device);
-    if (s.err == cudaSuccess) s.err = cudaGetSymbolAddress((void **)&s.ptr, g4_attention_scratch);
-  });
-  if (s.err != cudaSuccess || !s.ptr) {
-    g4_internal_set_error((std::string("attention scratch set-up failed: ") + cudaGetErrorString(s.err)).c_str());
-    return G4_ERR_CUDA;
+  std::lock_guard<std::mutex> g(g_scratch_mutex);
+  if (!g_scratch[device]) {
+    float *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress((void **)&p, g4_attention_scratch);
+    if (e != cudaSuccess || !p) {
+      cudaGetLastError();
+      g4_internal_set_error((std::string("attention scratch set-up failed: ") + cudaGetErrorString(e)).c_str());
+      return G4_ERR_CUDA;
+    }
+    g_scratch[device] = p;
   }
-  *out = s.ptr;
+  *out = g_scratch[device];
   return G4_OK;
 }
+
+// Device of a device-memory pointer, or -1 when it is not device memory.
+static int device_of(const void *p) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return attr.type == cudaMemoryTypeDevice ? attr.device : -1;
+}
+
+// Restores the calling thread's current device on every return path.
+struct DeviceRestore {
+  int dev = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  }
+  ~DeviceRestore() {
+    if (dev >= 0) cudaSetDevice(dev);
+  }
+};
 
 extern "C" int g4_op_attention_noalloc(const float *q, const float *cache, float *out, int32_t heads,
                                        int32_t head_dim, int32_t q_count, int32_t q_start,
@@ -88,13 +109,22 @@ extern "C" int g4_op_attention_noalloc(const float *q, const float *cache, float
     return set_error(G4_ERR_INVALID,
                      "g4_op_attention_noalloc needs %lld floats of scratch; its static array holds %lld "
                      "(use fewer query rows or g4_op_attention)", (long long)need, (long long)kScratchFloats);
-  cudaPointerAttributes attr;
-  if (cudaPointerGetAttributes(&attr, q) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
-    return set_error(G4_ERR_INVALID, "q is not device memory");
+  const int dev = device_of(q);
+  if (dev < 0) return set_error(G4_ERR_INVALID, "g4_op_attention_noalloc: q is not device memory");
+  if (device_of(cache) != dev || device_of(out) != dev)
+    return set_error(G4_ERR_INVALID, "g4_op_attention_noalloc: cache and out must be device memory on q's device %d", dev);
+  if (stream) {
+    int sdev = -1;
+    if (cudaStreamGetDevice((cudaStream_t)stream, &sdev) != cudaSuccess || sdev != dev) {
+      cudaGetLastError();
+      return set_error(G4_ERR_INVALID, "g4_op_attention_noalloc: the stream does not belong to q's device %d", dev);
+    }
+  }
+  DeviceRestore restore;
+  if (cudaSetDevice(dev) != cudaSuccess) return set_error(G4_ERR_CUDA, "g4_op_attention_noalloc: cannot make device %d current", dev);
   float *scratch = nullptr;
-  int rc = scratch_for(attr.device, &scratch);
+  int rc = scratch_for(dev, &scratch);
   if (rc) return rc;
-  cudaSetDevice(attr.device);
   g4::AttnArgs a;
   memset(&a, 0, sizeof(a));
   a.cols = q_count;

@@ -768,11 +768,10 @@ __global__ void __launch_bounds__(256, 1) k_decode_persist(const PPhase *ph, int
 
 cudaError_t launch_decode_persist(const PPhase *ph, int nph, unsigned *bar, int grid,
                                   cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
+  static DeviceOnce attr;
+  attr([&] {
     cudaFuncSetAttribute(k_decode_persist, cudaFuncAttributeMaxDynamicSharedMemorySize, PS_SMEM);
-    attr = true;
-  }
+  });
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(256);

@@ -336,10 +336,13 @@ int g4_op_softcap_argmax(const float *logits, float *capped, int32_t *token, int
  * arguments and results as g4_op_attention; the per-block scratch is a fixed 4 MiB file-scope
  * device array (1,048,576 floats; needed: q_count * blocks * heads * (head_dim + 2), blocks =
  * window ? ceil(window / 64) + 1 : ceil(kv_len / 64)) that each device loading the library keeps until
- * the process exits. Larger requests return G4_ERR_INVALID. The first call on a device looks up
+ * the process exits. Larger requests return G4_ERR_INVALID. q, cache, out (and the stream, when
+ * not NULL) must belong to one device; the call makes that device current for its duration and
+ * restores the caller's current device before it returns. The first call on a device looks up
  * the array's device address with that device current; make that first call before any stream
- * capture. Calls share the array: two calls that overlap on the GPU (different streams, or
- * different host threads) race on it and must be serialised by the caller.
+ * capture (a lookup that fails is not remembered: the next call tries again). Calls share the
+ * array: two calls that overlap on the GPU (different streams, or different host threads) race
+ * on it and must be serialised by the caller.
  */
 int g4_op_attention_noalloc(const float *q, const float *cache, float *out, int32_t heads,
                             int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,

@@ -154,8 +154,9 @@ def config2_tokens() -> dict:
 
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    ref = Path(args[0]) if args else Path(os.environ.get("G4_REFERENCE", "/root/reference"))
-    if ref.exists():
+    ref = args[0] if args else os.environ.get("G4_REFERENCE")
+    ref = Path(ref) if ref else None
+    if ref is not None and ref.exists():
         (HERE / "reference_constants.json").write_text(json.dumps(reference_constants(ref), indent=1))
     (HERE / "ref_vectors.json").write_text(json.dumps(ref_vectors()))
     if "--config2" in sys.argv:
