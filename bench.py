@@ -1,19 +1,24 @@
 """Benchmark: decode tokens/s of the quantized Gemma-4-E2B hot path on B200.
 
-Workload (one replica per GPU): the seeded synthetic Gemma-4-E2B-shaped model,
-a 128-token prompt (untimed prefill), then greedy decode steps at batch 1. `value` is tokens/s of
-the device-resident decode chain (each step's token stays on the device and feeds the next
+One GPU (the default): `value` is BASELINE config 2 -- the seeded synthetic Gemma-4-E2B-shaped
+model, a 128-token prompt (untimed prefill), then K greedy decode steps at batch 1 -- as tokens/s
+of the device-resident decode chain (each step's token stays on the device and feeds the next
 step); `e2e` is the same through the public C ABI (g4_decode: host token in, host token out,
 copies inside the timed region). `roofline` is the quantized GEMV (BASELINE config 1 shape,
-6144 x 1536 int4 x int8) timed live over weight copies larger than L2. `--batch 64` runs the
-batched-decode variant; with `--ctx-lo 128 --ctx-hi 4096` it is BASELINE config 4 (ragged
-contexts); `--workload prefill` is config 3 (2048-token prefill); `--only-gemv` is config 1.
+6144 x 1536 int4 x int8) timed live over weight copies larger than L2. The same line carries the
+other BASELINE configs as keys: `config1_gemv`, `config3_prefill` (2048-token prefill),
+`config4_b64` (64 sequences, prompts U[128,4096], 256 greedy steps) and `config5_box` (512
+sequences of 512-token prompts, 256 greedy steps, PLE table in 128 MiB slices). `cpu_baseline`
+is the oracle port on the host cores (all threads and one thread).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
-                  [--ctx-lo L --ctx-hi H] [--workload decode|prefill] [--only-gemv]
+Several GPUs (torchrun): one independent replica per GPU; `value` is config 5 -- the box's 512
+sequences split over the replicas (strong scaling) -- over K steps, and `config5_box` the same
+over the full 256 steps. The process group (gloo) carries only barriers and the max / sum of the
+measured figures.
 
-Under torchrun each rank is an independent replica on its own GPU (weak scaling, no
-collectives on the data path); rank 0 prints one JSON line.
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--quick]
+                  [--batch B [--ctx-lo L --ctx-hi H]] [--box] [--workload decode|prefill]
+                  [--only-gemv]
 """
 from __future__ import annotations
 
@@ -35,6 +40,10 @@ sys.path.insert(0, str(ROOT))
 SEED = 0x6E6D6134
 PROMPT = 128
 METRIC = "decode tok/s (B=1, B=64) per B200 & box; quant GEMV HBM GB/s vs peak"
+DTYPE = "int4xint8 (int32 acc) / f32"
+DATA = "synthetic (seeded random-init Gemma-4-E2B shape)"
+B64, B64_LO, B64_HI, B64_STEPS = 64, 128, 4096, 256
+BOX_SEQS, BOX_PROMPT, BOX_STEPS = 512, 512, 256
 
 # Algorithmic bytes of one B=1 decode token on the synthetic Gemma-4-E2B shape: int4 linears
 # incl. the tied int4 lm_head, the I8 PLE linears, the bf16 per_layer_model_projection, the f16
@@ -88,8 +97,14 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu: int):
-        self.gpu = gpu
+    def __init__(self, dev: int, active: bool = True):
+        self.active = active
+        self.gpu = str(dev)
+        try:   # the physical GPU behind the device ordinal, whatever CUDA_VISIBLE_DEVICES says
+            import torch
+            self.gpu = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+        except Exception:
+            pass
         self.samples = []
         self._stop = threading.Event()
         self._t = None
@@ -106,13 +121,15 @@ class ClockSampler:
             self._stop.wait(0.2)
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._run, daemon=True)
-        self._t.start()
+        if self.active:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
         return self
 
     def __exit__(self, *exc):
         self._stop.set()
-        self._t.join(timeout=10)
+        if self._t is not None:
+            self._t.join(timeout=10)
 
     def summary(self) -> dict:
         sm = [float(s[1]) for s in self.samples if len(s) >= 9 and s[1].replace(".", "").isdigit()]
@@ -129,24 +146,53 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def cpu_baseline(steps: int, n_threads: int) -> dict:
-    """The oracle port on the host cores: a bounded sample of the same decode workload."""
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def oracle_decode_rate(prompt_len: int, steps: int, n_threads: int, warmup: int = 0) -> tuple:
+    """The oracle port decoding one sequence after a `prompt_len`-token prompt (the prefill is
+    untimed set-up): (tokens/s, seconds, per-step seconds)."""
     from oracle import oracle as O
     O.build()
     O.threads(n_threads)
     m = O.Model(SEED)
-    prompt = O.synth_prompt(SEED, PROMPT)
-    s = O.Sequence(m, PROMPT + steps + 8)
+    prompt = O.synth_prompt(SEED, prompt_len)
+    s = O.Sequence(m, prompt_len + warmup + steps + 8)
     s.forward(prompt[:-1], 0, False, False)
-    tok, _, _ = s.forward(prompt[-1:], PROMPT - 1, True, True)
-    t0 = time.perf_counter()
-    for i in range(steps):
-        tok, _, _ = s.forward(np.array([tok], np.int32), PROMPT + i, True, True)
-    dt = time.perf_counter() - t0
+    tok, _, _ = s.forward(prompt[-1:], prompt_len - 1, True, True)
+    pos = prompt_len
+    for _ in range(warmup):
+        tok, _, _ = s.forward(np.array([tok], np.int32), pos, True, True)
+        pos += 1
+    per = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        tok, _, _ = s.forward(np.array([tok], np.int32), pos, True, True)
+        per.append(time.perf_counter() - t0)
+        pos += 1
     m.close()
-    return {"value": steps / dt, "unit": "tokens/s", "cores": n_threads, "kind": "port",
-            "sample": f"{steps} B=1 decode steps of config 2 after a 128-token prompt (oracle, "
-                      f"{n_threads} threads, {dt:.1f} s)"}
+    return steps / sum(per), sum(per), per
+
+
+def cpu_baseline(prompt_len: int, steps: int, n_threads: int, workload: str) -> dict:
+    """The oracle port on the host cores: a bounded sample of the same decode workload, on all
+    threads and on one thread."""
+    v, dt, _ = oracle_decode_rate(prompt_len, steps, n_threads)
+    v1, dt1, _ = oracle_decode_rate(prompt_len, 3, 1)
+    return {"value": v, "unit": "tokens/s", "cores": n_threads, "kind": "port",
+            "cpu_model": cpu_model(),
+            "single_thread": {"value": v1, "unit": "tokens/s", "cores": 1, "steps": 3,
+                              "seconds": dt1},
+            "sample": f"{steps} B=1 decode steps after a {prompt_len}-token prompt ({workload}; "
+                      f"oracle, {n_threads} threads, {dt:.1f} s; a batch of sequences costs the "
+                      f"CPU the same per token)"}
 
 
 def dist_env():
@@ -156,43 +202,48 @@ def dist_env():
     return world, rank, local
 
 
+L2_NOTE = "weights (0.93 GB per step) exceed L2 every step"
+
+
+def line_config(world: int) -> dict:
+    """The `config` of the bench line; both arms print the same one for the same N. One GPU:
+    BASELINE config 2. Several (torchrun): config 5, the box's 512 sequences over the replicas."""
+    if world == 1:
+        return {"workload": f"config 2: B=1 greedy decode after a {PROMPT}-token prompt",
+                "global_batch": 1, "seq_len": PROMPT, "parallelism": "replicas x1", "l2": L2_NOTE}
+    return {"workload": f"config 5: {BOX_SEQS} sequences over {world} replicas, {BOX_PROMPT}-token "
+                        "prompts, greedy decode, PLE table in 128 MiB slices",
+            "global_batch": BOX_SEQS, "seq_len": BOX_PROMPT, "parallelism": f"replicas x{world}",
+            "l2": L2_NOTE}
+
+
 def run_reference(args) -> None:
-    """--impl reference: the reference's own CPU arithmetic (the oracle port, all host cores)."""
+    """--impl reference: the reference's own CPU arithmetic (the oracle port; the reference is
+    TypeScript/WGSL and cannot run here) on all host cores, on the repo arm's config. Each step
+    is a bounded sample of two decode steps of one sequence at the workload's prompt length;
+    rank 0 alone runs under torchrun."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
     n = len(os.sched_getaffinity(0))
-    times = []
-    steps_per_sample = 2
-    from oracle import oracle as O
-    O.build()
-    O.threads(n)
-    m = O.Model(SEED)
-    prompt = O.synth_prompt(SEED, PROMPT)
-    s = O.Sequence(m, PROMPT + (args.warmup + args.steps) * steps_per_sample + 8)
-    s.forward(prompt[:-1], 0, False, False)
-    tok, _, _ = s.forward(prompt[-1:], PROMPT - 1, True, True)
-    pos = PROMPT
-    for it in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        for _ in range(steps_per_sample):
-            tok, _, _ = s.forward(np.array([tok], np.int32), pos, True, True)
-            pos += 1
-        if it >= args.warmup:
-            times.append(time.perf_counter() - t0)
-    m.close()
-    total = args.steps * steps_per_sample
-    v = total / sum(times)
+    prompt_len = PROMPT if world == 1 else BOX_PROMPT
+    per_sample = 2
+    v, total_s, per = oracle_decode_rate(prompt_len, args.steps * per_sample, n,
+                                         warmup=args.warmup * per_sample)
+    v1, dt1, _ = oracle_decode_rate(prompt_len, 2, 1)
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8/f32",
-        "data": "synthetic (seeded random-init Gemma-4-E2B shape)",
-        "config": {"workload": "config 2: B=1 greedy decode after a 128-token prompt",
-                   "global_batch": 1, "seq_len": PROMPT, "parallelism": "replicas"},
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total_s / args.steps,
+        "higher_is_better": True, "scaling": "weak" if world == 1 else "strong",
+        "vs_baseline": None, "dtype": DTYPE, "data": DATA, "config": line_config(world),
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": n, "kind": "port",
-                         "sample": f"{steps_per_sample} decode steps per step, oracle port "
-                                   "(the reference is TypeScript/WGSL and cannot run here)"},
+                         "cpu_model": cpu_model(),
+                         "single_thread": {"value": v1, "unit": "tokens/s", "cores": 1,
+                                           "steps": 2, "seconds": dt1},
+                         "sample": f"{per_sample} B=1 decode steps per step after a {prompt_len}-token "
+                                   "prompt, oracle port on all host threads (the reference is "
+                                   "TypeScript/WGSL and cannot run here; a batch costs the CPU the "
+                                   "same per token)"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -250,18 +301,38 @@ def measure_gemv(pkg, torch, copies: int, iters: int) -> dict:
             "timing": "cuda graph of launches" if graph is not None else "eager launches"}
 
 
+def reduce_max(torch, vals, world):
+    """Elementwise max over ranks of a few host floats (gloo: CPU tensors)."""
+    if world == 1:
+        return list(vals)
+    t = torch.tensor(list(vals), dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def reduce_sum(torch, vals, world):
+    if world == 1:
+        return list(vals)
+    t = torch.tensor(list(vals), dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+    return [float(v) for v in t]
+
+
+def barrier(torch, world):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
 def run_gemv_only(pkg, torch, args, world, rank) -> None:
     """Config 1 as its own line: GB/s of the GEMV over 64 distinct weight copies, each launch
     chained to the previous one (programmatic dependent launch inside one CUDA graph)."""
     peaks = load_peaks()
-    with ClockSampler(torch.cuda.current_device()) as clocks:
+    barrier(torch, world)
+    with ClockSampler(torch.cuda.current_device(), rank == 0) as clocks:
         g = measure_gemv(pkg, torch, copies=64, iters=64 * max(args.steps, 10))
-    if world > 1:
-        t = torch.tensor([g["seconds_per_launch"]], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        g["seconds_per_launch"] = float(t.item())
-        g["gbs"] = GEMV_BYTES / g["seconds_per_launch"] / 1e9
-        torch.distributed.destroy_process_group()
+    g["seconds_per_launch"] = reduce_max(torch, [g["seconds_per_launch"]], world)[0]
+    g["gbs"] = GEMV_BYTES / g["seconds_per_launch"] / 1e9
     if rank != 0:
         return
     print(json.dumps({
@@ -277,109 +348,202 @@ def run_gemv_only(pkg, torch, args, world, rank) -> None:
         "gpu_launches": 64 * max(args.steps, 10), "clocks": clocks.summary()}), flush=True)
 
 
-def run_prefill(pkg, torch, args, world, rank, dev) -> None:
-    """prefill of `--tokens` random ids with the KV-sharing exit (positions
-    0..n-2 run the producer layers only, the last position all layers and the head). One chunk:
-    the projections run as tcgen05 int8 GEMMs over all n-1 columns. Each step rewinds the KV
-    (src/kv.ts:247-254) and prefills again; the ids go host->device and the token comes back
-    inside the timed region."""
-    n = args.tokens
-    ctx = pkg.engine.Context(device=dev, max_seqs=1, max_context=n + 8, max_step_columns=n)
-    ctx.init_random(SEED)
-    prompt = np.array(pkg.plan.synth_prompt(SEED + 7919 * rank, n), np.int32)
-    stream = torch.cuda.ExternalStream(ctx.stream())
-    for _ in range(args.warmup):
-        ctx.kv_truncate(0, 0)
-        ctx.prefill(0, prompt, 0, True)
-    torch.cuda.synchronize()
-    launches = ctx.launches()
-    steps = max(1, args.steps // 20)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clocks:
-        torch.cuda.nvtx.range_push("timed")
-        e0.record(stream)
-        for _ in range(steps):
-            ctx.kv_truncate(0, 0)
-            ctx.prefill(0, prompt, 0, True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-    # End to end (host ids in, host token out) on its own clock, without the sampler's
-    # nvidia-smi processes starting inside the timed region.
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    h0 = time.perf_counter()
-    for _ in range(steps):
-        ctx.kv_truncate(0, 0)
-        ctx.prefill(0, prompt, 0, True)
-    torch.cuda.synchronize()
-    wall = time.perf_counter() - h0
-    dev_s = max(e0.elapsed_time(e1) / 1e3, 1e-9)
-    if world > 1:
-        t = torch.tensor([dev_s, wall], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        dev_s, wall = float(t[0]), float(t[1])
-    # Algorithmic int8 ops: 2 x producer-layer linear parameters x (n - 1) columns plus the
-    # last position through all layers and the lm_head.
+PREFILL_LAYERS = 15
+
+
+def prefill_ops(n: int) -> int:
+    """Algorithmic int8 ops of an n-token prefill with the KV-sharing exit: 2 x producer-layer
+    linear parameters x (n - 1) columns, plus the last position through all layers and the head."""
     H, PD, V = 1536, 256, 262144
     prod_params = mlp = 0
     for L in range(35):
         hd = 512 if L in {4, 9, 14, 19, 24, 29, 34} else 256
         p = 8 * hd * H + H * 8 * hd + 3 * 6144 * H + 2 * PD * H + (2 * hd * H if L < 15 else 0)
         mlp += p
-        if L < 15:
+        if L < PREFILL_LAYERS:
             prod_params += p
-    ops = 2 * prod_params * (n - 1) + 2 * (mlp + V * H)
+    return 2 * prod_params * (n - 1) + 2 * (mlp + V * H)
+
+
+def measure_prefill(pkg, torch, dev, n, steps, warmup, world, rank) -> dict:
+    """prefill of n random ids with the KV-sharing exit (positions 0..n-2 run
+    the producer layers only, the last position all layers and the head), one chunk: the
+    projections run as tcgen05 int8 GEMMs over all n-1 columns. Each step rewinds the KV
+    (src/kv.ts:247-254) and prefills again; the ids go host->device and the token comes back
+    inside every step, so the device-timed and the end-to-end figures share one loop shape."""
+    ctx = pkg.engine.Context(device=dev, max_seqs=1, max_context=n + 8, max_step_columns=n)
+    ctx.init_random(SEED)
+    prompt = np.array(pkg.plan.synth_prompt(SEED + 7919 * rank, n), np.int32)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    for _ in range(warmup):
+        ctx.kv_truncate(0, 0)
+        ctx.prefill(0, prompt, 0, True)
+    torch.cuda.synchronize()
+    launches = ctx.launches()
+    barrier(torch, world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev, rank == 0) as clocks:
+        e0.record(stream)
+        for _ in range(steps):
+            ctx.kv_truncate(0, 0)
+            ctx.prefill(0, prompt, 0, True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    # End to end (host ids in, host token out) on its own clock, without the sampler's
+    # nvidia-smi processes starting inside the timed region.
+    barrier(torch, world)
+    h0 = time.perf_counter()
+    for _ in range(steps):
+        ctx.kv_truncate(0, 0)
+        ctx.prefill(0, prompt, 0, True)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - h0
+    dev_s, wall = reduce_max(torch, [max(e0.elapsed_time(e1) / 1e3, 1e-9), wall], world)
+    ctx.close()
+    ops = prefill_ops(n)
     peaks = load_peaks()
     int8_peak = 2 * peaks.get("bf16_tflops", 1590.0)
     achieved = ops * steps / dev_s / 1e12
-    ctx.close()
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    return {"value": world * n * steps / dev_s, "unit": "tokens/s", "steps": steps,
+            "ms_per_step": 1000 * dev_s / steps, "launches_per_step": launches,
+            "e2e": {"value": world * n * steps / wall, "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
+                         "frac": achieved / int8_peak, "traffic": None,
+                         "peak_source": "2 x measured dense bf16 (int8 tensor rate)",
+                         "ops_per_step": ops,
+                         "kernel": "whole prefill (int8 GEMMs + attention + rest)"},
+            "clocks": clocks.summary()}
+
+
+def run_prefill(pkg, torch, args, world, rank, dev) -> None:
+    """Config 3 as its own line (one prefill per 20 --steps, at least one)."""
+    r = measure_prefill(pkg, torch, dev, args.tokens, max(1, args.steps // 20), args.warmup, world, rank)
     if rank != 0:
         return
+    n = args.tokens
     print(json.dumps({
         "metric": "prefill tokens/s (config 3, 2048-token prompt, KV-sharing exit)",
-        "value": world * n * steps / dev_s, "unit": "tokens/s", "n_gpus": world, "steps": steps,
-        "warmup": args.warmup, "ms_per_step": 1000 * dev_s / steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int4xint8 (int32 acc) / f32",
-        "data": "synthetic (seeded random-init Gemma-4-E2B shape)",
+        "value": r["value"], "unit": "tokens/s", "n_gpus": world, "steps": r["steps"],
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": DATA,
         "config": {"workload": f"config 3: prefill of {n} random ids, producer layers for 0..{n - 2}, "
                                "all layers + head for the last", "global_batch": world,
                    "seq_len": n, "parallelism": f"replicas x{world}", "l2": "weights exceed L2"},
-        "e2e": {"value": world * n * steps / wall, "unit": "tokens/s", "h2d_bytes_per_step": 4 * n,
-                "d2h_bytes_per_step": 4},
-        "gpu_launches": launches * steps,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
-                     "frac": achieved / int8_peak, "traffic": None,
-                     "peak_source": "2 x measured dense bf16 (int8 tensor rate)",
-                     "ops_per_step": ops, "kernel": "whole prefill (int8 GEMMs + attention + rest)"},
-        "clocks": clocks.summary()}), flush=True)
+        "e2e": r["e2e"], "gpu_launches": r["launches_per_step"] * r["steps"],
+        "roofline": r["roofline"], "clocks": r["clocks"]}), flush=True)
+
+
+def measure_decode(pkg, torch, dev, seq_ids, lens, steps, warmup, world, rank, slice_bytes=0,
+                   gemm_split_k=0) -> dict:
+    """Greedy decode of the sequences `seq_ids` (prompt b: `lens[i]` seeded ids from seed
+    SEED + b) on one replica: every prompt is prefilled (untimed), `warmup` steps run and are
+    rewound, then exactly `steps` steps from the prompts are timed twice:
+      * device chain: one CUDA graph per step, each step's token and position stay on the device
+        and feed the next (CUDA events on the context's stream);
+      * end to end through the C ABI (g4_decode / g4_decode_batch): host tokens in, host tokens
+        out every step, the copies inside the timed region (the KV rows past the prompts rewound
+        first, src/kv.ts:247-254).
+    Returns the slowest rank's times."""
+    B = len(seq_ids)
+    max_ctx = max(lens) + max(steps, warmup) + 8
+    chunk = max(B, 512 if max(lens) > 256 else 64)
+    ctx = pkg.engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=chunk,
+                             ple_slice_bytes=slice_bytes, gemm_split_k=gemm_split_k)
+    ctx.init_random(SEED)
+    prompts = [np.array(pkg.plan.synth_prompt(SEED + int(s), lens[i]), np.int32)
+               for i, s in enumerate(seq_ids)]
+    torch.cuda.synchronize()
+    p0 = time.perf_counter()
+    first = [ctx.prefill(b, prompts[b], 0, True) for b in range(B)]
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - p0
+    stream = torch.cuda.ExternalStream(ctx.stream())
+
+    ctx.step_stage(np.arange(B), first, lens)
+    for _ in range(warmup):
+        ctx.step_run_device(B)
+    torch.cuda.synchronize()
+    launches = ctx.launches()
+    for b in range(B):
+        ctx.kv_truncate(b, lens[b])
+    ctx.step_stage(np.arange(B), first, lens)
+    barrier(torch, world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev, rank == 0) as clocks:
+        e0.record(stream)
+        for _ in range(steps):
+            ctx.step_run_device(B)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    dev_s = e0.elapsed_time(e1) / 1e3
+    dev_tokens = ctx.step_read_tokens(B)
+
+    for b in range(B):
+        ctx.kv_truncate(b, lens[b])
+    prev = [int(t) for t in first]
+    barrier(torch, world)
+    h0 = time.perf_counter()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for i in range(steps):
+        if B == 1:
+            prev = [ctx.decode(0, prev[0], lens[0] + i)]
+        else:
+            prev = list(ctx.decode_batch(np.arange(B), prev, [lens[b] + i for b in range(B)]))
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_s = max(e2.elapsed_time(e3) / 1e3, time.perf_counter() - h0)
+    ctx.close()
+    if [int(t) for t in dev_tokens] != [int(t) for t in prev]:
+        raise RuntimeError("the device chain and the C-ABI decode disagree on the last tokens")
+    # Algorithmic bytes of the timed steps: weights and scales once per step, each sequence's
+    # KV rows at its own position.
+    tb = token_bytes(lens[0])
+    kv = sum(token_bytes(lens[b] + i)["kv"] for b in range(B) for i in range(0, steps, max(1, steps // 16)))
+    kv *= steps / len(range(0, steps, max(1, steps // 16)))
+    step_bytes = tb["weights"] + tb["scales"] + kv / steps
+    dev_s, e2e_s = reduce_max(torch, [dev_s, e2e_s], world)
+    total_bytes, total_seqs = reduce_sum(torch, [step_bytes * steps, B], world)
+    return {"dev_s": dev_s, "e2e_s": e2e_s, "launches_per_step": launches, "step_bytes": step_bytes,
+            "all_ranks_bytes": total_bytes, "seqs": int(total_seqs), "prefill_s": prefill_s,
+            "prefill_tokens": sum(lens), "clocks": clocks.summary()}
+
+
+def decode_summary(r: dict, steps: int, world: int, peaks: dict, h2d_per_seq=12, d2h_per_seq=4) -> dict:
+    """Throughput keys of one decode workload: tokens of all ranks over the slowest rank's time;
+    the HBM fraction is the algorithmic bytes all ranks moved over (N x measured peak)."""
+    gbs = r["all_ranks_bytes"] / r["dev_s"] / 1e9
+    return {"value": r["seqs"] * steps / r["dev_s"], "unit": "tokens/s", "steps": steps,
+            "ms_per_step": 1000 * r["dev_s"] / steps,
+            "e2e": {"value": r["seqs"] * steps / r["e2e_s"], "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d_per_seq * r["seqs"], "d2h_bytes_per_step": d2h_per_seq * r["seqs"]},
+            "step_bytes_per_replica": r["step_bytes"], "hbm_gbs_all_replicas": gbs,
+            "hbm_frac": gbs / (world * peaks["hbm_gbs"]),
+            "prefill_tokens_per_s": r["prefill_tokens"] / r["prefill_s"],
+            "gpu_launches_per_step": r["launches_per_step"], "clocks": r["clocks"]}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=120)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=24)
+    ap.add_argument("--quick", action="store_true",
+                    help="one GPU: the config 2 line alone (no config 1/3/4/5 keys)")
     ap.add_argument("--only-gemv", action="store_true",
                     help="BASELINE config 1 alone: the int4 x int8 GEMV [6144 x 1536] line")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="a decode line of this many sequences instead of the default workloads")
     ap.add_argument("--ctx-lo", type=int, default=PROMPT,
-                    help="prompt lengths uniform in [ctx-lo, ctx-hi] per sequence (seeded)")
+                    help="with --batch: prompt lengths uniform in [ctx-lo, ctx-hi] (seeded)")
     ap.add_argument("--ctx-hi", type=int, default=PROMPT)
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
     ap.add_argument("--box", action="store_true",
-                    help="config 5: 512 sequences split over the replicas, 512-token prompts, "
-                         "the per-layer-embedding table in 128 MiB vocab-row slices")
+                    help="config 5 as the line on any number of GPUs (the default under torchrun)")
     ap.add_argument("--tokens", type=int, default=2048, help="prefill workload: prompt length")
     ap.add_argument("--gemm-split-k", type=int, default=0, choices=[0, 1, 2],
                     help="g4_config.gemm_split_k: 0 cluster, 1 none, 2 workspace")
@@ -393,138 +557,102 @@ def main():
     import torch
     import __graft_entry__ as entry
     world, rank, local = dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        entry.load_package().replicas.init_group(torch, "nccl", 300.0, torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
-    dev = torch.cuda.current_device()
     pkg = entry.load_package()
-    if args.only_gemv:
-        run_gemv_only(pkg, torch, args, world, rank)
-        return
-    if args.workload == "prefill":
-        run_prefill(pkg, torch, args, world, rank, dev)
-        return
-    engine = pkg.engine
-    B = args.batch
-    slice_bytes = 0
-    if args.box:
-        lo, hi = pkg.replicas.replica_slice(512, world, rank)
-        B = hi - lo
-        args.ctx_lo = args.ctx_hi = 512
-        slice_bytes = 128 << 20
-    total_steps = args.warmup + args.steps
-    rng = np.random.default_rng(SEED + 1000 * rank)
-    lens = ([args.ctx_lo] * B if args.ctx_lo == args.ctx_hi
-            else [int(v) for v in rng.integers(args.ctx_lo, args.ctx_hi + 1, B)])
-    max_ctx = max(lens) + total_steps + 8
-    chunk = max(B, 512 if max(lens) > 256 else 64)
-    ctx = engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=chunk,
-                         ple_slice_bytes=slice_bytes, gemm_split_k=args.gemm_split_k)
-    ctx.init_random(SEED)
-    prompts = [np.array(pkg.plan.synth_prompt(SEED + b + 7919 * rank, lens[b]), np.int32) for b in range(B)]
-    torch.cuda.synchronize()
-    p0 = time.perf_counter()
-    first = [ctx.prefill(b, prompts[b], 0, True) for b in range(B)]
-    torch.cuda.synchronize()
-    prefill_s = time.perf_counter() - p0
-
-    # ---- device-resident decode chain (value)
-    ctx.step_stage(np.arange(B), first, lens)
-    stream = torch.cuda.ExternalStream(ctx.stream())
-    for _ in range(args.warmup):
-        ctx.step_run_device(B)
-    torch.cuda.synchronize()
-    launches_per_step = ctx.launches()
+    # Replicas share nothing on the data path: the group (gloo, host memory) carries only the
+    # barriers before timing and the max / sum of the measured figures.
+    torch.cuda.set_device(local if world > 1 else 0)
     if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clocks:
-        torch.cuda.nvtx.range_push("timed")   # profilers can keep to the timed steps
-        e0.record(stream)
-        for _ in range(args.steps):
-            ctx.step_run_device(B)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-    dev_s = e0.elapsed_time(e1) / 1e3
-    if world > 1:
-        t = torch.tensor([dev_s], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        dev_s = float(t.item())
-    ctx.step_read_tokens(B)
-
-    # ---- end to end through the C ABI: host token in, host token out, every step, over the
-    # same positions (the KV rows past the prompt are rewound, src/kv.ts:247-254)
-    for b in range(B):
-        ctx.kv_truncate(b, lens[b])
-    prev = [int(t) for t in first]
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    h0 = time.perf_counter()
-    e2 = torch.cuda.Event(enable_timing=True)
-    e3 = torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for i in range(args.steps):
-        if B == 1:
-            prev = [ctx.decode(0, prev[0], lens[0] + i)]
+        pkg.replicas.init_group(torch, "gloo", 300.0)
+    dev = torch.cuda.current_device()
+    try:
+        if args.only_gemv:
+            run_gemv_only(pkg, torch, args, world, rank)
+        elif args.workload == "prefill":
+            run_prefill(pkg, torch, args, world, rank, dev)
         else:
-            prev = list(ctx.decode_batch(np.arange(B), prev, [lens[b] + i for b in range(B)]))
-    e3.record(stream)
-    torch.cuda.synchronize()
-    e2e_s = max(e2.elapsed_time(e3) / 1e3, time.perf_counter() - h0)
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_s = float(t.item())
+            run_decode(pkg, torch, args, world, rank, dev)
+    finally:
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
 
-    # ---- roofline of the dominant kernel (quant GEMV, config 1 shape)
-    gemv = measure_gemv(pkg, torch, copies=64, iters=640)
+
+def run_decode(pkg, torch, args, world, rank, dev) -> None:
     peaks = load_peaks()
-    mids = [lens[b] + args.warmup + args.steps // 2 for b in range(B)]
-    tb = token_bytes(mids[0])
-    step_bytes = tb["weights"] + tb["scales"] + sum(token_bytes(m)["kv"] for m in mids)
-    value = world * B * args.steps / dev_s
-    if args.box:
-        workload = (f"config 5: 512 sequences over {world} replica(s) ({B} here), 512-token prompts, "
-                    f"{total_steps} greedy steps, PLE table in 128 MiB slices")
-    elif B == 1 and args.ctx_lo == args.ctx_hi == PROMPT:
-        workload = (f"config 2: B=1 greedy decode after a {PROMPT}-token prompt, contexts "
-                    f"{PROMPT}..{PROMPT + total_steps}")
+    box = args.box or world > 1
+    if box:
+        lo, hi = pkg.replicas.replica_slice(BOX_SEQS, world, rank)
+        seq_ids = list(range(lo, hi))
+        lens = [BOX_PROMPT] * len(seq_ids)
+        slice_bytes = 128 << 20
+    elif args.batch:
+        seq_ids = list(range(args.batch))
+        rng = np.random.default_rng(SEED + 1000 * rank)
+        lens = ([args.ctx_lo] * args.batch if args.ctx_lo == args.ctx_hi
+                else [int(v) for v in rng.integers(args.ctx_lo, args.ctx_hi + 1, args.batch)])
+        slice_bytes = 0
     else:
-        workload = (f"B={B} greedy decode per replica, prompt lengths "
-                    f"{'U[%d,%d]' % (args.ctx_lo, args.ctx_hi) if args.ctx_lo != args.ctx_hi else args.ctx_lo}"
-                    f" (seeded), {total_steps} steps")
+        seq_ids, lens, slice_bytes = [0], [PROMPT], 0
+    r = measure_decode(pkg, torch, dev, seq_ids, lens, args.steps, args.warmup, world, rank,
+                       slice_bytes, args.gemm_split_k)
+    main_s = decode_summary(r, args.steps, world, peaks)
+    if box:
+        config = line_config(world) if world > 1 else dict(line_config(2), parallelism="replicas x1")
+        scaling = "strong"
+    elif args.batch:
+        config = {"workload": f"B={args.batch} greedy decode, prompt lengths "
+                              f"{'U[%d,%d]' % (args.ctx_lo, args.ctx_hi) if args.ctx_lo != args.ctx_hi else args.ctx_lo} (seeded)",
+                  "global_batch": world * args.batch, "seq_len": max(lens),
+                  "parallelism": f"replicas x{world}", "l2": L2_NOTE}
+        scaling = "weak"
+    else:
+        config = line_config(1)
+        scaling = "weak"
+    gemv = measure_gemv(pkg, torch, copies=64, iters=640)
+    gemv_s = reduce_max(torch, [gemv["seconds_per_launch"]], world)[0]
+    gemv_gbs = GEMV_BYTES / gemv_s / 1e9
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dev_s / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4xint8 (int32 acc) / f32", "data": "synthetic (seeded random-init Gemma-4-E2B shape)",
-        "config": {"workload": workload,
-                   "global_batch": world * B, "seq_len": max(lens), "parallelism": f"replicas x{world}",
-                   "l2": "weights (0.93 GB per step) exceed L2 every step"},
-        "e2e": {"value": world * B * args.steps / e2e_s, "unit": "tokens/s",
-                "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B},
-        "gpu_launches": launches_per_step * args.steps,
-        "step_bytes": step_bytes,
-        "step_hbm_gbs": step_bytes * args.steps / dev_s / 1e9,
-        "prefill_tokens_per_s": sum(lens) / prefill_s,
+        "metric": METRIC, "value": main_s["value"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": main_s["ms_per_step"],
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": DTYPE,
+        "data": DATA, "config": config, "e2e": main_s["e2e"],
+        "gpu_launches": r["launches_per_step"] * args.steps,
+        "step_bytes": r["step_bytes"], "step_hbm_gbs": main_s["hbm_gbs_all_replicas"] / world,
+        "step_hbm_frac": main_s["hbm_frac"], "prefill_tokens_per_s": main_s["prefill_tokens_per_s"],
         "roofline": {"bound": "hbm", "kernel": "qgemv-4bit 6144x1536 (config 1)",
-                     "achieved": gemv["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": gemv["gbs"] / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC,
+                     "achieved": gemv_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gemv_gbs / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC,
                      "peak_source": peaks["source"], "bytes_per_launch": GEMV_BYTES,
-                     "us_per_launch": gemv["seconds_per_launch"] * 1e6, "timing": gemv["timing"]},
-        "clocks": clocks.summary(),
+                     "us_per_launch": gemv_s * 1e6, "timing": gemv["timing"]},
+        "clocks": main_s["clocks"],
     }
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.cpu_steps, len(os.sched_getaffinity(0)))
-    ctx.close()
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    if box:
+        # The same box workload over the BASELINE's full 256 greedy steps.
+        rb = measure_decode(pkg, torch, dev, seq_ids, lens, BOX_STEPS, args.warmup, world, rank, slice_bytes)
+        line["config5_box"] = dict(decode_summary(rb, BOX_STEPS, world, peaks), replicas=world,
+                                   sequences=BOX_SEQS)
+    elif not args.batch and not args.quick:
+        # One GPU, default run: BASELINE configs 1, 3, 4 and 5 as extra keys beside config 2.
+        line["config1_gemv"] = {"value": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / peaks["hbm_gbs"],
+                                "us_per_launch": gemv_s * 1e6,
+                                "workload": "64 distinct 6144x1536 int4 weight copies, one graph"}
+        rng = np.random.default_rng(SEED)
+        b64_lens = [int(v) for v in rng.integers(B64_LO, B64_HI + 1, B64)]
+        r4 = measure_decode(pkg, torch, dev, list(range(B64)), b64_lens, B64_STEPS, args.warmup, world, rank)
+        line["config4_b64"] = dict(decode_summary(r4, B64_STEPS, world, peaks),
+                                   contexts=f"U[{B64_LO},{B64_HI}] seeded, mean {np.mean(b64_lens):.0f}")
+        r5 = measure_decode(pkg, torch, dev, list(range(BOX_SEQS)), [BOX_PROMPT] * BOX_SEQS, BOX_STEPS,
+                            args.warmup, world, rank, 128 << 20)
+        line["config5_box"] = dict(decode_summary(r5, BOX_STEPS, world, peaks), replicas=1,
+                                   sequences=BOX_SEQS)
+        line["config3_prefill"] = measure_prefill(pkg, torch, dev, 2048, 5, 3, world, rank)
+        line["gpu_launches_all_workloads"] = (line["gpu_launches"] + 640
+                                              + r4["launches_per_step"] * B64_STEPS
+                                              + r5["launches_per_step"] * BOX_STEPS
+                                              + line["config3_prefill"]["launches_per_step"] * 5)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(BOX_PROMPT if box else PROMPT, args.cpu_steps,
+                                            len(os.sched_getaffinity(0)), config["workload"])
     if rank == 0:
         print(json.dumps(line), flush=True)
 
