@@ -58,6 +58,7 @@ SIGNATURES = {
     "g4_ctx_create": (C.c_int, [C.c_int, C.POINTER(Config), C.POINTER(_vp)]),
     "g4_ctx_destroy": (None, [_vp]),
     "g4_ctx_memory": (C.c_int, [_vp, _u64p, _u64p, _u64p]),
+    "g4_ctx_ple_slices": (C.c_int, [_vp, _i32p, _i32p, _i32p]),
     "g4_init_random": (C.c_int, [_vp, _u64]),
     "g4_upload_weight": (C.c_int, [_vp, C.c_char_p, _vp, _u64, _u64, _u64]),
     "g4_download_weight": (C.c_int, [_vp, C.c_char_p, _vp, _u64p]),
@@ -68,6 +69,7 @@ SIGNATURES = {
     "g4_decode": (C.c_int, [_vp, _i32, _i32, _i32, _i32p]),
     "g4_decode_ahead": (C.c_int, [_vp, _i32, _i32, _i32p]),
     "g4_decode_batch": (C.c_int, [_vp, _i32, _i32p, _i32p, _i32p, _i32p]),
+    "g4_verify": (C.c_int, [_vp, _i32, _i32p, _i32, _i32, _i32p]),
     "g4_step_stage": (C.c_int, [_vp, _i32, _i32p, _i32p, _i32p]),
     "g4_step_run_device": (C.c_int, [_vp, _i32, _i32]),
     "g4_step_read_tokens": (C.c_int, [_vp, _i32, _i32p]),

@@ -502,7 +502,9 @@ static int alloc_runtime(g4_ctx *ctx) {
   CK(cudaMalloc(&ctx->codes_ple, (size_t)maxc * ctx->PD));
   CK(cudaMalloc(&ctx->att_count, (size_t)maxc * 8 * 4));
   CK(cudaMemset(ctx->att_count, 0, (size_t)maxc * 8 * 4));
-  ctx->head_cols = std::min(maxc, std::max(ctx->cfg.max_seqs, 1));
+  // Logit rows: one per sequence of a decode batch, and at least G4_VERIFY_COLS for the
+  // positions of a verify pass.
+  ctx->head_cols = std::min(maxc, std::max(ctx->cfg.max_seqs, (int)G4_VERIFY_COLS));
   if ((rc = take(&ctx->logits, (size_t)ctx->head_cols * ctx->V))) return rc;
   CK(cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, ctx->dev));
   ctx->gemv_target = 2 * ctx->sms;
@@ -637,6 +639,16 @@ extern "C" int g4_ctx_memory(const g4_ctx *ctx, uint64_t *w, uint64_t *kvb, uint
   if (w) *w = ctx->arena_bytes + ctx->ple_slice_bytes;
   if (kvb) *kvb = ctx->kv_bytes;
   if (o) *o = ctx->other_bytes;
+  return G4_OK;
+}
+
+extern "C" int g4_ctx_ple_slices(const g4_ctx *ctx, int32_t *n_slices, int32_t *rows_per_slice,
+                                 int32_t *last_rows) {
+  if (!ctx) return fail(nullptr, G4_ERR_INVALID, "null context");
+  const int32_t n = (int32_t)ctx->ple_slices.size();
+  if (n_slices) *n_slices = n;
+  if (rows_per_slice) *rows_per_slice = ctx->ple_rps;
+  if (last_rows) *last_rows = n > 0 ? ctx->V - (n - 1) * ctx->ple_rps : 0;
   return G4_OK;
 }
 
@@ -1189,8 +1201,15 @@ static GemvArgs pro_args(int pro) {
 // Record the launches of one step: `cols` columns (already staged in d_step), layers
 // [0, n_layers), then the head when asked. Step order is planDecodeStep / planPrefillChunk
 // (src/plan.ts:487-824) with the fusions of the decode plan.
-static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false) {
+// One forward step over `cols` columns through `n_layers` layers. head: every column runs the
+// lm_head and its argmax. wide: the columns are consecutive positions of one sequence (a prefill
+// chunk, or a verify pass when head is set), so attention stores every column's KV row first and
+// then attends causally; otherwise (a decode step) each column is its own sequence and one fused
+// launch per layer stores and attends.
+static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false,
+                       bool wide = false) {
   const g4_arch &a = ctx->cfg.arch;
+  const bool fused_attn = head && !wide;
   const int H = ctx->H, PD = ctx->PD;
   const float eps = a.rms_eps;
   int32_t *d_seq = ctx->d_step, *d_pos = ctx->d_step + ctx->maxc, *d_tok = ctx->d_step + 2 * ctx->maxc;
@@ -1261,7 +1280,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       if (L > 0) cur ^= 1;
     }
     // ---- decode steps: prologue, attention and merge in one launch per layer
-    if (head) {
+    if (fused_attn) {
       AttnDec ad;
       memset(&ad, 0, sizeof(ad));
       ad.cols = cols;
@@ -1301,7 +1320,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       ctx->launches++;
     }
     // ---- attention prologue: q-norm-rope, kv-norm-rope-store (src/kernels/attnPrologue.ts)
-    if (!head) {
+    if (!fused_attn) {
       AttnPro ap;
       memset(&ap, 0, sizeof(ap));
       ap.cols = cols;
@@ -1329,7 +1348,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       ctx->launches++;
     }
     // ---- attention over the producer cache (kvRoleForLayer)
-    if (!head) {
+    if (!fused_attn) {
       AttnArgs at;
       memset(&at, 0, sizeof(at));
       at.cols = cols;
@@ -1527,22 +1546,25 @@ static int try_persist(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
   return G4_OK;
 }
 
-static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false) {
+static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false,
+                    bool wide = false) {
   bool done = false;
-  int prc = try_persist(ctx, cols, n_layers, head, advance, &done);
-  if (prc || done) return prc;
-  if (!ctx->cfg.use_graphs) return record_step(ctx, cols, n_layers, head, advance);
-  GraphKey key{cols, n_layers, head ? 1 : 0, advance ? 1 : 0};
+  if (!wide) {
+    int prc = try_persist(ctx, cols, n_layers, head, advance, &done);
+    if (prc || done) return prc;
+  }
+  if (!ctx->cfg.use_graphs) return record_step(ctx, cols, n_layers, head, advance, wide);
+  GraphKey key{cols, n_layers, head ? (wide ? 2 : 1) : 0, advance ? 1 : 0};
   auto it = ctx->graphs.find(key);
   if (it == ctx->graphs.end()) {
     // First use: run eagerly (sets kernel attributes, validates), then capture.
-    int rc = record_step(ctx, cols, n_layers, head, advance);
+    int rc = record_step(ctx, cols, n_layers, head, advance, wide);
     if (rc) return rc;
     int launches = ctx->launches;
     CK(cudaStreamSynchronize(ctx->st));
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(ctx->st, cudaStreamCaptureModeThreadLocal));
-    rc = record_step(ctx, cols, n_layers, head, advance);
+    rc = record_step(ctx, cols, n_layers, head, advance, wide);
     cudaError_t e = cudaStreamEndCapture(ctx->st, &g);
     if (rc) return rc;
     CK(e);
@@ -1668,6 +1690,27 @@ extern "C" int g4_decode_ahead(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t *o
   if ((rc = fetch_tokens(ctx, 1, out_token))) return rc;
   ctx->kv_len[seq] = pos + 1;
   ctx->last_cols = 1;
+  return G4_OK;
+}
+
+extern "C" int g4_verify(g4_ctx *ctx, int32_t seq, const int32_t *tokens, int32_t n, int32_t pos,
+                         int32_t *out_tokens) {
+  if (!ctx || !tokens || !out_tokens) return fail(ctx, G4_ERR_INVALID, "g4_verify: null argument");
+  const int max_n = std::min(ctx->maxc, ctx->head_cols);
+  if (n < 1 || n > max_n)
+    return fail(ctx, G4_ERR_INVALID, "gemma4 engine: a verify pass takes 1 to %d tokens, got %d", max_n, n);
+  int rc = check_seq_pos(ctx, seq, pos, n);
+  if (rc) return rc;
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= ctx->V) return fail(ctx, G4_ERR_INVALID, "token id %d outside the vocabulary", tokens[i]);
+  CK(cudaSetDevice(ctx->dev));
+  std::vector<int32_t> sq(n, seq), ps(n);
+  for (int i = 0; i < n; i++) ps[i] = pos + i;
+  if ((rc = stage(ctx, n, sq.data(), ps.data(), tokens, true))) return rc;
+  if ((rc = run_step(ctx, n, ctx->NL, true, false, n > 1))) return rc;
+  if ((rc = fetch_tokens(ctx, n, out_tokens))) return rc;
+  ctx->kv_len[seq] = pos + n;
+  ctx->last_cols = n;
   return G4_OK;
 }
 

@@ -12,7 +12,8 @@ import ctypes as C
 import numpy as np
 
 from . import _abi
-from .plan import GEMMA4_E2B, KvCacheState, prefill_chunks, run_greedy_loop
+from .plan import (GEMMA4_E2B, KvCacheState, LookupDrafter, SpeculationStats, prefill_chunks,
+                   run_greedy_loop, run_speculative_loop)
 
 
 class Context:
@@ -82,6 +83,12 @@ class Context:
         self._check(self.lib.g4_ctx_memory(self.h, C.byref(w), C.byref(k), C.byref(o)))
         return w.value, k.value, o.value
 
+    def ple_slices(self) -> tuple[int, int, int]:
+        """(slices, rows per slice, rows of the last slice) of the PLE code table."""
+        n, rps, last = C.c_int32(), C.c_int32(), C.c_int32()
+        self._check(self.lib.g4_ctx_ple_slices(self.h, C.byref(n), C.byref(rps), C.byref(last)))
+        return n.value, rps.value, last.value
+
     # forward
     def prefill(self, seq: int, ids, start: int, is_last: bool) -> int:
         ids = np.ascontiguousarray(ids, np.int32)
@@ -99,6 +106,12 @@ class Context:
         tok = C.c_int32(-1)
         self._check(self.lib.g4_decode_ahead(self.h, seq, pos, C.byref(tok)))
         return tok.value
+
+    def verify(self, seq: int, tokens, pos: int) -> list:
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(tokens.size, np.int32)
+        self._check(self.lib.g4_verify(self.h, seq, _abi.i32p(tokens), tokens.size, pos, _abi.i32p(out)))
+        return [int(t) for t in out]
 
     def decode_batch(self, seqs, tokens, positions) -> np.ndarray:
         seqs = np.ascontiguousarray(seqs, np.int32)
@@ -169,6 +182,14 @@ class CudaExecutor:
     def decode_ahead(self, position: int) -> int:
         return self.ctx.decode_ahead(self.seq, position)
 
+    def verify(self, tokens, position: int) -> list:
+        """The verify pass (src/runtime.ts:993-1014): tokens[0] is the last chosen token,
+        tokens[1:] a drafted continuation at `position` onward; answer[i] is the model's argmax
+        after tokens[i], exactly the plain greedy decode's choice there."""
+        if len(tokens) < 1:
+            raise ValueError("gemma4 engine: a verify pass takes at least 1 token, got 0")
+        return self.ctx.verify(self.seq, tokens, position)
+
 
 class Gemma4Mobile:
     """Gemma4Mobile.load / generate / reset / dispose (src/engine.ts:289-927) over the CUDA
@@ -188,8 +209,12 @@ class Gemma4Mobile:
         return cls(ctx)
 
     def generate(self, prompt_ids, max_new_tokens: int = 16, eos_ids=None, lookahead: bool = True,
-                 is_aborted=lambda: False):
-        """Greedy generation; yields token ids. Reuses the KV prefix of the previous call."""
+                 is_aborted=lambda: False, speculate: bool = False, max_columns: int = 2,
+                 drafter=None, stats: SpeculationStats | None = None):
+        """Greedy generation; yields token ids. Reuses the KV prefix of the previous call. With
+        `speculate`, passes verify a prompt-lookup draft of up to max_columns - 1 tokens
+        (src/engine.ts:660-707, src/draft.ts): the ids are the same, only the pass count
+        changes."""
         prompt = [int(t) for t in prompt_ids]
         eos = frozenset(eos_ids) if eos_ids is not None else self.eos_ids
         plan = self.kv_state.accept_prompt(prompt)
@@ -202,6 +227,14 @@ class Gemma4Mobile:
             first = self.executor.prefill(prompt[ch.start:ch.end], ch.start, last)
             self.kv_state.append(prompt[ch.start:ch.end])
         start = len(prompt)
+        if speculate:
+            for token, index in run_speculative_loop(
+                    first, max_new_tokens, eos, start, prompt, max_columns,
+                    drafter or LookupDrafter(), self.executor.decode, self.executor.verify,
+                    is_aborted, on_advance=lambda t, p: self.kv_state.append([t]), stats=stats):
+                yield token
+            self.ctx.kv_truncate(self.executor.seq, self.kv_state.length)
+            return
         for token, index in run_greedy_loop(
                 first, max_new_tokens, eos, start, self.executor.decode, is_aborted,
                 decode_ahead=self.executor.decode_ahead if lookahead else None):

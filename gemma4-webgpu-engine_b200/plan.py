@@ -312,3 +312,106 @@ def run_greedy_loop(first_token: int, max_new_tokens: int, eos_ids, start_positi
             return
         yield token, index
         prev = token
+
+
+# ---------------------------------------------------------------- speculative decode (draft.ts)
+
+LOOKUP_MAX_NGRAM = 8
+LOOKUP_MIN_NGRAM = 2
+
+
+class LookupDrafter:
+    """Prompt-lookup drafting (createLookupDrafter, src/draft.ts:60-98): take the last n tokens,
+    find their most recent earlier occurrence, propose what followed it; the longest n first
+    (max_ngram down to min_ngram), never padding past the end of what exists."""
+
+    def __init__(self, max_ngram: int = LOOKUP_MAX_NGRAM, min_ngram: int = LOOKUP_MIN_NGRAM):
+        self.hi = max(1, int(max_ngram))
+        self.lo = max(1, min(self.hi, int(min_ngram)))
+        self.name = f"lookup-{self.lo}-{self.hi}"
+
+    def propose(self, tokens, want: int) -> list:
+        wanted = max(0, int(want))
+        n_tok = len(tokens)
+        if wanted == 0 or n_tok < self.lo + 1:
+            return []
+        for n in range(min(self.hi, n_tok - 1), self.lo - 1, -1):
+            frm = n_tok - n
+            suffix = list(tokens[frm:])
+            for start in range(frm - 1, -1, -1):
+                if list(tokens[start:start + n]) != suffix:
+                    continue
+                out = list(tokens[start + n:start + n + wanted])
+                if out:
+                    return out
+        return []
+
+
+@dataclass
+class SpeculationStats:
+    """What a speculative run did (SpeculationStats, src/draft.ts:104-134)."""
+    passes: int = 0
+    proposed_drafts: int = 0
+    drafted_tokens: int = 0
+    accepted_drafts: int = 0
+    tokens: int = 0
+
+    def tokens_per_pass(self) -> float:
+        return 0.0 if self.passes == 0 else self.tokens / self.passes
+
+    def acceptance_rate(self) -> float:
+        return 0.0 if self.drafted_tokens == 0 else self.accepted_drafts / self.drafted_tokens
+
+
+def run_speculative_loop(first_token: int, max_new_tokens: int, eos_ids, start_position: int,
+                         history, max_columns: int, drafter, decode, verify,
+                         is_aborted=lambda: False, on_advance=None, stats=None):
+    """runSpeculativeLoop (src/draft.ts:233-330): the greedy loop with one pass per group of
+    tokens. A pass verifies [prev, *draft] when the drafter proposes and decodes prev otherwise;
+    the longest prefix of the draft the model agrees with is accepted, plus the model's own next
+    token. Yields (token, index) exactly as run_greedy_loop does for the same model."""
+    budget = max(0, int(max_new_tokens))
+    if budget == 0 or is_aborted():
+        return
+    if first_token in eos_ids:
+        return
+    yield first_token, 0
+    stats = stats if stats is not None else SpeculationStats()
+    hist = list(history) + [first_token]
+    max_draft = max(0, int(max_columns) - 1)
+    prev, position, index = first_token, start_position, 1
+    while index < budget:
+        if is_aborted():
+            return
+        want = min(max_draft, budget - index - 1)
+        draft = drafter.propose(hist, want) if want > 0 else []
+        stats.passes += 1
+        if draft:
+            stats.proposed_drafts += 1
+            stats.drafted_tokens += len(draft)
+            answer = list(verify([prev, *draft], position))
+            if not answer:
+                return
+            if len(answer) != len(draft) + 1:
+                raise RuntimeError(f"gemma4 engine: a verify pass over {len(draft) + 1} positions "
+                                   f"answered {len(answer)}")
+        else:
+            answer = [decode(prev, position)]
+        matched = 0
+        while matched < len(draft) and answer[matched] == draft[matched]:
+            matched += 1
+        stats.accepted_drafts += matched
+        if on_advance:
+            on_advance(prev, position)
+        for j in range(matched + 1):
+            token = answer[j]
+            if token in eos_ids:
+                return
+            yield token, index
+            index += 1
+            stats.tokens += 1
+            hist.append(token)
+            if j < matched and on_advance:
+                on_advance(token, position + 1 + j)
+        prev = answer[matched]
+        position += 1 + matched

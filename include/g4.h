@@ -192,6 +192,21 @@ int g4_decode(g4_ctx *ctx, int32_t seq, int32_t prev_token, int32_t pos, int32_t
 int g4_decode_ahead(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t *out_token);
 
 /*
+ * GpuExecutor.verify (src/runtime.ts:993-1014), the verify pass of a speculative decode:
+ * tokens[0] is the token the model chose last and tokens[1..n-1] a drafted continuation, placed
+ * at positions pos..pos+n-1 of `seq`; out_tokens[i] receives the model's argmax after tokens[i].
+ * Every column is computed with exactly the arithmetic of a one-token decode step (the
+ * column-for-column contract of src/kernels/qgemvWide.ts:8-71), so out_tokens[i] is what
+ * g4_decode would answer at pos + i given the same prefix. KV rows of all n positions are
+ * written; the caller keeps the accepted prefix with g4_kv_truncate and the next pass overwrites
+ * the rest. n is 1 to min(max_step_columns, max(max_seqs, G4_VERIFY_COLS)); the reference's wide
+ * kernel caps it at GEMV_WIDE_COLS (2).
+ */
+#define G4_VERIFY_COLS 8
+int g4_verify(g4_ctx *ctx, int32_t seq, const int32_t *tokens, int32_t n, int32_t pos,
+              int32_t *out_tokens);
+
+/*
  * Batched decode (new; the reference has no batch dimension): B independent sequences, one
  * column each, every column computed with exactly the arithmetic of a one-sequence step (the
  * column-for-column contract of src/kernels/qgemvWide.ts:8-71).
@@ -222,6 +237,14 @@ int g4_kv_length(const g4_ctx *ctx, int32_t seq, int32_t *n);
  * and its top-2 (value, index) pairs. Mirrors lastLogits (src/engine.ts:820-878).
  */
 int g4_read_logits(g4_ctx *ctx, int32_t col, float *out, int32_t n);
+
+/*
+ * The PLE code table's layout in this context: the number of vocab-row slices (1 when the table
+ * is one buffer), the rows of every slice but the last, and the last slice's rows. The slices a
+ * BufferManager.declareSplit would register (src/buffers.ts:291-326).
+ */
+int g4_ctx_ple_slices(const g4_ctx *ctx, int32_t *n_slices, int32_t *rows_per_slice,
+                      int32_t *last_rows);
 
 /* Device stream the context launches on (a cudaStream_t), for callers that time on it. */
 void *g4_ctx_stream(g4_ctx *ctx);

@@ -6,8 +6,13 @@
                             transliteration of the reference's own CPU oracles
   config2_tokens.json       the C oracle's greedy tokens for BASELINE config 2 (seeded synthetic
                             Gemma-4-E2B shape, 128-token prompt, 128 new tokens)
+  config3_prefill.json      the oracle's token and logits digest after a 2048-token prefill
+  config4_ragged.json       prompt lengths of the 64 ragged sequences, and for three of them the
+                            oracle's tokens and logits digests over prefill + 3 decode steps
+  config5_box.json          the same for three of the box's 512 sequences (512-token prompts)
 
-Usage: python tests/golden/make_golden.py [reference_root] [--config2]
+Usage: python tests/golden/make_golden.py [reference_root] [--vectors] [--config2] [--config3]
+                                          [--config4] [--config5]
 Test infrastructure only.
 """
 from __future__ import annotations
@@ -152,15 +157,96 @@ def config2_tokens() -> dict:
             "tokens": toks.tolist(), "top2_gaps": [float(g) for g in gaps]}
 
 
+def logits_digest(logits) -> dict:
+    """SHA-256 of the f32 logits' bytes (little-endian) plus a few readable values."""
+    import hashlib
+    x = np.ascontiguousarray(logits, np.float32)
+    return {"sha256": hashlib.sha256(x.tobytes()).hexdigest(), "first": [float(v) for v in x[:4]],
+            "max": float(x.max())}
+
+
+def oracle_steps(O, m, prompt, decode_steps: int) -> dict:
+    """Prefill with the KV-sharing exit (producer layers for all but the last position), then
+    greedy decode steps: the token and the logits digest of every step."""
+    n = len(prompt)
+    s = O.Sequence(m, n + decode_steps + 8)
+    if n > 1:
+        s.forward(prompt[:-1], 0, False, False)
+    tok, logits, _ = s.forward(prompt[-1:], n - 1, True, True, want_logits=True)
+    toks, digests = [tok], [logits_digest(logits)]
+    for i in range(decode_steps):
+        tok, logits, _ = s.forward(np.array([toks[-1]], np.int32), n + i, True, True, want_logits=True)
+        toks.append(tok)
+        digests.append(logits_digest(logits))
+    return {"prompt_len": n, "tokens": toks, "logits": digests}
+
+
+def config3_prefill() -> dict:
+    """a 2048-token prefill (prompt = synth_prompt(SEED, 2048))."""
+    from oracle import oracle as O
+    O.build()
+    m = O.Model(SEED)
+    r = oracle_steps(O, m, O.synth_prompt(SEED, 2048), 1)
+    return {"seed": SEED, "prompt_seed": SEED, **r}
+
+
+B64_LO, B64_HI, B64 = 128, 4096, 64
+
+
+def config4_lengths() -> list:
+    """The ragged prompt lengths of BASELINE config 4: U[128, 4096] from numpy's default_rng(SEED)
+    (the same draw bench.py makes)."""
+    return [int(v) for v in np.random.default_rng(SEED).integers(B64_LO, B64_HI + 1, B64)]
+
+
+def config4_ragged() -> dict:
+    """64 sequences, prompt b = synth_prompt(SEED + b, lens[b]); the oracle's
+    prefill and 3 decode steps for the shortest, the longest and sequence 0."""
+    from oracle import oracle as O
+    O.build()
+    m = O.Model(SEED)
+    lens = config4_lengths()
+    picks = sorted({int(np.argmin(lens)), int(np.argmax(lens)), 0})
+    seqs = {}
+    for b in picks:
+        seqs[str(b)] = oracle_steps(O, m, O.synth_prompt(SEED + b, lens[b]), 3)
+        print(f"config4 sequence {b} (len {lens[b]}) done", flush=True)
+    return {"seed": SEED, "lens": lens, "decode_steps": 3, "sequences": seqs}
+
+
+BOX_SEQS, BOX_PROMPT = 512, 512
+
+
+def config5_box() -> dict:
+    """BASELINE config 5 on one replica: 512 sequences of 512 tokens (prompt b =
+    synth_prompt(SEED + b, 512)); the oracle's prefill and 2 decode steps for three of them."""
+    from oracle import oracle as O
+    O.build()
+    m = O.Model(SEED)
+    seqs = {}
+    for b in (0, 257, 511):
+        seqs[str(b)] = oracle_steps(O, m, O.synth_prompt(SEED + b, BOX_PROMPT), 2)
+        print(f"config5 sequence {b} done", flush=True)
+    return {"seed": SEED, "sequences_total": BOX_SEQS, "prompt_len": BOX_PROMPT, "decode_steps": 2,
+            "sequences": seqs}
+
+
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
     ref = args[0] if args else os.environ.get("G4_REFERENCE")
     ref = Path(ref) if ref else None
     if ref is not None and ref.exists():
         (HERE / "reference_constants.json").write_text(json.dumps(reference_constants(ref), indent=1))
-    (HERE / "ref_vectors.json").write_text(json.dumps(ref_vectors()))
+    if "--vectors" in sys.argv or not any(a.startswith("--config") for a in sys.argv):
+        (HERE / "ref_vectors.json").write_text(json.dumps(ref_vectors()))
     if "--config2" in sys.argv:
         (HERE / "config2_tokens.json").write_text(json.dumps(config2_tokens(), indent=1))
+    if "--config3" in sys.argv:
+        (HERE / "config3_prefill.json").write_text(json.dumps(config3_prefill(), indent=1))
+    if "--config4" in sys.argv:
+        (HERE / "config4_ragged.json").write_text(json.dumps(config4_ragged(), indent=1))
+    if "--config5" in sys.argv:
+        (HERE / "config5_box.json").write_text(json.dumps(config5_box(), indent=1))
 
 
 if __name__ == "__main__":

@@ -277,3 +277,84 @@ def test_config2_full_model_greedy_128(pkg, O, cuda):
     assert toks == g["tokens"]
     ctx.close()
     om.close()
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_verify_pass_matches_sequential_decode(pkg, O, tiny, graphs):
+    """g4_verify (GpuExecutor.verify, src/runtime.ts:993-1014): answer[i] is the argmax after
+    tokens[i], with the logits of the one-token decode step bit for bit, on a draft that is right,
+    one that is wrong after its first token, and widths 2 to 8."""
+    a, om = tiny
+    prompt = O.synth_prompt(SEED + 9, 30, a.vocab_size)
+    n = len(prompt)
+    want, want_logits = oracle_run(O, om, prompt, 9)
+    ctx = make_ctx(pkg, a, max_seqs=1, use_graphs=graphs)
+    assert ctx.prefill(0, prompt, 0, True) == want[0]
+    for width in (2, 4, 8):
+        ctx.kv_truncate(0, n)
+        ans = ctx.verify(0, want[:width], n)
+        assert ans == want[1:width + 1], width
+        for i in range(width):
+            np.testing.assert_array_equal(ctx.logits(i).view(np.uint32), want_logits[i + 1].view(np.uint32))
+    # A wrong second token: the first answer is still the greedy token, and the next pass (a
+    # plain decode at the accepted position) overwrites the rejected row.
+    ctx.kv_truncate(0, n)
+    wrong = (want[1] + 1) % a.vocab_size
+    ans = ctx.verify(0, [want[0], wrong, want[2]], n)
+    assert ans[0] == want[1]
+    ctx.kv_truncate(0, n + 1)
+    assert ctx.decode(0, want[1], n + 1) == want[2]
+    np.testing.assert_array_equal(ctx.logits(0).view(np.uint32), want_logits[2].view(np.uint32))
+    with pytest.raises(pkg.G4Error, match="verify pass takes 1 to"):
+        ctx.verify(0, want[:9], n)
+    ctx.close()
+
+
+def test_speculative_generate_matches_plain(pkg, O, tiny):
+    """Gemma4Mobile.generate with speculation (prompt-lookup drafts checked by verify passes)
+    yields the plain greedy ids, in fewer passes when drafts are accepted."""
+    a, om = tiny
+    base = list(O.synth_prompt(SEED + 21, 12, a.vocab_size))
+    prompt = base + base[:8]            # a repeat, so the drafter has something to propose
+    plain_ctx = make_ctx(pkg, a, max_seqs=1)
+    plain = list(pkg.engine.Gemma4Mobile(plain_ctx).generate(prompt, max_new_tokens=24))
+    plain_ctx.close()
+    want, _ = om.generate(np.array(prompt, np.int32), 24, 128)
+    assert plain == list(want)
+    for cols in (2, 4):
+        ctx = make_ctx(pkg, a, max_seqs=1)
+        stats = pkg.plan.SpeculationStats()
+        model = pkg.engine.Gemma4Mobile(ctx)
+        spec = list(model.generate(prompt, max_new_tokens=24, speculate=True, max_columns=cols,
+                                   stats=stats))
+        assert spec == plain, cols
+        assert stats.passes + 1 <= 24
+        # The transcript the host keeps equals what the caches hold, so a follow-up prompt reuses it.
+        assert ctx.kv_length(0) == model.kv_state.length
+        assert model.kv_state.tokens == prompt + spec[:-1]
+        ctx.close()
+
+
+def test_verify_full_model(pkg, cuda):
+    """Config-2 shape: a verify pass over the golden greedy continuation answers the next golden
+    tokens, with logits bit-identical to the sequential decode steps."""
+    g = json.loads((GOLDEN / "config2_tokens.json").read_text())
+    prompt = np.array(g["prompt"], np.int32)
+    toks = g["tokens"]
+    logits = {}
+    for mode in ("verify", "decode"):
+        ctx = pkg.engine.Context(device=0, max_seqs=1, max_context=256, max_step_columns=64)
+        ctx.init_random(SEED)
+        assert ctx.prefill(0, prompt, 0, True) == toks[0]
+        if mode == "verify":
+            assert ctx.verify(0, toks[:8], 128) == toks[1:9]
+            logits[mode] = [ctx.logits(i).copy() for i in range(8)]
+        else:
+            got = []
+            for i in range(8):
+                got.append(ctx.decode(0, toks[i], 128 + i))
+                logits.setdefault(mode, []).append(ctx.logits(0).copy())
+            assert got == toks[1:9]
+        ctx.close()
+    for lv, ld in zip(logits["verify"], logits["decode"]):
+        np.testing.assert_array_equal(lv.view(np.uint32), ld.view(np.uint32))

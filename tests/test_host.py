@@ -88,3 +88,72 @@ def test_greedy_loop_semantics(P):
     assert list(P.run_greedy_loop(10, 1, set(), 0, decode)) == [(10, 0)]
     aborted = iter([False, True])
     assert list(P.run_greedy_loop(10, 5, set(), 0, decode, lambda: next(aborted, True))) == [(10, 0)]
+
+
+def test_lookup_drafter(P):
+    d = P.LookupDrafter()
+    assert d.name == "lookup-2-8"
+    # The suffix [7, 8] occurred earlier, followed by 9, 10.
+    assert d.propose([7, 8, 9, 10, 11, 7, 8], 3) == [9, 10, 11]
+    # The most recent earlier occurrence wins; proposals stop at the end of what exists.
+    assert d.propose([1, 2, 5, 1, 2, 6, 1, 2], 4) == [6, 1, 2]
+    # The longest matching suffix wins over a shorter, more recent one.
+    assert d.propose([3, 1, 2, 4, 9, 1, 2, 5, 3, 1, 2], 1) == [4]
+    assert d.propose([1, 2, 3], 2) == []          # no earlier occurrence
+    assert d.propose([1, 2, 1, 2], 0) == []        # nothing wanted
+    assert d.propose([1], 2) == []                 # too short for a 2-gram plus one
+
+
+class _FakeModel:
+    """A deterministic 'model': the next token is a fixed function of the previous one, so a
+    greedy run is known and verify's answers are checkable."""
+
+    def __init__(self, table):
+        self.table = table
+        self.passes = []
+
+    def next(self, t):
+        return self.table[t % len(self.table)]
+
+    def decode(self, prev, pos):
+        self.passes.append(("decode", pos, 1))
+        return self.next(prev)
+
+    def verify(self, tokens, pos):
+        self.passes.append(("verify", pos, len(tokens)))
+        return [self.next(t) for t in tokens]
+
+
+@pytest.mark.parametrize("max_columns", [2, 4, 8])
+def test_speculative_loop_matches_greedy_loop(P, max_columns):
+    table = [3, 4, 5, 3, 6, 7, 3, 4, 9, 2]   # 3 -> 4 -> 6 -> 3 ... repeats, so drafts hit
+    prompt = [1, 3, 4, 6, 3, 4]
+    m = _FakeModel(table)
+    greedy = [t for t, _ in P.run_greedy_loop(m.next(prompt[-1]), 20, set(), len(prompt), m.decode)]
+    m2 = _FakeModel(table)
+    stats = P.SpeculationStats()
+    advanced = []
+    spec = [t for t, _ in P.run_speculative_loop(
+        m2.next(prompt[-1]), 20, set(), len(prompt), prompt, max_columns, P.LookupDrafter(),
+        m2.decode, m2.verify, on_advance=lambda t, p: advanced.append((t, p)), stats=stats)]
+    assert spec == greedy
+    assert stats.tokens == 19 and stats.passes < 19          # drafts were accepted
+    assert stats.acceptance_rate() > 0.5
+    assert all(n <= max_columns for _, _, n in m2.passes)
+    # Every advanced row is a transcript token at its own position.
+    transcript = prompt + greedy
+    assert [t for t, _ in advanced] == transcript[len(prompt):len(prompt) + len(advanced)]
+    assert [p for _, p in advanced] == list(range(len(prompt), len(prompt) + len(advanced)))
+
+
+def test_speculative_loop_stops_and_refuses_short_answers(P):
+    table = [3, 4, 5, 3, 6, 7, 3, 4, 9, 2]
+    prompt = [1, 3, 4, 6, 3, 4]
+    m = _FakeModel(table)
+    spec = [t for t, _ in P.run_speculative_loop(m.next(prompt[-1]), 20, {3}, len(prompt), prompt, 4,
+                                                 P.LookupDrafter(), m.decode, m.verify)]
+    assert spec == [6]                   # the stop token (3) is never yielded
+    bad = _FakeModel(table)
+    with pytest.raises(RuntimeError, match="answered"):
+        list(P.run_speculative_loop(6, 20, set(), len(prompt), prompt + [6, 3, 4, 6], 4,
+                                    P.LookupDrafter(), bad.decode, lambda toks, pos: [1]))
