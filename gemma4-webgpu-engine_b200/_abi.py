@@ -70,6 +70,8 @@ SIGNATURES = {
     "g4_decode_ahead": (C.c_int, [_vp, _i32, _i32, _i32p]),
     "g4_decode_batch": (C.c_int, [_vp, _i32, _i32p, _i32p, _i32p, _i32p]),
     "g4_verify": (C.c_int, [_vp, _i32, _i32p, _i32, _i32, _i32p]),
+    "g4_op_wait_probe": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp]),
+    "g4_debug_fail_allocation": (C.c_int, [_i32]),
     "g4_step_stage": (C.c_int, [_vp, _i32, _i32p, _i32p, _i32p]),
     "g4_step_run_device": (C.c_int, [_vp, _i32, _i32]),
     "g4_step_read_tokens": (C.c_int, [_vp, _i32, _i32p]),

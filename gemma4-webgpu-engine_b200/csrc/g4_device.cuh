@@ -242,11 +242,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on an mbarrier phase: false once the iteration limit is reached.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-  for (int i = 0; i < (1 << 22); i++)
+// Bounded wait on an mbarrier phase: false once `limit` polls have not seen it complete.
+__device__ __forceinline__ bool mbar_wait_n(uint64_t *bar, uint32_t parity, int limit) {
+  for (int i = 0; i < limit; i++)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
+}
+// The poll limit of every wait in the library's kernels (build-time option; well under a second).
+#ifndef G4_WAIT_POLLS
+#define G4_WAIT_POLLS (1 << 22)
+#endif
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  return mbar_wait_n(bar, parity, G4_WAIT_POLLS);
 }
 __device__ __forceinline__ void l2_prefetch(const void *p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");

@@ -575,6 +575,39 @@ int trace_take(unsigned long long *out, int max_records) {
 }
 #endif
 
+// Failure-detection probe: thread 0 copies `bytes` into shared memory by a bulk copy completing
+// on one mbarrier, and arms a second mbarrier for `missing` bytes that no copy delivers. With
+// missing > 0 the bounded wait on the second barrier gives up after `limit` polls and raises the
+// device error flag, exactly as a kernel whose weight copy never lands does; the thread then waits
+// (bounded) for its own copy before the CTA exits. status: [second wait completed, copy landed,
+// byte sum of the copy].
+__global__ void k_wait_probe(const uint8_t *src, int bytes, int missing, int limit, int32_t *status) {
+  __shared__ __align__(128) uint8_t buf[4096];
+  __shared__ __align__(8) uint64_t bars[2];
+  if (threadIdx.x != 0) return;
+  mbar_init(&bars[0], 1);
+  mbar_init(&bars[1], 1);
+  mbar_fence_init();
+  mbar_expect_tx(&bars[0], (uint32_t)bytes);
+  bulk_g2s(buf, src, (uint32_t)bytes, &bars[0]);
+  mbar_expect_tx(&bars[1], (uint32_t)missing);
+  const bool done = mbar_wait_n(&bars[1], 0, limit);
+  if (!done) atomicExch(&g4_dev_error, 4);
+  const bool landed = mbar_wait(&bars[0], 0);
+  uint32_t sum = 0;
+  if (landed)
+    for (int i = 0; i < bytes; i++) sum += buf[i];
+  status[0] = done ? 1 : 0;
+  status[1] = landed ? 1 : 0;
+  status[2] = (int32_t)sum;
+}
+
+cudaError_t launch_wait_probe(const void *src, int bytes, int missing, int limit, int32_t *status,
+                              cudaStream_t st) {
+  k_wait_probe<<<1, 32, 0, st>>>((const uint8_t *)src, bytes, missing, limit, status);
+  return cudaGetLastError();
+}
+
 int device_error_take() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g4_dev_error, sizeof(int)) != cudaSuccess) return -1;

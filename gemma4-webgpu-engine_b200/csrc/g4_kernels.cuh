@@ -104,6 +104,8 @@ int gemv_stream_partition(GemvArgs &a, int sms);
 cudaError_t launch_gemv_stream(const GemvArgs &a, int bits, cudaStream_t st, bool pdl);
 // Nonzero when a bounded device wait gave up since the last call (then cleared).
 int device_error_take();
+cudaError_t launch_wait_probe(const void *src, int bytes, int missing, int limit, int32_t *status,
+                              cudaStream_t st);
 #ifdef G4_TRACE
 // Diagnostic build only: the (kernel id, time) records since the last call, then cleared.
 int trace_take(unsigned long long *out, int max_records);

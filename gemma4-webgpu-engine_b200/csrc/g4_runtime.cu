@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -183,6 +184,21 @@ static int fail(g4_ctx *c, int code, const char *fmt, ...) {
 // For the other translation units of the library: record a context-free error message.
 void g4_internal_set_error(const char *msg) { tl_error = msg; }
 
+// Out-of-memory injection for tests: armed with n > 0, the n-th device allocation a context makes
+// from then on fails as cudaMalloc does when the device is out of memory.
+static std::atomic<int> g_fail_alloc{0};
+
+static cudaError_t ctx_malloc(void **p, size_t bytes) {
+  int n = g_fail_alloc.load(std::memory_order_relaxed);
+  while (n > 0 && !g_fail_alloc.compare_exchange_weak(n, n - 1)) {
+  }
+  if (n == 1) {
+    *p = nullptr;
+    return cudaErrorMemoryAllocation;
+  }
+  return cudaMalloc(p, bytes);
+}
+
 extern "C" const char *g4_last_error(const g4_ctx *ctx) {
   return ctx ? ctx->err.c_str() : tl_error.c_str();
 }
@@ -325,7 +341,7 @@ static size_t weight_arena_bytes(const g4_arch &a) {
 static int alloc_weights(g4_ctx *ctx) {
   const g4_arch &a = ctx->cfg.arch;
   ctx->arena_bytes = weight_arena_bytes(a);
-  CK(cudaMalloc(&ctx->arena, ctx->arena_bytes));
+  CK(ctx_malloc((void **)&ctx->arena, ctx->arena_bytes));
   ctx->arena_used = 0;
   const int H = ctx->H;
   ctx->layers.assign(a.layer_count, Layer());
@@ -404,9 +420,9 @@ static int alloc_weights(g4_ctx *ctx) {
   ctx->ple_slices.assign(n, nullptr);
   for (int i = 0; i < n; i++) {
     size_t rows = i + 1 < n ? (size_t)rps : (size_t)last;
-    CK(cudaMalloc(&ctx->ple_slices[i], rows * row_bytes));
+    CK(ctx_malloc((void **)&ctx->ple_slices[i], rows * row_bytes));
   }
-  CK(cudaMalloc(&ctx->d_ple_slices, sizeof(uint8_t *) * n));
+  CK(ctx_malloc((void **)&ctx->d_ple_slices, sizeof(uint8_t *) * n));
   CK(cudaMemcpy(ctx->d_ple_slices, ctx->ple_slices.data(), sizeof(uint8_t *) * n, cudaMemcpyHostToDevice));
   ctx->ple_slice_bytes = total;
   ctx->tensors[std::string(LMP) + "embed_tokens_per_layer.embedding_quantized"] = {nullptr, total, true};
@@ -423,7 +439,7 @@ static int alloc_runtime(g4_ctx *ctx) {
     size_t hd = ctx->layers[L].hd;
     ctx->kv_stride[L] = 2 * (size_t)mctx * hd;
     size_t bytes = ctx->kv_stride[L] * ctx->cfg.max_seqs * 4;
-    CK(cudaMalloc(&ctx->kv[L], bytes));
+    CK(ctx_malloc((void **)&ctx->kv[L], bytes));
     CK(cudaMemset(ctx->kv[L], 0, bytes));
     ctx->kv_bytes += bytes;
   }
@@ -439,8 +455,8 @@ static int alloc_runtime(g4_ctx *ctx) {
         cs[(size_t)p * pairs + i] = (float)std::cos(ang);
         sn[(size_t)p * pairs + i] = (float)std::sin(ang);
       }
-    CK(cudaMalloc(cd, cs.size() * 4));
-    CK(cudaMalloc(sd, sn.size() * 4));
+    CK(ctx_malloc((void **)cd, cs.size() * 4));
+    CK(ctx_malloc((void **)sd, sn.size() * 4));
     CK(cudaMemcpy(*cd, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(*sd, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
     ctx->other_bytes += cs.size() * 8;
@@ -453,7 +469,7 @@ static int alloc_runtime(g4_ctx *ctx) {
   // Activation slots, sized once for the widest step (src/execute.ts:248-317).
   const size_t ghd = a.global_head_dim, nh = a.query_heads, ffn = std::max(a.producer_intermediate, a.consumer_intermediate);
   auto take = [&](float **p, size_t n) -> int {
-    CK(cudaMalloc(p, n * 4));
+    CK(ctx_malloc((void **)p, n * 4));
     CK(cudaMemset(*p, 0, n * 4));
     ctx->other_bytes += n * 4;
     return G4_OK;
@@ -481,26 +497,26 @@ static int alloc_runtime(g4_ctx *ctx) {
   ctx->gq_ld = (int)((std::max<size_t>({(size_t)ctx->H, ffn, nh * ghd}) + 127) & ~(size_t)127);
   ctx->gq_rows = std::max(maxc, 256);
   for (int i = 0; i < 3; i++) {
-    CK(cudaMalloc(&ctx->gq[i], (size_t)ctx->gq_rows * ctx->gq_ld));
+    CK(ctx_malloc((void **)&ctx->gq[i], (size_t)ctx->gq_rows * ctx->gq_ld));
     CK(cudaMemset(ctx->gq[i], 0, (size_t)ctx->gq_rows * ctx->gq_ld));
   }
   ctx->gacc_ld = ctx->gq_ld;
-  CK(cudaMalloc(&ctx->gacc, (size_t)maxc * ctx->gacc_ld * 4));
+  CK(ctx_malloc((void **)&ctx->gacc, (size_t)maxc * ctx->gacc_ld * 4));
   CK(cudaMemset(ctx->gacc, 0, (size_t)maxc * ctx->gacc_ld * 4));
-  CK(cudaMalloc(&ctx->gcnt, 8192 * 4));
+  CK(ctx_malloc((void **)&ctx->gcnt, 8192 * 4));
   CK(cudaMemset(ctx->gcnt, 0, 8192 * 4));
   ctx->gparts = (int)((a.vocab_size + 127) / 128);
-  CK(cudaMalloc(&ctx->gpv, (size_t)maxc * ctx->gparts * 4));
-  CK(cudaMalloc(&ctx->gpi, (size_t)maxc * ctx->gparts * 4));
+  CK(ctx_malloc((void **)&ctx->gpv, (size_t)maxc * ctx->gparts * 4));
+  CK(ctx_malloc((void **)&ctx->gpi, (size_t)maxc * ctx->gparts * 4));
   ctx->gemm_min_cols = ctx->cfg.gemm_min_columns > 0 ? ctx->cfg.gemm_min_columns : 16;
   ctx->gemm_split_k = ctx->cfg.gemm_split_k;
-  CK(cudaMalloc(&ctx->pbar, 2 * sizeof(unsigned)));
+  CK(ctx_malloc((void **)&ctx->pbar, 2 * sizeof(unsigned)));
   CK(cudaMemset(ctx->pbar, 0, 2 * sizeof(unsigned)));
   ctx->persist_grid = ctx->cfg.persistent_decode ? persist_max_grid(ctx->dev) : 0;
   ctx->ffn_max = (ffn + 15) & ~15;
-  CK(cudaMalloc(&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
-  CK(cudaMalloc(&ctx->codes_ple, (size_t)maxc * ctx->PD));
-  CK(cudaMalloc(&ctx->att_count, (size_t)maxc * 8 * 4));
+  CK(ctx_malloc((void **)&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
+  CK(ctx_malloc((void **)&ctx->codes_ple, (size_t)maxc * ctx->PD));
+  CK(ctx_malloc((void **)&ctx->att_count, (size_t)maxc * 8 * 4));
   CK(cudaMemset(ctx->att_count, 0, (size_t)maxc * 8 * 4));
   // Logit rows: one per sequence of a decode batch, and at least G4_VERIFY_COLS for the
   // positions of a verify pass.
@@ -513,11 +529,11 @@ static int alloc_runtime(g4_ctx *ctx) {
   ctx->head_cap = std::min(ctx->gemv_target, ctx->V);
   ctx->head_blocks = ctx->head_cap;
   if ((rc = take(&ctx->head_pv, (size_t)ctx->head_cols * ctx->head_cap))) return rc;
-  CK(cudaMalloc(&ctx->head_pi, (size_t)ctx->head_cols * ctx->head_cap * 4));
-  CK(cudaMalloc(&ctx->d_step, (size_t)3 * maxc * 4));
+  CK(ctx_malloc((void **)&ctx->head_pi, (size_t)ctx->head_cols * ctx->head_cap * 4));
+  CK(ctx_malloc((void **)&ctx->d_step, (size_t)3 * maxc * 4));
   CK(cudaMemset(ctx->d_step, 0, (size_t)3 * maxc * 4));
-  CK(cudaMalloc(&ctx->d_tok_out, (size_t)maxc * 4));
-  CK(cudaMalloc(&ctx->d_val_out, (size_t)maxc * 4));
+  CK(ctx_malloc((void **)&ctx->d_tok_out, (size_t)maxc * 4));
+  CK(ctx_malloc((void **)&ctx->d_val_out, (size_t)maxc * 4));
   for (int i = 0; i < g4_ctx::kStageSlots; i++) {
     CK(cudaMallocHost(&ctx->h_step[i], (size_t)3 * maxc * 4));
     CK(cudaEventCreateWithFlags(&ctx->stage_ev[i], cudaEventDisableTiming));
@@ -649,6 +665,11 @@ extern "C" int g4_ctx_ple_slices(const g4_ctx *ctx, int32_t *n_slices, int32_t *
   if (n_slices) *n_slices = n;
   if (rows_per_slice) *rows_per_slice = ctx->ple_rps;
   if (last_rows) *last_rows = n > 0 ? ctx->V - (n - 1) * ctx->ple_rps : 0;
+  return G4_OK;
+}
+
+extern "C" int g4_debug_fail_allocation(int32_t nth) {
+  g_fail_alloc.store(nth > 0 ? nth : 0);
   return G4_OK;
 }
 
@@ -1531,7 +1552,7 @@ static int try_persist(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       for (size_t i = 0; i + 1 < plan.size(); i++) plan[i].sync_after = 1;
       cudaFree(ctx->d_plan[k]);
       ctx->d_plan[k] = nullptr;
-      CK(cudaMalloc(&ctx->d_plan[k], plan.size() * sizeof(PPhase)));
+      CK(ctx_malloc((void **)&ctx->d_plan[k], plan.size() * sizeof(PPhase)));
       CK(cudaMemcpyAsync(ctx->d_plan[k], plan.data(), plan.size() * sizeof(PPhase),
                          cudaMemcpyHostToDevice, ctx->st));
       CK(cudaStreamSynchronize(ctx->st));
@@ -2157,6 +2178,20 @@ extern "C" int g4_op_softcap_argmax(const float *logits, float *capped, int32_t 
   if (e == cudaSuccess) e = launch_argmax_final(pv, pi, parts, 1, nullptr, token, (float *)(token + 1), st, false);
   cudaFreeAsync(pv, st);
   OPCK(e);
+  return G4_OK;
+}
+
+extern "C" int g4_op_wait_probe(const void *src, int32_t bytes, int32_t missing_bytes,
+                                int32_t poll_limit, int32_t *status, void *stream) {
+  if (!src || !status || bytes < 16 || bytes > 4096 || bytes % 16 || ((uintptr_t)src & 15) ||
+      missing_bytes < 0 || missing_bytes > (1 << 20) || poll_limit < 1 || poll_limit > (1 << 22))
+    return fail(nullptr, G4_ERR_INVALID, "g4_op_wait_probe: bad argument");
+  if (device_error_take() < 0) return fail(nullptr, G4_ERR_CUDA, "g4_op_wait_probe: cannot read the device error flag");
+  OPCK(launch_wait_probe(src, bytes, missing_bytes, poll_limit, status, (cudaStream_t)stream));
+  OPCK(cudaStreamSynchronize((cudaStream_t)stream));
+  if (device_error_take() > 0)
+    return fail(nullptr, G4_ERR_TIMEOUT, "a bounded device wait gave up after %d polls (its barrier "
+                "expected %d bytes that no copy delivers)", poll_limit, missing_bytes);
   return G4_OK;
 }
 

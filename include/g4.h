@@ -371,6 +371,27 @@ int g4_op_attention_noalloc(const float *q, const float *cache, float *out, int3
                             int32_t head_dim, int32_t q_count, int32_t q_start, int32_t kv_len,
                             int32_t window, int32_t max_context, void *stream);
 
+/*
+ * Failure detection without a fault (no counterpart in the reference, whose lost-device handling
+ * is src/engine.ts:791-798). A one-thread kernel copies `bytes` (16..4096, a multiple of 16) from
+ * `src` (16-byte aligned device memory) into shared memory through a bulk copy, and arms a second
+ * mbarrier for `missing_bytes` that no copy delivers. With missing_bytes > 0 its bounded wait gives
+ * up after `poll_limit` polls, raises the device error flag every library kernel raises when a
+ * wait gives up, waits for its own copy and exits; the call then returns G4_ERR_TIMEOUT and the
+ * device stays usable. status (device, 3 int32): [second wait completed, copy landed, byte sum].
+ * Synchronises `stream`.
+ */
+int g4_op_wait_probe(const void *src, int32_t bytes, int32_t missing_bytes, int32_t poll_limit,
+                     int32_t *status, void *stream);
+
+/*
+ * Out-of-memory injection for tests: with nth > 0, the nth device allocation a context makes from
+ * now on (g4_ctx_create's arena, tables, caches and activations) fails as cudaMalloc does when
+ * the device is out of memory; 0 disarms. The failing call returns G4_ERR_OOM, names the
+ * allocation in g4_last_error and releases what it had allocated.
+ */
+int g4_debug_fail_allocation(int32_t nth);
+
 /* Elementwise probes of the library's f32 exp and tanh (used by the attention softmax, GELU
  * and the softcap), for checking them against CUDA's expf/tanhf within error bounds. */
 int g4_op_math_probe(const float *x, float *exp_out, float *tanh_out, float *cuda_exp,
