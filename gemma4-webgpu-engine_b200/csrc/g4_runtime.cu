@@ -154,8 +154,11 @@ struct g4_ctx {
   uint64_t other_bytes = 0;
   std::map<GraphKey, cudaGraphExec_t> graphs;
   std::map<GraphKey, int> graph_launches;   // kernels in each graph
+  std::map<GraphKey, std::vector<std::string>> graph_roles;
   int sms = 148;
   int launches = 0;
+  // One "kernel<TAB>role" line per launch of the last forward call, in launch order.
+  std::vector<std::string> roles;
   int last_cols = 0;
   int staged_cols = 0;
   std::vector<int32_t> staged_seq, staged_pos;
@@ -197,6 +200,18 @@ static cudaError_t ctx_malloc(void **p, size_t bytes) {
     return cudaErrorMemoryAllocation;
   }
   return cudaMalloc(p, bytes);
+}
+
+// Record one launch of the step being built: its kernel family and the reference roles it covers
+// (module names without the model.language_model. prefix, or the fused step's role).
+static void note_launch(g4_ctx *ctx, const std::string &kernel, const std::string &role) {
+  ctx->launches++;
+  ctx->roles.push_back(kernel + "\t" + role);
+}
+
+static std::string short_module(const std::string &m) {
+  static const std::string pre = "model.language_model.";
+  return m.compare(0, pre.size(), pre) == 0 ? m.substr(pre.size()) : m;
 }
 
 extern "C" const char *g4_last_error(const g4_ctx *ctx) {
@@ -675,6 +690,18 @@ extern "C" int g4_debug_fail_allocation(int32_t nth) {
 
 extern "C" void *g4_ctx_stream(g4_ctx *ctx) { return ctx ? (void *)ctx->st : nullptr; }
 
+extern "C" int g4_last_launch_list(const g4_ctx *ctx, char *buf, uint64_t cap, uint64_t *needed) {
+  if (!ctx || !needed) return fail(nullptr, G4_ERR_INVALID, "null argument");
+  std::string all;
+  for (const std::string &r : ctx->roles) all += r + "\n";
+  *needed = all.size() + 1;
+  if (buf) {
+    if (cap < all.size() + 1) return fail(nullptr, G4_ERR_INVALID, "launch list needs %llu bytes", (unsigned long long)(all.size() + 1));
+    memcpy(buf, all.c_str(), all.size() + 1);
+  }
+  return G4_OK;
+}
+
 extern "C" int g4_last_launches(const g4_ctx *ctx, int32_t *n) {
   if (!ctx || !n) return fail(nullptr, G4_ERR_INVALID, "null argument");
   *n = ctx->launches;
@@ -906,6 +933,20 @@ struct Seg {
   float *y;
 };
 
+static std::string seg_roles(std::initializer_list<Seg> segs) {
+  std::string r;
+  for (auto &sg : segs) r += (r.empty() ? "" : ",") + short_module(sg.lin->module);
+  return r;
+}
+
+static std::string layer_role(int L, bool kv_store) {
+  return "layers." + std::to_string(L) + ".self_attn" + (kv_store ? ",kv_store" : "");
+}
+
+static std::string bits_name(const char *family, int bits, bool head = false) {
+  return std::string(family) + "-" + std::to_string(bits) + "bit" + (head ? "-head" : "");
+}
+
 struct WRef {
   const void *p;
   uint64_t bytes;
@@ -951,11 +992,11 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   q.cols = cols;
   CK(launch_quantize(q, ctx->gq[0], ctx->gq_ld, sc[0], nsc > 1 ? ctx->gq[1] : nullptr, nsc > 1 ? sc[1] : 0.0f,
                      ctx->st, true));
-  ctx->launches++;
+  note_launch(ctx, "quantize", seg_roles(segs));
   if (nsc > 2) {
     q.hidden_out = nullptr;
     CK(launch_quantize(q, ctx->gq[2], ctx->gq_ld, sc[2], nullptr, 0.0f, ctx->st, true));
-    ctx->launches++;
+    note_launch(ctx, "quantize", seg_roles(segs));
   }
   // Token tile: 64 or 128 columns; wider steps use 128-column tiles at two CTAs per SM (one
   // CTA's epilogue runs while the other's MMAs do), or 256-column tiles one per SM.
@@ -1011,7 +1052,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
       while (splits < 8 && 2 * splits * all_tiles <= 2 * ctx->sms && 2 * splits <= K / 128) splits *= 2;
     g.splits = splits;
     CK(launch_qgemm_multi(m, g, segs.begin()->lin->bits, bn, ctx->st, true));
-    ctx->launches++;
+    note_launch(ctx, bits_name("qgemm", segs.begin()->lin->bits), seg_roles(segs));
     return G4_OK;
   }
   i = 0;
@@ -1039,7 +1080,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
       if (splits > 1) {
         g.splits = splits;
         CK(launch_qgemm_cluster(l.tmw, *tx, g, l.bits, ctx->st, true));
-        ctx->launches++;
+        note_launch(ctx, bits_name("qgemm", l.bits), short_module(l.module));
         continue;
       }
     }
@@ -1081,7 +1122,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
       const int bn_l = bn == 64 && tiles >= 2 * ctx->sms ? -64 : bn;
       CK(launch_qgemm(l.tmw, *tx, g, l.bits, bn_l, ctx->st, true));
     }
-    ctx->launches++;
+    note_launch(ctx, bits_name("qgemm", l.bits, head), short_module(l.module));
   }
   return G4_OK;
 }
@@ -1152,7 +1193,7 @@ static int plan_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, G
   ph.g = a;
   if (!ok) ctx->plan_ok = false;
   ctx->plan->push_back(ph);
-  ctx->launches++;
+  note_launch(ctx, bits_name("qgemv", segs.begin()->lin->bits, head), seg_roles(segs));
   return G4_OK;
 }
 
@@ -1206,7 +1247,7 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
       ctx->cur_parts = blocks;
     }
     CK(launch_gemv(a, l0->bits, ctx->st, true));
-    ctx->launches++;
+    note_launch(ctx, bits_name("qgemv", l0->bits, head), seg_roles(segs));
   }
   return G4_OK;
 }
@@ -1235,6 +1276,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
   const float eps = a.rms_eps;
   int32_t *d_seq = ctx->d_step, *d_pos = ctx->d_step + ctx->maxc, *d_tok = ctx->d_step + 2 * ctx->maxc;
   ctx->launches = 0;
+  ctx->roles.clear();
   // ---- embed phase (planEmbed, src/plan.ts:727-736)
   if (ctx->plan) {
     PPhase e;
@@ -1265,7 +1307,9 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, n_layers, PD,
                           ctx->ple_cols, eps, (float)0.7071067811865476, ctx->st, true));
   }
-  ctx->launches += 3;
+  note_launch(ctx, "embed-gather", "embed_tokens,embed_tokens_per_layer");
+  note_launch(ctx, "dense-bf16", "per_layer_model_projection");
+  note_launch(ctx, "ple-combine", "per_layer_projection_norm");
   int cur = 0;
   int rc;
   for (int L = 0; L < n_layers; L++) {
@@ -1338,7 +1382,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       } else {
         CK(launch_attn_decode(ad, ctx->st, true));
       }
-      ctx->launches++;
+      note_launch(ctx, "attention-decode", layer_role(L, ly.producer));
     }
     // ---- attention prologue: q-norm-rope, kv-norm-rope-store (src/kernels/attnPrologue.ts)
     if (!fused_attn) {
@@ -1366,7 +1410,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       ap.refs.pos = d_pos;
       ap.eps = eps;
       CK(launch_attn_prologue(ap, ctx->st, true));
-      ctx->launches++;
+      note_launch(ctx, "attn-prologue", layer_role(L, ly.producer));
     }
     // ---- attention over the producer cache (kvRoleForLayer)
     if (!fused_attn) {
@@ -1391,10 +1435,11 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       if (cols > 1) {
         // A prefill chunk: consecutive positions of one sequence, query-tiled.
         CK(launch_attention_prefill(at, ctx->st, true));
-        ctx->launches++;
+        note_launch(ctx, "attention-prefill", layer_role(L, false));
       } else {
         CK(launch_attention(at, ctx->st, true));
-        ctx->launches += 2;
+        note_launch(ctx, "attention-blocks", layer_role(L, false));
+        note_launch(ctx, "attention-merge", layer_role(L, false));
       }
     }
     // ---- o_proj
@@ -1529,7 +1574,8 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
                              ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
       if (advance) CK(launch_advance(d_pos, cols, ctx->st, true));
     }
-    ctx->launches += advance ? 2 : 1;
+    note_launch(ctx, "argmax-final", "argmax");
+    if (advance) note_launch(ctx, "advance", "position advance");
   }
   return G4_OK;
 }
@@ -1562,7 +1608,9 @@ static int try_persist(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
   }
   if (ctx->plan_state[k] != 1) return G4_OK;
   CK(launch_decode_persist(ctx->d_plan[k], ctx->plan_n[k], ctx->pbar, ctx->persist_grid, ctx->st));
-  ctx->launches = 1;
+  ctx->launches = 0;
+  ctx->roles.clear();
+  note_launch(ctx, "decode-persistent", "every phase of the step");
   *done = true;
   return G4_OK;
 }
@@ -1582,6 +1630,7 @@ static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance
     int rc = record_step(ctx, cols, n_layers, head, advance, wide);
     if (rc) return rc;
     int launches = ctx->launches;
+    std::vector<std::string> roles = ctx->roles;
     CK(cudaStreamSynchronize(ctx->st));
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(ctx->st, cudaStreamCaptureModeThreadLocal));
@@ -1594,12 +1643,15 @@ static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance
     cudaGraphDestroy(g);
     ctx->graphs[key] = ex;
     ctx->graph_launches[key] = launches;
+    ctx->graph_roles[key] = roles;
     ctx->launches = launches;
+    ctx->roles = roles;
     // The eager run already advanced the step; the graph serves the next calls.
     return G4_OK;
   }
   CK(cudaGraphLaunch(it->second, ctx->st));
   ctx->launches = ctx->graph_launches[key];
+  ctx->roles = ctx->graph_roles[key];
   return G4_OK;
 }
 
@@ -1662,19 +1714,24 @@ extern "C" int g4_prefill(g4_ctx *ctx, int32_t seq, const int32_t *ids, int32_t 
   // producer-only chunk (src/plan.ts:160-192, 812-824).
   int body = is_last ? n - 1 : n;
   int launches = 0;
+  std::vector<std::string> roles;
   for (int c0 = 0; c0 < body; c0 += ctx->maxc) {
     int cols = std::min(ctx->maxc, body - c0);
     for (int i = 0; i < cols; i++) ps[i] = start_pos + c0 + i;
     if ((rc = stage(ctx, cols, sq.data(), ps.data(), ids + c0, true))) return rc;
     if ((rc = record_step(ctx, cols, nl_prod, false))) return rc;
     launches += ctx->launches;
+    roles.insert(roles.end(), ctx->roles.begin(), ctx->roles.end());
   }
   ctx->launches = launches;
+  ctx->roles = roles;
   if (is_last) {
     ps[0] = start_pos + n - 1;
     if ((rc = stage(ctx, 1, sq.data(), ps.data(), ids + n - 1, true))) return rc;
     if ((rc = run_step(ctx, 1, nl_all, true))) return rc;
     ctx->launches += launches;
+    roles.insert(roles.end(), ctx->roles.begin(), ctx->roles.end());
+    ctx->roles = roles;
     int32_t tok;
     if ((rc = fetch_tokens(ctx, 1, &tok))) return rc;
     if (out_token) *out_token = tok;

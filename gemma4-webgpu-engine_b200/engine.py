@@ -156,6 +156,14 @@ class Context:
         self._check(self.lib.g4_last_launches(self.h, C.byref(n)))
         return n.value
 
+    def launch_list(self) -> list:
+        """(kernel, roles) of every launch of the last forward call, in launch order."""
+        need = C.c_uint64(0)
+        self._check(self.lib.g4_last_launch_list(self.h, None, 0, C.byref(need)))
+        buf = C.create_string_buffer(need.value)
+        self._check(self.lib.g4_last_launch_list(self.h, buf, need.value, C.byref(need)))
+        return [tuple(line.split("\t", 1)) for line in buf.value.decode().splitlines()]
+
     def stream(self) -> int:
         return self.lib.g4_ctx_stream(self.h)
 

@@ -102,66 +102,99 @@ def prefill_chunks(start: int, prompt_length: int, chunk_size: int = DEFAULT_PRE
 
 @dataclass(frozen=True)
 class DispatchStep:
-    kernel: str
-    phase: str
+    kernel: str    # the executor's kernel family (g4_last_launch_list's first field)
+    phase: str     # embed, attn, mlp, ple, head
     layer: int
-    role: str
+    modules: str   # the checkpoint modules or roles the launch covers (its second field)
+    covers: str = ""   # the reference dispatch roles the fused launch replaces
 
 
-def plan_layer(arch: Gemma4Arch, layer: int) -> list:
-    """One decode layer as the fused steps this build launches, each named by the reference
-    roles it covers."""
+GEMV_MAX_COLUMNS = 8   # the streaming GEMV takes up to 8 columns per launch
+
+
+def plan_layer(arch: Gemma4Arch, layer: int, mode: str = "decode", cols: int = 1) -> list:
+    """One layer as the executor launches it on the GEMV path (steps narrower than the
+    tensor-core threshold), each launch named by its kernel and the modules it covers. A decode
+    step fuses the attention prologue, blocks and merge into one launch per layer; a prefill chunk
+    runs the prologue, then the query-tiled attention (blocks and merge for a single column)."""
     producer = is_kv_producer(arch, layer)
+    p = f"layers.{layer}."
     s = []
-    add = lambda k, ph, r: s.append(DispatchStep(k, ph, layer, r))
+    reps = (cols + GEMV_MAX_COLUMNS - 1) // GEMV_MAX_COLUMNS
+
+    def add(kernel, phase, modules, covers="", n=1):
+        for _ in range(n):
+            s.append(DispatchStep(kernel, phase, layer, modules, covers))
+
     pre = "input_layernorm" if layer == 0 else "previous tail join"
-    add("qgemv-4bit", "attn", f"{pre}; q_proj" + (", k_proj, v_proj" if producer else ""))
-    add("attn-prologue", "attn", "q_norm per head, rope q" +
-        ("; k_norm, v_norm weightless, rope k, kv store" if producer else ""))
-    add("attention-blocks", "attn", "attention")
-    add("attention-merge", "attn", "attention split fold")
-    add("qgemv-4bit", "attn", "o_proj")
-    add("qgemv-4bit", "mlp", "post_attention_layernorm plus residual, pre_feedforward_layernorm; "
-        "gate_proj, up_proj")
-    add("qgemv-4bit", "mlp", "gelu times up, down_proj")
-    add("qgemv-8bit", "ple", "post_feedforward_layernorm plus residual; per_layer_input_gate")
-    add("qgemv-8bit", "ple", "gate times per layer row, per_layer_projection")
+    qkv = p + "self_attn.q_proj" + (f",{p}self_attn.k_proj,{p}self_attn.v_proj" if producer else "")
+    add("qgemv-4bit", "attn", qkv, f"{pre}; q_proj" + (", k_proj, v_proj" if producer else ""), reps)
+    att = p + "self_attn" + (",kv_store" if producer else "")
+    pro = "q_norm per head, rope q" + ("; k_norm, v_norm weightless, rope k, kv store" if producer else "")
+    if mode == "decode":
+        add("attention-decode", "attn", att, pro + "; attention; attention split fold")
+    else:
+        add("attn-prologue", "attn", att, pro)
+        if cols > 1:
+            add("attention-prefill", "attn", p + "self_attn", "attention; attention split fold")
+        else:
+            add("attention-blocks", "attn", p + "self_attn", "attention")
+            add("attention-merge", "attn", p + "self_attn", "attention split fold")
+    add("qgemv-4bit", "attn", p + "self_attn.o_proj", "o_proj", reps)
+    add("qgemv-4bit", "mlp", f"{p}mlp.gate_proj,{p}mlp.up_proj",
+        "post_attention_layernorm plus residual, pre_feedforward_layernorm; gate_proj, up_proj", reps)
+    add("qgemv-4bit", "mlp", p + "mlp.down_proj", "gelu times up, down_proj", reps)
+    add("qgemv-8bit", "ple", p + "per_layer_input_gate",
+        "post_feedforward_layernorm plus residual; per_layer_input_gate", reps)
+    add("qgemv-8bit", "ple", p + "per_layer_projection",
+        "gate times per layer row, per_layer_projection", reps)
     return s
 
 
 def plan_embed(arch: Gemma4Arch) -> list:
     return [
-        DispatchStep("embed-gather", "embed", -1, "embed_tokens gather, per layer embedding gather"),
-        DispatchStep("dense-bf16", "embed", -1, "per_layer_model_projection"),
-        DispatchStep("ple-combine", "embed", -1,
+        DispatchStep("embed-gather", "embed", -1, "embed_tokens,embed_tokens_per_layer",
+                     "embed_tokens gather, per layer embedding gather"),
+        DispatchStep("dense-bf16", "embed", -1, "per_layer_model_projection",
+                     "per_layer_model_projection"),
+        DispatchStep("ple-combine", "embed", -1, "per_layer_projection_norm",
                      "per_layer_projection_norm, per layer inputs add, per layer inputs scale"),
     ]
 
 
-def plan_head(arch: Gemma4Arch) -> list:
-    return [
-        DispatchStep("qgemv-4bit-head", "head", -1,
-                     "post_per_layer_input_norm plus residual, layer_scalar, final norm; lm_head; "
-                     "tanh(logits / 30) * 30; argmax partials"),
-        DispatchStep("argmax-final", "head", -1, "argmax final"),
-    ]
+def plan_head(arch: Gemma4Arch, cols: int = 1, advance: bool = False) -> list:
+    reps = (cols + GEMV_MAX_COLUMNS - 1) // GEMV_MAX_COLUMNS
+    s = [DispatchStep("qgemv-4bit-head", "head", -1, "lm_head",
+                      "post_per_layer_input_norm plus residual, layer_scalar, final norm; lm_head; "
+                      "tanh(logits / 30) * 30; argmax partials")] * reps
+    s.append(DispatchStep("argmax-final", "head", -1, "argmax", "argmax final"))
+    if advance:
+        s.append(DispatchStep("advance", "head", -1, "position advance", "next step's position"))
+    return s
 
 
-def plan_decode_step(arch: Gemma4Arch = GEMMA4_E2B) -> list:
+def plan_decode_step(arch: Gemma4Arch = GEMMA4_E2B, cols: int = 1, advance: bool = False) -> list:
+    """planDecodeStep (src/plan.ts:487-784) as this executor launches it: the embed, every layer,
+    the head. `cols` sequences of one position each on the GEMV path."""
     steps = list(plan_embed(arch))
     for layer in range(arch.layer_count):
-        steps += plan_layer(arch, layer)
-    steps += plan_head(arch)
+        steps += plan_layer(arch, layer, "decode", cols)
+    steps += plan_head(arch, cols, advance)
     return steps
 
 
-def plan_prefill_chunk(arch: Gemma4Arch, is_last: bool) -> list:
-    steps = list(plan_embed(arch))
-    n = arch.layer_count if is_last else arch.kv_producer_layers
-    for layer in range(n):
-        steps += plan_layer(arch, layer)
+def plan_prefill_chunk(arch: Gemma4Arch, is_last: bool, cols: int = 1) -> list:
+    """A prefill chunk of `cols` positions (src/plan.ts:790-824): the producer layers over every
+    position but the last chunk's final one, which then runs as a one-column decode step through
+    all layers and the head (the KV-sharing exit)."""
+    body = cols - 1 if is_last else cols
+    steps = []
+    if body > 0:
+        steps += plan_embed(arch)
+        for layer in range(arch.kv_producer_layers):
+            steps += plan_layer(arch, layer, "prefill", body)
     if is_last:
-        steps += plan_head(arch)
+        steps += plan_decode_step(arch, 1)
     return steps
 
 

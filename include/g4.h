@@ -252,6 +252,16 @@ void *g4_ctx_stream(g4_ctx *ctx);
 /* Launch count of the last forward call, as recorded by the executor. */
 int g4_last_launches(const g4_ctx *ctx, int32_t *launches);
 
+/*
+ * The launches of the last forward call, one "kernel<TAB>roles" line each in launch order: the
+ * kernel family (qgemv-4bit, attention-decode, qgemm-8bit, ...) and the reference modules or roles
+ * it covers (e.g. "layers.3.self_attn.q_proj,layers.3.self_attn.k_proj,layers.3.self_attn.v_proj").
+ * The executor's compiled plan, for comparison with planDecodeStep's dispatch list (src/plan.ts:
+ * 487-859, src/engine.ts:919-922). `*needed` receives the bytes including the terminating NUL;
+ * buf may be NULL to ask for that size.
+ */
+int g4_last_launch_list(const g4_ctx *ctx, char *buf, uint64_t cap, uint64_t *needed);
+
 /* ------------------------------------------------------------------ per-operator calls */
 /*
  * The operator API (the registry's Kernel.bind, src/kernels/registry.ts:108-119), one entry per

@@ -358,3 +358,61 @@ def test_verify_full_model(pkg, cuda):
         ctx.close()
     for lv, ld in zip(logits["verify"], logits["decode"]):
         np.testing.assert_array_equal(lv.view(np.uint32), ld.view(np.uint32))
+
+
+def _plan_arch(pkg, a):
+    return pkg.plan.Gemma4Arch(
+        layer_count=a.layer_count, hidden_size=a.hidden_size,
+        global_layers=tuple(L for L in range(a.layer_count) if (a.global_layer_mask >> L) & 1),
+        sliding_window=a.sliding_window, kv_producer_layers=a.kv_producer_layers,
+        producer_intermediate=a.producer_intermediate, consumer_intermediate=a.consumer_intermediate,
+        vocab_size=a.vocab_size)
+
+
+def _launches(ctx):
+    return [(k, r) for k, r in ctx.launch_list()]
+
+
+def _planned(steps):
+    return [(s.kernel, s.modules) for s in steps]
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_executor_launches_match_plan(pkg, O, tiny, graphs):
+    """The executor's compiled plan (g4_last_launch_list) is plan.py's dispatch list launch for
+    launch: kernel family and covered modules, for prefill chunks, decode steps (eager, captured
+    and replayed), a decode batch and the device-resident advancing step."""
+    a, _ = tiny
+    P = pkg.plan
+    arch = _plan_arch(pkg, a)
+    ctx = make_ctx(pkg, a, max_seqs=4, use_graphs=graphs)
+    prompt = O.synth_prompt(SEED + 31, 10, a.vocab_size)
+    ctx.prefill(0, prompt[:9], 0, False)
+    assert _launches(ctx) == _planned(P.plan_prefill_chunk(arch, False, 9))
+    tok = ctx.prefill(0, prompt[9:], 9, True)
+    assert _launches(ctx) == _planned(P.plan_prefill_chunk(arch, True, 1))
+    assert ctx.launches() == len(ctx.launch_list())
+    for i in range(3):   # eager, captured, replayed
+        tok = ctx.decode(0, tok, 10 + i)
+        assert _launches(ctx) == _planned(P.plan_decode_step(arch, 1))
+    toks = [ctx.prefill(b, prompt[:4 + b], 0, True) for b in (1, 2, 3)]
+    ctx.decode_batch([1, 2, 3], toks, [5, 6, 7])
+    assert _launches(ctx) == _planned(P.plan_decode_step(arch, 3))
+    ctx.step_stage([0], [tok], [13])
+    ctx.step_run_device(1)
+    assert _launches(ctx) == _planned(P.plan_decode_step(arch, 1, advance=True))
+    ctx.close()
+
+
+def test_executor_launches_match_plan_full_model(pkg, cuda):
+    """Gemma-4-E2B shape: one B=1 decode step is planDecodeStep's 250 launches as plan.py lists
+    them (embed 3, 35 layers x 7, head 2)."""
+    P = pkg.plan
+    ctx = pkg.engine.Context(device=0, max_seqs=1, max_context=64, max_step_columns=16)
+    ctx.init_random(SEED)
+    tok = ctx.prefill(0, np.arange(1, 9, dtype=np.int32), 0, True)
+    ctx.decode(0, tok, 8)
+    got = _launches(ctx)
+    want = _planned(P.plan_decode_step(P.GEMMA4_E2B, 1))
+    assert len(got) == 250 and got == want
+    ctx.close()

@@ -70,8 +70,15 @@ def test_decode_census(P):
     steps = P.plan_decode_step(P.GEMMA4_E2B)
     c = P.census(steps)
     assert c["qgemv-4bit"] == 35 * 4 and c["qgemv-8bit"] == 35 * 2
-    assert c["attention-blocks"] == 35 and c["argmax-final"] == 1
-    assert len(P.plan_prefill_chunk(P.GEMMA4_E2B, False)) == 3 + 15 * 9
+    assert c["attention-decode"] == 35 and c["argmax-final"] == 1 and c["qgemv-4bit-head"] == 1
+    assert len(steps) == 3 + 35 * 7 + 2          # 250 launches per B=1 token
+    # Producers store KV; consumers attend over producer 13 / 14's cache.
+    assert steps[3].modules.endswith("v_proj") and steps[3 + 7 * 20].modules.endswith("q_proj")
+    assert P.census(P.plan_decode_step(P.GEMMA4_E2B, cols=12))["qgemv-4bit"] == 35 * 4 * 2
+    chunk = P.plan_prefill_chunk(P.GEMMA4_E2B, False, cols=8)
+    assert len(chunk) == 3 + 15 * 8
+    last = P.plan_prefill_chunk(P.GEMMA4_E2B, True, cols=1)
+    assert last == P.plan_decode_step(P.GEMMA4_E2B)
 
 
 def test_greedy_loop_semantics(P):
