@@ -33,6 +33,7 @@ class Arch(C.Structure):
         ("kv_producer_layers", C.c_int32), ("producer_intermediate", C.c_int32),
         ("consumer_intermediate", C.c_int32), ("vocab_size", C.c_int32), ("ple_dim", C.c_int32),
         ("attn_bits", C.c_int32), ("mlp_bits", C.c_int32), ("ple_bits", C.c_int32),
+        ("consumer_mlp_bits", C.c_int32), ("head_bits", C.c_int32), ("head_calibrated", C.c_int32),
         ("rms_eps", C.c_float), ("final_softcap", C.c_float), ("rope_theta_sliding", C.c_float),
         ("rope_theta_global", C.c_float), ("partial_rotary_factor", C.c_float),
     ]
@@ -43,7 +44,7 @@ class Config(C.Structure):
         ("arch", Arch), ("max_seqs", C.c_int32), ("max_context", C.c_int32),
         ("max_step_columns", C.c_int32), ("use_graphs", C.c_int32),
         ("ple_slice_bytes", C.c_uint64), ("gemm_min_columns", C.c_int32),
-        ("persistent_decode", C.c_int32), ("gemm_split_k", C.c_int32),
+        ("gemm_split_k", C.c_int32),
     ]
 
 
@@ -71,6 +72,8 @@ SIGNATURES = {
     "g4_decode_batch": (C.c_int, [_vp, _i32, _i32p, _i32p, _i32p, _i32p]),
     "g4_verify": (C.c_int, [_vp, _i32, _i32p, _i32, _i32, _i32p]),
     "g4_op_wait_probe": (C.c_int, [_vp, _i32, _i32, _i32, _vp, _vp]),
+    "g4_op_repack_tile16": (C.c_int, [_vp, _vp, _i32, _i32, _i32, _vp]),
+    "g4_arch_checkpoint": (C.c_int, [C.POINTER(Arch)]),
     "g4_debug_fail_allocation": (C.c_int, [_i32]),
     "g4_step_stage": (C.c_int, [_vp, _i32, _i32p, _i32p, _i32p]),
     "g4_step_run_device": (C.c_int, [_vp, _i32, _i32]),

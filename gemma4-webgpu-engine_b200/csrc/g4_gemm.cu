@@ -93,6 +93,22 @@ int make_tmap_u8(CUtensorMap *m, const void *base, uint64_t inner, uint64_t oute
   return r == CUDA_SUCCESS ? 0 : -3;
 }
 
+// 32-bit elements (the 2-bit family's interleaved tiles: inner = K words, outer = tiles).
+int make_tmap_u32(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return -1;
+  if (((uintptr_t)base & 15) || (row_stride & 15) || box_inner > 256 || box_outer > 256) return -2;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(base), dims, strides, box,
+                  elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
 // ------------------------------------------------------------------ device helpers
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
@@ -195,6 +211,7 @@ struct GemmShape {
   static constexpr int A_BYTES = GM_BM * GM_BK;          // 16 KB
   static constexpr int B_BYTES = BN * GM_BK;
   static constexpr int P_BYTES = GM_BM * GM_BK / 2;      // packed int4 staging, 8 KB
+  static constexpr int P2_BYTES = GM_BM * GM_BK / 4;     // 2-bit tiles: 8 x 128 words, 4 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES;
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
   static constexpr int SMEM = 1024 + BAR_OFF + (3 * STAGES + 2) * 8 + 64 + 4 * 32 * 8;
@@ -265,12 +282,14 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
   grid_launch_dependents();
   // The producer requests the first stages' weights before the dependency wait (weights never
   // depend on the previous kernel), so their fetch overlaps that kernel's tail.
-  const uint32_t wbytes = BITS == 4 ? S::P_BYTES : S::A_BYTES;
+  const uint32_t wbytes = BITS == 4 ? S::P_BYTES : (BITS == 2 ? S::P2_BYTES : S::A_BYTES);
   const int npre = KT < NS ? KT : NS;
   auto load_w = [&](int kt) {
     const int s = kt % NS, kg = kt_begin + kt;
     if (BITS == 4)
       tma_load_2d(P(s), tmW, kg * (GM_BK / 2), n0, &full[s]);
+    else if (BITS == 2)
+      tma_load_2d(P(s), tmW, kg * GM_BK, n0 / 16, &full[s]);
     else
       tma_load_2d(A(s), tmW, kg * GM_BK, n0, &full[s]);
   };
@@ -320,7 +339,7 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
       constexpr uint32_t IDESC = idesc_i8(BN);
       for (int kt = 0; kt < KT; kt++) {
         const int s = kt % NS;
-        uint64_t *ready = BITS == 4 ? &aready[s] : &full[s];
+        uint64_t *ready = BITS != 8 ? &aready[s] : &full[s];
         if (!mbar_wait(ready, (uint32_t)((kt / NS) & 1))) {
           atomicExch(&g4_gemm_error, 1);
           flags[0] = 1;
@@ -337,6 +356,50 @@ __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
     }
   } else {
     const int tu = t - 64;   // 0..127
+    if (BITS == 2) {
+      // Thread tu: tile tu / 16 of the stage's eight, 16-column chunk (tu / 2) % 8, rows
+      // 8 (tu % 2) .. + 7 of the tile; 16 words in, 8 rows x 16 signed codes (u - 2) out.
+      const int lt = tu >> 4, ch = (tu >> 1) & 7, half = tu & 1;
+      for (int kt = 0; kt < KT; kt++) {
+        const int s = kt % NS;
+        if (!mbar_wait(&full[s], (uint32_t)((kt / NS) & 1))) {
+          atomicExch(&g4_gemm_error, 1);
+          flags[0] = 1;
+          break;
+        }
+        const uint4 *src = reinterpret_cast<const uint4 *>(P(s) + lt * 512 + ch * 64);
+        uint32_t w[16];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const uint4 v = src[q];
+          w[4 * q] = v.x;
+          w[4 * q + 1] = v.y;
+          w[4 * q + 2] = v.z;
+          w[4 * q + 3] = v.w;
+        }
+        uint8_t *dst = A(s);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const int rr = 8 * half + i, row = 16 * lt + rr;
+          uint32_t o[4];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const uint32_t lo = __byte_perm(w[4 * q] >> (2 * rr), w[4 * q + 1] >> (2 * rr), 0x0040);
+            const uint32_t hi = __byte_perm(w[4 * q + 2] >> (2 * rr), w[4 * q + 3] >> (2 * rr), 0x0040);
+            uint32_t v = __byte_perm(lo, hi, 0x5410) & 0x03030303u;
+            // u - 2 as signed bytes: flip bit 1; where it is then set (u < 2), set bits 2..7.
+            v ^= 0x02020202u;
+            v |= (v & 0x02020202u) * 0x7Fu;
+            o[q] = v;
+          }
+          *reinterpret_cast<uint4 *>(dst + (row >> 3) * 1024 + (row & 7) * 128 + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aready[s]);
+      }
+    }
     if (BITS == 4) {
       for (int kt = 0; kt < KT; kt++) {
         const int s = kt % NS;
@@ -885,7 +948,7 @@ static cudaError_t launch_gemm_cluster_t(const GemmMaps &maps, const GemmArgs &a
 
 static cudaError_t launch_cluster_maps(const GemmMaps &m, const GemmArgs &a, int bits, cudaStream_t st, bool pdl) {
   if (a.K % GM_BK != 0 || a.N < 1 || a.M < 1 || a.head || a.splits > a.K / GM_BK ||
-      (bits != 4 && bits != 8))
+      (bits != 2 && bits != 4 && bits != 8))
     return cudaErrorInvalidValue;
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
@@ -904,6 +967,12 @@ static cudaError_t launch_cluster_maps(const GemmMaps &m, const GemmArgs &a, int
     case 281: return launch_gemm_cluster_t<8, 2, 3>(m, a, st, pdl);
     case 481: return launch_gemm_cluster_t<8, 4, 3>(m, a, st, pdl);
     case 881: return launch_gemm_cluster_t<8, 8, 3>(m, a, st, pdl);
+    case 220: return launch_gemm_cluster_t<2, 2, 0>(m, a, st, pdl);
+    case 420: return launch_gemm_cluster_t<2, 4, 0>(m, a, st, pdl);
+    case 820: return launch_gemm_cluster_t<2, 8, 0>(m, a, st, pdl);
+    case 221: return launch_gemm_cluster_t<2, 2, 3>(m, a, st, pdl);
+    case 421: return launch_gemm_cluster_t<2, 4, 3>(m, a, st, pdl);
+    case 821: return launch_gemm_cluster_t<2, 8, 3>(m, a, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -926,6 +995,7 @@ cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, i
   if (bn == -128) {
     if (bits == 4) return launch_gemm_t<4, 128, EPI_Y, 2>(m, a, st, pdl);
     if (bits == 8) return launch_gemm_t<8, 128, EPI_Y, 2>(m, a, st, pdl);
+    if (bits == 2) return launch_gemm_t<2, 128, EPI_Y, 2>(m, a, st, pdl);
     return cudaErrorInvalidValue;
   }
   // More CTAs than SMs: three stages, two CTAs per SM.
@@ -935,6 +1005,7 @@ cudaError_t launch_qgemm_multi(const GemmMaps &m, const GemmArgs &a, int bits, i
   const bool two = gemm_x_tiles(a) * ((a.M + 63) / 64) > sms;
   if (bits == 4) return two ? launch_gemm_t<4, 64, EPI_Y, 3>(m, a, st, pdl) : launch_gemm_t<4, 64, EPI_Y>(m, a, st, pdl);
   if (bits == 8) return two ? launch_gemm_t<8, 64, EPI_Y, 3>(m, a, st, pdl) : launch_gemm_t<8, 64, EPI_Y>(m, a, st, pdl);
+  if (bits == 2) return two ? launch_gemm_t<2, 64, EPI_Y, 3>(m, a, st, pdl) : launch_gemm_t<2, 64, EPI_Y>(m, a, st, pdl);
   return cudaErrorInvalidValue;
 }
 
@@ -975,6 +1046,10 @@ cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const G
   if (bits == 8) {
     if (a.head) return launch_gemm_b<8, EPI_HEAD>(tmW, tmX, a, bn, st, pdl);
     return launch_gemm_b<8, EPI_Y>(tmW, tmX, a, bn, st, pdl);
+  }
+  if (bits == 2) {
+    if (a.head) return launch_gemm_b<2, EPI_HEAD>(tmW, tmX, a, bn, st, pdl);
+    return launch_gemm_b<2, EPI_Y>(tmW, tmX, a, bn, st, pdl);
   }
   return cudaErrorInvalidValue;
 }

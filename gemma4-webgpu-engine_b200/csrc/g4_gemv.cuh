@@ -1,7 +1,7 @@
-// Device code shared by the per-launch kernels (g4_kernels.cu) and the persistent decode kernel
-// (g4_persist.cu): the linear's prologues (activation snap to int8 codes in the dp4a layout, the
-// fused norms and joins), the weight-ring sizing, the attention block range, and the per-head
-// norm + rotation. Same arithmetic in both, so both paths give the same bits.
+// Device code shared by the GEMV kernels (g4_kernels.cu, g4_gemv2.cu): the linear's prologues
+// (activation snap to int8 codes, the fused norms and joins), the weight-ring sizing, the
+// attention block range, and the per-head norm + rotation. Same arithmetic everywhere, so every
+// path gives the same bits.
 #pragma once
 #include <float.h>
 #include "g4_device.cuh"
@@ -92,13 +92,13 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, const ProGai
   }
   const float in_r = __fdiv_rn(1.0f, in_scale);
   if (PRO == PRO_X || PRO == PRO_GELU) {
-    // K <= 8192: at most eight vec4 chunks per thread, loaded four at a time.
+    // K <= 16384: at most sixteen vec4 chunks per thread, loaded four at a time.
     const float4 *src = reinterpret_cast<const float4 *>(a.src + (size_t)c * a.ld_src);
     const float4 *up = PRO == PRO_GELU
                            ? reinterpret_cast<const float4 *>(a.up + (size_t)c * a.ld_up + a.up_off)
                            : nullptr;
 #pragma unroll 1
-    for (int i0 = 0; i0 < 8 && t + 256 * i0 < nc; i0 += 4) {
+    for (int i0 = 0; i0 < 16 && t + 256 * i0 < nc; i0 += 4) {
       float4 xv[4], uv[4];
 #pragma unroll
       for (int i = 0; i < 4; i++)
@@ -170,6 +170,66 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, const ProGai
   return xs;
 }
 
+// The same prologues for an uncalibrated linear (input scale 0.0): column c's activation vector
+// is kept in f32 (xf, K floats) instead of being snapped to codes.
+template <int PRO>
+__device__ __forceinline__ void gemv_prologue_f32(const GemvArgs &a, const ProGains &pg, int c,
+                                                  float *xf, float *red, bool write_hidden) {
+  const int t = threadIdx.x;
+  const int K = a.K;
+  const int nc = K >> 2;
+  float4 *dst = reinterpret_cast<float4 *>(xf);
+  if (PRO == PRO_X || PRO == PRO_GELU) {
+    const float4 *src = reinterpret_cast<const float4 *>(a.src + (size_t)c * a.ld_src);
+    const float4 *up = PRO == PRO_GELU
+                           ? reinterpret_cast<const float4 *>(a.up + (size_t)c * a.ld_up + a.up_off)
+                           : nullptr;
+    for (int i = t; i < nc; i += 256) dst[i] = up ? f4_gelu_mul(src[i], up[i]) : src[i];
+    return;
+  }
+  const float4 *src = reinterpret_cast<const float4 *>(a.src + (size_t)c * a.ld_src);
+  const float4 *res = PRO != PRO_NORM ? reinterpret_cast<const float4 *>(a.res + (size_t)c * a.ld_res)
+                                        : nullptr;
+  float4 sv[2], rv[2];
+  int cnt = 0;
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+    if (t + 256 * i < nc) {
+      sv[i] = src[t + 256 * i];
+      if (res) rv[i] = res[t + 256 * i];
+      cnt = i + 1;
+    }
+  const float inv1 = rms_inv(block_sumsq256_regs<2>(sv, cnt, red), K, a.eps);
+  float4 xv[2];
+  if (PRO == PRO_NORM) {
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+      if (i < cnt) xv[i] = f4_norm_apply(sv[i], inv1, pg.g1[i]);
+  } else {
+    float4 h[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+      if (i < cnt) {
+        h[i] = f4_add(rv[i], f4_norm_apply(sv[i], inv1, pg.g1[i]));
+        if (PRO == PRO_JOIN) h[i] = f4_scale(h[i], a.alpha);
+        if (write_hidden)
+          reinterpret_cast<float4 *>(a.hidden_out + (size_t)c * a.ld_res)[t + 256 * i] = h[i];
+      }
+    if (PRO == PRO_NORMRES) {
+#pragma unroll
+      for (int i = 0; i < 2; i++)
+        if (i < cnt) xv[i] = h[i];
+    } else {
+      const float inv2 = rms_inv(block_sumsq256_regs<2>(h, cnt, red), K, a.eps);
+#pragma unroll
+      for (int i = 0; i < 2; i++)
+        if (i < cnt) xv[i] = f4_norm_apply(h[i], inv2, pg.g2[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+    if (i < cnt) dst[t + 256 * i] = xv[i];
+}
 
 constexpr int GS_RING = 96 * 1024;   // shared-memory ring per CTA
 constexpr int GS_MAX_STAGES = 8;

@@ -15,21 +15,6 @@ __device__ unsigned long long g4_trace_buf[1 << 16];
 __device__ unsigned int g4_trace_n;
 #endif
 
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                            cudaStream_t st, bool pdl, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
-}
 
 // =====================================================================================
 // Quantized linear (qgemv / qgemm column contract, src/kernels/qgemv.ts:413-690 and
@@ -608,14 +593,19 @@ cudaError_t launch_wait_probe(const void *src, int bytes, int missing, int limit
   return cudaGetLastError();
 }
 
+int gemv2_error_take();
+
 int device_error_take() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g4_dev_error, sizeof(int)) != cudaSuccess) return -1;
   if (v) cudaMemcpyToSymbol(g4_dev_error, &zero, sizeof(int));
-  return v;
+  const int v2 = gemv2_error_take();
+  if (v2 < 0) return -1;
+  return v ? v : v2;
 }
 
 cudaError_t launch_gemv(const GemvArgs &a, int bits, cudaStream_t st, bool pdl) {
+  if (bits == 2) return launch_gemv2(a, st, pdl);
   if (a.seg[0].in_scale == 0.0f) {
     // Uncalibrated f32 path: one column, one segment, x or gelu prologue only.
     if (a.cols != 1 || a.nseg != 1 || !(a.pro == PRO_X || a.pro == PRO_GELU) || a.head)
@@ -634,14 +624,15 @@ cudaError_t launch_gemv(const GemvArgs &a, int bits, cudaStream_t st, bool pdl) 
 
 // =====================================================================================
 // Gathers (embed-gather / ple-gather-4bit(-sliced), src/kernels/embedGather.ts:176-261,
-// 547-577): one thread per packed word of 8 int4 codes; the embed scale folds into the row
-// scale first, then one multiply per element.
+// 547-577): one thread per 8 columns of a row; the embed scale folds into the row scale first,
+// then one multiply per element. The embedding is int4 rows (zero point 8) or the 2-bit family's
+// interleaved tiles (zero point 2: column k of row r at bits 2 (r % 16) of word (r / 16) H + k).
 // =====================================================================================
 
 __global__ void __launch_bounds__(256)
 k_embed(const int32_t *tokens, const uint8_t *embed_w, const uint16_t *embed_s, float embed_scale,
         const uint8_t *const *ple_slices, int ple_rps, const uint16_t *ple_s, int H, int ple_cols,
-        int ple_group, float *residual, float *ple_id) {
+        int ple_group, float *residual, float *ple_id, int embed_bits) {
   grid_launch_dependents();
   grid_wait();
   G4_TRACE_POINT(3001);
@@ -653,6 +644,20 @@ k_embed(const int32_t *tokens, const uint8_t *embed_w, const uint16_t *embed_s, 
   uint32_t word;
   float scale;
   float *dst;
+  if (w < hw && embed_bits == 2) {
+    const uint4 *tw = reinterpret_cast<const uint4 *>(embed_w + ((size_t)(row / 16) * H + 8 * w) * 4);
+    const uint4 q0 = tw[0], q1 = tw[1];
+    const int sh = 2 * (row % 16);
+    scale = __fmul_rn(embed_scale, f16_bits_to_f32(embed_s[row]));
+    const uint32_t cw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = __fmul_rn((float)((int)((cw[j] >> sh) & 3u) - 2), scale);
+    dst = residual + (size_t)c * H + 8 * w;
+    reinterpret_cast<float4 *>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    return;
+  }
   if (w < hw) {
     word = reinterpret_cast<const uint32_t *>(embed_w)[(size_t)row * hw + w];
     scale = __fmul_rn(embed_scale, f16_bits_to_f32(embed_s[row]));
@@ -675,11 +680,11 @@ k_embed(const int32_t *tokens, const uint8_t *embed_w, const uint16_t *embed_s, 
 cudaError_t launch_embed(const int32_t *tokens, int cols, const uint8_t *embed_w,
                          const uint16_t *embed_s, float embed_scale, const uint8_t *const *ple_slices,
                          int ple_rps, const uint16_t *ple_s, int H, int ple_cols, int ple_group,
-                         float *residual, float *ple_id, cudaStream_t st, bool pdl) {
+                         float *residual, float *ple_id, cudaStream_t st, bool pdl, int embed_bits) {
   int words = H / 8 + ple_cols / 8;
   dim3 grid((words + 255) / 256, cols);
   return launch_k(k_embed, grid, dim3(256), 0, st, pdl, tokens, embed_w, embed_s, embed_scale,
-                  ple_slices, ple_rps, ple_s, H, ple_cols, ple_group, residual, ple_id);
+                  ple_slices, ple_rps, ple_s, H, ple_cols, ple_group, residual, ple_id, embed_bits);
 }
 
 // Operator form: one table (or one slice of it), arbitrary group size.

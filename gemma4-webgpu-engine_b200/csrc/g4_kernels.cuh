@@ -33,6 +33,24 @@ struct DeviceOnce {
   }
 };
 
+// A kernel launch, chained to the previous kernel of the stream by programmatic dependent launch
+// when `pdl` is set (the kernel then calls griddepcontrol.wait before reading its inputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 // Activation prologue a quantized linear applies before snapping its input to int8 codes.
 enum Prologue : int {
   PRO_X = 0,        // x = src
@@ -51,11 +69,11 @@ enum Epilogue : int {
   EPI_HEAD = 2,        // lm_head: softcap, logits, per-CTA argmax partials (set through `head`)
 };
 
-// Byte offset of activation element k inside a column's code vector. int8 weights read codes in
-// order; int4 weights read each 8-element group as [x0 x2 x4 x6 | x1 x3 x5 x7] (even and odd
-// nibbles of a packed word).
+// Byte offset of activation element k inside a column's code vector. int8 and 2-bit weights read
+// codes in order; int4 weights read each 8-element group as [x0 x2 x4 x6 | x1 x3 x5 x7] (even and
+// odd nibbles of a packed word).
 __host__ __device__ __forceinline__ int code_pos(int k, int bits) {
-  if (bits == 8) return k;
+  if (bits != 4) return k;
   return (k & ~7) + 2 * ((k >> 2) & 1) + 4 * (k & 1) + ((k >> 1) & 1);
 }
 
@@ -116,6 +134,18 @@ int gemm_trace_take(unsigned long long *out, int max_records);
 // Calibrated launches need gemv_stream_partition first.
 cudaError_t launch_gemv(const GemvArgs &a, int bits, cudaStream_t st, bool pdl);
 
+// The 2-bit family on the interleaved 16-row tile layout: tile t (rows 16t .. 16t + 15) is K u32
+// words, word k holding row 16t + i at bits 2i (src/kernels/qlayout.ts:160-234). Weight bytes of
+// a 2-bit linear are ceil(N / 16) * K * 4. launch_gemv2 needs gemv2_partition first; a segment
+// with in_scale 0.0 runs the f32 path.
+cudaError_t launch_repack_tile16(const void *row_words, void *tile_words, int N, int K, cudaStream_t st);
+cudaError_t launch_tile16_to_rows(const void *tile_words, void *row_words, int N, int K, cudaStream_t st);
+int gemv2_partition(GemvArgs &a, int sms);
+cudaError_t launch_gemv2(const GemvArgs &a, cudaStream_t st, bool pdl);
+__host__ __device__ __forceinline__ size_t tile16_bytes(int N, int K) {
+  return (size_t)((N + 15) / 16) * (size_t)K * 4;
+}
+
 // Per-column step addressing shared by the embed, attention and head kernels.
 struct ColRefs {
   const int32_t *seq;   // sequence slot per column (nullable: 0)
@@ -126,7 +156,8 @@ struct ColRefs {
 cudaError_t launch_embed(const int32_t *tokens, int cols, const uint8_t *embed_w,
                          const uint16_t *embed_s, float embed_scale, const uint8_t *const *ple_slices,
                          int ple_rows_per_slice, const uint16_t *ple_s, int H, int ple_cols,
-                         int ple_group, float *residual, float *ple_id, cudaStream_t st, bool pdl);
+                         int ple_group, float *residual, float *ple_id, cudaStream_t st, bool pdl,
+                         int embed_bits = 4);
 
 cudaError_t launch_embed_op(const uint8_t *codes, const uint16_t *scales, const int32_t *ids,
                             float *dst, int slots, int cols, int group, float out_scale,
@@ -202,6 +233,8 @@ struct GemmMaps {
   CUtensorMap w[3];   // weights of each segment
   CUtensorMap x[3];   // activation codes each segment reads
 };
+int make_tmap_u32(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
+                  uint64_t row_stride, uint32_t box_inner, uint32_t box_outer);
 int make_tmap_u8(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
                  uint64_t row_stride, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 cudaError_t launch_qgemm(const CUtensorMap &tmW, const CUtensorMap &tmX, const GemmArgs &a, int bits,

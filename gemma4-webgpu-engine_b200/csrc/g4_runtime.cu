@@ -22,7 +22,6 @@
 #include "../../include/g4.h"
 #include "g4_device.cuh"
 #include "g4_kernels.cuh"
-#include "g4_persist.cuh"
 #include "g4_gemv.cuh"
 
 using namespace g4;
@@ -42,10 +41,18 @@ struct Linear {
 };
 
 // The tensor map the tensor-core linear loads weights through: int4 packed rows (box 64 bytes x
-// 128 rows, unpacked on chip) or int8 rows (box 128 x 128, 128-byte swizzle). Needs K % 128 == 0.
+// 128 rows, unpacked on chip), 2-bit tiles, or int8 rows (box 128 x 128, 128-byte swizzle).
+// Needs K % 128 == 0.
 static void linear_tmap(Linear &l) {
   l.has_tm = false;
-  if (!l.w || l.K % 128 != 0 || (l.bits != 4 && l.bits != 8)) return;
+  if (!l.w || l.K % 128 != 0) return;
+  if (l.bits == 2) {
+    // 2-bit tiles: u32 words [tiles][K], box 128 words x 8 tiles (128 rows), unpacked on chip.
+    l.has_tm = make_tmap_u32(&l.tmw, l.w, (uint64_t)l.K, (uint64_t)((l.N + 15) / 16),
+                             (uint64_t)l.K * 4, 128, 8) == 0;
+    return;
+  }
+  if (l.bits != 4 && l.bits != 8) return;
   const uint64_t rb = (uint64_t)l.K * l.bits / 8;
   l.has_tm = make_tmap_u8(&l.tmw, l.w, rb, (uint64_t)l.N, rb, l.bits == 4 ? 64 : 128, 128, l.bits == 8) == 0;
 }
@@ -61,8 +68,10 @@ struct Layer {
 
 struct TensorRef {
   void *ptr;
-  uint64_t bytes;
-  bool sliced;  // the PLE code table split into vocab-row slices
+  uint64_t bytes;       // the checkpoint layout's bytes (what upload and download move)
+  bool sliced;          // the PLE code table split into vocab-row slices
+  int t16_rows = 0;     // > 0: a 2-bit tensor held in the interleaved tile layout (rows x t16_k)
+  int t16_k = 0;
 };
 
 struct GraphKey {
@@ -124,15 +133,6 @@ struct g4_ctx {
   float *cur_pv = nullptr;
   int32_t *cur_pi = nullptr;
   int cur_parts = 0;
-  // Persistent B=1 decode: the phase list per advance flag (built from record_step in plan
-  // mode), its grid, and the grid-barrier words.
-  std::vector<PPhase> *plan = nullptr;    // plan mode: record_step appends phases here
-  bool plan_ok = true;
-  PPhase *d_plan[2] = {nullptr, nullptr};
-  int plan_n[2] = {0, 0};
-  int plan_state[2] = {0, 0};              // 0 not built, 1 built, -1 not eligible
-  int persist_grid = 0;
-  unsigned *pbar = nullptr;
   uint8_t *codes_mlp = nullptr;     // down_proj input codes [maxc][ffn_max]
   uint8_t *codes_ple = nullptr;     // per_layer_projection input codes [maxc][PD]
   int ffn_max = 0;
@@ -153,6 +153,9 @@ struct g4_ctx {
   int32_t *h_tok = nullptr;    // pinned token outputs
   uint64_t other_bytes = 0;
   std::map<GraphKey, cudaGraphExec_t> graphs;
+  // 2-bit tensors being uploaded in pieces: the checkpoint bytes so far, repacked when complete.
+  std::map<std::string, std::vector<uint8_t>> t16_staging;
+  std::map<std::string, uint64_t> t16_received;
   std::map<GraphKey, int> graph_launches;   // kernels in each graph
   std::map<GraphKey, std::vector<std::string>> graph_roles;
   int sms = 148;
@@ -242,11 +245,24 @@ extern "C" int g4_arch_default(g4_arch *a) {
   a->attn_bits = 4;
   a->mlp_bits = 4;
   a->ple_bits = 8;
+  a->consumer_mlp_bits = 4;
+  a->head_bits = 4;
+  a->head_calibrated = 1;
   a->rms_eps = 1e-6f;
   a->final_softcap = 30.0f;
   a->rope_theta_sliding = 1e4f;
   a->rope_theta_global = 1e6f;
   a->partial_rotary_factor = 0.25f;
+  return G4_OK;
+}
+
+extern "C" int g4_arch_checkpoint(g4_arch *a) {
+  int rc = g4_arch_default(a);
+  if (rc) return rc;
+  a->consumer_intermediate = 12288;
+  a->consumer_mlp_bits = 2;
+  a->head_bits = 2;
+  a->head_calibrated = 0;
   return G4_OK;
 }
 
@@ -260,7 +276,6 @@ extern "C" int g4_config_default(g4_config *cfg) {
   cfg->use_graphs = 1;
   cfg->ple_slice_bytes = 0;
   cfg->gemm_min_columns = 16;
-  cfg->persistent_decode = 0;
   cfg->gemm_split_k = 0;
   return G4_OK;
 }
@@ -305,16 +320,25 @@ static std::string layer_name(int L, const char *suffix) {
   return std::string(LMP) + "layers." + std::to_string(L) + "." + suffix;
 }
 
+// Device bytes of a linear's codes: row-major packed, or the interleaved tiles at 2 bits.
+static size_t linear_bytes(size_t N, size_t K, int bits) {
+  return bits == 2 ? tile16_bytes((int)N, (int)K) : N * K * bits / 8;
+}
+
 static int make_linear(g4_ctx *ctx, Linear &lin, const std::string &module, int N, int K, int bits) {
   lin.N = N;
   lin.K = K;
   lin.bits = bits;
   lin.module = module;
-  size_t wb = (size_t)N * K * bits / 8;
-  lin.w = (uint8_t *)arena_take(ctx, wb);
+  lin.w = (uint8_t *)arena_take(ctx, linear_bytes(N, K, bits));
   lin.s = (uint16_t *)arena_take(ctx, (size_t)N * 2);
   if (!lin.w || !lin.s) return fail(ctx, G4_ERR_OOM, "weight arena exhausted at %s", module.c_str());
-  ctx->tensors[module + ".weight"] = {lin.w, wb, false};
+  TensorRef tr{lin.w, (uint64_t)N * K * bits / 8, false};
+  if (bits == 2) {
+    tr.t16_rows = N;
+    tr.t16_k = K;
+  }
+  ctx->tensors[module + ".weight"] = tr;
   ctx->tensors[module + ".weight_scale"] = {lin.s, (uint64_t)N * 2, false};
   return G4_OK;
 }
@@ -327,26 +351,27 @@ static float *make_f32(g4_ctx *ctx, const std::string &name, size_t n) {
 
 static size_t weight_arena_bytes(const g4_arch &a) {
   size_t H = a.hidden_size, total = 0;
-  auto lin = [&](size_t N, size_t K, int bits) { total += ((N * K * bits / 8 + 255) & ~255ull) + ((N * 2 + 255) & ~255ull); };
+  auto lin = [&](size_t N, size_t K, int bits) { total += ((linear_bytes(N, K, bits) + 255) & ~255ull) + ((N * 2 + 255) & ~255ull); };
   for (int L = 0; L < a.layer_count; L++) {
     size_t hd = is_global(a, L) ? a.global_head_dim : a.sliding_head_dim;
     bool prod = L < a.kv_producer_layers;
     size_t ffn = prod ? a.producer_intermediate : a.consumer_intermediate;
+    const int mb = prod ? a.mlp_bits : a.consumer_mlp_bits;
     lin(a.query_heads * hd, H, 4);
     if (prod) {
       lin(hd, H, 4);
       lin(hd, H, 4);
     }
     lin(H, a.query_heads * hd, 4);
-    lin(ffn, H, 4);
-    lin(ffn, H, 4);
-    lin(H, ffn, 4);
+    lin(ffn, H, mb);
+    lin(ffn, H, mb);
+    lin(H, ffn, mb);
     lin(a.ple_dim, H, 8);
     lin(H, a.ple_dim, 8);
     total += 5 * ((H * 4 + 255) & ~255ull) + 2 * ((hd * 4 + 255) & ~255ull);
   }
   size_t V = a.vocab_size, ple_cols = (size_t)a.layer_count * a.ple_dim;
-  total += V * H / 2 + 256 + V * 2 + 256;                 // embed (tied lm_head)
+  total += linear_bytes(V, H, a.head_bits) + 256 + V * 2 + 256;   // embed (tied lm_head)
   total += V * a.layer_count * 2 + 256;                    // PLE scales
   total += ple_cols * H * 2 + 256;                         // PLMP bf16
   total += a.ple_dim * 4 + 256 + H * 4 + 256;              // norms
@@ -366,6 +391,7 @@ static int alloc_weights(g4_ctx *ctx) {
     ly.producer = L < a.kv_producer_layers;
     ly.hd = ly.global ? a.global_head_dim : a.sliding_head_dim;
     int ffn = ly.producer ? a.producer_intermediate : a.consumer_intermediate;
+    const int mb = ly.producer ? a.mlp_bits : a.consumer_mlp_bits;
     int qrows = a.query_heads * ly.hd;
     int rc;
     if ((rc = make_linear(ctx, ly.q, layer_name(L, "self_attn.q_proj"), qrows, H, 4))) return rc;
@@ -374,9 +400,9 @@ static int alloc_weights(g4_ctx *ctx) {
       if ((rc = make_linear(ctx, ly.v, layer_name(L, "self_attn.v_proj"), ly.hd, H, 4))) return rc;
     }
     if ((rc = make_linear(ctx, ly.o, layer_name(L, "self_attn.o_proj"), H, qrows, 4))) return rc;
-    if ((rc = make_linear(ctx, ly.gate, layer_name(L, "mlp.gate_proj"), ffn, H, 4))) return rc;
-    if ((rc = make_linear(ctx, ly.up, layer_name(L, "mlp.up_proj"), ffn, H, 4))) return rc;
-    if ((rc = make_linear(ctx, ly.down, layer_name(L, "mlp.down_proj"), H, ffn, 4))) return rc;
+    if ((rc = make_linear(ctx, ly.gate, layer_name(L, "mlp.gate_proj"), ffn, H, mb))) return rc;
+    if ((rc = make_linear(ctx, ly.up, layer_name(L, "mlp.up_proj"), ffn, H, mb))) return rc;
+    if ((rc = make_linear(ctx, ly.down, layer_name(L, "mlp.down_proj"), H, ffn, mb))) return rc;
     if ((rc = make_linear(ctx, ly.pleg, layer_name(L, "per_layer_input_gate"), a.ple_dim, H, 8))) return rc;
     if ((rc = make_linear(ctx, ly.plep, layer_name(L, "per_layer_projection"), H, a.ple_dim, 8))) return rc;
     ly.ln_in = make_f32(ctx, layer_name(L, "input_layernorm.weight"), H);
@@ -400,7 +426,8 @@ static int alloc_weights(g4_ctx *ctx) {
     }
   }
   size_t V = ctx->V;
-  ctx->embed_w = (uint8_t *)arena_take(ctx, V * H / 2);
+  const int hb = a.head_bits;
+  ctx->embed_w = (uint8_t *)arena_take(ctx, linear_bytes(V, H, hb));
   ctx->embed_s = (uint16_t *)arena_take(ctx, V * 2);
   ctx->ple_s = (uint16_t *)arena_take(ctx, V * ctx->NL * 2);
   ctx->plmp_w = (uint16_t *)arena_take(ctx, (size_t)ctx->ple_cols * H * 2);
@@ -408,7 +435,14 @@ static int alloc_weights(g4_ctx *ctx) {
   ctx->final_norm = make_f32(ctx, std::string(LMP) + "norm.weight", H);
   if (!ctx->embed_w || !ctx->embed_s || !ctx->ple_s || !ctx->plmp_w || !ctx->plmp_norm || !ctx->final_norm)
     return fail(ctx, G4_ERR_OOM, "weight arena exhausted at the embedding tables");
-  ctx->tensors[std::string(LMP) + "embed_tokens.embedding_quantized"] = {ctx->embed_w, V * H / 2, false};
+  {
+    TensorRef tr{ctx->embed_w, V * H * hb / 8, false};
+    if (hb == 2) {
+      tr.t16_rows = (int)V;
+      tr.t16_k = H;
+    }
+    ctx->tensors[std::string(LMP) + "embed_tokens.embedding_quantized"] = tr;
+  }
   ctx->tensors[std::string(LMP) + "embed_tokens.embedding_scale"] = {ctx->embed_s, V * 2, false};
   ctx->tensors[std::string(LMP) + "embed_tokens_per_layer.embedding_scale"] = {ctx->ple_s, V * ctx->NL * 2, false};
   ctx->tensors[std::string(LMP) + "per_layer_model_projection.weight"] = {ctx->plmp_w, (uint64_t)ctx->ple_cols * H * 2, false};
@@ -417,7 +451,7 @@ static int alloc_weights(g4_ctx *ctx) {
   ctx->lm.s = ctx->embed_s;
   ctx->lm.N = ctx->V;
   ctx->lm.K = H;
-  ctx->lm.bits = 4;
+  ctx->lm.bits = hb;
   ctx->lm.module = "lm_head";
   for (Layer &ly : ctx->layers)
     for (Linear *l : {&ly.q, &ly.k, &ly.v, &ly.o, &ly.gate, &ly.up, &ly.down, &ly.pleg, &ly.plep})
@@ -525,9 +559,6 @@ static int alloc_runtime(g4_ctx *ctx) {
   CK(ctx_malloc((void **)&ctx->gpi, (size_t)maxc * ctx->gparts * 4));
   ctx->gemm_min_cols = ctx->cfg.gemm_min_columns > 0 ? ctx->cfg.gemm_min_columns : 16;
   ctx->gemm_split_k = ctx->cfg.gemm_split_k;
-  CK(ctx_malloc((void **)&ctx->pbar, 2 * sizeof(unsigned)));
-  CK(cudaMemset(ctx->pbar, 0, 2 * sizeof(unsigned)));
-  ctx->persist_grid = ctx->cfg.persistent_decode ? persist_max_grid(ctx->dev) : 0;
   ctx->ffn_max = (ffn + 15) & ~15;
   CK(ctx_malloc((void **)&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
   CK(ctx_malloc((void **)&ctx->codes_ple, (size_t)maxc * ctx->PD));
@@ -565,8 +596,13 @@ extern "C" int g4_ctx_create(int cuda_device, const g4_config *cfg_in, g4_ctx **
   const g4_arch &a = cfg.arch;
   if (a.kv_heads != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "only one KV head is supported");
   if (a.query_heads != 8) return fail(nullptr, G4_ERR_UNSUPPORTED, "the attention kernels are built for 8 query heads");
-  if (a.attn_bits != 4 || a.mlp_bits != 4 || a.ple_bits != 8)
-    return fail(nullptr, G4_ERR_UNSUPPORTED, "weight widths attn 4 / mlp 4 / ple 8 only (2-bit families are not built)");
+  if (a.attn_bits != 4 || a.mlp_bits != 4 || a.ple_bits != 8 ||
+      (a.consumer_mlp_bits != 4 && a.consumer_mlp_bits != 2) || (a.head_bits != 4 && a.head_bits != 2))
+    return fail(nullptr, G4_ERR_UNSUPPORTED, "weight widths: attn 4, producer MLP 4, PLE 8, consumer MLP 4 or 2, head 4 or 2");
+  if (!a.head_calibrated && a.head_bits != 2)
+    return fail(nullptr, G4_ERR_UNSUPPORTED, "an uncalibrated (f32-path) head is built for the 2-bit family only");
+  if ((a.consumer_mlp_bits == 2 || a.head_bits == 2) && a.hidden_size % 128 != 0)
+    return fail(nullptr, G4_ERR_UNSUPPORTED, "the 2-bit family needs the hidden size a multiple of 128");
   if (a.hidden_size % 256 != 0 || a.hidden_size > 2048)
     return fail(nullptr, G4_ERR_UNSUPPORTED, "hidden size must be a multiple of 256 up to 2048");
   if ((a.sliding_head_dim != 256 && a.sliding_head_dim != 512) || (a.global_head_dim != 256 && a.global_head_dim != 512))
@@ -610,7 +646,6 @@ extern "C" int g4_trace_reset(void) {
   unsigned long long dummy[2];
   trace_take(dummy, 0);
   gemm_trace_take(dummy, 0);
-  persist_trace_take(dummy, 0);
   return 0;
 }
 #endif
@@ -622,8 +657,6 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
     const int n = trace_take(rec.data(), 1 << 15);
     if (FILE *f = fopen(path, "w")) {
       for (int i = 0; i < n; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
-      const int m = persist_trace_take(rec.data(), 1 << 15);
-      for (int i = 0; i < m; i++) fprintf(f, "%llu %llu\n", 100000000ull + rec[2 * i], rec[2 * i + 1]);
       const int gm = gemm_trace_take(rec.data(), 1 << 15);
       for (int i = 0; i < gm; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
       fclose(f);
@@ -651,8 +684,6 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   cudaFree(ctx->gpi);
   cudaFree(ctx->gacc);
   cudaFree(ctx->gcnt);
-  cudaFree(ctx->pbar);
-  for (int i = 0; i < 2; i++) cudaFree(ctx->d_plan[i]);
   cudaFree(ctx->codes_ple);
   cudaFree(ctx->d_step);
   cudaFree(ctx->d_tok_out);
@@ -741,10 +772,30 @@ static float bf16_round(float f) {
   return r;
 }
 
+// The checkpoint layout's words of a 2-bit tensor, generated into a staging buffer and repacked
+// into the tile layout the kernels read (src/kernels/repack.ts:17-209).
+static int gen_tile16(g4_ctx *ctx, void *dst, int N, int K, uint64_t key) {
+  const size_t wb = (size_t)N * K / 4;
+  void *tmp = nullptr;
+  CK(ctx_malloc(&tmp, wb));
+  cudaError_t e = launch_gen_words((uint32_t *)tmp, wb / 4, key, 0, ctx->st);
+  if (e == cudaSuccess) e = launch_repack_tile16(tmp, dst, N, K, ctx->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->st);
+  cudaFree(tmp);
+  CK(e);
+  return G4_OK;
+}
+
 static int gen_linear(g4_ctx *ctx, Linear &lin, uint64_t seed, int L, int kw, int ks, int site) {
   size_t wb = (size_t)lin.N * lin.K * lin.bits / 8;
-  CK(launch_gen_words((uint32_t *)lin.w, wb / 4, stream_key(seed, layer_stream(L, kw)), 0, ctx->st));
-  double div = lin.bits == 8 ? 16.0 : 1.0;
+  if (lin.bits == 2) {
+    int rc = gen_tile16(ctx, lin.w, lin.N, lin.K, stream_key(seed, layer_stream(L, kw)));
+    if (rc) return rc;
+  } else {
+    CK(launch_gen_words((uint32_t *)lin.w, wb / 4, stream_key(seed, layer_stream(L, kw)), 0, ctx->st));
+  }
+  // Row scales keep activations O(1): int8 codes are 16x larger than int4, 2-bit ones 4x smaller.
+  double div = lin.bits == 8 ? 16.0 : (lin.bits == 2 ? 0.25 : 1.0);
   CK(launch_gen_f16(lin.s, (size_t)lin.N, stream_key(seed, layer_stream(L, ks)), 1e-3 / div, 1e-2 / div, ctx->st));
   lin.in_scale = synth_srq(seed, L, site, 0);
   lin.out_scale = synth_srq(seed, L, site, 1);
@@ -785,8 +836,14 @@ extern "C" int g4_init_random(g4_ctx *ctx, uint64_t seed) {
     ly.layer_scalar = bf16_round((float)(0.03 + (0.9 - 0.03) * u));
   }
   const size_t V = ctx->V;
-  CK(launch_gen_words((uint32_t *)ctx->embed_w, V * H / 8, stream_key(seed, layer_stream(-1, TK_EMBED_W)), 0, ctx->st));
-  CK(launch_gen_f16(ctx->embed_s, V, stream_key(seed, layer_stream(-1, TK_EMBED_S)), 1e-3, 1e-2, ctx->st));
+  const uint64_t ekey = stream_key(seed, layer_stream(-1, TK_EMBED_W));
+  const double ediv = ctx->lm.bits == 2 ? 0.25 : 1.0;
+  if (ctx->lm.bits == 2) {
+    if ((rc = gen_tile16(ctx, ctx->embed_w, (int)V, H, ekey))) return rc;
+  } else {
+    CK(launch_gen_words((uint32_t *)ctx->embed_w, V * H / 8, ekey, 0, ctx->st));
+  }
+  CK(launch_gen_f16(ctx->embed_s, V, stream_key(seed, layer_stream(-1, TK_EMBED_S)), 1e-3 / ediv, 1e-2 / ediv, ctx->st));
   CK(launch_gen_f16(ctx->ple_s, V * ctx->NL, stream_key(seed, layer_stream(-1, TK_PLE_S)), 1e-3, 1e-2, ctx->st));
   CK(launch_gen_plmp(ctx->plmp_w, (size_t)ctx->ple_cols * H, stream_key(seed, layer_stream(-1, TK_PLMP_W)), 0.04419417382415922, ctx->st));
   if ((rc = gen_gain(ctx, ctx->plmp_norm, ctx->PD, seed, -1, TK_PLMP_NORM))) return rc;
@@ -805,13 +862,13 @@ extern "C" int g4_init_random(g4_ctx *ctx, uint64_t seed) {
       CK(launch_gen_words(dst, nw, key, row0 * words_per_row, ctx->st));
     }
   }
-  ctx->lm.in_scale = synth_srq(seed, -1, S_LM, 0);
-  ctx->lm.out_scale = synth_srq(seed, -1, S_LM, 1);
+  // An uncalibrated head (the checkpoint's, src/quant.ts:574-585) keeps both scales 0.0.
+  ctx->lm.in_scale = ctx->cfg.arch.head_calibrated ? synth_srq(seed, -1, S_LM, 0) : 0.0f;
+  ctx->lm.out_scale = ctx->cfg.arch.head_calibrated ? synth_srq(seed, -1, S_LM, 1) : 0.0f;
   CK(cudaStreamSynchronize(ctx->st));
   ctx->weights_ready = true;
   for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
   ctx->graphs.clear();
-  ctx->plan_state[0] = ctx->plan_state[1] = 0;
   return G4_OK;
 }
 
@@ -831,7 +888,26 @@ extern "C" int g4_upload_weight(g4_ctx *ctx, const char *name, const void *bytes
   if (total != r.bytes) return fail(ctx, G4_ERR_INVALID, "%s holds %llu bytes, upload says %llu", name, (unsigned long long)r.bytes, (unsigned long long)total);
   if (offset + n > total) return fail(ctx, G4_ERR_INVALID, "%s: bytes [%llu, %llu) past the end", name, (unsigned long long)offset, (unsigned long long)(offset + n));
   CK(cudaSetDevice(ctx->dev));
-  if (!r.sliced) {
+  if (r.t16_rows > 0) {
+    // The checkpoint layout arrives in pieces; once the last byte is in, it is repacked into the
+    // tile layout (src/kernels/repack.ts:17-209).
+    std::vector<uint8_t> &st = ctx->t16_staging[name];
+    st.resize(total);
+    memcpy(st.data() + offset, bytes, n);
+    uint64_t &got = ctx->t16_received[name];
+    got += n;
+    if (got >= total) {
+      void *tmp = nullptr;
+      CK(ctx_malloc(&tmp, total));
+      cudaError_t e = cudaMemcpy(tmp, st.data(), total, cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = launch_repack_tile16(tmp, r.ptr, r.t16_rows, r.t16_k, ctx->st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->st);
+      cudaFree(tmp);
+      ctx->t16_staging.erase(name);
+      ctx->t16_received.erase(name);
+      CK(e);
+    }
+  } else if (!r.sliced) {
     CK(cudaMemcpy((uint8_t *)r.ptr + offset, bytes, n, cudaMemcpyHostToDevice));
   } else {
     const uint64_t slice_bytes = (uint64_t)ctx->ple_rps * (ctx->ple_cols / 2);
@@ -859,7 +935,15 @@ extern "C" int g4_download_weight(g4_ctx *ctx, const char *name, void *bytes, ui
   }
   CK(cudaSetDevice(ctx->dev));
   CK(cudaStreamSynchronize(ctx->st));
-  if (!r.sliced) {
+  if (r.t16_rows > 0) {
+    void *tmp = nullptr;
+    CK(ctx_malloc(&tmp, r.bytes));
+    cudaError_t e = launch_tile16_to_rows(r.ptr, tmp, r.t16_rows, r.t16_k, ctx->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->st);
+    if (e == cudaSuccess) e = cudaMemcpy(bytes, tmp, r.bytes, cudaMemcpyDeviceToHost);
+    cudaFree(tmp);
+    CK(e);
+  } else if (!r.sliced) {
     CK(cudaMemcpy(bytes, r.ptr, r.bytes, cudaMemcpyDeviceToHost));
   } else {
     const uint64_t row_bytes = ctx->ple_cols / 2;
@@ -913,7 +997,6 @@ extern "C" int g4_set_scalar(g4_ctx *ctx, const char *name, float value) {
   *slot = value;
   for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
   ctx->graphs.clear();
-  ctx->plan_state[0] = ctx->plan_state[1] = 0;
   return G4_OK;
 }
 
@@ -1112,7 +1195,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     // 2048-token prefill than two per-tile CTAs per SM (tail imbalance, twice the DRAM reads), so
     // the executor keeps the per-tile kernel; g4_op_qgemm uses the loop for wide calls.
     const int tiles128 = ((l.N + 127) / 128) * ((cols + 127) / 128);
-    if (ctx->gemm_persist && !head && g.splits <= 1 && tiles128 > ctx->sms) {
+    if (ctx->gemm_persist && !head && g.splits <= 1 && tiles128 > ctx->sms && l.bits != 2) {
       const CUtensorMap *tx128 = codes_tmap(ctx, which[i - 1], K, 128);
       if (!tx128) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
       CK(launch_qgemm_persist(l.tmw, *tx128, g, l.bits, std::min(tiles128, ctx->sms), ctx->st, true));
@@ -1127,79 +1210,8 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   return G4_OK;
 }
 
-// Plan mode: the launch becomes one phase of the persistent decode kernel (one column), its rows
-// partitioned over the persistent grid; shapes the kernel does not cover mark the plan ineligible.
-static int plan_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs a, bool head) {
-  const Linear *l0 = segs.begin()->lin;
-  const int bits = l0->bits, K = l0->K, row_bytes = K * bits / 8;
-  const int rs = gs_row_split(row_bytes);
-  bool ok = cols == 1 && row_bytes <= persist_slot_bytes() && row_bytes % rs == 0 &&
-            row_bytes / rs <= 1024 && (row_bytes / rs) % 16 == 0 && K <= 6144;
-  a.K = K;
-  a.cols = 1;
-  a.nseg = 0;
-  for (auto &s : segs) {
-    GemvSeg &g = a.seg[a.nseg++];
-    g.w = s.lin->w;
-    g.s = s.lin->s;
-    g.y = s.y;
-    g.acc_out = nullptr;
-    g.N = s.lin->N;
-    g.in_scale = s.lin->in_scale;
-    g.out_scale = s.lin->out_scale;
-    ok = ok && s.lin->bits == bits && s.lin->K == K && s.lin->in_scale != 0.0f;
-  }
-  // The segments' CTA counts round up; shrink the target until they fit the persistent grid.
-  const int P = ctx->persist_grid;
-  for (int target = P; target > 0; target--) {
-    gemv_stream_partition(a, target);
-    if (a.n_blocks_total <= P) break;
-  }
-  int max_rows = 0;
-  for (int i = 0; i < a.nseg; i++) {
-    const int nb = a.pair ? a.n_blocks_total
-                          : (i + 1 < a.nseg ? a.seg[i + 1].block_begin : a.n_blocks_total) - a.seg[i].block_begin;
-    max_rows = std::max(max_rows, (a.seg[i].N + nb - 1) / nb);
-  }
-  PPhase ph;
-  memset(&ph, 0, sizeof(ph));
-  ph.kind = PK_GEMV;
-  ph.bits = bits;
-  ph.rs = rs;
-  const int pro = a.pro, epi = head ? EPI_HEAD : a.epi;
-  if (bits == 4 && pro == PRO_NORM && epi == EPI_Y) ph.variant = PV_Q0;
-  else if (bits == 4 && pro == PRO_JOIN && epi == EPI_Y) ph.variant = PV_QKV;
-  else if (bits == 4 && pro == PRO_X && epi == EPI_Y) ph.variant = PV_O1;
-  else if (bits == 4 && pro == PRO_JOIN && epi == EPI_GELU_CODES && a.pair) ph.variant = PV_GATEUP;
-  else if (bits == 4 && pro == PRO_CODES && epi == EPI_Y) ph.variant = PV_DOWN;
-  else if (bits == 8 && pro == PRO_NORMRES && epi == EPI_GELU_CODES && !a.pair) ph.variant = PV_PLEG;
-  else if (bits == 8 && pro == PRO_CODES && epi == EPI_Y) ph.variant = PV_PLEP;
-  else if (bits == 4 && pro == PRO_JOIN && epi == EPI_HEAD) ph.variant = PV_HEAD;
-  else ok = false;
-  if (epi == EPI_GELU_CODES) ok = ok && max_rows <= 64;
-  ok = ok && max_rows <= (a.pair ? persist_max_rows() / 2 : persist_max_rows());
-  for (int i = 0; i < 4; i++) a.prefetch_bytes[i] = 0;
-  if (head) {
-    a.head = 1;
-    a.logits = ctx->logits;
-    a.ld_logits = ctx->V;
-    a.part_val = ctx->head_pv;
-    a.part_idx = ctx->head_pi;
-    ok = ok && a.n_blocks_total <= ctx->head_cap * ctx->head_cols;
-    ctx->cur_pv = ctx->head_pv;
-    ctx->cur_pi = ctx->head_pi;
-    ctx->cur_parts = a.n_blocks_total;
-  }
-  ph.g = a;
-  if (!ok) ctx->plan_ok = false;
-  ctx->plan->push_back(ph);
-  note_launch(ctx, bits_name("qgemv", segs.begin()->lin->bits, head), seg_roles(segs));
-  return G4_OK;
-}
-
 static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, GemvArgs proto,
                       bool head = false, std::initializer_list<WRef> prefetch = {}) {
-  if (ctx->plan) return plan_linear(ctx, segs, cols, proto, head);
   if (gemm_eligible(ctx, segs, cols, proto)) return run_linear_gemm(ctx, segs, cols, proto, head);
   const Linear *l0 = segs.begin()->lin;
   for (int c0 = 0; c0 < cols; c0 += 8) {
@@ -1217,7 +1229,8 @@ static int run_linear(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, Ge
       g.in_scale = s.lin->in_scale;
       g.out_scale = s.lin->out_scale;
     }
-    const int blocks = gemv_stream_partition(a, ctx->gemv_target);
+    const int blocks = l0->bits == 2 ? gemv2_partition(a, ctx->gemv_target)
+                                     : gemv_stream_partition(a, ctx->gemv_target);
     int np = 0;
     if (c0 == 0)
       for (auto &w : prefetch)
@@ -1278,35 +1291,15 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
   ctx->launches = 0;
   ctx->roles.clear();
   // ---- embed phase (planEmbed, src/plan.ts:727-736)
-  if (ctx->plan) {
-    PPhase e;
-    memset(&e, 0, sizeof(e));
-    e.kind = PK_EMBED;
-    e.em = {d_tok, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
-            (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H, ctx->ple_cols, PD,
-            ctx->res[0], ctx->ple_id};
-    ctx->plan->push_back(e);
-    PPhase d;
-    memset(&d, 0, sizeof(d));
-    d.kind = PK_DENSE;
-    d.de = {ctx->plmp_w, ctx->res[0], ctx->ple_proj, ctx->ple_cols, H, (float)std::pow((double)H, -0.5)};
-    ctx->plan->push_back(d);
-    PPhase c;
-    memset(&c, 0, sizeof(c));
-    c.kind = PK_COMBINE;
-    c.co = {ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, ctx->NL, PD, eps, (float)0.7071067811865476};
-    ctx->plan->push_back(c);
-  } else {
-    CK(launch_embed(d_tok, cols, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
-                    (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H,
-                    ctx->ple_cols, PD, ctx->res[0], ctx->ple_id, ctx->st, true));
-    // Per-layer inputs of the layers this step runs (rows are layer-major): a prefill chunk's
-    // producer-only columns need the first n_layers groups only.
-    CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, n_layers * PD, H, cols,
-                         (float)std::pow((double)H, -0.5), ctx->st, true));
-    CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, n_layers, PD,
-                          ctx->ple_cols, eps, (float)0.7071067811865476, ctx->st, true));
-  }
+  CK(launch_embed(d_tok, cols, ctx->embed_w, ctx->embed_s, (float)std::sqrt((double)H),
+                  (const uint8_t *const *)ctx->d_ple_slices, ctx->ple_rps, ctx->ple_s, H,
+                  ctx->ple_cols, PD, ctx->res[0], ctx->ple_id, ctx->st, true, ctx->lm.bits));
+  // Per-layer inputs of the layers this step runs (rows are layer-major): a prefill chunk's
+  // producer-only columns need the first n_layers groups only.
+  CK(launch_dense_bf16(ctx->plmp_w, ctx->res[0], H, ctx->ple_proj, ctx->ple_cols, n_layers * PD, H, cols,
+                       (float)std::pow((double)H, -0.5), ctx->st, true));
+  CK(launch_ple_combine(ctx->ple_proj, ctx->ple_id, ctx->plmp_norm, ctx->ple_in, cols, n_layers, PD,
+                        ctx->ple_cols, eps, (float)0.7071067811865476, ctx->st, true));
   note_launch(ctx, "embed-gather", "embed_tokens,embed_tokens_per_layer");
   note_launch(ctx, "dense-bf16", "per_layer_model_projection");
   note_launch(ctx, "ple-combine", "per_layer_projection_norm");
@@ -1372,16 +1365,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       ad.counter = ctx->att_count;
       ad.out = ctx->attn;
       ad.eps = eps;
-      if (ctx->plan) {
-        PPhase ph;
-        memset(&ph, 0, sizeof(ph));
-        ph.kind = PK_ATTN;
-        ph.at = ad;
-        if (cols != 1 || (hd != 256 && hd != 512)) ctx->plan_ok = false;
-        ctx->plan->push_back(ph);
-      } else {
-        CK(launch_attn_decode(ad, ctx->st, true));
-      }
+      CK(launch_attn_decode(ad, ctx->st, true));
       note_launch(ctx, "attention-decode", layer_role(L, ly.producer));
     }
     // ---- attention prologue: q-norm-rope, kv-norm-rope-store (src/kernels/attnPrologue.ts)
@@ -1562,66 +1546,17 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     p.eps = eps;
     p.softcap = a.final_softcap;
     if ((rc = run_linear(ctx, {{&ctx->lm, nullptr}}, cols, p, true))) return rc;
-    if (ctx->plan) {
-      PPhase m;
-      memset(&m, 0, sizeof(m));
-      m.kind = PK_ARGMAX;
-      m.am = {ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, d_tok, ctx->d_tok_out, ctx->d_val_out, d_pos,
-              advance ? 1 : 0};
-      ctx->plan->push_back(m);
-    } else {
-      CK(launch_argmax_final(ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, cols, d_tok,
-                             ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
-      if (advance) CK(launch_advance(d_pos, cols, ctx->st, true));
-    }
+    CK(launch_argmax_final(ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, cols, d_tok,
+                           ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
+    if (advance) CK(launch_advance(d_pos, cols, ctx->st, true));
     note_launch(ctx, "argmax-final", "argmax");
     if (advance) note_launch(ctx, "advance", "position advance");
   }
   return G4_OK;
 }
 
-// The persistent decode step for one column: the phase list is built once per advance flag (from
-// record_step in plan mode) and launched as one cooperative kernel; 0 when not eligible.
-static int try_persist(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance, bool *done) {
-  *done = false;
-  if (cols != 1 || !head || n_layers != ctx->NL || ctx->persist_grid <= 0) return G4_OK;
-  const int k = advance ? 1 : 0;
-  if (ctx->plan_state[k] == 0) {
-    std::vector<PPhase> plan;
-    ctx->plan = &plan;
-    ctx->plan_ok = true;
-    int rc = record_step(ctx, cols, n_layers, head, advance);
-    ctx->plan = nullptr;
-    if (rc) return rc;
-    ctx->plan_state[k] = -1;
-    if (ctx->plan_ok && !plan.empty()) {
-      for (size_t i = 0; i + 1 < plan.size(); i++) plan[i].sync_after = 1;
-      cudaFree(ctx->d_plan[k]);
-      ctx->d_plan[k] = nullptr;
-      CK(ctx_malloc((void **)&ctx->d_plan[k], plan.size() * sizeof(PPhase)));
-      CK(cudaMemcpyAsync(ctx->d_plan[k], plan.data(), plan.size() * sizeof(PPhase),
-                         cudaMemcpyHostToDevice, ctx->st));
-      CK(cudaStreamSynchronize(ctx->st));
-      ctx->plan_n[k] = (int)plan.size();
-      ctx->plan_state[k] = 1;
-    }
-  }
-  if (ctx->plan_state[k] != 1) return G4_OK;
-  CK(launch_decode_persist(ctx->d_plan[k], ctx->plan_n[k], ctx->pbar, ctx->persist_grid, ctx->st));
-  ctx->launches = 0;
-  ctx->roles.clear();
-  note_launch(ctx, "decode-persistent", "every phase of the step");
-  *done = true;
-  return G4_OK;
-}
-
 static int run_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool advance = false,
                     bool wide = false) {
-  bool done = false;
-  if (!wide) {
-    int prc = try_persist(ctx, cols, n_layers, head, advance, &done);
-    if (prc || done) return prc;
-  }
   if (!ctx->cfg.use_graphs) return record_step(ctx, cols, n_layers, head, advance, wide);
   GraphKey key{cols, n_layers, head ? (wide ? 2 : 1) : 0, advance ? 1 : 0};
   auto it = ctx->graphs.find(key);
@@ -1687,11 +1622,9 @@ static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos,
 static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
   CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)cols * 4, cudaMemcpyDeviceToHost, ctx->st));
   CK(cudaStreamSynchronize(ctx->st));
-  if (device_error_take() > 0 || gemm_error_take() > 0 || persist_error_take() > 0) {
-    // A block that gave up may have left its column's finished-block count (or the persistent
-    // kernel its barrier words) behind.
+  if (device_error_take() > 0 || gemm_error_take() > 0) {
+    // A block that gave up may have left its column's finished-block count behind.
     cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 8 * 4, ctx->st);
-    cudaMemsetAsync(ctx->pbar, 0, 2 * sizeof(unsigned), ctx->st);
     cudaStreamSynchronize(ctx->st);
     return fail(ctx, G4_ERR_TIMEOUT, "a bounded device wait gave up (a bulk copy never completed)");
   }
@@ -1897,12 +1830,19 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
                            float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
                            int32_t *acc_out, void *stream) {
   if (!wq || !scales || !x || !y) return fail(nullptr, G4_ERR_INVALID, "g4_op_qgemv: null pointer");
-  if (bits != 4 && bits != 8) return fail(nullptr, G4_ERR_INVALID, "bits must be 4 or 8");
-  const int span = bits == 4 ? 256 : 128;
+  if (bits != 2 && bits != 4 && bits != 8) return fail(nullptr, G4_ERR_INVALID, "bits must be 2, 4 or 8");
+  // The K spans of src/kernels/qgemv.ts:1258, 1305-1310.
+  const int span = bits == 2 ? 512 : (bits == 4 ? 256 : 128);
   if (N < 1 || K < span || K % span != 0 || cols < 1)
     return fail(nullptr, G4_ERR_INVALID, "qgemv-%dbit needs K a multiple of %d, got %d (N %d, cols %d)", bits, span, K, N, cols);
-  if (in_scale == 0.0f && cols != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "the f32 path takes one column");
-  if ((size_t)K * bits / 8 > 4096 || (size_t)8 * K > 64 * 1024) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  if (bits == 2) {
+    // The interleaved tile layout (g4_op_repack_tile16 makes it from the checkpoint's rows).
+    if (K > 16384 || (in_scale == 0.0f && K > 3072))
+      return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide for qgemv-2bit", K);
+  } else {
+    if (in_scale == 0.0f && cols != 1) return fail(nullptr, G4_ERR_UNSUPPORTED, "the f32 path takes one column");
+    if ((size_t)K * bits / 8 > 4096 || (size_t)8 * K > 64 * 1024) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  }
   cudaStream_t st = (cudaStream_t)stream;
   const int sms = device_sms();
   for (int c0 = 0; c0 < cols; c0 += 8) {
@@ -1922,7 +1862,10 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
     a.seg[0].out_scale = out_scale;
     a.src = x + (size_t)c0 * K;
     a.ld_src = K;
-    gemv_stream_partition(a, 2 * sms);
+    if (bits == 2)
+      gemv2_partition(a, 2 * sms);
+    else
+      gemv_stream_partition(a, 2 * sms);
     OPCK(launch_gemv(a, bits, st, true));
   }
   OPCK(cudaGetLastError());
@@ -1933,12 +1876,12 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
                            float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
                            void *stream) {
   if (!wq || !scales || !x || !y) return fail(nullptr, G4_ERR_INVALID, "g4_op_qgemm: null pointer");
-  if (bits != 4 && bits != 8) return fail(nullptr, G4_ERR_INVALID, "bits must be 4 or 8");
-  const int span = bits == 4 ? 256 : 128;
+  if (bits != 2 && bits != 4 && bits != 8) return fail(nullptr, G4_ERR_INVALID, "bits must be 2, 4 or 8");
+  const int span = bits == 2 ? 512 : (bits == 4 ? 256 : 128);
   if (N < 1 || K < span || K % span != 0 || cols < 1)
     return fail(nullptr, G4_ERR_INVALID, "qgemm-%dbit needs K a multiple of %d, got %d (N %d, cols %d)", bits, span, K, N, cols);
   if (in_scale == 0.0f) return fail(nullptr, G4_ERR_UNSUPPORTED, "the tensor-core path needs a calibrated site");
-  if (K > 8192) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  if (K > 16384) return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
   cudaStream_t st = (cudaStream_t)stream;
   const int rows = std::max(cols, 256);
   uint8_t *codes = nullptr;
@@ -1956,13 +1899,15 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
   CUtensorMap tw, tx;
   // Token tiles: 64, 128, 128 at two CTAs per SM (up to 256 columns), then the persistent tile
   // loop (128-column tiles).
-  const bool persist = cols > 256;
+  const bool persist = cols > 256 && bits != 2;
   const int bn = cols <= 64 ? 64 : (cols <= 128 ? 128 : -128);
   const int bnv = bn < 0 ? -bn : bn;
   const uint64_t rb = (uint64_t)K * bits / 8;
   int rc = G4_OK;
   if (e == cudaSuccess) {
-    if (make_tmap_u8(&tw, wq, rb, (uint64_t)N, rb, bits == 4 ? 64 : 128, 128, bits == 8) ||
+    const int wmap = bits == 2 ? make_tmap_u32(&tw, wq, (uint64_t)K, (uint64_t)((N + 15) / 16), (uint64_t)K * 4, 128, 8)
+                               : make_tmap_u8(&tw, wq, rb, (uint64_t)N, rb, bits == 4 ? 64 : 128, 128, bits == 8);
+    if (wmap ||
         make_tmap_u8(&tx, codes, (uint64_t)K, (uint64_t)rows, (uint64_t)K, 128, bnv, true)) {
       rc = fail(nullptr, G4_ERR_CUDA, "tensor map encoding failed");
     } else {
@@ -2014,6 +1959,18 @@ extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, f
   if (rc) return rc;
   OPCK(e);
   OPCK(cudaGetLastError());
+  return G4_OK;
+}
+
+extern "C" int g4_op_repack_tile16(const void *row_words, void *tile_words, int32_t N, int32_t K,
+                                   int32_t to_rows, void *stream) {
+  if (!row_words || !tile_words || N < 1 || K < 16 || K % 16)
+    return fail(nullptr, G4_ERR_INVALID, "g4_op_repack_tile16: bad argument (N %d, K %d)", N, K);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (to_rows)
+    OPCK(launch_tile16_to_rows(tile_words, (void *)row_words, N, K, st));
+  else
+    OPCK(launch_repack_tile16(row_words, tile_words, N, K, st));
   return G4_OK;
 }
 

@@ -74,8 +74,14 @@ typedef struct g4_arch {
   int32_t vocab_size;            /* 262144 */
   int32_t ple_dim;               /* 256 */
   int32_t attn_bits;             /* 4 */
-  int32_t mlp_bits;              /* 4 (the checkpoint's 2-bit consumer MLP is not built) */
+  int32_t mlp_bits;              /* 4: the producer layers' MLP */
   int32_t ple_bits;              /* 8, the I8 PLE linears (src/quant.ts:610-620) */
+  int32_t consumer_mlp_bits;     /* 4, or 2: the checkpoint's consumer MLP on the interleaved
+                                    2-bit layout (src/plan.ts:116-122, src/quant.ts:598-609) */
+  int32_t head_bits;             /* 4, or 2: the embedding and its tied lm_head (src/quant.ts:
+                                    550-585; the 2-bit table is gathered from the tile layout) */
+  int32_t head_calibrated;       /* 1: the head's SRQ scales are set (integer path); 0: both are
+                                    0.0, the f32 path of the checkpoint's head (needs head_bits 2) */
   float rms_eps;                 /* 1e-6 */
   float final_softcap;           /* 30 */
   float rope_theta_sliding;      /* 1e4 */
@@ -85,6 +91,10 @@ typedef struct g4_arch {
 
 /* Fill `arch` with the Gemma-4-E2B-shaped synthetic architecture of the benchmark configs. */
 int g4_arch_default(g4_arch *arch);
+
+/* The checkpoint's layout (google/gemma-4-E2B-it-qat-mobile, src/plan.ts:116-122): as the default
+ * but consumer MLP 2-bit at width 12288, and a 2-bit uncalibrated embedding / lm_head. */
+int g4_arch_checkpoint(g4_arch *arch);
 
 /* --------------------------------------------------------------------------- context */
 
@@ -97,9 +107,6 @@ typedef struct g4_config {
   uint64_t ple_slice_bytes;  /* 0: PLE table is one buffer; else the vocab-row slice cap */
   int32_t gemm_min_columns;  /* steps this wide or wider run their linears on the tcgen05 int8
                                 GEMM (prefill chunks, batched decode); 0: 16 */
-  int32_t persistent_decode; /* 1: a one-column decode step runs as one persistent cooperative
-                                kernel (grid barriers between phases, bit-identical); 0 (default):
-                                one launch per kernel, chained by programmatic dependent launch */
   int32_t gemm_split_k;      /* K split of tensor-core launches with fewer tiles than SMs (all
                                 bit-identical): 0 (default) over a thread-block cluster, partials
                                 summed in distributed shared memory; 1 never; 2 through a global
@@ -107,7 +114,7 @@ typedef struct g4_config {
 } g4_config;
 
 /* Defaults: g4_arch_default, max_seqs 1, max_context 2048, max_step_columns 64, graphs on,
- * gemm_min_columns 16, persistent_decode 0, gemm_split_k 0. */
+ * gemm_min_columns 16, gemm_split_k 0. */
 int g4_config_default(g4_config *cfg);
 
 /*
@@ -272,14 +279,25 @@ int g4_last_launch_list(const g4_ctx *ctx, char *buf, uint64_t cap, uint64_t *ne
 /*
  * Quantized linear, `cols` activation columns (qgemv-4bit / qgemv-8bit / qgemm-4bit, and the
  * M-wide family: src/kernels/qgemv.ts:413-690, 1131-1176; src/kernels/qgemm.ts:532-552;
- * src/kernels/qgemvWide.ts:452). wq: packed weights [N, K*bits/8] bytes; scales: f16 [N];
- * x: f32 [cols, K]; y: f32 [cols, N]; acc_out: int32 [cols, N] or NULL (the exact integer
- * accumulators on a calibrated site). bits is 4 or 8; K a multiple of 256 (4-bit) or 128
- * (8-bit) (src/kernels/qgemv.ts:1258, 1305-1310). in_scale 0 selects the f32 path.
+ * src/kernels/qgemvWide.ts:452; qgemv-2bit, src/kernels/qgemv.ts:693-868). wq: packed weights
+ * [N, K*bits/8] bytes, or at 2 bits the interleaved tile layout [ceil(N/16), K] u32
+ * (g4_op_repack_tile16); scales: f16 [N]; x: f32 [cols, K]; y: f32 [cols, N]; acc_out: int32
+ * [cols, N] or NULL (the exact integer accumulators on a calibrated site). bits is 2, 4 or 8; K a
+ * multiple of 512 (2-bit), 256 (4-bit) or 128 (8-bit) (src/kernels/qgemv.ts:1258, 1305-1310).
+ * in_scale 0 selects the f32 path (one column at 4 and 8 bits, K <= 3072 at 2 bits).
  */
 int g4_op_qgemv(const void *wq, const void *scales, const float *x, float in_scale,
                 float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
                 int32_t *acc_out, void *stream);
+
+/*
+ * The 2-bit family's layout change (src/kernels/repack.ts:17-209, src/kernels/qlayout.ts:186-227):
+ * to_rows 0 repacks the checkpoint's rows (row r: K / 16 u32 words, code k at bits 2 (k % 16) of
+ * word k / 16) into the interleaved tiles (word k of tile t holds row 16 t + i at bits 2 i, rows
+ * past N zero); to_rows 1 is the inverse. K a multiple of 16. Device pointers.
+ */
+int g4_op_repack_tile16(const void *row_words, void *tile_words, int32_t N, int32_t K,
+                        int32_t to_rows, void *stream);
 
 /*
  * The prefill / batched form (qgemm-4bit, src/kernels/qgemm.ts:76-110, 490-552, 565-636: every

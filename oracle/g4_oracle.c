@@ -204,6 +204,18 @@ static float butterfly32(const float *v) {
   return a[0];
 }
 
+/* The same butterfly with the masks descending (16, 8, 4, 2, 1): the row reduction of the 2-bit
+ * family's f32 path. */
+static float butterfly32_desc(const float *v) {
+  float a[32], b[32];
+  memcpy(a, v, sizeof(a));
+  for (int m = 16; m >= 1; m >>= 1) {
+    for (int i = 0; i < 32; i++) b[i] = a[i] + a[i ^ m];
+    memcpy(a, b, sizeof(a));
+  }
+  return a[0];
+}
+
 /*
  * Sum of squares of v[0..n) in the norm kernels' order (n a multiple of 4): 256 lanes, lane t
  * walks vec4 chunks t, t + 256, ... with an fma per component; each 32-lane group closes with
@@ -243,6 +255,10 @@ static inline int code4(const uint8_t *row, int k) {
 }
 
 static inline int code8(const uint8_t *row, int k) { return (int)(int8_t)row[k]; }
+
+/* 2-bit codes in the checkpoint's row layout (src/quant.ts:27-96): 16 per u32 word, code k at
+ * bits 2 (k % 16), so byte k / 4 holds codes at bits 2 (k % 4); unsigned 0..3, zero point 2. */
+static inline int ucode2(const uint8_t *row, int k) { return (row[k >> 2] >> (2 * (k & 3))) & 3; }
 
 /*
  * qgemvOracle (src/kernels/qgemv.ts:1131-1176) over `cols` columns (qgemmOracle,
@@ -285,11 +301,35 @@ void g4o_qgemv(const uint8_t *wq, const uint16_t *scales_f16, const float *x, fl
             s += lo * xr[2 * j] + hi * xr[2 * j + 1];
           }
           a = s - 8 * xsum[c];
+        } else if (bits == 2) {
+          /* sum((u - 2) x) = sum(u x) - 2 sum(x) (src/kernels/qgemv.ts:693-868). */
+          int32_t s = 0;
+          for (int k = 0; k < K; k++) s += ucode2(row, k) * xr[k];
+          a = s - 2 * xsum[c];
         } else {
           for (int k = 0; k < K; k++) a += code8(row, k) * xr[k];
         }
         if (acc) acc[(size_t)c * N + r] = a;
         out = (in_scale * scale) * (float)a;
+      } else if (bits == 2) {
+        /* The 2-bit family's f32 path: lane l takes k = 128 b + 4 l + j (b ascending, then j),
+         * one fused multiply-add per code, its own activation sum s_l; lane partial
+         * acc_l - 2 s_l; lanes closed by the descending butterfly; then (1 * scale) * sum. */
+        const float *xr = x + (size_t)c * K;
+        float lanes[32];
+        for (int l = 0; l < 32; l++) {
+          float a = 0.0f, sx = 0.0f;
+          for (int b = 0; b < K / 128; b++)
+            for (int j = 0; j < 4; j++) {
+              int k = 128 * b + 4 * l + j;
+              sx = sx + xr[k];
+              a = fmaf((float)ucode2(row, k), xr[k], a);
+            }
+          lanes[l] = a - 2.0f * sx;
+        }
+        float sum = butterfly32_desc(lanes);
+        if (acc) acc[(size_t)c * N + r] = 0;
+        out = (1.0f * scale) * sum;
       } else {
         const float *xr = x + (size_t)c * K;
         int n_chunks = row_bytes / 16;
@@ -729,6 +769,10 @@ void g4o_arch_default(g4o_arch *a) {
   a->theta_sliding = 1e4f;
   a->theta_global = 1e6f;
   a->partial_rotary = 0.25f;
+  a->consumer_ffn = 6144;
+  a->consumer_mlp_bits = 4;
+  a->head_bits = 4;
+  a->head_calibrated = 1;
 }
 
 /* Synthetic tensor kinds; a layer tensor's hash stream is ((layer + 1) << 8) | kind. */
@@ -823,7 +867,8 @@ static void make_linear(o_linear *L, uint64_t seed, int layer, int kw, int ks, i
   L->w = (uint8_t *)malloc(bytes);
   L->s = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)N);
   gen_words(L->w, bytes, seed, layer_stream(layer, kw));
-  double div = bits == 8 ? 16.0 : 1.0;
+  /* Row scales keep activations O(1): int8 codes are 16x larger than int4, 2-bit ones 4x smaller. */
+  double div = bits == 8 ? 16.0 : (bits == 2 ? 0.25 : 1.0);
   gen_f16(L->s, (size_t)N, seed, layer_stream(layer, ks), 1e-3 / div, 1e-2 / div);
   L->in_scale = srq_scale(seed, layer, site, 0);
   L->out_scale = srq_scale(seed, layer, site, 1);
@@ -853,9 +898,11 @@ g4o_model *g4o_model_synth(const g4o_arch *a, uint64_t seed) {
       make_linear(&ly->v, seed, L, TK_V_W, TK_V_S, S_V, ly->hd, H, 4);
     }
     make_linear(&ly->o, seed, L, TK_O_W, TK_O_S, S_O, H, qrows, 4);
-    make_linear(&ly->gate, seed, L, TK_GATE_W, TK_GATE_S, S_GATE, a->ffn, H, 4);
-    make_linear(&ly->up, seed, L, TK_UP_W, TK_UP_S, S_UP, a->ffn, H, 4);
-    make_linear(&ly->down, seed, L, TK_DOWN_W, TK_DOWN_S, S_DOWN, H, a->ffn, 4);
+    const int ffn = ly->producer ? a->ffn : a->consumer_ffn;
+    const int mb = ly->producer ? 4 : a->consumer_mlp_bits;
+    make_linear(&ly->gate, seed, L, TK_GATE_W, TK_GATE_S, S_GATE, ffn, H, mb);
+    make_linear(&ly->up, seed, L, TK_UP_W, TK_UP_S, S_UP, ffn, H, mb);
+    make_linear(&ly->down, seed, L, TK_DOWN_W, TK_DOWN_S, S_DOWN, H, ffn, mb);
     make_linear(&ly->pleg, seed, L, TK_PLEG_W, TK_PLEG_S, S_PLEG, a->ple_dim, H, 8);
     make_linear(&ly->plep, seed, L, TK_PLEP_W, TK_PLEP_S, S_PLEP, H, a->ple_dim, 8);
     ly->ln_in = make_gain(H, seed, L, TK_LN_IN);
@@ -870,10 +917,12 @@ g4o_model *g4o_model_synth(const g4o_arch *a, uint64_t seed) {
     ly->layer_scalar = ls;
   }
   size_t V = (size_t)a->vocab;
-  m->embed_w = (uint8_t *)malloc(V * (size_t)H / 2);
-  gen_words(m->embed_w, V * (size_t)H / 2, seed, layer_stream(-1, TK_EMBED_W));
+  const size_t embed_bytes = V * (size_t)H * (size_t)a->head_bits / 8;
+  m->embed_w = (uint8_t *)malloc(embed_bytes);
+  gen_words(m->embed_w, embed_bytes, seed, layer_stream(-1, TK_EMBED_W));
   m->embed_s = (uint16_t *)malloc(sizeof(uint16_t) * V);
-  gen_f16(m->embed_s, V, seed, layer_stream(-1, TK_EMBED_S), 1e-3, 1e-2);
+  const double ediv = a->head_bits == 2 ? 0.25 : 1.0;
+  gen_f16(m->embed_s, V, seed, layer_stream(-1, TK_EMBED_S), 1e-3 / ediv, 1e-2 / ediv);
   size_t ple_cols = (size_t)a->layer_count * a->ple_dim;
   m->ple_w = (uint8_t *)malloc(V * ple_cols / 2);
   gen_words(m->ple_w, V * ple_cols / 2, seed, layer_stream(-1, TK_PLE_W));
@@ -896,9 +945,10 @@ g4o_model *g4o_model_synth(const g4o_arch *a, uint64_t seed) {
   m->lm.s = m->embed_s;
   m->lm.N = a->vocab;
   m->lm.K = H;
-  m->lm.bits = 4;
-  m->lm.in_scale = srq_scale(seed, -1, S_LM, 0);
-  m->lm.out_scale = srq_scale(seed, -1, S_LM, 1);
+  m->lm.bits = a->head_bits;
+  /* An uncalibrated head (the checkpoint's, src/quant.ts:574-585) has both scales 0.0. */
+  m->lm.in_scale = a->head_calibrated ? srq_scale(seed, -1, S_LM, 0) : 0.0f;
+  m->lm.out_scale = a->head_calibrated ? srq_scale(seed, -1, S_LM, 1) : 0.0f;
   return m;
 }
 
@@ -974,7 +1024,7 @@ const void *g4o_model_tensor(const g4o_model *m, const char *name, uint64_t *byt
   size_t H = (size_t)m->a.hidden, V = (size_t)m->a.vocab;
   size_t ple_cols = (size_t)m->a.layer_count * m->a.ple_dim;
   if (!strcmp(name, "model.language_model.embed_tokens.embedding_quantized")) {
-    *bytes = V * H / 2;
+    *bytes = V * H * (size_t)m->a.head_bits / 8;
     return m->embed_w;
   }
   if (!strcmp(name, "model.language_model.embed_tokens.embedding_scale")) {
@@ -1153,9 +1203,10 @@ static void forward_one(const g4o_model *m, g4o_seq *s, int id, int pos, int n_l
   float *att = (float *)malloc(sizeof(float) * a->q_heads * a->global_hd);
   float *kk = (float *)malloc(sizeof(float) * a->global_hd);
   float *vv = (float *)malloc(sizeof(float) * a->global_hd);
-  float *gate = (float *)malloc(sizeof(float) * a->ffn);
-  float *up = (float *)malloc(sizeof(float) * a->ffn);
-  float *act = (float *)malloc(sizeof(float) * a->ffn);
+  const int ffn_max = a->ffn > a->consumer_ffn ? a->ffn : a->consumer_ffn;
+  float *gate = (float *)malloc(sizeof(float) * ffn_max);
+  float *up = (float *)malloc(sizeof(float) * ffn_max);
+  float *act = (float *)malloc(sizeof(float) * ffn_max);
   float *pg = (float *)malloc(sizeof(float) * PD);
   float *pa = (float *)malloc(sizeof(float) * PD);
   float *cs = (float *)malloc(sizeof(float) * a->global_hd);
@@ -1163,7 +1214,15 @@ static void forward_one(const g4o_model *m, g4o_seq *s, int id, int pos, int n_l
 
   /* ---- embed phase (planEmbed, src/plan.ts:727-736) */
   int32_t ids1 = id;
-  g4o_embed_gather(m->embed_w, m->embed_s, &ids1, h, 1, H, H, (float)sqrt((double)H), 0, 0);
+  if (a->head_bits == 2) {
+    /* embed-gather-2bit (src/kernels/embedGather.ts:236-256, 319-344): (u - 2) times the row
+     * scale with sqrt(H) folded in first. */
+    const uint8_t *er = m->embed_w + (size_t)id * H / 4;
+    float scale = (float)sqrt((double)H) * g4o_f16_to_f32(m->embed_s[id]);
+    for (int k = 0; k < H; k++) h[k] = (float)(ucode2(er, k) - 2) * scale;
+  } else {
+    g4o_embed_gather(m->embed_w, m->embed_s, &ids1, h, 1, H, H, (float)sqrt((double)H), 0, 0);
+  }
   g4o_embed_gather(m->ple_w, m->ple_s, &ids1, ple_id, 1, ple_cols, PD, 16.0f, 0, 0);
   g4o_dense_bf16(m->plmp_w, h, ple_proj, ple_cols, H, 1, (float)pow((double)H, -0.5));
   for (int g = 0; g < NL; g++) {
@@ -1198,7 +1257,7 @@ static void forward_one(const g4o_model *m, g4o_seq *s, int id, int pos, int n_l
     g4o_norm_residual_norm(tmp, ly->ln_post_attn, h, ly->ln_pre_ffn, 1.0f, h, x, 1, H, a->eps);
     run_linear(&ly->gate, S_GATE, x, gate);
     run_linear(&ly->up, S_UP, x, up);
-    for (int i = 0; i < a->ffn; i++) act[i] = g4o_gelu(gate[i]) * up[i];
+    for (int i = 0; i < ly->gate.N; i++) act[i] = g4o_gelu(gate[i]) * up[i];
     run_linear(&ly->down, S_DOWN, act, tmp);
     g4o_norm_residual(tmp, ly->ln_post_ffn, h, h, 1, H, a->eps);
     run_linear(&ly->pleg, S_PLEG, h, pg);

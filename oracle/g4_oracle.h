@@ -95,6 +95,10 @@ typedef struct g4o_arch {
   uint64_t global_mask;
   int32_t window, producers, ffn, vocab, ple_dim;
   float eps, softcap, theta_sliding, theta_global, partial_rotary;
+  /* The checkpoint's families (src/plan.ts:116-122, src/quant.ts:574-609): consumer layers' MLP
+   * width and bits (2: the interleaved 2-bit family), the embedding / tied head bits, and whether
+   * the head is calibrated (0: both activation scales 0.0, the f32 path). */
+  int32_t consumer_ffn, consumer_mlp_bits, head_bits, head_calibrated;
 } g4o_arch;
 
 void g4o_arch_default(g4o_arch *a);

@@ -48,7 +48,8 @@ class Arch(C.Structure):
         ("window", C.c_int32), ("producers", C.c_int32), ("ffn", C.c_int32),
         ("vocab", C.c_int32), ("ple_dim", C.c_int32), ("eps", C.c_float),
         ("softcap", C.c_float), ("theta_sliding", C.c_float), ("theta_global", C.c_float),
-        ("partial_rotary", C.c_float),
+        ("partial_rotary", C.c_float), ("consumer_ffn", C.c_int32),
+        ("consumer_mlp_bits", C.c_int32), ("head_bits", C.c_int32), ("head_calibrated", C.c_int32),
     ]
 
 

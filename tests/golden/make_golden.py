@@ -144,6 +144,25 @@ def ref_vectors() -> dict:
         cases[f"rope_{kind}"] = {"hd": hd_, "rot": rot, "theta": theta, "positions": [0, 1, 77, 2047],
                                  "cos": c, "sin": s,
                                  "inv_freq_last_rotating": R.rope_inverse_frequencies(hd_, rot, theta)[rot - 1]}
+    # The 2-bit family (src/kernels/qgemv.ts:693-868): fixtures in the interleaved tile layout,
+    # 21 rows (a partial last tile) at K 512, the reference's fixture scales.
+    rng2 = np.random.default_rng(SEED + 2)
+    rows2, k2 = 21, 512
+    row_words = [int(w) for w in rng2.integers(0, 2 ** 32, rows2 * k2 // 16, dtype=np.uint64)]
+    tile_words = R.row_words_to_tile16(row_words, rows2, k2)
+    assert R.tile16_to_row_words(tile_words, rows2, k2) == row_words
+    scales2 = np.float16(rng2.uniform(4e-3, 4e-2, rows2))
+    x2 = (rng2.integers(-64, 65, k2) / 8.0).astype(np.float32)
+    sc2 = [float(v) for v in scales2]
+    xs2 = [float(v) for v in x2]
+    for name, ins, outs in (("thirds", 0.1875, 0.0625), ("clamping", 0.015625, 0.0),
+                            ("uncalibrated", 0.0, 0.0)):
+        cases[f"qgemv2_{k2}_{name}"] = {
+            "bits": 2, "k": k2, "rows": rows2, "in_scale": ins, "out_scale": outs,
+            "row_words": row_words, "tile_words": tile_words,
+            "scales_f16": scales2.view(np.uint16).tolist(), "x": xs2,
+            "y": R.qgemv_oracle(2, tile_words, sc2, xs2, rows2, k2, ins, outs),
+            "acc": R.qgemv_acc(2, tile_words, xs2, rows2, k2, ins) if ins else None}
     return cases
 
 

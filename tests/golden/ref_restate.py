@@ -62,15 +62,69 @@ def unpack_int8(packed, width):
     return [(b - 256 if b > 127 else b) for b in packed[:width]]
 
 
+# src/kernels/qlayout.ts:28-54 unpackWordsLikeShader at 2 bits: code k at bits 2 (k % 16) of
+# word k / 16, zero point 2.
+def unpack_2bit_words(words, width):
+    return [((words[i >> 4] >> (2 * (i & 15))) & 3) - 2 for i in range(width)]
+
+
+# src/kernels/qlayout.ts:172-175 tile16Words
+def tile16_words(rows, k):
+    if k % 16:
+        raise ValueError(f"tile16Words: k must be a multiple of 16, got {k}")
+    return -(-rows // 16) * k
+
+
+# src/kernels/qlayout.ts:186-206 rowWordsToTile16
+def row_words_to_tile16(row_words, rows, k):
+    k_words = k // 16
+    out = [0] * tile16_words(rows, k)
+    for row in range(rows):
+        tile, shift = row // 16, 2 * (row % 16)
+        dst, src = tile * k, row * k_words
+        for w in range(k_words):
+            word = row_words[src + w]
+            for i in range(16):
+                code = (word >> (2 * i)) & 3
+                out[dst + w * 16 + i] |= code << shift
+    return out
+
+
+# src/kernels/qlayout.ts:209-227 tile16ToRowWords
+def tile16_to_row_words(tile_words, rows, k):
+    k_words = k // 16
+    out = [0] * (rows * k_words)
+    for row in range(rows):
+        tile, shift = row // 16, 2 * (row % 16)
+        src, dst = tile * k, row * k_words
+        for kk in range(k):
+            code = (tile_words[src + kk] >> shift) & 3
+            out[dst + (kk >> 4)] |= code << (2 * (kk & 15))
+    return out
+
+
+def _row_codes(bits, packed, r, k, num_rows):
+    if bits == 2:
+        # The 2-bit family's buffers are in the interleaved layout; read back to row words.
+        return unpack_2bit_words(packed[r * (k // 16):(r + 1) * (k // 16)], k)
+    row_bytes = k * bits // 8
+    row = packed[r * row_bytes:(r + 1) * row_bytes]
+    return unpack_int4(row, k) if bits == 4 else unpack_int8(row, k)
+
+
+def _as_rows(bits, packed, num_rows, k):
+    """2-bit: `packed` is the tile layout as u32 words; returns row words."""
+    return tile16_to_row_words(packed, num_rows, k) if bits == 2 else packed
+
+
 # src/kernels/qgemv.ts:1131-1176 qgemvOracle
 def qgemv_oracle(bits, packed, scales, x, num_rows, k, in_scale=0.0, out_scale=0.0):
-    row_bytes = k * bits // 8
     calibrated = in_scale != 0
     x_codes = srq_codes(x[:k], in_scale) if calibrated else None
+    packed = _as_rows(bits, packed, num_rows, k)
     out = []
     for r in range(num_rows):
-        row = packed[r * row_bytes:(r + 1) * row_bytes]
-        codes = unpack_int4(row, k) if bits == 4 else unpack_int8(row, k)
+        codes = _row_codes(bits, packed, r, k, num_rows)
         scale = fround(scales[r])
         s = 0.0
         if x_codes is not None:
@@ -86,12 +140,11 @@ def qgemv_oracle(bits, packed, scales, x, num_rows, k, in_scale=0.0, out_scale=0
 
 def qgemv_acc(bits, packed, x, num_rows, k, in_scale):
     """The exact integer accumulators of the calibrated path."""
-    row_bytes = k * bits // 8
     x_codes = srq_codes(x[:k], in_scale)
+    packed = _as_rows(bits, packed, num_rows, k)
     accs = []
     for r in range(num_rows):
-        row = packed[r * row_bytes:(r + 1) * row_bytes]
-        codes = unpack_int4(row, k) if bits == 4 else unpack_int8(row, k)
+        codes = _row_codes(bits, packed, r, k, num_rows)
         accs.append(int(sum(c * int(q) for c, q in zip(codes, x_codes))))
     return accs
 

@@ -86,36 +86,6 @@ def test_generation_bit_exact(pkg, O, tiny, graphs):
     ctx.close()
 
 
-def test_persistent_decode_matches_launch_chain(pkg, O, tiny):
-    """A one-column decode step as one persistent cooperative kernel (grid barriers between the
-    phases) gives the launch chain's logits bit for bit, step after step, with and without the
-    device-side position advance."""
-    a, om = tiny
-    prompt = O.synth_prompt(SEED + 5, 37, a.vocab_size)
-    runs = []
-    for persistent in (True, False):
-        ctx = make_ctx(pkg, a, persistent_decode=persistent)
-        tok = ctx.prefill(0, prompt, 0, True)
-        logits = [ctx.logits(0).copy()]
-        toks = [tok]
-        for i in range(1, 6):
-            toks.append(ctx.decode(0, toks[-1], len(prompt) + i - 1))
-            logits.append(ctx.logits(0).copy())
-            # The persistent step is one kernel launch; the chain is one per kernel.
-            assert (ctx.launches() == 1) == persistent, ctx.launches()
-        ctx.step_stage([0], [toks[-1]], [len(prompt) + 5])
-        for _ in range(4):
-            ctx.step_run_device(1)
-        toks += list(ctx.step_read_tokens(1))
-        runs.append((toks, logits))
-        ctx.close()
-    assert runs[0][0] == runs[1][0]
-    for la, lb in zip(runs[0][1], runs[1][1]):
-        np.testing.assert_array_equal(la.view(np.uint32), lb.view(np.uint32))
-    want, _ = om.generate(prompt, 6, 128)
-    assert runs[0][0][:6] == list(want)
-
-
 def test_engine_generate_lookahead(pkg, O, tiny):
     a, om = tiny
     ctx = make_ctx(pkg, a)

@@ -84,7 +84,13 @@ def test_qgemv_golden(O, V):
     for name, c in V.items():
         if not name.startswith("qgemv"):
             continue
-        packed = np.frombuffer(bytes.fromhex(c["packed"]), np.uint8)
+        if c["bits"] == 2:
+            # The fixtures hold the tile layout; the oracle reads the checkpoint's rows. On the f32
+            # path the codes are integers and x sits on the 1/8 grid, so every partial sum is
+            # exact in f32 whatever the order, and zero tolerance holds there too.
+            packed = np.array(c["row_words"], np.uint32).view(np.uint8)
+        else:
+            packed = np.frombuffer(bytes.fromhex(c["packed"]), np.uint8)
         scales = np.array(c["scales_f16"], np.uint16)
         x = np.array(c["x"], np.float32)
         y, acc = O.qgemv(packed, scales, x, c["in_scale"], c["out_scale"], c["bits"], c["rows"], c["k"])
@@ -184,3 +190,26 @@ def test_oracle_mirror_close_to_reference(O):
         a = O.rms_norm(src, g, 3, width)
         b = O.rms_norm(src, g, 3, width, ref=True)
         assert np.max(np.abs(a - b)) < 3e-4
+
+
+def test_tile16_layout_restatement(V):
+    """The interleaved 2-bit layout (src/kernels/qlayout.ts:160-234) as restated: round trip, the
+    code of (row, k) at bits 2 (row % 16) of word (row / 16) K + k, padded rows zero."""
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location(
+        "ref_restate", Path(__file__).resolve().parent / "golden" / "ref_restate.py")
+    R = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(R)
+    c = V["qgemv2_512_thirds"]
+    rows, k = c["rows"], c["k"]
+    tw = np.array(c["tile_words"], np.uint32)
+    rw = np.array(c["row_words"], np.uint32)
+    assert tw.size == -(-rows // 16) * k
+    for row in (0, 7, 15, 16, 20):
+        for kk in (0, 1, 15, 16, 511):
+            want = (int(rw[row * (k // 16) + kk // 16]) >> (2 * (kk % 16))) & 3
+            assert (int(tw[(row // 16) * k + kk]) >> (2 * (row % 16))) & 3 == want
+    # rows 21..31 of the last tile are zero codes
+    assert all((int(w) >> 2 * r) & 3 == 0 for w in tw[k:] for r in range(5, 16))
+    assert R.tile16_to_row_words(list(map(int, tw)), rows, k) == list(map(int, rw))
