@@ -44,6 +44,7 @@ DTYPE = "int4xint8 (int32 acc) / f32"
 DATA = "synthetic (seeded random-init Gemma-4-E2B shape)"
 B64, B64_LO, B64_HI, B64_STEPS = 64, 128, 4096, 256
 BOX_SEQS, BOX_PROMPT, BOX_STEPS = 512, 512, 256
+CTX_KW: dict = {}    # extra g4_config fields from the command line (engine.Context keywords)
 
 # Algorithmic bytes of one B=1 decode token on the synthetic Gemma-4-E2B shape: int4 linears
 # incl. the tied int4 lm_head, the I8 PLE linears, the bf16 per_layer_model_projection, the f16
@@ -371,7 +372,7 @@ def measure_prefill(pkg, torch, dev, n, steps, warmup, world, rank) -> dict:
     projections run as tcgen05 int8 GEMMs over all n-1 columns. Each step rewinds the KV
     (src/kv.ts:247-254) and prefills again; the ids go host->device and the token comes back
     inside every step, so the device-timed and the end-to-end figures share one loop shape."""
-    ctx = pkg.engine.Context(device=dev, max_seqs=1, max_context=n + 8, max_step_columns=n)
+    ctx = pkg.engine.Context(device=dev, max_seqs=1, max_context=n + 8, max_step_columns=n, **CTX_KW)
     ctx.init_random(SEED)
     prompt = np.array(pkg.plan.synth_prompt(SEED + 7919 * rank, n), np.int32)
     stream = torch.cuda.ExternalStream(ctx.stream())
@@ -449,7 +450,7 @@ def measure_decode(pkg, torch, dev, seq_ids, lens, steps, warmup, world, rank, s
     max_ctx = max(lens) + max(steps, warmup) + 8
     chunk = max(B, 512 if max(lens) > 256 else 64)
     ctx = pkg.engine.Context(device=dev, max_seqs=B, max_context=max_ctx, max_step_columns=chunk,
-                             ple_slice_bytes=slice_bytes, gemm_split_k=gemm_split_k)
+                             ple_slice_bytes=slice_bytes, gemm_split_k=gemm_split_k, **CTX_KW)
     ctx.init_random(SEED)
     prompts = [np.array(pkg.plan.synth_prompt(SEED + int(s), lens[i]), np.int32)
                for i, s in enumerate(seq_ids)]
@@ -547,7 +548,10 @@ def main():
     ap.add_argument("--tokens", type=int, default=2048, help="prefill workload: prompt length")
     ap.add_argument("--gemm-split-k", type=int, default=0, choices=[0, 1, 2],
                     help="g4_config.gemm_split_k: 0 cluster, 1 none, 2 workspace")
+    ap.add_argument("--gemm-shadow-min-columns", type=int, default=0,
+                    help="g4_config.gemm_shadow_min_columns: 0 default (512), negative off")
     args = ap.parse_args()
+    CTX_KW["gemm_shadow_min_columns"] = args.gemm_shadow_min_columns
     if args.warmup < 3:
         ap.error("at least 3 warm-up steps")
     if args.impl == "reference":

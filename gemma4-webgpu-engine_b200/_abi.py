@@ -44,7 +44,7 @@ class Config(C.Structure):
         ("arch", Arch), ("max_seqs", C.c_int32), ("max_context", C.c_int32),
         ("max_step_columns", C.c_int32), ("use_graphs", C.c_int32),
         ("ple_slice_bytes", C.c_uint64), ("gemm_min_columns", C.c_int32),
-        ("gemm_split_k", C.c_int32),
+        ("gemm_shadow_min_columns", C.c_int32), ("gemm_split_k", C.c_int32),
     ]
 
 

@@ -95,6 +95,50 @@ cudaError_t launch_tile16_to_rows(const void *tile_words, void *row_words, int N
   return cudaGetLastError();
 }
 
+// Signed int8 copies of packed weights for the tensor-core path (row-major [N][K], code - zero
+// point): the GEMM then loads them by TMA straight into its swizzled tile with no unpack.
+// int4: one thread per packed u32 (8 codes, low nibble first); 2-bit tiles: one thread per 4
+// consecutive k of a row.
+__global__ void __launch_bounds__(256) k_widen_int4(const uint32_t *w4, uint2 *w8, size_t words) {
+  const size_t i = (size_t)blockIdx.x * 256 + threadIdx.x;
+  if (i >= words) return;
+  const uint32_t w = w4[i];
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    lo |= (uint32_t)(uint8_t)((int)((w >> (4 * j)) & 15u) - 8) << (8 * j);
+    hi |= (uint32_t)(uint8_t)((int)((w >> (4 * j + 16)) & 15u) - 8) << (8 * j);
+  }
+  w8[i] = make_uint2(lo, hi);
+}
+
+__global__ void __launch_bounds__(256) k_widen_tile16(const uint32_t *tiles, uint32_t *w8, int N, int K) {
+  const size_t i = (size_t)blockIdx.x * 256 + threadIdx.x;
+  const int kq = K / 4;
+  if (i >= (size_t)N * kq) return;
+  const int row = (int)(i / kq), k = 4 * (int)(i % kq);
+  const uint32_t *tw = tiles + (size_t)(row / 16) * K + k;
+  const int shift = 2 * (row % 16);
+  uint32_t out = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) out |= (uint32_t)(uint8_t)((int)((tw[j] >> shift) & 3u) - 2) << (8 * j);
+  w8[i] = out;
+}
+
+cudaError_t launch_widen_weights(const void *w, int bits, int N, int K, void *w8, cudaStream_t st) {
+  if (N < 1 || K < 16 || K % 16) return cudaErrorInvalidValue;
+  if (bits == 4) {
+    const size_t words = (size_t)N * K / 8;
+    k_widen_int4<<<(unsigned)((words + 255) / 256), 256, 0, st>>>((const uint32_t *)w, (uint2 *)w8, words);
+  } else if (bits == 2) {
+    const size_t n = (size_t)N * (K / 4);
+    k_widen_tile16<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const uint32_t *)w, (uint32_t *)w8, N, K);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ the GEMV
 
 // Shared memory of one CTA: the ring, barriers, column sums, reduction scratch, per-warp argmax

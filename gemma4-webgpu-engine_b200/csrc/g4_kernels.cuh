@@ -141,6 +141,8 @@ cudaError_t launch_gemv(const GemvArgs &a, int bits, cudaStream_t st, bool pdl);
 cudaError_t launch_repack_tile16(const void *row_words, void *tile_words, int N, int K, cudaStream_t st);
 cudaError_t launch_tile16_to_rows(const void *tile_words, void *row_words, int N, int K, cudaStream_t st);
 int gemv2_partition(GemvArgs &a, int sms);
+// Signed int8 row-major copy [N][K] (code - zero point) of int4 rows or 2-bit tiles.
+cudaError_t launch_widen_weights(const void *w, int bits, int N, int K, void *w8, cudaStream_t st);
 cudaError_t launch_gemv2(const GemvArgs &a, cudaStream_t st, bool pdl);
 __host__ __device__ __forceinline__ size_t tile16_bytes(int N, int K) {
   return (size_t)((N + 15) / 16) * (size_t)K * 4;

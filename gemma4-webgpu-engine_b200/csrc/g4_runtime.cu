@@ -38,6 +38,11 @@ struct Linear {
   std::string module;
   CUtensorMap tmw;          // TMA view of w for the tensor-core path (has_tm)
   bool has_tm = false;
+  // Signed int8 copy [N][K] of int4 / 2-bit codes for wide tensor-core steps (no unpack), and its
+  // 128-byte-swizzled TMA view.
+  int8_t *w8 = nullptr;
+  CUtensorMap tmw8;
+  bool has_tm8 = false;
 };
 
 // The tensor map the tensor-core linear loads weights through: int4 packed rows (box 64 bytes x
@@ -125,6 +130,12 @@ struct g4_ctx {
   int gacc_ld = 0;
   int gemm_split_k = 0;   // g4_config::gemm_split_k
   bool gemm_persist = false;
+  // int8 weight copies: steps of at least shadow_min_cols columns run their int4 / 2-bit linears
+  // on them; refreshed from the packed weights before the next forward after any weight change.
+  uint8_t *shadow = nullptr;
+  size_t shadow_bytes = 0;
+  int shadow_min_cols = 0;
+  bool shadow_dirty = false;
   // Token tile of steps wider than 128 columns: 128 columns at two CTAs per SM (-128), measured
   // 10% faster on a 2048-token prefill than 256-column tiles at one CTA per SM.
   int gemm_wide_bn = -128;
@@ -277,6 +288,7 @@ extern "C" int g4_config_default(g4_config *cfg) {
   cfg->ple_slice_bytes = 0;
   cfg->gemm_min_columns = 16;
   cfg->gemm_split_k = 0;
+  cfg->gemm_shadow_min_columns = 0;
   return G4_OK;
 }
 
@@ -457,6 +469,26 @@ static int alloc_weights(g4_ctx *ctx) {
     for (Linear *l : {&ly.q, &ly.k, &ly.v, &ly.o, &ly.gate, &ly.up, &ly.down, &ly.pleg, &ly.plep})
       linear_tmap(*l);
   linear_tmap(ctx->lm);
+  // int8 copies of the int4 / 2-bit linears for wide tensor-core steps (about 1.3 GB at the full
+  // shape; HBM is plentiful and a prefill GEMM is bound by the unpack otherwise).
+  ctx->shadow_min_cols = ctx->cfg.gemm_shadow_min_columns == 0 ? 512 : ctx->cfg.gemm_shadow_min_columns;
+  if (ctx->shadow_min_cols > 0) {
+    std::vector<Linear *> ls;
+    for (Layer &ly : ctx->layers)
+      for (Linear *l : {&ly.q, &ly.k, &ly.v, &ly.o, &ly.gate, &ly.up, &ly.down})
+        if (l->w && l->bits != 8 && l->K % 128 == 0) ls.push_back(l);
+    if (ctx->lm.K % 128 == 0) ls.push_back(&ctx->lm);
+    size_t total = 0;
+    for (Linear *l : ls) total += ((size_t)l->N * l->K + 255) & ~(size_t)255;
+    CK(ctx_malloc((void **)&ctx->shadow, total));
+    ctx->shadow_bytes = total;
+    size_t off = 0;
+    for (Linear *l : ls) {
+      l->w8 = (int8_t *)(ctx->shadow + off);
+      off += ((size_t)l->N * l->K + 255) & ~(size_t)255;
+      l->has_tm8 = make_tmap_u8(&l->tmw8, l->w8, (uint64_t)l->K, (uint64_t)l->N, (uint64_t)l->K, 128, 128, true) == 0;
+    }
+  }
   // The PLE code table: one buffer or vocab-row slices (src/tableSplit.ts:125-215).
   const uint64_t row_bytes = (uint64_t)ctx->ple_cols / 2;
   const uint64_t total = row_bytes * V;
@@ -668,6 +700,7 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   if (ctx->st) cudaStreamSynchronize(ctx->st);
   for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
   cudaFree(ctx->arena);
+  cudaFree(ctx->shadow);
   for (void *p : ctx->ple_slices) cudaFree(p);
   cudaFree(ctx->d_ple_slices);
   for (float *p : ctx->kv) cudaFree(p);
@@ -867,6 +900,7 @@ extern "C" int g4_init_random(g4_ctx *ctx, uint64_t seed) {
   ctx->lm.out_scale = ctx->cfg.arch.head_calibrated ? synth_srq(seed, -1, S_LM, 1) : 0.0f;
   CK(cudaStreamSynchronize(ctx->st));
   ctx->weights_ready = true;
+  ctx->shadow_dirty = ctx->shadow != nullptr;
   for (auto &kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
   ctx->graphs.clear();
   return G4_OK;
@@ -920,6 +954,7 @@ extern "C" int g4_upload_weight(g4_ctx *ctx, const char *name, const void *bytes
       done += take;
     }
   }
+  ctx->shadow_dirty = ctx->shadow != nullptr;
   ctx->weights_ready = true;
   return G4_OK;
 }
@@ -1073,6 +1108,11 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   }
   q.K = K;
   q.cols = cols;
+  // Wide steps read the int8 copies (no unpack in the GEMM); the int32 sums are the same.
+  bool sh = ctx->shadow && !ctx->shadow_dirty && cols >= ctx->shadow_min_cols;
+  for (auto &sg : segs) sh = sh && sg.lin->w8 && sg.lin->has_tm8;
+  auto wmap = [&](const Linear &l) -> const CUtensorMap & { return sh ? l.tmw8 : l.tmw; };
+  auto wbits = [&](const Linear &l) { return sh ? 8 : l.bits; };
   CK(launch_quantize(q, ctx->gq[0], ctx->gq_ld, sc[0], nsc > 1 ? ctx->gq[1] : nullptr, nsc > 1 ? sc[1] : 0.0f,
                      ctx->st, true));
   note_launch(ctx, "quantize", seg_roles(segs));
@@ -1094,7 +1134,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   }
   const int nseg = (int)segs.size();
   bool same_bits = true;
-  for (auto &sg : segs) same_bits = same_bits && sg.lin->bits == segs.begin()->lin->bits;
+  for (auto &sg : segs) same_bits = same_bits && wbits(*sg.lin) == wbits(*segs.begin()->lin);
   if (nseg > 1 && nseg <= 3 && !head && (bn == 64 || bn == -128) && same_bits && ctx->gemm_split_k != 2) {
     // q/k/v or gate/up: one launch, the segments' tiles end to end along x, each CTA with its
     // segment's weight and code tensor maps; with 64-token tiles, few tiles split K over a cluster.
@@ -1107,7 +1147,7 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
       const Linear &l = *sg.lin;
       const CUtensorMap *tx = codes_tmap(ctx, which[si], K, bn < 0 ? -bn : bn);
       if (!tx) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
-      m.w[si] = l.tmw;
+      m.w[si] = wmap(l);
       m.x[si] = *tx;
       if (si == 0) {
         g.N = l.N;
@@ -1134,8 +1174,8 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     if (ctx->gemm_split_k == 0 && bn == 64)
       while (splits < 8 && 2 * splits * all_tiles <= 2 * ctx->sms && 2 * splits <= K / 128) splits *= 2;
     g.splits = splits;
-    CK(launch_qgemm_multi(m, g, segs.begin()->lin->bits, bn, ctx->st, true));
-    note_launch(ctx, bits_name("qgemm", segs.begin()->lin->bits), seg_roles(segs));
+    CK(launch_qgemm_multi(m, g, wbits(*segs.begin()->lin), bn, ctx->st, true));
+    note_launch(ctx, bits_name("qgemm", wbits(*segs.begin()->lin)), seg_roles(segs));
     return G4_OK;
   }
   i = 0;
@@ -1162,8 +1202,8 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
       while (splits < 8 && 2 * splits * tiles <= 2 * ctx->sms && 2 * splits <= kts) splits *= 2;
       if (splits > 1) {
         g.splits = splits;
-        CK(launch_qgemm_cluster(l.tmw, *tx, g, l.bits, ctx->st, true));
-        note_launch(ctx, bits_name("qgemm", l.bits), short_module(l.module));
+        CK(launch_qgemm_cluster(wmap(l), *tx, g, wbits(l), ctx->st, true));
+        note_launch(ctx, bits_name("qgemm", wbits(l)), short_module(l.module));
         continue;
       }
     }
@@ -1195,17 +1235,17 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
     // 2048-token prefill than two per-tile CTAs per SM (tail imbalance, twice the DRAM reads), so
     // the executor keeps the per-tile kernel; g4_op_qgemm uses the loop for wide calls.
     const int tiles128 = ((l.N + 127) / 128) * ((cols + 127) / 128);
-    if (ctx->gemm_persist && !head && g.splits <= 1 && tiles128 > ctx->sms && l.bits != 2) {
+    if (ctx->gemm_persist && !head && g.splits <= 1 && tiles128 > ctx->sms && wbits(l) != 2) {
       const CUtensorMap *tx128 = codes_tmap(ctx, which[i - 1], K, 128);
       if (!tx128) return fail(ctx, G4_ERR_CUDA, "activation-code tensor map for K %d failed", K);
-      CK(launch_qgemm_persist(l.tmw, *tx128, g, l.bits, std::min(tiles128, ctx->sms), ctx->st, true));
+      CK(launch_qgemm_persist(wmap(l), *tx128, g, wbits(l), std::min(tiles128, ctx->sms), ctx->st, true));
     } else {
       // Many 64-token tiles (the lm_head of a decode batch: 2,048): three stages, two CTAs per SM,
       // so one CTA's epilogue runs beside the other's main loop.
       const int bn_l = bn == 64 && tiles >= 2 * ctx->sms ? -64 : bn;
-      CK(launch_qgemm(l.tmw, *tx, g, l.bits, bn_l, ctx->st, true));
+      CK(launch_qgemm(wmap(l), *tx, g, wbits(l), bn_l, ctx->st, true));
     }
-    note_launch(ctx, bits_name("qgemm", l.bits, head), short_module(l.module));
+    note_launch(ctx, bits_name("qgemm", wbits(l), head), short_module(l.module));
   }
   return G4_OK;
 }
@@ -1603,8 +1643,23 @@ static int check_seq_pos(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t n) {
 // Copy one step's columns into the device step buffer. The pinned source slot is rewritten only
 // once the copy that last read it has executed on the stream (consecutive prefill chunks are
 // enqueued without a host wait).
+// Rebuild the int8 weight copies after a weight change (before any step uses them).
+static int refresh_shadows(g4_ctx *ctx) {
+  if (!ctx->shadow_dirty) return G4_OK;
+  auto widen = [&](Linear &l) -> cudaError_t {
+    return l.w8 ? launch_widen_weights(l.w, l.bits, l.N, l.K, l.w8, ctx->st) : cudaSuccess;
+  };
+  for (Layer &ly : ctx->layers)
+    for (Linear *l : {&ly.q, &ly.k, &ly.v, &ly.o, &ly.gate, &ly.up, &ly.down}) CK(widen(*l));
+  CK(widen(ctx->lm));
+  ctx->shadow_dirty = false;
+  return G4_OK;
+}
+
 static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos, const int32_t *toks,
                  bool tokens_too) {
+  int rc = refresh_shadows(ctx);
+  if (rc) return rc;
   const int slot = ctx->stage_next;
   ctx->stage_next = (slot + 1) % g4_ctx::kStageSlots;
   CK(cudaEventSynchronize(ctx->stage_ev[slot]));

@@ -22,7 +22,7 @@ class Context:
     def __init__(self, device: int = 0, max_seqs: int = 1, max_context: int = 2048,
                  max_step_columns: int = 64, use_graphs: bool = True, ple_slice_bytes: int = 0,
                  arch: _abi.Arch | None = None, gemm_min_columns: int = 16,
-                 gemm_split_k: int = 0):
+                 gemm_split_k: int = 0, gemm_shadow_min_columns: int = 0):
         lib = _abi.load()
         cfg = _abi.config_default()
         if arch is not None:
@@ -34,6 +34,7 @@ class Context:
         cfg.ple_slice_bytes = ple_slice_bytes
         cfg.gemm_min_columns = gemm_min_columns
         cfg.gemm_split_k = gemm_split_k
+        cfg.gemm_shadow_min_columns = gemm_shadow_min_columns
         h = C.c_void_p()
         _abi.check(lib.g4_ctx_create(device, C.byref(cfg), C.byref(h)))
         self.lib = lib

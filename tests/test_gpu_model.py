@@ -386,3 +386,33 @@ def test_executor_launches_match_plan_full_model(pkg, cuda):
     want = _planned(P.plan_decode_step(P.GEMMA4_E2B, 1))
     assert len(got) == 250 and got == want
     ctx.close()
+
+
+@pytest.mark.parametrize("checkpoint", [False, True])
+def test_int8_weight_copies_bit_identical(pkg, O, tiny, checkpoint):
+    """Wide tensor-core steps on the int8 weight copies (gemm_shadow_min_columns) give the packed
+    path's logits bit for bit: a 600-token prefill chunk and a 40-sequence decode batch, with the
+    int4 family and with the checkpoint's 2-bit family; and the copies follow a weight upload."""
+    a = entry.tiny_checkpoint_arch(pkg) if checkpoint else tiny[0]
+    prompt = O.synth_prompt(SEED + 12, 600, a.vocab_size)
+    outs = []
+    for shadow in (32, -1):
+        ctx = make_ctx(pkg, a, max_seqs=40, max_context=1024, max_step_columns=1024,
+                       gemm_shadow_min_columns=shadow)
+        t = ctx.prefill(0, prompt, 0, True)
+        lg = [ctx.logits(0).copy()]
+        toks = [ctx.prefill(b, prompt[:5 + b], 0, True) for b in range(1, 40)]
+        out = ctx.decode_batch(np.arange(1, 40), toks, [5 + b for b in range(1, 40)])
+        lg += [ctx.logits(c).copy() for c in (0, 38)]
+        name = "model.language_model.layers.0.mlp.up_proj.weight"
+        w = ctx.download(name)
+        w[:4096] ^= 0x33
+        ctx.upload(name, w)
+        ctx.kv_truncate(0, 0)
+        t2 = ctx.prefill(0, prompt, 0, True)
+        lg.append(ctx.logits(0).copy())
+        outs.append((t, list(out), t2, lg))
+        ctx.close()
+    assert outs[0][:3] == outs[1][:3]
+    for la, lb in zip(outs[0][3], outs[1][3]):
+        np.testing.assert_array_equal(la.view(np.uint32), lb.view(np.uint32))
