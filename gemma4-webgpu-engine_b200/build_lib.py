@@ -40,6 +40,23 @@ def needs_build() -> bool:
 
 
 TRACE_LIB = LIB_DIR / "trace" / "libgemma4_cuda.so"
+NAPI_SRC = PKG / "napi" / "g4_napi.c"
+NAPI_ADDON = LIB_DIR / "gemma4_cuda.node"
+
+
+def build_napi(verbose: bool = False) -> Path:
+    """The Node-API addon (gemma4_cuda.node) over libgemma4_cuda.so. Node's napi_* symbols stay
+    undefined until Node (or another Node-API host) loads the addon."""
+    if NAPI_ADDON.exists() and NAPI_ADDON.stat().st_mtime > max(
+            NAPI_SRC.stat().st_mtime, LIB.stat().st_mtime, (PKG / "napi" / "node_api_min.h").stat().st_mtime):
+        return NAPI_ADDON
+    cmd = [os.environ.get("CC", "gcc"), "-O2", "-std=c11", "-fPIC", "-shared", "-Wall", "-Wextra",
+           "-Wno-unused-parameter", str(NAPI_SRC), "-o", str(NAPI_ADDON), f"-L{LIB_DIR}",
+           "-lgemma4_cuda", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return NAPI_ADDON
 
 
 def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
@@ -74,3 +91,5 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Pa
 
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))
+    if "--trace" not in sys.argv:
+        print(build_napi(verbose=True))
