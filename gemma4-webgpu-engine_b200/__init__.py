@@ -5,7 +5,7 @@ the ctypes binding (`_abi`), the reference's host interfaces (`engine`: Gemma4Mo
 ForwardExecutor seam; `plan`: prefill chunks, dispatch lists, KV reuse, table split;
 `replicas`: the request split across one replica per GPU).
 """
-from . import _abi, engine, plan, replicas  # noqa: F401
+from . import _abi, engine, loader, plan, replicas  # noqa: F401
 from ._abi import G4Error, load  # noqa: F401
 
-__all__ = ["G4Error", "load", "plan", "engine", "replicas"]
+__all__ = ["G4Error", "load", "plan", "engine", "loader", "replicas"]
