@@ -480,6 +480,17 @@ def measure_decode(pkg, torch, dev, seq_ids, lens, steps, warmup, world, rank, s
     dev_s = e0.elapsed_time(e1) / 1e3
     dev_tokens = ctx.step_read_tokens(B)
 
+    # The C-ABI path launches its own graph (host-staged tokens): warm it as well, so the timed
+    # region holds no graph capture.
+    for b in range(B):
+        ctx.kv_truncate(b, lens[b])
+    prev = [int(t) for t in first]
+    for i in range(warmup):
+        if B == 1:
+            prev = [ctx.decode(0, prev[0], lens[0] + i)]
+        else:
+            prev = list(ctx.decode_batch(np.arange(B), prev, [lens[b] + i for b in range(B)]))
+    torch.cuda.synchronize()
     for b in range(B):
         ctx.kv_truncate(b, lens[b])
     prev = [int(t) for t in first]
@@ -549,7 +560,7 @@ def main():
     ap.add_argument("--gemm-split-k", type=int, default=0, choices=[0, 1, 2],
                     help="g4_config.gemm_split_k: 0 cluster, 1 none, 2 workspace")
     ap.add_argument("--gemm-shadow-min-columns", type=int, default=0,
-                    help="g4_config.gemm_shadow_min_columns: 0 default (512), negative off")
+                    help="g4_config.gemm_shadow_min_columns: 0 default (every tensor-core step), negative off")
     args = ap.parse_args()
     CTX_KW["gemm_shadow_min_columns"] = args.gemm_shadow_min_columns
     if args.warmup < 3:

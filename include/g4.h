@@ -110,7 +110,8 @@ typedef struct g4_config {
   int32_t gemm_shadow_min_columns; /* steps at least this wide run their int4 / 2-bit linears on
                                 int8 copies of the weights held beside the packed ones (the GEMM
                                 then loads them by TMA with no unpack; same integer sums, about
-                                1.3 GB more HBM at the full shape); 0: 512; negative: no copies */
+                                1.3 GB more HBM at the full shape); 0: every tensor-core step;
+                                negative: no copies */
   int32_t gemm_split_k;      /* K split of tensor-core launches with fewer tiles than SMs (all
                                 bit-identical): 0 (default) over a thread-block cluster, partials
                                 summed in distributed shared memory; 1 never; 2 through a global
@@ -118,7 +119,7 @@ typedef struct g4_config {
 } g4_config;
 
 /* Defaults: g4_arch_default, max_seqs 1, max_context 2048, max_step_columns 64, graphs on,
- * gemm_min_columns 16, gemm_shadow_min_columns 0 (512), gemm_split_k 0. */
+ * gemm_min_columns 16, gemm_shadow_min_columns 0 (every tensor-core step), gemm_split_k 0. */
 int g4_config_default(g4_config *cfg);
 
 /*
