@@ -35,6 +35,12 @@ namespace g4 {
 // Raised when a bounded wait on a weight copy gives up (device variables are per translation
 // unit here, so this file keeps its own; device_error_take reads both).
 __device__ int g4_gemv2_error;
+#ifdef G4_TRACE
+// Diagnostic build: this unit's own record buffer (device variables are per unit); its records
+// are not collected.
+__device__ unsigned long long g4_trace_buf[1 << 16];
+__device__ unsigned int g4_trace_n;
+#endif
 
 int gemv2_error_take() {
   int v = 0, zero = 0;
