@@ -250,21 +250,31 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def measure_gemv(pkg, torch, copies: int, iters: int) -> dict:
-    """the int4 x int8 GEMV [6144 x 1536], timed over `copies` distinct weight
-    buffers (together larger than L2) with CUDA events on the launching stream."""
+def gemv_shape(bits: int) -> tuple:
+    """(N, K, algorithmic bytes per launch) of the GEMV line: BASELINE config 1 at 4 bits; at 2
+    bits the checkpoint's consumer gate / up projection [12288 x 1536] on the interleaved tile
+    layout (the same 4.7 MB of weights)."""
+    n, k = (GEMV_N, GEMV_K) if bits == 4 else (2 * GEMV_N, GEMV_K)
+    return n, k, n * k * bits // 8 + 2 * n + k + 2 * n
+
+
+def measure_gemv(pkg, torch, copies: int, iters: int, bits: int = 4) -> dict:
+    """the int4 x int8 GEMV [6144 x 1536] (or the 2-bit line, gemv_shape),
+    timed over `copies` distinct weight buffers (together larger than L2) with CUDA events on the
+    launching stream."""
     lib = pkg._abi.load()
+    n, k, nbytes = gemv_shape(bits)
     g = torch.Generator(device="cuda").manual_seed(SEED)
-    ws = [torch.randint(0, 256, (GEMV_N * GEMV_K // 2,), dtype=torch.uint8, device="cuda", generator=g)
+    ws = [torch.randint(0, 256, (n * k * bits // 8,), dtype=torch.uint8, device="cuda", generator=g)
           for _ in range(copies)]
-    sc = (torch.rand(GEMV_N, device="cuda", generator=g) * 9e-3 + 1e-3).half().view(torch.int16)
-    x = (torch.randint(-127, 128, (GEMV_K,), device="cuda", generator=g).float() * 0.02)
-    y = torch.empty(GEMV_N, device="cuda")
+    sc = (torch.rand(n, device="cuda", generator=g) * 9e-3 + 1e-3).half().view(torch.int16)
+    x = (torch.randint(-127, 128, (k,), device="cuda", generator=g).float() * 0.02)
+    y = torch.empty(n, device="cuda")
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
     def launch(w):
-        rc = lib.g4_op_qgemv(w.data_ptr(), sc.data_ptr(), x.data_ptr(), 0.02, 0.0, 4, GEMV_N, GEMV_K, 1,
+        rc = lib.g4_op_qgemv(w.data_ptr(), sc.data_ptr(), x.data_ptr(), 0.02, 0.0, bits, n, k, 1,
                              y.data_ptr(), None, sp)
         assert rc == 0, pkg._abi.last_error()
 
@@ -298,7 +308,7 @@ def measure_gemv(pkg, torch, copies: int, iters: int) -> dict:
     torch.cuda.synchronize()
     per = e0.elapsed_time(e1) / (reps * copies) / 1e3
     del ws
-    return {"seconds_per_launch": per, "gbs": GEMV_BYTES / per / 1e9,
+    return {"seconds_per_launch": per, "gbs": nbytes / per / 1e9, "bytes_per_launch": nbytes,
             "timing": "cuda graph of launches" if graph is not None else "eager launches"}
 
 
@@ -329,22 +339,27 @@ def run_gemv_only(pkg, torch, args, world, rank) -> None:
     """Config 1 as its own line: GB/s of the GEMV over 64 distinct weight copies, each launch
     chained to the previous one (programmatic dependent launch inside one CUDA graph)."""
     peaks = load_peaks()
+    bits = args.gemv_bits
+    n, k, nbytes = gemv_shape(bits)
     barrier(torch, world)
     with ClockSampler(torch.cuda.current_device(), rank == 0) as clocks:
-        g = measure_gemv(pkg, torch, copies=64, iters=64 * max(args.steps, 10))
+        g = measure_gemv(pkg, torch, copies=64, iters=64 * max(args.steps, 10), bits=bits)
     g["seconds_per_launch"] = reduce_max(torch, [g["seconds_per_launch"]], world)[0]
-    g["gbs"] = GEMV_BYTES / g["seconds_per_launch"] / 1e9
+    g["gbs"] = nbytes / g["seconds_per_launch"] / 1e9
     if rank != 0:
         return
+    what = ("config 1, int4 x int8, 6144 x 1536" if bits == 4 else
+            "2-bit tile layout x int8, 12288 x 1536 (checkpoint consumer gate / up)")
     print(json.dumps({
-        "metric": "quant GEMV HBM GB/s (config 1, int4 x int8, 6144 x 1536)", "value": world * g["gbs"],
+        "metric": f"quant GEMV HBM GB/s ({what})", "value": world * g["gbs"],
         "unit": "GB/s", "n_gpus": world, "steps": max(args.steps, 10), "warmup": args.warmup,
         "ms_per_step": 64 * g["seconds_per_launch"] * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int4xint8 (int32 acc)", "data": "synthetic (seeded)",
-        "config": {"workload": "config 1: 64 distinct 6144x1536 int4 weight copies (302 MB > L2), one graph",
-                   "l2": "inputs larger than L2"},
+        "vs_baseline": None, "dtype": f"int{bits}xint8 (int32 acc)", "data": "synthetic (seeded)",
+        "config": {"workload": f"64 distinct {n}x{k} {bits}-bit weight copies ({64 * nbytes / 1e6:.0f} MB > L2), "
+                               "one graph", "l2": "inputs larger than L2"},
         "roofline": {"bound": "hbm", "achieved": g["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": g["gbs"] / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC,
+                     "frac": g["gbs"] / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC if bits == 4 else None,
+                     "bytes_per_launch": nbytes,
                      "peak_source": peaks["source"], "us_per_launch": g["seconds_per_launch"] * 1e6},
         "gpu_launches": 64 * max(args.steps, 10), "clocks": clocks.summary()}), flush=True)
 
@@ -384,12 +399,14 @@ def measure_prefill(pkg, torch, dev, n, steps, warmup, world, rank) -> dict:
     barrier(torch, world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev, rank == 0) as clocks:
+        torch.cuda.nvtx.range_push("timed")   # lets a profiler keep only these launches
         e0.record(stream)
         for _ in range(steps):
             ctx.kv_truncate(0, 0)
             ctx.prefill(0, prompt, 0, True)
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     # End to end (host ids in, host token out) on its own clock, without the sampler's
     # nvidia-smi processes starting inside the timed region.
     barrier(torch, world)
@@ -472,11 +489,13 @@ def measure_decode(pkg, torch, dev, seq_ids, lens, steps, warmup, world, rank, s
     barrier(torch, world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev, rank == 0) as clocks:
+        torch.cuda.nvtx.range_push("timed")    # lets a profiler keep only these launches
         e0.record(stream)
         for _ in range(steps):
             ctx.step_run_device(B)
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     dev_s = e0.elapsed_time(e1) / 1e3
     dev_tokens = ctx.step_read_tokens(B)
 
@@ -548,6 +567,8 @@ def main():
                     help="one GPU: the config 2 line alone (no config 1/3/4/5 keys)")
     ap.add_argument("--only-gemv", action="store_true",
                     help="BASELINE config 1 alone: the int4 x int8 GEMV [6144 x 1536] line")
+    ap.add_argument("--gemv-bits", type=int, default=4, choices=[2, 4],
+                    help="with --only-gemv: 2 times the checkpoint's 2-bit consumer gate / up instead")
     ap.add_argument("--batch", type=int, default=0,
                     help="a decode line of this many sequences instead of the default workloads")
     ap.add_argument("--ctx-lo", type=int, default=PROMPT,

@@ -1218,27 +1218,35 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
   constexpr int NH = 8, NC = HD / 4, QT = 2048 / HD, NP = QT * NH;   // pairs per CTA
   constexpr int PA = NP / 8;                   // score micro-tile pairs (8 pair groups)
   constexpr int KVR = HD <= 256 ? 64 : 32;     // K / V rows staged at a time
-  constexpr int LDK = HD + 4;                  // padded row (floats)
+  // Padded row (floats): a quarter warp's score loads read two adjacent rows x four 16-byte
+  // columns, and a 64-byte row shift puts those eight pieces in eight different bank groups.
+  constexpr int LDK = HD + 16;
   constexpr int PB = 8, DB = 2;                // PV micro-tile: pairs x vec4 columns
   constexpr int NDG = NC / DB;                 // PV column groups
   static_assert((NP / PB) * NDG == 256, "PV tiling covers the CTA");
   extern __shared__ __align__(16) float sm[];
   float *qs = sm;                              // [NP][HD]
-  float *kv = qs + NP * HD;                    // [KVR][LDK]
-  float *ss = kv + KVR * LDK;                  // [NP][64] scores, then probabilities
+  float *kv = qs + NP * HD;                    // [2][KVR][LDK] K / V stages, double-buffered
+  float *ss = kv + 2 * KVR * LDK;              // [NP][64] scores, then probabilities
   float *mb = ss + NP * ATT_BLK;               // [NP] block max
   float *lb = mb + NP;                         // [NP] block sum
   float *RM = lb + NP;                         // [NP] running max
   float *RL = RM + NP;                         // [NP] running sum
   float *ea = RL + NP;                         // [NP]
   float *ec = ea + NP;                         // [NP]
-  int *mode = reinterpret_cast<int *>(ec + NP);  // [NP] 0 skip, 1 copy, 2 fold
+  uint64_t *sbar = reinterpret_cast<uint64_t *>(ec + NP);   // [2] stage buffers' copies
+  int *mode = reinterpret_cast<int *>(sbar + 2);  // [NP] 0 skip, 1 copy, 2 fold
   int *qp = mode + NP;                         // [QT] positions
   int *qlo = qp + QT;                          // [QT] window start
   grid_launch_dependents();
+  const int t = threadIdx.x;
+  if (t == 0) {
+    mbar_init(&sbar[0], 1);
+    mbar_init(&sbar[1], 1);
+    mbar_fence_init();
+  }
   grid_wait();
   G4_TRACE_POINT(2100 + HD);
-  const int t = threadIdx.x;
   // The last query tiles of a chunk see the most keys: they start first (longest work first).
   const int c0 = ((int)gridDim.x - 1 - (int)blockIdx.x) * QT;
   const int nq = min(QT, a.cols - c0);
@@ -1266,6 +1274,33 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
     ulo = min(ulo, qlo[q]);
     uhi = max(uhi, qp[q]);
   }
+  // K and V rows reach shared memory by one bulk copy per row into the padded layout, a stage
+  // ahead: stage s (block b0 + s / SPB; its K halves, then its V halves) lands in buffer s & 1
+  // while stage s - 1 is computed. Only the rows some query of the tile can see are copied; the
+  // other rows of a stage keep stale values, whose scores are masked and whose V rows are never
+  // read.
+  constexpr int SPB = 2 * (ATT_BLK / KVR);     // stages per block
+  const int b0 = ulo / ATT_BLK;
+  const int nstage = (uhi / ATT_BLK - b0 + 1) * SPB;
+  auto issue = [&](int st) {
+    const int b = b0 + st / SPB, w = st % SPB, r0 = (w % (SPB / 2)) * KVR;
+    const int jb = b * ATT_BLK;
+    const int j0 = max(max(jb, ulo), jb + r0), j1 = min(min(jb + ATT_BLK - 1, uhi), jb + r0 + KVR - 1);
+    const int n = j1 >= j0 ? j1 - j0 + 1 : 0;
+    const float *src = w < SPB / 2 ? K : V;
+    float *dst = kv + (size_t)(st & 1) * KVR * LDK;
+    const int lane = t & 31;
+    if (lane == 0) mbar_expect_tx(&sbar[st & 1], (uint32_t)n * HD * 4);
+    __syncwarp();
+    for (int i = lane; i < n; i += 32)
+      bulk_g2s(dst + (size_t)(j0 + i - jb - r0) * LDK, src + (size_t)(j0 + i) * HD, HD * 4, &sbar[st & 1]);
+  };
+  // Bounded wait for stage st; on a timeout the flag is raised and the stage is used as it is.
+  auto stage_wait = [&](int st) {
+    if (!mbar_wait(&sbar[st & 1], (uint32_t)((st >> 1) & 1)) && t == 0) atomicExch(&g4_dev_error, 2);
+  };
+  if (t < 32) issue(0);
+  int stg = 0;
   // Score thread: accumulator m, pair group pg (pairs pg*PA ..), position group jg.
   const int m = t & 3, mt = t >> 2, pg = mt >> 3, jg = mt & 7;
   // PV thread: pairs pb*PB .., vec4 columns dg + NDG * d.
@@ -1282,14 +1317,11 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
     // ---- scores, KVR rows of K at a time
 #pragma unroll 1
     for (int r0 = 0; r0 < ATT_BLK; r0 += KVR) {
-      __syncthreads();   // the previous stage's rows are no longer read
-      for (int i = t; i < KVR * NC; i += 256) {
-        const int r = i / NC, k4 = i - r * NC, j = jb + r0 + r;
-        reinterpret_cast<float4 *>(kv + (size_t)r * LDK)[k4] =
-            (j >= jlo && j <= jhi) ? reinterpret_cast<const float4 *>(K + (size_t)j * HD)[k4]
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      __syncthreads();
+      __syncthreads();   // the previous stage's rows are no longer read: its buffer takes the next
+      if (t < 32 && stg + 1 < nstage) issue(stg + 1);
+      stage_wait(stg);
+      const float *kvs = kv + (size_t)(stg & 1) * KVR * LDK;
+      stg++;
       constexpr int JB = KVR / 8;               // this stage's positions per score thread
       float acc[PA][JB];
 #pragma unroll
@@ -1302,7 +1334,7 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
 #pragma unroll
         for (int x = 0; x < PA; x++) qv[x] = reinterpret_cast<const float4 *>(qs + (size_t)(pg * PA + x) * HD)[cc];
 #pragma unroll
-        for (int y = 0; y < JB; y++) kk[y] = reinterpret_cast<const float4 *>(kv + (size_t)(jg + 8 * y) * LDK)[cc];
+        for (int y = 0; y < JB; y++) kk[y] = reinterpret_cast<const float4 *>(kvs + (size_t)(jg + 8 * y) * LDK)[cc];
 #pragma unroll
         for (int x = 0; x < PA; x++)
 #pragma unroll
@@ -1352,32 +1384,60 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
     }
 #pragma unroll 1
     for (int r0 = 0; r0 < ATT_BLK; r0 += KVR) {
-      __syncthreads();   // scores / the previous V stage are no longer read
+      __syncthreads();   // scores / the previous stage are no longer read: its buffer takes the next
       const int slo = max(jlo - jb, r0), shi = min(jhi - jb, r0 + KVR - 1);
-      for (int i = t; i < KVR * NC; i += 256) {
-        const int r = i / NC, k4 = i - r * NC, jl = r0 + r;
-        reinterpret_cast<float4 *>(kv + (size_t)r * LDK)[k4] =
-            (jl >= slo && jl <= shi) ? reinterpret_cast<const float4 *>(V + (size_t)(jb + jl) * HD)[k4]
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      __syncthreads();
-#pragma unroll 2
-      for (int jl = slo; jl <= shi; jl++) {
+      if (t < 32 && stg + 1 < nstage) issue(stg + 1);
+      stage_wait(stg);
+      const float *kvs = kv + (size_t)(stg & 1) * KVR * LDK;
+      stg++;
+      // Ascending rows; the probabilities of four aligned rows come in one 16-byte load per pair.
+      auto pv_row = [&](int jl, const float *pj) {
         float4 v4[DB];
 #pragma unroll
-        for (int d = 0; d < DB; d++) v4[d] = reinterpret_cast<const float4 *>(kv + (size_t)(jl - r0) * LDK)[dg + NDG * d];
+        for (int d = 0; d < DB; d++) v4[d] = reinterpret_cast<const float4 *>(kvs + (size_t)(jl - r0) * LDK)[dg + NDG * d];
 #pragma unroll
         for (int i = 0; i < PB; i++) {
-          const float pj = ss[(pb * PB + i) * ATT_BLK + jl];
 #pragma unroll
           for (int d = 0; d < DB; d++) {
-            o[i][d].x = fmaf(pj, v4[d].x, o[i][d].x);
-            o[i][d].y = fmaf(pj, v4[d].y, o[i][d].y);
-            o[i][d].z = fmaf(pj, v4[d].z, o[i][d].z);
-            o[i][d].w = fmaf(pj, v4[d].w, o[i][d].w);
+            o[i][d].x = fmaf(pj[i], v4[d].x, o[i][d].x);
+            o[i][d].y = fmaf(pj[i], v4[d].y, o[i][d].y);
+            o[i][d].z = fmaf(pj[i], v4[d].z, o[i][d].z);
+            o[i][d].w = fmaf(pj[i], v4[d].w, o[i][d].w);
           }
-          l[i] = __fadd_rn(l[i], pj);
+          l[i] = __fadd_rn(l[i], pj[i]);
         }
+      };
+      int jl = slo;
+      for (; jl <= shi && (jl & 3); jl++) {
+        float pj[PB];
+#pragma unroll
+        for (int i = 0; i < PB; i++) pj[i] = ss[(pb * PB + i) * ATT_BLK + jl];
+        pv_row(jl, pj);
+      }
+#pragma unroll 1
+      for (; jl + 3 <= shi; jl += 4) {
+        float4 p4[PB];
+#pragma unroll
+        for (int i = 0; i < PB; i++) p4[i] = *reinterpret_cast<const float4 *>(ss + (pb * PB + i) * ATT_BLK + jl);
+        float pj[PB];
+#pragma unroll
+        for (int i = 0; i < PB; i++) pj[i] = p4[i].x;
+        pv_row(jl, pj);
+#pragma unroll
+        for (int i = 0; i < PB; i++) pj[i] = p4[i].y;
+        pv_row(jl + 1, pj);
+#pragma unroll
+        for (int i = 0; i < PB; i++) pj[i] = p4[i].z;
+        pv_row(jl + 2, pj);
+#pragma unroll
+        for (int i = 0; i < PB; i++) pj[i] = p4[i].w;
+        pv_row(jl + 3, pj);
+      }
+      for (; jl <= shi; jl++) {
+        float pj[PB];
+#pragma unroll
+        for (int i = 0; i < PB; i++) pj[i] = ss[(pb * PB + i) * ATT_BLK + jl];
+        pv_row(jl, pj);
       }
     }
     if (dg == 0) {
@@ -1445,7 +1505,8 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
 template <int HD>
 static size_t attn_prefill_smem() {
   constexpr int NP = (2048 / HD) * 8, KVR = HD <= 256 ? 64 : 32;
-  return ((size_t)NP * HD + (size_t)KVR * (HD + 4) + (size_t)NP * ATT_BLK + 7 * NP + 2 * (2048 / HD)) * 4;
+  return ((size_t)NP * HD + 2 * (size_t)KVR * (HD + 16) + (size_t)NP * ATT_BLK + 6 * NP + 4 + NP +
+          2 * (2048 / HD)) * 4;
 }
 
 cudaError_t launch_attention_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
