@@ -1213,6 +1213,24 @@ __global__ void __launch_bounds__(256) k_attn_merge(const AttnArgs a) {
 // per chunk for PA x 8 x 4 FMAs; a PV thread owns 8 pairs x 2 vec4 columns. K and V rows are
 // staged KVR at a time (all 64 at head dim 256, 32 at 512) in one padded buffer; the positions
 // of score group jg are jg, jg + 8, ... so the padded rows a warp reads fall in distinct banks.
+// Four consecutive outputs k0 .. k0 + 3 of column col, snapped to the next linear's codes
+// (srq_code_r, the snap every prologue uses).
+// k0 is a multiple of 4: K order takes one 32-bit store; the int4 GEMV's order keeps codes k0 and
+// k0 + 2 adjacent, and k0 + 1 and k0 + 3 (two 16-bit stores, as the GEMV prologue writes them).
+__device__ __forceinline__ void attn_codes4(const AttnCodes &cd, int col, int k0, float4 v) {
+  if (!cd.out) return;
+  const float r = __fdiv_rn(1.0f, cd.scale);
+  const uint32_t q0 = srq_code_r(v.x, cd.scale, r) & 255, q1 = srq_code_r(v.y, cd.scale, r) & 255;
+  const uint32_t q2 = srq_code_r(v.z, cd.scale, r) & 255, q3 = srq_code_r(v.w, cd.scale, r) & 255;
+  uint8_t *o = cd.out + (size_t)col * cd.ld;
+  if (cd.bits == 4) {
+    *reinterpret_cast<uint16_t *>(o + code_pos(k0, 4)) = (uint16_t)(q0 | (q2 << 8));
+    *reinterpret_cast<uint16_t *>(o + code_pos(k0 + 1, 4)) = (uint16_t)(q1 | (q3 << 8));
+  } else {
+    *reinterpret_cast<uint32_t *>(o + k0) = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
   constexpr int NH = 8, NC = HD / 4, QT = 2048 / HD, NP = QT * NH;   // pairs per CTA
@@ -1497,6 +1515,7 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
         r.z = __fdiv_rn(O[i][d].z, L);
         r.w = __fdiv_rn(O[i][d].w, L);
         reinterpret_cast<float4 *>(a.out + (size_t)(c0 + q) * NH * HD + (size_t)h * HD)[dg + NDG * d] = r;
+        attn_codes4(a.codes, c0 + q, h * HD + 4 * (dg + NDG * d), r);
       }
     }
   }
@@ -1740,20 +1759,51 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     const int r0 = b * ATT_BLK + ph * VROWS;
     const int ja = max(j0, r0), jb = min(j1, r0 + VROWS - 1);
     if (pv) {
-#pragma unroll 4
-      for (int j = ja; j <= jb; j++) {
-        const int jl = j - b * ATT_BLK;
+      // Ascending rows; the probabilities of four aligned rows come in one 16-byte load per head.
+      auto pv_row = [&](int j, const float *pj) {
         const float *vrow = cur && j == p ? vn : vs + (size_t)(j - r0) * HD;
         const float4 v4 = reinterpret_cast<const float4 *>(vrow)[dc];
 #pragma unroll
         for (int hh = 0; hh < HPT; hh++) {
-          const float pj = ps[(hg * HPT + hh) * ATT_BLK + jl];
-          o[hh].x = fmaf(pj, v4.x, o[hh].x);
-          o[hh].y = fmaf(pj, v4.y, o[hh].y);
-          o[hh].z = fmaf(pj, v4.z, o[hh].z);
-          o[hh].w = fmaf(pj, v4.w, o[hh].w);
-          l[hh] = __fadd_rn(l[hh], pj);
+          o[hh].x = fmaf(pj[hh], v4.x, o[hh].x);
+          o[hh].y = fmaf(pj[hh], v4.y, o[hh].y);
+          o[hh].z = fmaf(pj[hh], v4.z, o[hh].z);
+          o[hh].w = fmaf(pj[hh], v4.w, o[hh].w);
+          l[hh] = __fadd_rn(l[hh], pj[hh]);
         }
+      };
+      const float *pbase = ps + (size_t)hg * HPT * ATT_BLK - b * ATT_BLK;   // indexed by j
+      int j = ja;
+      for (; j <= jb && (j & 3); j++) {
+        float pj[HPT];
+#pragma unroll
+        for (int hh = 0; hh < HPT; hh++) pj[hh] = pbase[hh * ATT_BLK + j];
+        pv_row(j, pj);
+      }
+#pragma unroll 1
+      for (; j + 3 <= jb; j += 4) {
+        float4 p4[HPT];
+#pragma unroll
+        for (int hh = 0; hh < HPT; hh++) p4[hh] = *reinterpret_cast<const float4 *>(pbase + hh * ATT_BLK + j);
+        float pj[HPT];
+#pragma unroll
+        for (int hh = 0; hh < HPT; hh++) pj[hh] = p4[hh].x;
+        pv_row(j, pj);
+#pragma unroll
+        for (int hh = 0; hh < HPT; hh++) pj[hh] = p4[hh].y;
+        pv_row(j + 1, pj);
+#pragma unroll
+        for (int hh = 0; hh < HPT; hh++) pj[hh] = p4[hh].z;
+        pv_row(j + 2, pj);
+#pragma unroll
+        for (int hh = 0; hh < HPT; hh++) pj[hh] = p4[hh].w;
+        pv_row(j + 3, pj);
+      }
+      for (; j <= jb; j++) {
+        float pj[HPT];
+#pragma unroll
+        for (int hh = 0; hh < HPT; hh++) pj[hh] = pbase[hh * ATT_BLK + j];
+        pv_row(j, pj);
       }
     }
   }
@@ -1768,6 +1818,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
         r.z = __fdiv_rn(o[hh].z, l[hh]);
         r.w = __fdiv_rn(o[hh].w, l[hh]);
         reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD + (size_t)h * HD)[dc] = r;
+        attn_codes4(a.codes, c, h * HD + 4 * dc, r);
       }
     }
     return;
@@ -1894,6 +1945,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       r.z = __fdiv_rn(O[i].z, L);
       r.w = __fdiv_rn(O[i].w, L);
       reinterpret_cast<float4 *>(a.out + (size_t)c * NH * HD + (size_t)h0 * HD)[t + 256 * i] = r;
+      attn_codes4(a.codes, c, h0 * HD + 4 * (t + 256 * i), r);
     }
   }
   if (t == 0) *cnt = 0;

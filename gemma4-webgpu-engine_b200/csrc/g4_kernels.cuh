@@ -188,6 +188,13 @@ struct AttnPro {
 };
 cudaError_t launch_attn_prologue(const AttnPro &a, cudaStream_t st, bool pdl);
 
+// The next linear's int8 input codes, written by an attention kernel beside its f32 output
+// (o_proj's snap to its input scale): out [cols][ld] at code_pos(k, bits) (bits 4: the int4
+// streaming GEMV's dp4a order; 8: K order, for the tensor-core path). out NULL: not written.
+struct AttnCodes {
+  uint8_t *out; int ld; float scale; int bits;
+};
+
 struct AttnArgs {
   int cols, heads, hd, window, max_ctx;
   int kv_cap;                        // > 0: attend j < kv_cap as well as j <= p
@@ -197,6 +204,7 @@ struct AttnArgs {
   int max_blocks;                    // partial slots per column
   float *part_o; float *part_m; float *part_l;
   float *out;                        // [cols, heads * hd]
+  AttnCodes codes;                   // prefill kernel only
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl);
 // The same attention for a prefill chunk (columns = consecutive positions of one sequence),
@@ -271,6 +279,7 @@ struct AttnDec {
   int32_t *counter;                  // [cols][8]
   float *out;                        // [cols, 8 * hd]
   float eps;
+  AttnCodes codes;
 };
 cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl);
 

@@ -146,6 +146,7 @@ struct g4_ctx {
   int cur_parts = 0;
   uint8_t *codes_mlp = nullptr;     // down_proj input codes [maxc][ffn_max]
   uint8_t *codes_ple = nullptr;     // per_layer_projection input codes [maxc][PD]
+  uint8_t *codes_attn = nullptr;    // o_proj input codes written by attention [maxc][heads * hd]
   int ffn_max = 0;
   float *logits = nullptr;
   float *head_pv = nullptr;
@@ -595,6 +596,7 @@ static int alloc_runtime(g4_ctx *ctx) {
   ctx->ffn_max = (ffn + 15) & ~15;
   CK(ctx_malloc((void **)&ctx->codes_mlp, (size_t)maxc * ctx->ffn_max));
   CK(ctx_malloc((void **)&ctx->codes_ple, (size_t)maxc * ctx->PD));
+  CK(ctx_malloc((void **)&ctx->codes_attn, (size_t)maxc * a.query_heads * std::max(a.sliding_head_dim, a.global_head_dim)));
   CK(ctx_malloc((void **)&ctx->att_count, (size_t)maxc * 8 * 4));
   CK(cudaMemset(ctx->att_count, 0, (size_t)maxc * 8 * 4));
   // Logit rows: one per sequence of a decode batch, and at least G4_VERIFY_COLS for the
@@ -713,6 +715,7 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   cudaFree(ctx->head_pi);
   cudaFree(ctx->att_count);
   cudaFree(ctx->codes_mlp);
+  cudaFree(ctx->codes_attn);
   for (int i = 0; i < 3; i++) cudaFree(ctx->gq[i]);
   cudaFree(ctx->gpv);
   cudaFree(ctx->gpi);
@@ -728,6 +731,7 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
   cudaFreeHost(ctx->h_tok);
   if (ctx->st) cudaStreamDestroy(ctx->st);
   delete ctx;
+  cudaGetLastError();   // a failed release must not surface in the next context's first launch
 }
 
 extern "C" int g4_ctx_memory(const g4_ctx *ctx, uint64_t *w, uint64_t *kvb, uint64_t *o) {
@@ -1090,7 +1094,10 @@ static const CUtensorMap *codes_tmap(g4_ctx *ctx, int buf, int K, int bn) {
 // The tensor-core path of a linear launch group: the prologue runs once per column into int8
 // codes (one code vector per distinct input scale), then one tcgen05 GEMM per segment.
 static bool gemm_eligible(g4_ctx *ctx, std::initializer_list<Seg> segs, int cols, const GemvArgs &p) {
-  if (cols < ctx->gemm_min_cols || p.pro == PRO_CODES || p.epi != EPI_Y || p.pair) return false;
+  // Precomputed codes reach the tensor-core path only in its own code buffer (attention writes
+  // o_proj's there).
+  if (cols < ctx->gemm_min_cols || (p.pro == PRO_CODES && p.src_codes != ctx->gq[0]) || p.epi != EPI_Y || p.pair)
+    return false;
   for (auto &sg : segs)
     if (!sg.lin->has_tm || sg.lin->in_scale == 0.0f || sg.lin->K % 128 != 0) return false;
   return true;
@@ -1114,9 +1121,11 @@ static int run_linear_gemm(g4_ctx *ctx, std::initializer_list<Seg> segs, int col
   for (auto &sg : segs) sh = sh && sg.lin->w8 && sg.lin->has_tm8;
   auto wmap = [&](const Linear &l) -> const CUtensorMap & { return sh ? l.tmw8 : l.tmw; };
   auto wbits = [&](const Linear &l) { return sh ? 8 : l.bits; };
-  CK(launch_quantize(q, ctx->gq[0], ctx->gq_ld, sc[0], nsc > 1 ? ctx->gq[1] : nullptr, nsc > 1 ? sc[1] : 0.0f,
-                     ctx->st, true));
-  note_launch(ctx, "quantize", seg_roles(segs));
+  if (q.pro != PRO_CODES) {
+    CK(launch_quantize(q, ctx->gq[0], ctx->gq_ld, sc[0], nsc > 1 ? ctx->gq[1] : nullptr, nsc > 1 ? sc[1] : 0.0f,
+                       ctx->st, true));
+    note_launch(ctx, "quantize", seg_roles(segs));
+  }
   if (nsc > 2) {
     q.hidden_out = nullptr;
     CK(launch_quantize(q, ctx->gq[2], ctx->gq_ld, sc[2], nullptr, 0.0f, ctx->st, true));
@@ -1378,6 +1387,14 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       if (rc) return rc;
       if (L > 0) cur ^= 1;
     }
+    // o_proj's input codes come straight from the attention kernel (fused decode, query-tiled
+    // prefill): into the tensor-core path's code buffer, or in the streaming GEMV's order.
+    const bool o_gemm = gemm_eligible(ctx, {{&ly.o, ctx->proj}}, cols, pro_args(PRO_X));
+    AttnCodes oc;
+    memset(&oc, 0, sizeof(oc));
+    if (ly.o.in_scale != 0.0f && (fused_attn || cols > 1) && (o_gemm || ly.o.bits == 4 || ly.o.bits == 8))
+      oc = o_gemm ? AttnCodes{ctx->gq[0], ctx->gq_ld, ly.o.in_scale, 8}
+                  : AttnCodes{ctx->codes_attn, qrows, ly.o.in_scale, ly.o.bits};
     // ---- decode steps: prologue, attention and merge in one launch per layer
     if (fused_attn) {
       AttnDec ad;
@@ -1406,6 +1423,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       ad.counter = ctx->att_count;
       ad.out = ctx->attn;
       ad.eps = eps;
+      ad.codes = oc;
       CK(launch_attn_decode(ad, ctx->st, true));
       note_launch(ctx, "attention-decode", layer_role(L, ly.producer));
     }
@@ -1458,6 +1476,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       at.part_l = ctx->part_l;
       at.out = ctx->attn;
       if (cols > 1) {
+        at.codes = oc;
         // A prefill chunk: consecutive positions of one sequence, query-tiled.
         CK(launch_attention_prefill(at, ctx->st, true));
         note_launch(ctx, "attention-prefill", layer_role(L, false));
@@ -1469,9 +1488,14 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     }
     // ---- o_proj
     {
-      GemvArgs p = pro_args(PRO_X);
+      GemvArgs p = pro_args(oc.out ? PRO_CODES : PRO_X);
       p.src = ctx->attn;
       p.ld_src = qrows;
+      if (oc.out) {
+        p.src = nullptr;
+        p.src_codes = oc.out;
+        p.ld_codes = oc.ld;
+      }
       if ((rc = run_linear(ctx, {{&ly.o, ctx->proj}}, cols, p, false, {wref(ly.down)}))) return rc;
     }
     // gelu(gate) * up is formed once, by the gate/up launch (each CTA owns the same rows of
