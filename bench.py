@@ -258,24 +258,29 @@ def gemv_shape(bits: int) -> tuple:
     return n, k, n * k * bits // 8 + 2 * n + k + 2 * n
 
 
-def measure_gemv(pkg, torch, copies: int, iters: int, bits: int = 4) -> dict:
+def measure_gemv(pkg, torch, copies: int, iters: int, bits: int = 4, codes_input: bool = True) -> dict:
     """the int4 x int8 GEMV [6144 x 1536] (or the 2-bit line, gemv_shape),
     timed over `copies` distinct weight buffers (together larger than L2) with CUDA events on the
-    launching stream."""
+    launching stream. The activations are the config's int8 codes (scale 0.02) fed to
+    g4_op_qgemv_codes, or (codes_input False) the same values as f32 through g4_op_qgemv, whose
+    prologue snaps them."""
     lib = pkg._abi.load()
     n, k, nbytes = gemv_shape(bits)
     g = torch.Generator(device="cuda").manual_seed(SEED)
     ws = [torch.randint(0, 256, (n * k * bits // 8,), dtype=torch.uint8, device="cuda", generator=g)
           for _ in range(copies)]
     sc = (torch.rand(n, device="cuda", generator=g) * 9e-3 + 1e-3).half().view(torch.int16)
-    x = (torch.randint(-127, 128, (k,), device="cuda", generator=g).float() * 0.02)
+    codes = torch.randint(-127, 128, (k,), device="cuda", generator=g).to(torch.int8)
+    x = codes.float() * 0.02
     y = torch.empty(n, device="cuda")
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
+    fn = lib.g4_op_qgemv_codes if codes_input else lib.g4_op_qgemv
+    src = codes if codes_input else x
+
     def launch(w):
-        rc = lib.g4_op_qgemv(w.data_ptr(), sc.data_ptr(), x.data_ptr(), 0.02, 0.0, bits, n, k, 1,
-                             y.data_ptr(), None, sp)
+        rc = fn(w.data_ptr(), sc.data_ptr(), src.data_ptr(), 0.02, 0.0, bits, n, k, 1, y.data_ptr(), None, sp)
         assert rc == 0, pkg._abi.last_error()
 
     for w in ws[:8]:
@@ -343,7 +348,8 @@ def run_gemv_only(pkg, torch, args, world, rank) -> None:
     n, k, nbytes = gemv_shape(bits)
     barrier(torch, world)
     with ClockSampler(torch.cuda.current_device(), rank == 0) as clocks:
-        g = measure_gemv(pkg, torch, copies=64, iters=64 * max(args.steps, 10), bits=bits)
+        g = measure_gemv(pkg, torch, copies=64, iters=64 * max(args.steps, 10), bits=bits,
+                         codes_input=args.gemv_input == "codes")
     g["seconds_per_launch"] = reduce_max(torch, [g["seconds_per_launch"]], world)[0]
     g["gbs"] = nbytes / g["seconds_per_launch"] / 1e9
     if rank != 0:
@@ -356,7 +362,9 @@ def run_gemv_only(pkg, torch, args, world, rank) -> None:
         "ms_per_step": 64 * g["seconds_per_launch"] * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": f"int{bits}xint8 (int32 acc)", "data": "synthetic (seeded)",
         "config": {"workload": f"64 distinct {n}x{k} {bits}-bit weight copies ({64 * nbytes / 1e6:.0f} MB > L2), "
-                               "one graph", "l2": "inputs larger than L2"},
+                               "one graph", "l2": "inputs larger than L2",
+                   "input": "int8 activation codes (g4_op_qgemv_codes)" if args.gemv_input == "codes"
+                            else "f32 activations snapped in the prologue (g4_op_qgemv)"},
         "roofline": {"bound": "hbm", "achieved": g["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": g["gbs"] / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC if bits == 4 else None,
                      "bytes_per_launch": nbytes,
@@ -569,6 +577,8 @@ def main():
                     help="BASELINE config 1 alone: the int4 x int8 GEMV [6144 x 1536] line")
     ap.add_argument("--gemv-bits", type=int, default=4, choices=[2, 4],
                     help="with --only-gemv: 2 times the checkpoint's 2-bit consumer gate / up instead")
+    ap.add_argument("--gemv-input", default="codes", choices=["codes", "f32"],
+                    help="with --only-gemv: int8 activation codes (config 1) or f32 activations")
     ap.add_argument("--batch", type=int, default=0,
                     help="a decode line of this many sequences instead of the default workloads")
     ap.add_argument("--ctx-lo", type=int, default=PROMPT,
@@ -645,7 +655,8 @@ def run_decode(pkg, torch, args, world, rank, dev) -> None:
         config = line_config(1)
         scaling = "weak"
     gemv = measure_gemv(pkg, torch, copies=64, iters=640)
-    gemv_s = reduce_max(torch, [gemv["seconds_per_launch"]], world)[0]
+    gemv_f32 = measure_gemv(pkg, torch, copies=64, iters=640, codes_input=False)
+    gemv_s, gemv_f32_s = reduce_max(torch, [gemv["seconds_per_launch"], gemv_f32["seconds_per_launch"]], world)
     gemv_gbs = GEMV_BYTES / gemv_s / 1e9
     line = {
         "metric": METRIC, "value": main_s["value"], "unit": "tokens/s", "n_gpus": world,
@@ -659,7 +670,10 @@ def run_decode(pkg, torch, args, world, rank, dev) -> None:
                      "achieved": gemv_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": gemv_gbs / peaks["hbm_gbs"], "traffic": GEMV_TRAFFIC,
                      "peak_source": peaks["source"], "bytes_per_launch": GEMV_BYTES,
-                     "us_per_launch": gemv_s * 1e6, "timing": gemv["timing"]},
+                     "us_per_launch": gemv_s * 1e6, "timing": gemv["timing"],
+                     "input": "int8 activation codes (config 1), g4_op_qgemv_codes",
+                     "f32_input": {"achieved": GEMV_BYTES / gemv_f32_s / 1e9, "us_per_launch": gemv_f32_s * 1e6,
+                                   "via": "g4_op_qgemv (f32 x snapped in the prologue)"}},
         "clocks": main_s["clocks"],
     }
     if box:
@@ -671,7 +685,8 @@ def run_decode(pkg, torch, args, world, rank, dev) -> None:
         # One GPU, default run: BASELINE configs 1, 3, 4 and 5 as extra keys beside config 2.
         line["config1_gemv"] = {"value": gemv_gbs, "unit": "GB/s", "frac": gemv_gbs / peaks["hbm_gbs"],
                                 "us_per_launch": gemv_s * 1e6,
-                                "workload": "64 distinct 6144x1536 int4 weight copies, one graph"}
+                                "workload": "64 distinct 6144x1536 int4 weight copies, one graph, int8 activation codes",
+                                "f32_input_gbs": GEMV_BYTES / gemv_f32_s / 1e9}
         rng = np.random.default_rng(SEED)
         b64_lens = [int(v) for v in rng.integers(B64_LO, B64_HI + 1, B64)]
         r4 = measure_decode(pkg, torch, dev, list(range(B64)), b64_lens, B64_STEPS, args.warmup, world, rank)

@@ -85,6 +85,7 @@ SIGNATURES = {
     "g4_last_launches": (C.c_int, [_vp, _i32p]),
     "g4_last_launch_list": (C.c_int, [_vp, C.c_char_p, _u64, _u64p]),
     "g4_op_qgemv": (C.c_int, [_vp, _vp, _vp, _f, _f, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "g4_op_qgemv_codes": (C.c_int, [_vp, _vp, _vp, _f, _f, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     "g4_op_qgemm": (C.c_int, [_vp, _vp, _vp, _f, _f, _i32, _i32, _i32, _i32, _vp, _vp]),
     "g4_op_qgemv_gelu": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _f, _f, _i32, _i32, _i32, _i32,
                                    _vp, _vp]),

@@ -82,6 +82,12 @@ __device__ __forceinline__ int gemv_prologue_col(const GemvArgs &a, const ProGai
 #pragma unroll
     for (int i = 0; i < 4; i++)
       if (t + 256 * i < n16) {
+        if (BITS == 4 && a.codes_plain) {
+          // K order -> the dp4a order of each 8-code group (code_pos): even codes, then odd.
+          const uint32_t x = v[i].x, y = v[i].y, z = v[i].z, w = v[i].w;
+          v[i] = make_uint4(__byte_perm(x, y, 0x6420), __byte_perm(x, y, 0x7531),
+                            __byte_perm(z, w, 0x6420), __byte_perm(z, w, 0x7531));
+        }
         reinterpret_cast<uint4 *>(codes)[t + 256 * i] = v[i];
         xs = dp4a_ss(v[i].x, 0x01010101, xs);
         xs = dp4a_ss(v[i].y, 0x01010101, xs);

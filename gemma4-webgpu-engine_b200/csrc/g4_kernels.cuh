@@ -113,6 +113,7 @@ struct GemvArgs {
   const float *epi_up; int epi_ld_up; int epi_up_off;
   uint8_t *codes_out; int codes_ld; float codes_scale; int codes_bits;
   const uint8_t *src_codes; int ld_codes;   // PRO_CODES
+  int codes_plain;   // PRO_CODES at 4 bits: src_codes in K order (the operator API), else dp4a order
 };
 
 // The streaming GEMV: one CTA per SM (or fewer), each streaming a contiguous row slice of one

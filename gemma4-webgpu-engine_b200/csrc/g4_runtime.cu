@@ -1952,6 +1952,47 @@ extern "C" int g4_op_qgemv(const void *wq, const void *scales, const float *x, f
   return G4_OK;
 }
 
+extern "C" int g4_op_qgemv_codes(const void *wq, const void *scales, const int8_t *codes, float in_scale,
+                                 float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
+                                 int32_t *acc_out, void *stream) {
+  if (!wq || !scales || !codes || !y) return fail(nullptr, G4_ERR_INVALID, "g4_op_qgemv_codes: null pointer");
+  if (bits != 2 && bits != 4 && bits != 8) return fail(nullptr, G4_ERR_INVALID, "bits must be 2, 4 or 8");
+  if (in_scale == 0.0f) return fail(nullptr, G4_ERR_INVALID, "int8 activation codes need their scale (in_scale != 0)");
+  const int span = bits == 2 ? 512 : (bits == 4 ? 256 : 128);
+  if (N < 1 || K < span || K % span != 0 || cols < 1)
+    return fail(nullptr, G4_ERR_INVALID, "qgemv-%dbit needs K a multiple of %d, got %d (N %d, cols %d)", bits, span, K, N, cols);
+  if (K > 16384 || (bits != 2 && (size_t)K * bits / 8 > 4096))
+    return fail(nullptr, G4_ERR_UNSUPPORTED, "K %d too wide", K);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int sms = device_sms();
+  for (int c0 = 0; c0 < cols; c0 += 8) {
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.pro = PRO_CODES;
+    a.alpha = 1.0f;
+    a.K = K;
+    a.cols = std::min(8, cols - c0);
+    a.nseg = 1;
+    a.seg[0].w = (const uint8_t *)wq;
+    a.seg[0].s = (const uint16_t *)scales;
+    a.seg[0].y = y + (size_t)c0 * N;
+    a.seg[0].acc_out = acc_out ? acc_out + (size_t)c0 * N : nullptr;
+    a.seg[0].N = N;
+    a.seg[0].in_scale = in_scale;
+    a.seg[0].out_scale = out_scale;
+    a.src_codes = (const uint8_t *)codes + (size_t)c0 * K;
+    a.ld_codes = K;
+    a.codes_plain = 1;
+    if (bits == 2)
+      gemv2_partition(a, 2 * sms);
+    else
+      gemv_stream_partition(a, 2 * sms);
+    OPCK(launch_gemv(a, bits, st, true));
+  }
+  OPCK(cudaGetLastError());
+  return G4_OK;
+}
+
 extern "C" int g4_op_qgemm(const void *wq, const void *scales, const float *x, float in_scale,
                            float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
                            void *stream) {

@@ -296,6 +296,17 @@ int g4_op_qgemv(const void *wq, const void *scales, const float *x, float in_sca
                 int32_t *acc_out, void *stream);
 
 /*
+ * The same linear on int8 activation codes (the wNa8o8 form of BASELINE config 1: the column
+ * already snapped, x = codes * in_scale): codes int8 [cols, K] in K order, in_scale != 0. The
+ * accumulators and outputs equal g4_op_qgemv's on x = codes * in_scale; the prologue only loads
+ * the codes (no snap).
+ */
+int g4_op_qgemv_codes(const void *wq, const void *scales, const int8_t *codes, float in_scale,
+                      float out_scale, int32_t bits, int32_t N, int32_t K, int32_t cols, float *y,
+                      int32_t *acc_out, void *stream);
+
+/*
+ * The 2-bit family's layout change/*
  * The 2-bit family's layout change (src/kernels/repack.ts:17-209, src/kernels/qlayout.ts:186-227):
  * to_rows 0 repacks the checkpoint's rows (row r: K / 16 u32 words, code k at bits 2 (k % 16) of
  * word k / 16) into the interleaved tiles (word k of tile t holds row 16 t + i at bits 2 i, rows

@@ -60,6 +60,35 @@ def x_on_grid(cols, K, scale):
 
 
 @pytest.mark.parametrize("bits,N,K,cols", [
+    (4, 6144, 1536, 1), (4, 1000, 1536, 3), (4, 1536, 6144, 1), (4, 777, 256, 9),
+    (8, 256, 1536, 1), (8, 1536, 256, 5), (2, 12288, 1536, 1), (2, 1000, 1024, 3),
+])
+def test_qgemv_codes_input(cuda, lib, O, bits, N, K, cols):
+    """g4_op_qgemv_codes (int8 activation codes in K order, BASELINE config 1's wNa8o8 form) gives
+    g4_op_qgemv's accumulators and outputs on x = codes * in_scale, bit for bit (the oracle's
+    qgemv on the same x checks both)."""
+    wbytes = (N + 15) // 16 * K * 4 if bits == 2 else N * K * bits // 8
+    wq = RNG.integers(0, 256, wbytes, dtype=np.uint8)
+    sc = f16_scales(N)
+    codes = RNG.integers(-127, 128, (cols, K)).astype(np.int8)
+    in_s, out_s = np.float32(0.02), np.float32(0.0625)
+    x = (codes.astype(np.float32) * in_s).astype(np.float32)
+    dw, ds, dx, dc = dev(cuda, wq), dev(cuda, sc), dev(cuda, x), dev(cuda, codes)
+    outs = []
+    for fn, src in (("g4_op_qgemv", dx), ("g4_op_qgemv_codes", dc)):
+        dy = cuda.zeros((cols, N), dtype=cuda.float32, device="cuda")
+        dacc = cuda.zeros((cols, N), dtype=cuda.int32, device="cuda")
+        call(lib, fn, p(dw), p(ds), p(src), in_s, out_s, bits, N, K, cols, p(dy), p(dacc), None)
+        outs.append((host(dacc), host(dy)))
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(outs[0][1].view(np.uint32), outs[1][1].view(np.uint32))
+    if bits != 2:
+        y_ref, acc_ref = O.qgemv(wq, sc, x, in_s, out_s, bits, N, K, cols)
+        np.testing.assert_array_equal(outs[1][0], acc_ref)
+        np.testing.assert_array_equal(outs[1][1].view(np.uint32), y_ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("bits,N,K,cols", [
     (4, 6144, 1536, 1), (4, 1000, 1536, 3), (4, 1536, 6144, 1), (4, 1536, 2048, 2),
     (4, 1536, 4096, 1), (4, 777, 256, 8), (4, 2560, 1536, 13),
     (8, 256, 1536, 1), (8, 1536, 256, 5), (8, 300, 1536, 9),
