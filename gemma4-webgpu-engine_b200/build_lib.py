@@ -15,7 +15,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libgemma4_cuda.so"
-SOURCES = ["g4_kernels.cu", "g4_gemv2.cu", "g4_gemm.cu", "g4_runtime.cu", "g4_noalloc.cu"]
+SOURCES = ["g4_kernels.cu", "g4_gemv2.cu", "g4_gemm.cu", "g4_ple.cu", "g4_runtime.cu", "g4_noalloc.cu"]
 HEADERS = ["g4_device.cuh", "g4_kernels.cuh", "g4_gemv.cuh"]
 
 NVCC_FLAGS = [

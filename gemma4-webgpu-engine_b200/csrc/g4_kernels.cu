@@ -889,12 +889,12 @@ cudaError_t launch_dense_bf16(const uint16_t *w, const float *x, int ld_x, float
     const int row_ctas = K <= 1536 ? (N + 31) / 32 : (N + 15) / 16;
     int gy = 1;
     double best = 0.0;
-    for (int y = 1; y <= 16 && (y == 1 || cols / y >= 16); y++) {
-      const int ctas = row_ctas * y, waves = (ctas + sms - 1) / sms;
-      const double eff = (double)ctas / ((double)waves * sms) - 0.01 * y;   // small cost per split
+    for (int split = 1; split <= 16 && (split == 1 || cols / split >= 16); split++) {
+      const int ctas = row_ctas * split, waves = (ctas + sms - 1) / sms;
+      const double eff = (double)ctas / ((double)waves * sms) - 0.01 * split;   // small cost per split
       if (eff > best) {
         best = eff;
-        gy = y;
+        gy = split;
       }
     }
     if (K <= 1536) {

@@ -129,6 +129,7 @@ cudaError_t launch_wait_probe(const void *src, int bytes, int missing, int limit
 // Diagnostic build only: the (kernel id, time) records since the last call, then cleared.
 int trace_take(unsigned long long *out, int max_records);
 int gemm_trace_take(unsigned long long *out, int max_records);
+int ple_trace_take(unsigned long long *out, int max_records);
 #endif
 
 // A quantized linear launch (the streaming kernel, or the f32 path when in_scale is 0).
@@ -283,6 +284,29 @@ struct AttnDec {
   AttnCodes codes;
 };
 cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl);
+
+// The per-layer-input tail of a decode batch (g4_ple.cu): per_layer_input_gate, gelu(gate) x the
+// layer's per-layer input, per_layer_projection, on one cluster of 16 CTAs. Both linears int8,
+// PD = 256, 1 <= cols <= 64; codes: the gate's input codes [cols][ld_codes] in K order.
+struct PleArgs {
+  // The post-FFN norm-residual: h = res + rms_norm(src) * g1 (written to hidden_out by one CTA)
+  // is the gate's input.
+  const float *src; int ld_src;
+  const float *res; int ld_res;                              // hidden_out has ld_res too
+  const float *g1; float eps;
+  float *hidden_out;
+  const uint8_t *w1; const uint16_t *s1; float in1, out1;   // per_layer_input_gate [PD][H]
+  const uint8_t *w2; const uint16_t *s2; float in2, out2;   // per_layer_projection [H][PD]
+  const float *ple_in; int ld_ple; int ple_off;              // per-layer inputs [cols][ld_ple]
+  float *y; int ld_y;                                        // [cols][H]
+  const void *prefetch[4]; uint64_t prefetch_bytes[4];       // later weights to pull into L2
+  int cols, H;
+};
+// The per-layer-input tail of a decode step of 1..16 columns as one cluster launch (g4_ple.cu).
+bool ple_block_fits(int H, int PD, int cols);
+size_t ple_block_smem(int H, int cols);
+cudaError_t launch_ple_block(const PleArgs &a, cudaStream_t st, bool pdl);
+int ple_error_take();
 
 // Decode chain: position[c] += 1 after a step (its argmax already sits in the token slot).
 cudaError_t launch_advance(int32_t *pos, int cols, cudaStream_t st, bool pdl);

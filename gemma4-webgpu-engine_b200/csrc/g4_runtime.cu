@@ -147,6 +147,7 @@ struct g4_ctx {
   uint8_t *codes_mlp = nullptr;     // down_proj input codes [maxc][ffn_max]
   uint8_t *codes_ple = nullptr;     // per_layer_projection input codes [maxc][PD]
   uint8_t *codes_attn = nullptr;    // o_proj input codes written by attention [maxc][heads * hd]
+  int ple_block = -1;               // the fused per-layer-input tail fits this device (-1: not asked)
   int ffn_max = 0;
   float *logits = nullptr;
   float *head_pv = nullptr;
@@ -681,6 +682,7 @@ extern "C" int g4_trace_reset(void) {
   unsigned long long dummy[2];
   trace_take(dummy, 0);
   gemm_trace_take(dummy, 0);
+  ple_trace_take(dummy, 0);
   return 0;
 }
 #endif
@@ -694,6 +696,8 @@ extern "C" void g4_ctx_destroy(g4_ctx *ctx) {
       for (int i = 0; i < n; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
       const int gm = gemm_trace_take(rec.data(), 1 << 15);
       for (int i = 0; i < gm; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
+      const int pm = ple_trace_take(rec.data(), 1 << 15);
+      for (int i = 0; i < pm; i++) fprintf(f, "%llu %llu\n", rec[2 * i], rec[2 * i + 1]);
       fclose(f);
     }
   }
@@ -1551,8 +1555,52 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
                             nx ? wref(nx->v) : WRef{nullptr, 0}})))
         return rc;
     }
+    // A decode step of 1..16 columns on the GEMV path runs the per-layer-input tail (post-FFN
+    // norm-residual, gate, gelu x per-layer input, projection) as one cluster launch
+    // (g4_ple.cu); it gives the two GEMVs' bits.
+    bool ple_fused = ple_codes && cols <= 16 && ly.pleg.bits == 8 && ly.plep.bits == 8 &&
+                     ly.pleg.N == PD && ly.pleg.K == H && ly.plep.N == H && ly.plep.K == PD;
+    if (ple_fused && ctx->ple_block < 0) ctx->ple_block = ple_block_fits(H, PD, 16) ? 1 : 0;
+    ple_fused = ple_fused && ctx->ple_block == 1;
+    if (ple_fused) {
+      PleArgs pa;
+      memset(&pa, 0, sizeof(pa));
+      pa.src = ctx->proj;
+      pa.ld_src = H;
+      pa.res = ctx->res[cur];
+      pa.ld_res = H;
+      pa.g1 = ly.ln_post_ffn;
+      pa.eps = eps;
+      pa.hidden_out = ctx->res[cur ^ 1];
+      pa.w1 = ly.pleg.w;
+      pa.s1 = ly.pleg.s;
+      pa.in1 = ly.pleg.in_scale;
+      pa.out1 = ly.pleg.out_scale;
+      pa.w2 = ly.plep.w;
+      pa.s2 = ly.plep.s;
+      pa.in2 = ly.plep.in_scale;
+      pa.out2 = ly.plep.out_scale;
+      pa.ple_in = ctx->ple_in;
+      pa.ld_ple = ctx->ple_cols;
+      pa.ple_off = L * PD;
+      pa.y = ctx->proj;
+      pa.ld_y = H;
+      pa.cols = cols;
+      pa.H = H;
+      const Layer *nx = L + 1 < n_layers ? &ctx->layers[L + 1] : nullptr;
+      if (nx) {
+        const WRef pf[3] = {wref(nx->o), wref(nx->gate), wref(nx->up)};
+        for (int i = 0; i < 3; i++) {
+          pa.prefetch[i] = pf[i].p;
+          pa.prefetch_bytes[i] = pf[i].bytes;
+        }
+      }
+      CK(launch_ple_block(pa, ctx->st, true));
+      note_launch(ctx, "ple-block", short_module(ly.pleg.module) + "," + short_module(ly.plep.module));
+      cur ^= 1;
+    }
     // ---- per_layer_input_gate over the post-FFN norm-residual (the residual itself)
-    {
+    if (!ple_fused) {
       GemvArgs p = pro_args(PRO_NORMRES);
       p.src = ctx->proj;
       p.ld_src = H;
@@ -1578,7 +1626,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
       cur ^= 1;
     }
     // ---- per_layer_projection over gelu(gate) * the layer's per-layer input row
-    {
+    if (!ple_fused) {
       GemvArgs p = pro_args(ple_codes ? PRO_CODES : PRO_GELU);
       p.src = ctx->pleg_out;
       p.ld_src = PD;
@@ -1702,7 +1750,7 @@ static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos,
 static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
   CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)cols * 4, cudaMemcpyDeviceToHost, ctx->st));
   CK(cudaStreamSynchronize(ctx->st));
-  if (device_error_take() > 0 || gemm_error_take() > 0) {
+  if (device_error_take() > 0 || gemm_error_take() > 0 || ple_error_take() > 0) {
     // A block that gave up may have left its column's finished-block count behind.
     cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 8 * 4, ctx->st);
     cudaStreamSynchronize(ctx->st);

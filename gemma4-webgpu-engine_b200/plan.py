@@ -110,6 +110,16 @@ class DispatchStep:
 
 
 GEMV_MAX_COLUMNS = 8   # the streaming GEMV takes up to 8 columns per launch
+PLE_BLOCK_MAX_COLUMNS = 16   # the fused per-layer-input tail takes up to 16 columns per launch
+
+
+def ple_block_eligible(arch: Gemma4Arch, cols: int) -> bool:
+    """Whether the executor runs a layer's per-layer-input tail (post-FFN norm-residual,
+    per_layer_input_gate, gelu times the per-layer row, per_layer_projection) as one cluster
+    launch: a PD of 256, a hidden size that is a multiple of 256 and at most 2048, and 1..16
+    columns on the GEMV path."""
+    return (arch.ple_dim == 256 and arch.hidden_size % 256 == 0 and arch.hidden_size <= 2048
+            and 1 <= cols <= PLE_BLOCK_MAX_COLUMNS)
 
 
 def plan_layer(arch: Gemma4Arch, layer: int, mode: str = "decode", cols: int = 1) -> list:
@@ -144,10 +154,15 @@ def plan_layer(arch: Gemma4Arch, layer: int, mode: str = "decode", cols: int = 1
     add("qgemv-4bit", "mlp", f"{p}mlp.gate_proj,{p}mlp.up_proj",
         "post_attention_layernorm plus residual, pre_feedforward_layernorm; gate_proj, up_proj", reps)
     add("qgemv-4bit", "mlp", p + "mlp.down_proj", "gelu times up, down_proj", reps)
-    add("qgemv-8bit", "ple", p + "per_layer_input_gate",
-        "post_feedforward_layernorm plus residual; per_layer_input_gate", reps)
-    add("qgemv-8bit", "ple", p + "per_layer_projection",
-        "gate times per layer row, per_layer_projection", reps)
+    if ple_block_eligible(arch, cols):
+        add("ple-block", "ple", f"{p}per_layer_input_gate,{p}per_layer_projection",
+            "post_feedforward_layernorm plus residual; per_layer_input_gate; "
+            "gate times per layer row, per_layer_projection")
+    else:
+        add("qgemv-8bit", "ple", p + "per_layer_input_gate",
+            "post_feedforward_layernorm plus residual; per_layer_input_gate", reps)
+        add("qgemv-8bit", "ple", p + "per_layer_projection",
+            "gate times per layer row, per_layer_projection", reps)
     return s
 
 

@@ -31,7 +31,9 @@ _FIXED = {3001: "embed", 3002: "dense (per-layer inputs)", 3003: "per-layer comb
           2356: "prefill attention hd256", 2612: "prefill attention hd512",
           5401: "gemm int4 64 tok", 5402: "gemm int4 128 tok", 5801: "gemm int8 64 tok",
           5802: "gemm int8 128 tok", 5411: "gemm int4 64 tok, cluster split",
-          5811: "gemm int8 64 tok, cluster split"}
+          5811: "gemm int8 64 tok, cluster split",
+          3010: "per-layer tail [to the wait]", 3011: "per-layer tail [prologue]",
+          3012: "per-layer tail [gate + code exchange]"}
 
 
 # GEMM records (id + offset): block 0's accumulator complete, block 0 done, the last CTA done,

@@ -306,7 +306,6 @@ int g4_op_qgemv_codes(const void *wq, const void *scales, const int8_t *codes, f
                       int32_t *acc_out, void *stream);
 
 /*
- * The 2-bit family's layout change/*
  * The 2-bit family's layout change (src/kernels/repack.ts:17-209, src/kernels/qlayout.ts:186-227):
  * to_rows 0 repacks the checkpoint's rows (row r: K / 16 u32 words, code k at bits 2 (k % 16) of
  * word k / 16) into the interleaved tiles (word k of tile t holds row 16 t + i at bits 2 i, rows

@@ -69,14 +69,20 @@ def test_table_split_plans(P, pkg, O):
 def test_decode_census(P):
     steps = P.plan_decode_step(P.GEMMA4_E2B)
     c = P.census(steps)
-    assert c["qgemv-4bit"] == 35 * 4 and c["qgemv-8bit"] == 35 * 2
+    assert c["qgemv-4bit"] == 35 * 4 and c["ple-block"] == 35 and "qgemv-8bit" not in c
     assert c["attention-decode"] == 35 and c["argmax-final"] == 1 and c["qgemv-4bit-head"] == 1
-    assert len(steps) == 3 + 35 * 7 + 2          # 250 launches per B=1 token
+    assert len(steps) == 3 + 35 * 6 + 2          # 215 launches per B=1 token
     # Producers store KV; consumers attend over producer 13 / 14's cache.
-    assert steps[3].modules.endswith("v_proj") and steps[3 + 7 * 20].modules.endswith("q_proj")
-    assert P.census(P.plan_decode_step(P.GEMMA4_E2B, cols=12))["qgemv-4bit"] == 35 * 4 * 2
+    assert steps[3].modules.endswith("v_proj") and steps[3 + 6 * 20].modules.endswith("q_proj")
+    assert steps[3 + 5].modules == "layers.0.per_layer_input_gate,layers.0.per_layer_projection"
+    c12 = P.census(P.plan_decode_step(P.GEMMA4_E2B, cols=12))
+    assert c12["qgemv-4bit"] == 35 * 4 * 2 and c12["ple-block"] == 35   # one tail launch for 12
+    # Past 16 columns, or with a hidden size the cluster launch does not take, the two GEMVs.
+    assert P.census(P.plan_decode_step(P.GEMMA4_E2B, cols=17))["qgemv-8bit"] == 35 * 2 * 3
+    odd = P.Gemma4Arch(hidden_size=2560)
+    assert P.census(P.plan_decode_step(odd))["qgemv-8bit"] == 35 * 2
     chunk = P.plan_prefill_chunk(P.GEMMA4_E2B, False, cols=8)
-    assert len(chunk) == 3 + 15 * 8
+    assert len(chunk) == 3 + 15 * 7
     last = P.plan_prefill_chunk(P.GEMMA4_E2B, True, cols=1)
     assert last == P.plan_decode_step(P.GEMMA4_E2B)
 
