@@ -204,13 +204,14 @@ constexpr int GM_BM = 128;       // weight rows per tile (MMA M)
 constexpr int GM_BK = 128;       // K per stage: one 128-byte swizzle atom of int8
 
 // NSTAGE 0: the default depth (3 at BN 256, 6 at BN 64, else 4, one CTA per SM); 2 (BN 128) or
-// 3 (BN 64): two CTAs share an SM (their epilogues overlap each other's main loops).
-template <int BN, int NSTAGE = 0>
+// 3 (BN 64): two CTAs share an SM (their epilogues overlap each other's main loops). Int8
+// weights land in the MMA tile directly, so their stages carry no packed staging buffer.
+template <int BN, int NSTAGE = 0, int BITS = 4>
 struct GemmShape {
   static constexpr int STAGES = NSTAGE ? NSTAGE : (BN >= 256 ? 3 : (BN <= 64 ? 6 : 4));
   static constexpr int A_BYTES = GM_BM * GM_BK;          // 16 KB
   static constexpr int B_BYTES = BN * GM_BK;
-  static constexpr int P_BYTES = GM_BM * GM_BK / 2;      // packed int4 staging, 8 KB
+  static constexpr int P_BYTES = BITS == 8 ? 0 : GM_BM * GM_BK / 2;   // packed staging, 8 KB
   static constexpr int P2_BYTES = GM_BM * GM_BK / 4;     // 2-bit tiles: 8 x 128 words, 4 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + P_BYTES;
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
@@ -224,7 +225,7 @@ struct GemmShape {
 template <int BITS, int BN, int EPI, int NSTAGE, int CLU>
 __global__ void __launch_bounds__(192, (NSTAGE == 2 || NSTAGE == 3) ? 2 : 1)
     k_qgemm_tc(const __grid_constant__ GemmMaps maps, const GemmArgs a) {
-  using S = GemmShape<BN, NSTAGE>;
+  using S = GemmShape<BN, NSTAGE, BITS>;
   constexpr int NS = S::STAGES;
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
   uint8_t *gsm = gsm_raw + ((1024 - (smem_u32(gsm_raw) & 1023)) & 1023);
@@ -900,7 +901,7 @@ static GemmMaps one_map(const CUtensorMap &tmW, const CUtensorMap &tmX) {
 template <int BITS, int BN, int EPI, int NSTAGE = 0>
 static cudaError_t launch_gemm_t(const GemmMaps &maps, const GemmArgs &a, cudaStream_t st, bool pdl) {
   auto k = k_qgemm_tc<BITS, BN, EPI, NSTAGE, 0>;
-  const int smem = GemmShape<BN, NSTAGE>::SMEM;
+  const int smem = GemmShape<BN, NSTAGE, BITS>::SMEM;
   static DeviceOnce attr;
   attr([&] {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -923,7 +924,7 @@ static cudaError_t launch_gemm_t(const GemmMaps &maps, const GemmArgs &a, cudaSt
 template <int BITS, int CLU, int NSTAGE>
 static cudaError_t launch_gemm_cluster_t(const GemmMaps &maps, const GemmArgs &a, cudaStream_t st, bool pdl) {
   auto k = k_qgemm_tc<BITS, 64, EPI_Y, NSTAGE, CLU>;
-  const int smem = GemmShape<64, NSTAGE>::SMEM;
+  const int smem = GemmShape<64, NSTAGE, BITS>::SMEM;
   static DeviceOnce attr;
   attr([&] {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -953,6 +954,8 @@ static cudaError_t launch_cluster_maps(const GemmMaps &m, const GemmArgs &a, int
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // Three stages (two CTAs per SM) when the launch has more CTAs than SMs; else six, so a CTA's
+  // whole K range (at most six 128-deep tiles at these splits) is requested before the wait.
   const bool two = gemm_x_tiles(a) * ((a.M + 63) / 64) * a.splits > sms;
   switch (a.splits * 100 + bits * 10 + (two ? 1 : 0)) {
     case 240: return launch_gemm_cluster_t<4, 2, 0>(m, a, st, pdl);
