@@ -237,6 +237,31 @@ __device__ __forceinline__ void gemv_prologue_f32(const GemvArgs &a, const ProGa
     if (i < cnt) dst[t + 256 * i] = xv[i];
 }
 
+// CTAs for the segments of one launch in proportion to their units (rows or row tiles): at least
+// one per segment, at most units[i] each, `target` in total (the launch's resident CTAs: one
+// more CTA would run as a second wave that the whole launch waits for). Floors first, then the
+// CTAs left over go to the largest remainders (ties: the earlier segment).
+inline void split_ctas(const long long *units, int n, int target, long long *nb) {
+  long long total = 0, rem[3];
+  for (int i = 0; i < n; i++) total += units[i];
+  if (target > total) target = (int)total;
+  long long used = 0;
+  for (int i = 0; i < n; i++) {
+    nb[i] = units[i] * target / total;
+    rem[i] = units[i] * target % total;
+    if (nb[i] < 1) nb[i] = 1;
+    used += nb[i];
+  }
+  for (long long left = target - used; left > 0; left--) {
+    int best = -1;
+    for (int i = 0; i < n; i++)
+      if (nb[i] < units[i] && (best < 0 || rem[i] > rem[best])) best = i;
+    if (best < 0) break;
+    nb[best]++;
+    rem[best] = -1;
+  }
+}
+
 constexpr int GS_RING = 96 * 1024;   // shared-memory ring per CTA
 constexpr int GS_MAX_STAGES = 8;
 

@@ -485,17 +485,13 @@ int gemv2_partition(GemvArgs &a, int sms) {
     a.n_blocks_total = nb;
     return nb;
   }
-  long long total = 0;
-  for (int i = 0; i < a.nseg; i++) total += (a.seg[i].N + 15) / 16;
-  const int target = (int)(total < sms ? total : sms);
+  long long tiles[3], nb[3];
+  for (int i = 0; i < a.nseg; i++) tiles[i] = (a.seg[i].N + 15) / 16;
+  split_ctas(tiles, a.nseg, sms, nb);
   int begin = 0;
   for (int i = 0; i < a.nseg; i++) {
-    const long long tiles = (a.seg[i].N + 15) / 16;
-    long long nb = (tiles * target + total - 1) / total;
-    if (nb < 1) nb = 1;
-    if (nb > tiles) nb = tiles;
     a.seg[i].block_begin = begin;
-    begin += (int)nb;
+    begin += (int)nb[i];
   }
   a.n_blocks_total = begin;
   return begin;

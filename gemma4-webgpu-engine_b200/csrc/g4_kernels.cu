@@ -450,28 +450,9 @@ int gemv_stream_partition(GemvArgs &a, int sms) {
     a.n_blocks_total = nb;
     return nb;
   }
-  // CTAs in proportion to the rows, at least one per segment, the total at most `sms` (one CTA
-  // per SM: an SM given two finishes last and the whole launch waits for it). Floors first, then
-  // the CTAs left over go to the largest remainders (ties: the earlier segment).
-  long long total = 0;
-  for (int i = 0; i < a.nseg; i++) total += a.seg[i].N;
-  const int target = (int)(total < sms ? total : sms);
-  long long nb[3], rem[3];
-  int used = 0;
-  for (int i = 0; i < a.nseg; i++) {
-    nb[i] = a.seg[i].N * (long long)target / total;
-    rem[i] = a.seg[i].N * (long long)target % total;
-    if (nb[i] < 1) nb[i] = 1;
-    used += (int)nb[i];
-  }
-  for (int left = target - used; left > 0; left--) {
-    int best = -1;
-    for (int i = 0; i < a.nseg; i++)
-      if (nb[i] < a.seg[i].N && (best < 0 || rem[i] > rem[best])) best = i;
-    if (best < 0) break;
-    nb[best]++;
-    rem[best] = -1;
-  }
+  long long rows[3], nb[3];
+  for (int i = 0; i < a.nseg; i++) rows[i] = a.seg[i].N;
+  split_ctas(rows, a.nseg, sms, nb);
   int begin = 0;
   for (int i = 0; i < a.nseg; i++) {
     a.seg[i].block_begin = begin;
