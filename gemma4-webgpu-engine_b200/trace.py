@@ -32,8 +32,8 @@ _FIXED = {3001: "embed", 3002: "dense (per-layer inputs)", 3003: "per-layer comb
           5401: "gemm int4 64 tok", 5402: "gemm int4 128 tok", 5801: "gemm int8 64 tok",
           5802: "gemm int8 128 tok", 5411: "gemm int4 64 tok, cluster split",
           5811: "gemm int8 64 tok, cluster split",
-          3010: "per-layer tail [to the wait]", 3011: "per-layer tail [prologue]",
-          3012: "per-layer tail [gate + code exchange]"}
+          3010: "per-layer tail [prologue]", 3011: "per-layer tail [gate + code exchange]",
+          3012: "per-layer tail [projection + release]"}
 
 
 # GEMM records (id + offset): block 0's accumulator complete, block 0 done, the last CTA done,
@@ -88,6 +88,8 @@ def main() -> None:
     ap.add_argument("--ctx-hi", type=int, default=128)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--gemm-split-k", type=int, default=0, choices=[0, 1, 2])
+    ap.add_argument("--dump", type=int, default=0,
+                    help="also print the first N records of the last step in time order")
     args = ap.parse_args()
     import numpy as np
     import __graft_entry__ as entry
@@ -127,6 +129,15 @@ def main() -> None:
     print(f"{'kernel':34s} {'launches':>8s} {'us/launch':>10s} {'share':>7s}")
     for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1]):
         print(f"{k:34s} {n:8d} {t / n:10.2f} {100 * t / tot:6.1f}%")
+    if args.dump:
+        # Each record's interval runs to the next record; the last-CTA records of a GEMM carry the
+        # latest time over its CTAs, so they sort where that event happened.
+        srt = sorted(rec, key=lambda r: r[1])
+        starts = [i for i, (k, _) in enumerate(srt) if k == 3001]
+        last = srt[starts[-1]:] if starts else srt
+        print(f"first {args.dump} records of the last step (us from its start, us to the next record):")
+        for (k, ta), (_, tb) in zip(last[:args.dump], last[1:args.dump + 1]):
+            print(f"{(ta - last[0][1]) / 1000.0:10.2f} {(tb - ta) / 1000.0:8.2f}  {kernel_name(k)}")
 
 
 if __name__ == "__main__":
