@@ -51,6 +51,11 @@ int gemm_trace_take(unsigned long long *out, int max_records) {
 }
 #endif
 
+int *gemm_error_addr() {
+  void *p = nullptr;
+  return cudaGetSymbolAddress(&p, g4_gemm_error) == cudaSuccess ? (int *)p : nullptr;
+}
+
 int gemm_error_take() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g4_gemm_error, sizeof(int)) != cudaSuccess) return -1;

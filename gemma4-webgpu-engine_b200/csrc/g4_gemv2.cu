@@ -42,6 +42,11 @@ __device__ unsigned long long g4_trace_buf[1 << 16];
 __device__ unsigned int g4_trace_n;
 #endif
 
+int *gemv2_error_addr() {
+  void *p = nullptr;
+  return cudaGetSymbolAddress(&p, g4_gemv2_error) == cudaSuccess ? (int *)p : nullptr;
+}
+
 int gemv2_error_take() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g4_gemv2_error, sizeof(int)) != cudaSuccess) return -1;

@@ -593,6 +593,11 @@ cudaError_t launch_wait_probe(const void *src, int bytes, int missing, int limit
 
 int gemv2_error_take();
 
+int *dev_error_addr() {
+  void *p = nullptr;
+  return cudaGetSymbolAddress(&p, g4_dev_error) == cudaSuccess ? (int *)p : nullptr;
+}
+
 int device_error_take() {
   int v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g4_dev_error, sizeof(int)) != cudaSuccess) return -1;
@@ -1990,13 +1995,21 @@ __device__ __forceinline__ void amax_take(float &bv, int &bi, float v, int i) {
 
 __global__ void __launch_bounds__(256)
 k_argmax_final(const float *part_val, const int32_t *part_idx, int n_parts, int32_t *token_dev,
-               int32_t *token_out, float *value_out) {
+               int32_t *token_out, float *value_out, const ErrFlags flags, int32_t *flag_out) {
   __shared__ float sv[8];
   __shared__ int si[8];
   grid_launch_dependents();
   grid_wait();
   G4_TRACE_POINT(3004);
   const int c = blockIdx.x, t = threadIdx.x, lane = t & 31;
+  if (flag_out && c == 0 && t == 32) {
+    // Every earlier kernel of the step has completed (each waited on the one before it).
+    int v = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (flags.p[i]) v |= __ldcg(flags.p[i]);
+    flag_out[0] = v;
+  }
   float bv = -FLT_MAX;
   int bi = 0x7fffffff;
   for (int i = t; i < n_parts; i += 256)
@@ -2022,9 +2035,12 @@ k_argmax_final(const float *part_val, const int32_t *part_idx, int n_parts, int3
 
 cudaError_t launch_argmax_final(const float *part_val, const int32_t *part_idx, int n_parts,
                                 int cols, int32_t *token_dev, int32_t *token_out,
-                                float *value_out, cudaStream_t st, bool pdl) {
+                                float *value_out, cudaStream_t st, bool pdl,
+                                const ErrFlags *flags, int32_t *flag_out) {
+  ErrFlags f = {};
+  if (flags) f = *flags;
   return launch_k(k_argmax_final, dim3(cols), dim3(256), 0, st, pdl, part_val, part_idx, n_parts,
-                  token_dev, token_out, value_out);
+                  token_dev, token_out, value_out, f, flags ? flag_out : nullptr);
 }
 
 __global__ void k_advance(int32_t *pos, int cols) {

@@ -311,9 +311,21 @@ int ple_error_take();
 // Decode chain: position[c] += 1 after a step (its argmax already sits in the token slot).
 cudaError_t launch_advance(int32_t *pos, int cols, cudaStream_t st, bool pdl);
 
+// The sticky error flags of the library's kernels (one per translation unit: streaming GEMV and
+// attention, 2-bit GEMV, tensor-core GEMM, per-layer-input tail), by device address.
+struct ErrFlags {
+  const int *p[4];
+};
+int *dev_error_addr();
+int *gemv2_error_addr();
+int *gemm_error_addr();
+int *ple_error_addr();
+// flag_out (optional): the OR of the flags, written once the step's earlier kernels are complete,
+// so a host reads tokens and flags with one copy.
 cudaError_t launch_argmax_final(const float *part_val, const int32_t *part_idx, int n_parts,
                                 int cols, int32_t *token_dev, int32_t *token_out,
-                                float *value_out, cudaStream_t st, bool pdl);
+                                float *value_out, cudaStream_t st, bool pdl,
+                                const ErrFlags *flags = nullptr, int32_t *flag_out = nullptr);
 
 // Standalone norm / elementwise kernels (operator API).
 cudaError_t launch_rms_norm(const float *src, const float *gain, float *dst, int rows, int width,

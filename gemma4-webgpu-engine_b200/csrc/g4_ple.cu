@@ -44,6 +44,11 @@ int ple_trace_take(unsigned long long *out, int max_records) {
 }
 #endif
 
+int *ple_error_addr() {
+  void *p = nullptr;
+  return cudaGetSymbolAddress(&p, g4_ple_error) == cudaSuccess ? (int *)p : nullptr;
+}
+
 int ple_error_take() {
   int v = 0, z = 0;
   if (cudaMemcpyFromSymbol(&v, g4_ple_error, sizeof(int)) != cudaSuccess) return 0;

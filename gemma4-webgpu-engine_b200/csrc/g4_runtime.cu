@@ -163,7 +163,8 @@ struct g4_ctx {
   int32_t *h_step[kStageSlots] = {nullptr, nullptr, nullptr, nullptr};
   cudaEvent_t stage_ev[kStageSlots] = {nullptr, nullptr, nullptr, nullptr};
   int stage_next = 0;
-  int32_t *h_tok = nullptr;    // pinned token outputs
+  int32_t *h_tok = nullptr;    // pinned token outputs, then the step's error word
+  ErrFlags errf = {};          // the kernels' sticky error flags, by device address
   uint64_t other_bytes = 0;
   std::map<GraphKey, cudaGraphExec_t> graphs;
   // 2-bit tensors being uploaded in pieces: the checkpoint bytes so far, repacked when complete.
@@ -614,13 +615,19 @@ static int alloc_runtime(g4_ctx *ctx) {
   CK(ctx_malloc((void **)&ctx->head_pi, (size_t)ctx->head_cols * ctx->head_cap * 4));
   CK(ctx_malloc((void **)&ctx->d_step, (size_t)3 * maxc * 4));
   CK(cudaMemset(ctx->d_step, 0, (size_t)3 * maxc * 4));
-  CK(ctx_malloc((void **)&ctx->d_tok_out, (size_t)maxc * 4));
+  // The tokens of a step, then one word: the OR of the error flags (k_argmax_final).
+  CK(ctx_malloc((void **)&ctx->d_tok_out, (size_t)(maxc + 1) * 4));
   CK(ctx_malloc((void **)&ctx->d_val_out, (size_t)maxc * 4));
   for (int i = 0; i < g4_ctx::kStageSlots; i++) {
     CK(cudaMallocHost(&ctx->h_step[i], (size_t)3 * maxc * 4));
     CK(cudaEventCreateWithFlags(&ctx->stage_ev[i], cudaEventDisableTiming));
   }
-  CK(cudaMallocHost(&ctx->h_tok, (size_t)maxc * 4));
+  CK(cudaMallocHost(&ctx->h_tok, (size_t)(maxc + 1) * 4));
+  int *fl[4] = {dev_error_addr(), gemv2_error_addr(), gemm_error_addr(), ple_error_addr()};
+  for (int i = 0; i < 4; i++) {
+    if (!fl[i]) return fail(ctx, G4_ERR_CUDA, "cannot resolve the device address of an error flag");
+    ctx->errf.p[i] = fl[i];
+  }
   return G4_OK;
 }
 
@@ -1660,7 +1667,7 @@ static int record_step(g4_ctx *ctx, int cols, int n_layers, bool head, bool adva
     p.softcap = a.final_softcap;
     if ((rc = run_linear(ctx, {{&ctx->lm, nullptr}}, cols, p, true))) return rc;
     CK(launch_argmax_final(ctx->cur_pv, ctx->cur_pi, ctx->cur_parts, cols, d_tok,
-                           ctx->d_tok_out, ctx->d_val_out, ctx->st, true));
+                           ctx->d_tok_out, ctx->d_val_out, ctx->st, true, &ctx->errf, ctx->d_tok_out + cols));
     if (advance) CK(launch_advance(d_pos, cols, ctx->st, true));
     note_launch(ctx, "argmax-final", "argmax");
     if (advance) note_launch(ctx, "advance", "position advance");
@@ -1747,10 +1754,12 @@ static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos,
   return G4_OK;
 }
 
+// The step's tokens and its error word in one copy; the flags themselves are read (and cleared)
+// only when the word says one is set.
 static int fetch_tokens(g4_ctx *ctx, int cols, int32_t *out) {
-  CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)cols * 4, cudaMemcpyDeviceToHost, ctx->st));
+  CK(cudaMemcpyAsync(ctx->h_tok, ctx->d_tok_out, (size_t)(cols + 1) * 4, cudaMemcpyDeviceToHost, ctx->st));
   CK(cudaStreamSynchronize(ctx->st));
-  if (device_error_take() > 0 || gemm_error_take() > 0 || ple_error_take() > 0) {
+  if (ctx->h_tok[cols] != 0 && (device_error_take() > 0 || gemm_error_take() > 0 || ple_error_take() > 0)) {
     // A block that gave up may have left its column's finished-block count behind.
     cudaMemsetAsync(ctx->att_count, 0, (size_t)ctx->maxc * 8 * 4, ctx->st);
     cudaStreamSynchronize(ctx->st);
