@@ -1720,9 +1720,6 @@ static int check_seq_pos(g4_ctx *ctx, int32_t seq, int32_t pos, int32_t n) {
   return G4_OK;
 }
 
-// Copy one step's columns into the device step buffer. The pinned source slot is rewritten only
-// once the copy that last read it has executed on the stream (consecutive prefill chunks are
-// enqueued without a host wait).
 // Rebuild the int8 weight copies after a weight change (before any step uses them).
 static int refresh_shadows(g4_ctx *ctx) {
   if (!ctx->shadow_dirty) return G4_OK;
@@ -1736,6 +1733,9 @@ static int refresh_shadows(g4_ctx *ctx) {
   return G4_OK;
 }
 
+// Copy one step's columns into the device step buffer. The pinned source slot is rewritten only
+// once the copy that last read it has executed on the stream (consecutive prefill chunks are
+// enqueued without a host wait).
 static int stage(g4_ctx *ctx, int cols, const int32_t *seqs, const int32_t *pos, const int32_t *toks,
                  bool tokens_too) {
   int rc = refresh_shadows(ctx);
