@@ -162,7 +162,8 @@ __host__ __device__ __forceinline__ GsLayout gs_layout(int ring, int cols, int m
 #endif
 
 template <int BITS, int COLS, int RS, int PRO, int EPI>
-__global__ void __launch_bounds__(256, (PRO == PRO_X && EPI == EPI_Y && COLS == 1) ? 4 : G4_GEMV_MIN_BLOCKS)
+__global__ void __launch_bounds__(256, ((PRO == PRO_X || PRO == PRO_CODES) && EPI == EPI_Y && COLS == 1)
+                                           ? 4 : G4_GEMV_MIN_BLOCKS)
     k_qgemv_stream(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int ring_bytes = a.ring_bytes;
