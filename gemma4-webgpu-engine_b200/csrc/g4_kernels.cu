@@ -3,6 +3,8 @@
 // Reference citations are path:line inside the reference project (TypeScript + WGSL).
 #include <cuda_fp16.h>
 #include <float.h>
+#include <map>
+#include <mutex>
 
 #include "g4_device.cuh"
 #include "g4_kernels.cuh"
@@ -1585,7 +1587,29 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl) {
 //     ascending block order exactly as k_attn_merge (a single block divides directly).
 // =====================================================================================
 
+// Shared memory of one CTA: V staging, query rows, the new K / V rows, scores, probabilities,
+// maxima, barriers and a flag; with CL, then the cluster's block partials (held by the leader).
 template <int HD, int NHL>
+__host__ __device__ constexpr size_t attn_decode_smem_base() {
+  return ((size_t)(NHL == 8 ? ATT_BLK / 2 : ATT_BLK) * HD + NHL * HD + 2 * HD + 2 * NHL * ATT_BLK + 8) * 4 + 32;
+}
+constexpr int ATT_CL_MAX = 16;   // blocks of one (column, head) in one cluster, at most
+
+__device__ __forceinline__ uint32_t att_mapa(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void att_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// CL (one head per CTA, a launch's blocks of one (column, head) forming one thread-block cluster
+// along y): each block's partial goes into the shared memory of the cluster's first block by
+// distributed-shared-memory stores, one cluster barrier replaces the global partials, the fence,
+// the finished-block count and the L2 reads of the merge, and the first block merges in the same
+// order. Every CTA of the cluster takes that barrier exactly once, blocks past the context too.
+template <int HD, int NHL, bool CL = false>
 __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
   // NHL query heads per CTA: 8 (one CTA per (column, block)) or 1 (grid z = head).
   constexpr int NH = 8;
@@ -1605,6 +1629,9 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
   float *ms = ps + NHL * ATT_BLK;     // [8]
   uint64_t *bar = reinterpret_cast<uint64_t *>(ms + 8);    // [VH], 8-byte aligned: offsets above
   int *flag = reinterpret_cast<int *>(bar + VH);           // are multiples of 8 floats
+  // CL: [ATT_CL_MAX][HD] partial outputs, then ATT_CL_MAX maxima and ATT_CL_MAX sums.
+  float *cpart = reinterpret_cast<float *>(reinterpret_cast<char *>(sm) + attn_decode_smem_base<HD, NHL>());
+  float *cm = cpart + ATT_CL_MAX * HD, *cl = cm + ATT_CL_MAX;
   const int c = blockIdx.x, bi = blockIdx.y, t = threadIdx.x, lane = t & 31, w = t >> 5;
   const int h0 = blockIdx.z * NHL;    // first head of this CTA
 
@@ -1638,7 +1665,10 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     attn_range(r, c, &p, &lo, &hi);
   }
   const int b = lo / ATT_BLK + bi;
-  if (b * ATT_BLK > hi) return;
+  if (b * ATT_BLK > hi) {
+    if constexpr (CL) att_cluster_sync();
+    return;
+  }
   const int nb = hi / ATT_BLK - lo / ATT_BLK + 1;
   const int j0 = max(b * ATT_BLK, lo), j1 = min(b * ATT_BLK + ATT_BLK - 1, hi);
   const int seq = a.refs.seq ? a.refs.seq[c] : 0;
@@ -1689,6 +1719,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
                               store_kv ? V + (size_t)p * HD : nullptr, lane);
   }
   __syncthreads();
+  G4_TRACE_POINT(102000 + HD);
 
   // Scores (as k_attn_blocks).
   {
@@ -1741,6 +1772,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
     ps[h * ATT_BLK + lane + 32] = (jb >= j0 && jb <= j1) ? g4_exp(__fsub_rn(s1, mx)) : 0.0f;
     if (lane == 0) ms[h] = mx;
   }
+  G4_TRACE_POINT(202000 + HD);
   vwait(0);
   __syncthreads();
   const int dc = t % NC, hg = t / NC;
@@ -1810,6 +1842,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       }
     }
   }
+  G4_TRACE_POINT(302000 + HD);
   if (nb == 1) {
     if (pv) {
 #pragma unroll
@@ -1824,27 +1857,53 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
         attn_codes4(a.codes, c, h * HD + 4 * dc, r);
       }
     }
+    if constexpr (CL) att_cluster_sync();
     return;
   }
-  if (pv) {
-#pragma unroll
-    for (int hh = 0; hh < HPT; hh++) {
-      const int hl = hg * HPT + hh, h = h0 + hl;
-      const size_t slot = ((size_t)c * a.max_blocks + bi) * NH + h;
-      reinterpret_cast<float4 *>(a.part_o + slot * HD)[dc] = o[hh];
+  int *cnt = a.counter + c * (NH / NHL) + blockIdx.z;
+  if constexpr (CL) {
+    // One head per CTA (HPT 1): the partial into the first block's shared memory, then the barrier.
+    if (pv) {
+      const uint32_t dst = att_mapa(cpart + (size_t)bi * HD + 4 * dc, 0);
+      asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(o[0].x), "f"(o[0].y),
+                   "f"(o[0].z), "f"(o[0].w)
+                   : "memory");
       if (dc == 0) {
-        a.part_m[slot] = ms[hl];
-        a.part_l[slot] = l[hh];
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(att_mapa(cm + bi, 0)), "f"(ms[0]) : "memory");
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(att_mapa(cl + bi, 0)), "f"(l[0]) : "memory");
       }
     }
+    att_cluster_sync();
+    G4_TRACE_POINT(402000 + HD);
+    if (bi != 0) return;
+  } else {
+    if (pv) {
+#pragma unroll
+      for (int hh = 0; hh < HPT; hh++) {
+        const int hl = hg * HPT + hh, h = h0 + hl;
+        const size_t slot = ((size_t)c * a.max_blocks + bi) * NH + h;
+        reinterpret_cast<float4 *>(a.part_o + slot * HD)[dc] = o[hh];
+        if (dc == 0) {
+          a.part_m[slot] = ms[hl];
+          a.part_l[slot] = l[hh];
+        }
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (t == 0) *flag = atomicAdd(cnt, 1) == nb - 1;
+    __syncthreads();
+    G4_TRACE_POINT(402000 + HD);
+    if (!*flag) return;
+    __threadfence();
   }
-  __threadfence();
-  __syncthreads();
-  int *cnt = a.counter + c * (NH / NHL) + blockIdx.z;
-  if (t == 0) *flag = atomicAdd(cnt, 1) == nb - 1;
-  __syncthreads();
-  if (!*flag) return;
-  __threadfence();
+#ifdef G4_TRACE
+  if (blockIdx.x == 0 && blockIdx.z == 0 && t == 0) {   // the merge of column 0, head group 0
+    unsigned long long now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    G4_TRACE_REC(502000 + HD, now);
+  }
+#endif
   // The merge, in k_attn_merge's order, for this CTA's heads. Per head, M_k = max(m_0..m_k) is
   // an exact prefix max, so lane k of warp hl computes ea_k = exp(M_{k-1} - M_k),
   // ec_k = exp(m_k - M_k) and l_k * ec_k in parallel; lane 0 then runs
@@ -1861,23 +1920,36 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
   float4 O[F];
   float4 nx[KB][F];
   const float4 *po = reinterpret_cast<const float4 *>(a.part_o + (base + h0) * HD);
+  // Block k's partial output, vec4 i (CL: from this CTA's shared memory).
+  auto ld_o = [&](int k, int i) -> float4 {
+    if constexpr (CL) return reinterpret_cast<const float4 *>(cpart)[(size_t)k * (HD / 4) + i];
+    else return __ldcg(po + (size_t)k * NH * HD / 4 + i);
+  };
 #pragma unroll
   for (int i = 0; i < F; i++)
-    if (t + 256 * i < NV) O[i] = __ldcg(po + t + 256 * i);
+    if (t + 256 * i < NV) O[i] = ld_o(0, t + 256 * i);
 #pragma unroll
   for (int kk = 0; kk < KB; kk++)
     if (1 + kk < nb) {
 #pragma unroll
       for (int i = 0; i < F; i++)
-        if (t + 256 * i < NV) nx[kk][i] = __ldcg(po + (size_t)(1 + kk) * NH * HD / 4 + t + 256 * i);
+        if (t + 256 * i < NV) nx[kk][i] = ld_o(1 + kk, t + 256 * i);
     }
   if (w < NHL) {
     const int h = h0 + w;
     float carry = -FLT_MAX, Lrun = 0.0f;
     for (int k0 = 0; k0 < nb; k0 += 32) {
       const int k = k0 + lane;
-      const float mk = k < nb ? __ldcg(a.part_m + base + (size_t)k * NH + h) : -FLT_MAX;
-      const float lk = k < nb ? __ldcg(a.part_l + base + (size_t)k * NH + h) : 0.0f;
+      float mk = -FLT_MAX, lk = 0.0f;
+      if (k < nb) {
+        if constexpr (CL) {
+          mk = cm[k];
+          lk = cl[k];
+        } else {
+          mk = __ldcg(a.part_m + base + (size_t)k * NH + h);
+          lk = __ldcg(a.part_l + base + (size_t)k * NH + h);
+        }
+      }
       float Mk = mk;   // inclusive prefix max within the chunk, then with the carry
 #pragma unroll
       for (int o2 = 1; o2 < 32; o2 <<= 1) {
@@ -1934,7 +2006,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
 #pragma unroll
         for (int i = 0; i < F; i++)
           if (t + 256 * i < NV)
-            nx[kk][i] = __ldcg(po + (size_t)(k0 + KB + kk) * NH * HD / 4 + t + 256 * i);
+            nx[kk][i] = ld_o(k0 + KB + kk, t + 256 * i);
       }
   }
 #pragma unroll
@@ -1951,13 +2023,19 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnDec a) {
       attn_codes4(a.codes, c, h0 * HD + 4 * (t + 256 * i), r);
     }
   }
-  if (t == 0) *cnt = 0;
+#ifdef G4_TRACE
+  if (blockIdx.x == 0 && blockIdx.z == 0 && t == 0) {
+    unsigned long long now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+    G4_TRACE_REC(602000 + HD, now);
+  }
+#endif
+  if (!CL && t == 0) *cnt = 0;
 }
 
-template <int HD, int NHL>
+template <int HD, int NHL, bool CL = false>
 static size_t attn_decode_smem() {
-  constexpr int VROWS = NHL == 8 ? ATT_BLK / 2 : ATT_BLK;
-  return ((size_t)VROWS * HD + NHL * HD + 2 * HD + 2 * NHL * ATT_BLK + 8) * 4 + 32;
+  return attn_decode_smem_base<HD, NHL>() + (CL ? ((size_t)ATT_CL_MAX * HD + 2 * ATT_CL_MAX) * 4 : 0);
 }
 
 template <int HD, int NHL>
@@ -1972,12 +2050,77 @@ static cudaError_t launch_attn_decode_t(const AttnDec &a, cudaStream_t st, bool 
                   attn_decode_smem<HD, NHL>(), st, pdl, a);
 }
 
+// One-head CTAs whose blocks of one (column, head) form a cluster of a.max_blocks along y.
+template <int HD>
+static cudaLaunchConfig_t attn_cl_config(const AttnDec &a, cudaStream_t st, cudaLaunchAttribute *attr, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.cols, a.max_blocks, 8);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = attn_decode_smem<HD, 1, true>();
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = a.max_blocks;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cfg;
+}
+
+template <int HD>
+static cudaError_t attn_cl_attrs() {
+  cudaError_t e = cudaFuncSetAttribute(k_attn_decode<HD, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_decode_smem<HD, 1, true>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_attn_decode<HD, 1, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
+// Whether a cluster of a.max_blocks such CTAs can be resident on the current device (asked once
+// per device and block count).
+template <int HD>
+static bool attn_cl_fits(const AttnDec &a) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, bool> known;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = known.find({dev, a.max_blocks});
+  if (it != known.end()) return it->second;
+  bool ok = attn_cl_attrs<HD>() == cudaSuccess;
+  if (ok) {
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = attn_cl_config<HD>(a, nullptr, attr, false);
+    int n = 0;
+    ok = cudaOccupancyMaxActiveClusters(&n, k_attn_decode<HD, 1, true>, &cfg) == cudaSuccess && n >= 1;
+  }
+  if (!ok) cudaGetLastError();
+  known[{dev, a.max_blocks}] = ok;
+  return ok;
+}
+
+template <int HD>
+static cudaError_t launch_attn_decode_cl(const AttnDec &a, cudaStream_t st, bool pdl) {
+  static DeviceOnce attr_set;
+  attr_set([&] { attn_cl_attrs<HD>(); });
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = attn_cl_config<HD>(a, st, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, k_attn_decode<HD, 1, true>, a);
+}
+
 cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl) {
   // The merge keeps three factors per (block, head) in the (32- or 64-row) V buffer.
   if ((size_t)3 * a.max_blocks * 8 + 8 > (size_t)(ATT_BLK / 2) * a.hd) return cudaErrorInvalidValue;
   // Few columns: one CTA per (column, block, head) spreads a latency-bound step over more SMs;
   // a wide batch keeps all 8 heads of a block in one CTA (the V block is staged once for them).
   const bool split = a.cols * a.max_blocks <= 64;
+  // One-head CTAs of 2..16 blocks merge inside a thread-block cluster.
+  if (split && a.max_blocks >= 2 && a.max_blocks <= ATT_CL_MAX) {
+    if (a.hd == 256 && attn_cl_fits<256>(a)) return launch_attn_decode_cl<256>(a, st, pdl);
+    if (a.hd == 512 && attn_cl_fits<512>(a)) return launch_attn_decode_cl<512>(a, st, pdl);
+  }
   if (a.hd == 256) return split ? launch_attn_decode_t<256, 1>(a, st, pdl) : launch_attn_decode_t<256, 8>(a, st, pdl);
   if (a.hd == 512) return split ? launch_attn_decode_t<512, 1>(a, st, pdl) : launch_attn_decode_t<512, 8>(a, st, pdl);
   return cudaErrorInvalidValue;

@@ -285,9 +285,9 @@ struct AttnDec {
 };
 cudaError_t launch_attn_decode(const AttnDec &a, cudaStream_t st, bool pdl);
 
-// The per-layer-input tail of a decode batch (g4_ple.cu): per_layer_input_gate, gelu(gate) x the
-// layer's per-layer input, per_layer_projection, on one cluster of 16 CTAs. Both linears int8,
-// PD = 256, 1 <= cols <= 64; codes: the gate's input codes [cols][ld_codes] in K order.
+// The per-layer-input tail of a decode step (g4_ple.cu): the post-FFN norm-residual,
+// per_layer_input_gate, gelu(gate) x the layer's per-layer input, per_layer_projection, on one
+// cluster of 16 CTAs. Both linears int8, PD = 256, H a multiple of 256 up to 2048, 1..16 columns.
 struct PleArgs {
   // The post-FFN norm-residual: h = res + rms_norm(src) * g1 (written to hidden_out by one CTA)
   // is the gate's input.

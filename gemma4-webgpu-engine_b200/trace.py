@@ -34,6 +34,16 @@ _FIXED = {3001: "embed", 3002: "dense (per-layer inputs)", 3003: "per-layer comb
           5811: "gemm int8 64 tok, cluster split",
           3010: "per-layer tail [prologue]", 3011: "per-layer tail [gate + code exchange]",
           3012: "per-layer tail [projection + release]"}
+# Decode attention phases: block 0 of the launch, and the merge from the CTA that runs it
+# (column 0, first head group).
+for _hd in (256, 512):
+    _FIXED.update({2000 + _hd: f"attention hd{_hd} [range, norms]",
+                   102000 + _hd: f"attention hd{_hd} [scores, softmax]",
+                   202000 + _hd: f"attention hd{_hd} [V wait, PV]",
+                   302000 + _hd: f"attention hd{_hd} [partial, count]",
+                   402000 + _hd: f"attention hd{_hd} [to the merge]",
+                   502000 + _hd: f"attention hd{_hd} [merge]",
+                   602000 + _hd: f"attention hd{_hd} [release]"})
 
 
 # GEMM records (id + offset): block 0's accumulator complete, block 0 done, the last CTA done,
