@@ -75,6 +75,7 @@ SIGNATURES = {
     "g4_op_repack_tile16": (C.c_int, [_vp, _vp, _i32, _i32, _i32, _vp]),
     "g4_arch_checkpoint": (C.c_int, [C.POINTER(Arch)]),
     "g4_debug_fail_allocation": (C.c_int, [_i32]),
+    "g4_debug_raise_error_flag": (C.c_int, [_vp, _i32]),
     "g4_step_stage": (C.c_int, [_vp, _i32, _i32p, _i32p, _i32p]),
     "g4_step_run_device": (C.c_int, [_vp, _i32, _i32]),
     "g4_step_read_tokens": (C.c_int, [_vp, _i32, _i32p]),

@@ -768,6 +768,14 @@ extern "C" int g4_debug_fail_allocation(int32_t nth) {
   return G4_OK;
 }
 
+extern "C" int g4_debug_raise_error_flag(g4_ctx *ctx, int32_t unit) {
+  if (!ctx || unit < 0 || unit > 3) return fail(ctx, G4_ERR_INVALID, "g4_debug_raise_error_flag: unit %d outside 0..3", unit);
+  CK(cudaSetDevice(ctx->dev));
+  const int one = 1;
+  CK(cudaMemcpy(const_cast<int *>(ctx->errf.p[unit]), &one, sizeof(int), cudaMemcpyHostToDevice));
+  return G4_OK;
+}
+
 extern "C" void *g4_ctx_stream(g4_ctx *ctx) { return ctx ? (void *)ctx->st : nullptr; }
 
 extern "C" int g4_last_launch_list(const g4_ctx *ctx, char *buf, uint64_t cap, uint64_t *needed) {

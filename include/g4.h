@@ -435,6 +435,15 @@ int g4_op_wait_probe(const void *src, int32_t bytes, int32_t missing_bytes, int3
  */
 int g4_debug_fail_allocation(int32_t nth);
 
+/*
+ * Error-path injection for tests: sets the sticky error flag that one unit of the library's
+ * kernels raises when a bounded device wait gives up (0 streaming GEMV and attention, 1 2-bit
+ * GEMV, 2 tensor-core GEMM, 3 per-layer-input tail), as if such a wait had run out, without any
+ * kernel failing. The next call that returns tokens (g4_decode, g4_decode_batch, g4_verify,
+ * g4_prefill with is_last) then returns G4_ERR_TIMEOUT and clears it, as a real timeout does.
+ */
+int g4_debug_raise_error_flag(g4_ctx *ctx, int32_t unit);
+
 /* Elementwise probes of the library's f32 exp and tanh (used by the attention softmax, GELU
  * and the softcap), for checking them against CUDA's expf/tanhf within error bounds. */
 int g4_op_math_probe(const float *x, float *exp_out, float *tanh_out, float *cuda_exp,

@@ -42,6 +42,43 @@ def test_bounded_wait_gives_up_and_device_stays_usable(pkg, lib, O, cuda):
     assert got == list(want)
 
 
+def test_step_reports_each_units_error_flag(pkg, lib, O, cuda):
+    """A step reads its tokens and one error word (the OR of the four kernel units' sticky
+    flags) with a single copy. A flag raised on the host, as a bounded wait that ran out would
+    raise it, makes the next token-returning call fail with G4_ERR_TIMEOUT and is cleared; the
+    same call then succeeds and the tokens still match the oracle. Covered on the GEMV path
+    (B=1) and on the tensor-core path (a 20-column decode batch)."""
+    a = entry.tiny_arch(pkg)
+    om = O.Model(SEED, entry.oracle_arch(O, a))
+    ctx = pkg.engine.Context(device=0, max_seqs=20, max_context=64, max_step_columns=32, arch=a)
+    ctx.init_random(SEED)
+    prompt = O.synth_prompt(SEED + 5, 9, a.vocab_size)
+    want, _ = om.generate(prompt, 3, 64)
+    tok = ctx.prefill(0, prompt, 0, True)
+    assert tok == want[0]
+    for unit in range(4):
+        assert lib.g4_debug_raise_error_flag(ctx.h, unit) == 0
+        with pytest.raises(pkg._abi.G4Error) as e:
+            ctx.decode(0, tok, len(prompt))
+        assert e.value.code == G4_ERR_TIMEOUT
+        assert "bounded device wait gave up" in str(e.value)
+        assert ctx.decode(0, tok, len(prompt)) == want[1]
+    B = 20
+    prompts = [O.synth_prompt(SEED + 60 + b, 4 + b % 5, a.vocab_size) for b in range(B)]
+    toks = [ctx.prefill(b, prompts[b], 0, True) for b in range(B)]
+    pos = [len(p) for p in prompts]
+    assert lib.g4_debug_raise_error_flag(ctx.h, 2) == 0
+    with pytest.raises(pkg._abi.G4Error) as e:
+        ctx.decode_batch(np.arange(B), toks, pos)
+    assert e.value.code == G4_ERR_TIMEOUT
+    out = ctx.decode_batch(np.arange(B), toks, pos)
+    for b in (0, 11, B - 1):
+        ref, _ = om.generate(prompts[b], 2, 64)
+        assert out[b] == ref[1], b
+    assert lib.g4_debug_raise_error_flag(ctx.h, 4) == -1      # no such unit
+    ctx.close()
+
+
 def test_wait_probe_rejects_bad_arguments(lib, cuda):
     torch = cuda
     src = torch.zeros(64, dtype=torch.uint8, device="cuda")
