@@ -79,8 +79,8 @@ def token_bytes(ctx_len: int) -> dict:
 GEMV_N, GEMV_K = 6144, 1536
 GEMV_BYTES = GEMV_N * GEMV_K // 2 + 2 * GEMV_N + GEMV_K + 2 * GEMV_N  # W + scales + x(int8) + y(f16)
 # dram__bytes_read.sum + dram__bytes_write.sum of one config-1 GEMV launch, from an ncu capture
-# of this kernel on the config-1 shape (the weights cross DRAM once).
-GEMV_TRAFFIC = 4_792_832
+# of this kernel (int8 codes in) on the config-1 shape (the weights cross DRAM once).
+GEMV_TRAFFIC = 4_779_776
 
 
 def load_peaks() -> dict:
