@@ -205,6 +205,34 @@ def test_prefill_chunking_and_sliced_table(pkg, O, tiny):
     ctx.close()
 
 
+def test_cluster_merged_attention_long_contexts(pkg, O):
+    """Decode steps whose one-head attention CTAs of a (column, head) span 9 (sliding window 512)
+    and 11 (global, a 700-position cache) blocks: clusters past the portable size of 8, whose
+    first block merges the partials from its own shared memory. Logits bit-identical to the
+    oracle at B=1, and tokens equal to the oracle's for a three-sequence batch whose contexts
+    span 2 to 11 blocks."""
+    a = entry.tiny_arch(pkg)
+    a.sliding_window = 512
+    om = O.Model(SEED, entry.oracle_arch(O, a))
+    ctx = make_ctx(pkg, a, max_seqs=4, max_context=700, max_step_columns=64)
+    prompt = O.synth_prompt(SEED + 71, 600, a.vocab_size)
+    want, want_logits = oracle_run(O, om, prompt, 3, 700)
+    tok = ctx.prefill(0, prompt, 0, True)
+    got = [tok]
+    for i in range(1, 3):
+        got.append(ctx.decode(0, got[-1], len(prompt) + i - 1))
+        np.testing.assert_array_equal(ctx.logits(0).view(np.uint32), want_logits[i].view(np.uint32))
+    assert got == list(want)
+    lens = [90, 330, 650]
+    prompts = [O.synth_prompt(SEED + 80 + b, n, a.vocab_size) for b, n in enumerate(lens)]
+    toks = [ctx.prefill(1 + b, prompts[b], 0, True) for b in range(3)]
+    out = ctx.decode_batch(np.arange(1, 4), toks, lens)
+    for b in range(3):
+        ref, _ = om.generate(prompts[b], 2, 700)
+        assert out[b] == ref[1], b
+    ctx.close()
+
+
 def test_invalid_calls(pkg, tiny):
     a, _ = tiny
     ctx = make_ctx(pkg, a)
